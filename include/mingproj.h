@@ -1,0 +1,190 @@
+/*
+ * mingproj — C-ABI of the B200 (sm_100a) kernel library for the Ming-Image
+ * DiT's block-linear hot path: the seven LoRA-able projections of every
+ * block (to_q, to_k, to_v, to_out.0, feed_forward.w1 / w3 / w2) and the
+ * per-block adaLN modulation Linear.
+ *
+ * Reference interface this replaces (vpipe-ming-image, paths relative to
+ * that project):
+ *   - the `lin` lambda of MingDitMetal::forward, src/ming-dit.cc:1763-1771
+ *       lin(x, x_elem_off, QWeight, y, y_elem_off, M, N, K, lora::Stack)
+ *     = `lin_base` (src/ming-dit.cc:1721-1758) + lora::Applier::apply;
+ *   - `fill_mod`, src/ming-dit.cc:2266-2273 (adaLN Linear + bias + fold);
+ *   - `load_qw_` / QWeight, src/ming-dit.cc:802-831 and :446-452 (pack
+ *     upload), with the pack shapes pinned by tests/ming-quant-test.cc:
+ *     526-530;
+ *   - `bind_loras_` / `lora_for_` / `set_lora_scale`,
+ *     src/ming-dit.cc:2918-3039 (slot binding and live strengths).
+ *
+ * Conventions:
+ *   - Plain pointers and sizes only. Device pointers are CUDA device
+ *     addresses on the context's device; "host or device" arguments are
+ *     copied with unified addressing and may be either.
+ *   - Every call returns an mp_status. Nothing aborts or exits. On failure
+ *     mp_last_error() says why.
+ *   - One host thread per context. Launches are stream-ordered on the
+ *     stream passed in (a cudaStream_t; NULL = the legacy default stream).
+ *   - Strengths in force when a projection is enqueued are captured by
+ *     value into that launch.
+ */
+#ifndef MINGPROJ_H
+#define MINGPROJ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MP_MAX_SLOTS 8     /* src/ming-dit.h:117 kMaxLoraSlots; src/ming-model-config-stage.h:45 */
+#define MP_MAX_SEGMENTS 16 /* row segments with their own strength vector */
+#define MP_GROUP 64        /* quantization group along K (src/ming-quant-family.h:31-47) */
+
+typedef enum {
+  MP_OK = 0,
+  MP_EINVAL = 1,   /* bad argument: shape, alignment, slot, rank */
+  MP_ENOMEM = 2,   /* device allocation failed */
+  MP_ECUDA = 3,    /* a CUDA runtime / driver call failed (includes "no device") */
+  MP_ETIMEOUT = 4  /* a device-side bounded wait gave up (reported by mp_sync_check) */
+} mp_status;
+
+typedef enum {
+  MP_QUANT_AFFINE = 0,    /* w = scale * q + bias, q unsigned (w8: 0..255, w4: 0..15) */
+  MP_QUANT_SYMMETRIC = 1  /* w = scale * q, q signed 8-bit (-127..127), no bias */
+} mp_quant_mode;
+
+typedef struct mp_ctx mp_ctx;
+typedef struct mp_weight mp_weight;
+typedef struct mp_modset mp_modset;
+
+/* One projection weight, torch Linear layout [n out, k in]. */
+typedef struct {
+  int32_t n;     /* output features */
+  int32_t k;     /* input features; multiple of 64 */
+  int32_t bits;  /* 0 = dense bf16, 8 or 4 = packed codes */
+  int32_t group; /* must be MP_GROUP for packed weights */
+  int32_t mode;  /* mp_quant_mode, packed weights only */
+} mp_weight_desc;
+
+/* What the context ran, counted at the launch site (the reference's
+ * DitEngagement, src/ming-dit.h:55-103, restricted to this path). */
+typedef struct {
+  int64_t linear_calls; /* projections run */
+  int64_t lora_proj;    /* of those, projections carrying >= 1 live adapter */
+  int64_t gemm_w8;      /* projections whose base was packed 8-bit */
+  int64_t gemm_w4;      /* ... packed 4-bit */
+  int64_t gemm_dense;   /* ... dense bf16 */
+  int64_t lora_down;    /* rank-space pre-GEMM launches */
+  int64_t modulation;   /* batched modulation launches */
+  int64_t kernels;      /* kernel launches of this library */
+  double flops;         /* algorithmic FLOPs: 2MNK + sum_live 2 M r (K + N), modulation 2 M N K */
+  double bytes;         /* minimal HBM bytes: weights + factors + x + y */
+} mp_engagement;
+
+/* ---- context ---------------------------------------------------------- */
+
+/* Replaces: the per-DiT Metal state set up by MingDitMetal::load_
+ * (src/ming-dit.cc:1076-1415). Binds `device`; fails with MP_ECUDA when no
+ * CUDA device is usable. */
+int mp_create(int device, mp_ctx** out);
+int mp_destroy(mp_ctx* ctx);
+/* Last failure message of this context (never NULL). */
+const char* mp_last_error(const mp_ctx* ctx);
+/* Name of a status code. */
+const char* mp_status_string(int status);
+/* Synchronizes `stream` and reports device-side failures: MP_ETIMEOUT when
+ * any kernel of this context gave up a bounded wait since the last check.
+ * Replaces: the commit/wait of the forward (src/ming-dit.cc:2564-2571). */
+int mp_sync_check(mp_ctx* ctx, void* stream);
+/* Device-side wait limit in nanoseconds (default 2e9). */
+int mp_set_wait_limit(mp_ctx* ctx, uint64_t ns);
+
+/* ---- weights ---------------------------------------------------------- */
+
+/* Uploads one projection weight. Replaces: load_qw_ (src/ming-dit.cc:
+ * 802-831) — codes uploaded raw, scales/biases narrowed to bf16 (:816-822).
+ *   packed: `data` = U32 codes [n, k*bits/32] exactly as the pack stores
+ *           them (code j of a word at bits [j*bits, (j+1)*bits)), `scales`
+ *           and `biases` = bf16 [n, k/64] (`biases` NULL for symmetric);
+ *   dense:  `data` = bf16 [n, k]; scales/biases NULL.
+ * All pointers host or device. */
+int mp_weight_upload(mp_ctx* ctx, const mp_weight_desc* desc, const void* data,
+                     const uint16_t* scales, const uint16_t* biases, mp_weight** out);
+int mp_weight_free(mp_ctx* ctx, mp_weight* w);
+/* Reads back the stored codes bytes (or dense weight) into `dst` (host or
+ * device, `bytes` long) — the bit-exact upload round trip. */
+int mp_weight_read_codes(mp_ctx* ctx, const mp_weight* w, void* dst, size_t bytes);
+
+/* ---- LoRA slots ------------------------------------------------------- */
+
+/* Binds slot `slot` of weight `w`: a = bf16 [rank, k] with the adapter's
+ * alpha/rank already folded in, b = bf16 [n, rank]; host or device.
+ * Replaces: Adapter::bind per projection inside bind_loras_
+ * (src/ming-dit.cc:2954-2968). A shape the caller got wrong returns
+ * MP_EINVAL; the caller refuses the whole slot, as bind_loras_ does
+ * (:2971-2983). Rebinding a slot replaces its factors. */
+int mp_lora_bind(mp_ctx* ctx, mp_weight* w, int slot, const uint16_t* a, const uint16_t* b,
+                 int rank);
+int mp_lora_unbind(mp_ctx* ctx, mp_weight* w, int slot);
+
+/* Live strength of `slot` for every projection of the context. Exactly 0
+ * drops the slot from the stacked contraction: the result is then
+ * bit-identical to a launch without that slot. Replaces: set_lora_scale
+ * (src/ming-dit.cc:3024-3039). Default 1.0. */
+int mp_set_strength(mp_ctx* ctx, int slot, float s);
+int mp_get_strength(const mp_ctx* ctx, int slot, float* s);
+/* Per-row-segment strengths (a batch of images with their own strength
+ * vectors): `s` = float [batch][MP_MAX_SLOTS], `row_starts` = int32
+ * [batch + 1] token-row boundaries of the x passed to the next launches.
+ * batch = 0 returns to the per-slot strengths. No counterpart in the
+ * reference (one strength per slot there); it extends a6 to batches. */
+int mp_set_strengths_rows(mp_ctx* ctx, const float* s, const int32_t* row_starts, int batch);
+
+/* ---- projections ------------------------------------------------------ */
+
+/* y[m, n] = x[m, k] · deq(W)^T + sum over live slots s_i · (x A_i^T) B_i^T,
+ * bf16 in / bf16 out, f32 accumulation, one pass over K with the adapters
+ * appended as extra K tiles. x: device bf16, 16-byte aligned, ldx a
+ * multiple of 8 elements. y: device bf16, ldy >= n.
+ * Replaces: lin (src/ming-dit.cc:1763-1771). */
+int mp_linear(mp_ctx* ctx, const mp_weight* w, const void* x, int64_t ldx, void* y, int64_t ldy,
+              int m, void* stream);
+
+/* `count` projections of the same input x (q/k/v, or w1/w3): the rank-space
+ * pre-GEMM of all their live adapters runs ONCE over x, then each base
+ * projection. Replaces: the three (two) consecutive lin calls on `nrm` at
+ * src/ming-dit.cc:2078-2080 and :2155-2156. */
+int mp_linear_shared(mp_ctx* ctx, const mp_weight* const* ws, void* const* ys,
+                     const int64_t* ldys, int count, const void* x, int64_t ldx, int m,
+                     void* stream);
+
+/* ---- modulation -------------------------------------------------------- */
+
+/* The adaLN Linears of `n_blocks` modulated blocks, prepared for one
+ * batched launch. ada[i]: weight [4H, K_ada] (packed or dense); ada_bias[i]:
+ * bf16 [4H]; an1[i] / fn1[i]: bf16 [H] norm gains to fold (1 + scale) into,
+ * or NULL. Host or device pointers. Replaces: the per-block adaLN weights
+ * loaded by load_block_ (src/ming-dit.cc:858-864). */
+int mp_modulation_create(mp_ctx* ctx, int n_blocks, const mp_weight* const* ada,
+                         const uint16_t* const* ada_bias, const uint16_t* const* an1,
+                         const uint16_t* const* fn1, mp_modset** out);
+int mp_modulation_free(mp_ctx* ctx, mp_modset* set);
+/* mods[b, i, :] = W_b · temb[i] + bias_b (bf16 [n_blocks, m, 4H]);
+ * nw1[b, i, :] = an1_b · (1 + mods[b, i, 0:H]), nw3[b, i, :] = fn1_b ·
+ * (1 + mods[b, i, 2H:3H]) (bf16 [n_blocks, m, H]; either may be NULL).
+ * temb: device bf16 [m, K_ada], m <= 4. Replaces: fill_mod
+ * (src/ming-dit.cc:2266-2273) for every modulated block at once. */
+int mp_modulation_all(mp_ctx* ctx, const mp_modset* set, const void* temb, int m, void* mods,
+                      void* nw1, void* nw3, void* stream);
+
+/* ---- engagement -------------------------------------------------------- */
+
+int mp_engagement_get(const mp_ctx* ctx, mp_engagement* out);
+int mp_engagement_reset(mp_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MINGPROJ_H */

@@ -1,0 +1,141 @@
+"""The oracle itself: its C and numpy restatements agree, the pack code layout
+round-trips bit-exactly, and the structural facts the reference's tests pin
+hold (pack shapes and dtypes, detection rule, FLOP formula)."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from mingproj import pack as P
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_pack_unpack_round_trip(bits):
+    rng = np.random.default_rng(bits)
+    q = rng.integers(0, 1 << bits, size=(37, 256), dtype=np.int32)
+    codes = P.pack_codes(q, bits)
+    # tests/ming-quant-test.cc:526-530: codes U32 [N, K*bits/32]
+    assert codes.dtype == np.uint32 and codes.shape == (37, 256 * bits // 32)
+    assert np.array_equal(O.unpack_codes(codes, 256, bits), q)
+    assert np.array_equal(O.unpack_codes_np(codes, 256, bits), q)
+    assert np.array_equal(O.pack_codes(q, bits), codes)
+    assert np.array_equal(O.pack_codes_np(q, bits), codes)
+
+
+def test_code_order_lsb_first():
+    # code j of a word at bits [j*bits, (j+1)*bits): a known-answer word
+    q8 = np.array([[0x11, 0x22, 0x33, 0x44]], dtype=np.int32)
+    assert P.pack_codes(q8, 8)[0, 0] == 0x44332211
+    q4 = np.array([[1, 2, 3, 4, 5, 6, 7, 8]], dtype=np.int32)
+    assert P.pack_codes(q4, 4)[0, 0] == 0x87654321
+
+
+def test_symmetric_codes_are_signed_bytes():
+    q = np.array([[-127, -1, 0, 127]], dtype=np.int32)
+    codes = P.pack_codes(q, 8)
+    assert np.array_equal(O.unpack_codes(codes, 4, 8, symmetric=True), q)
+    assert np.array_equal(O.unpack_codes_np(codes, 4, 8, symmetric=True), q)
+
+
+def test_dequant_known_answer():
+    # one row, one group: w = s*q + b with exactly representable values
+    q = np.arange(64, dtype=np.int32)[None, :] % 16
+    codes = P.pack_codes(q, 4)
+    s = P.f32_to_bf16_bits(np.array([[0.5]], dtype=np.float32))
+    b = P.f32_to_bf16_bits(np.array([[-4.0]], dtype=np.float32))
+    w = O.dequant(codes, s, b, 1, 64, 4)
+    assert np.array_equal(w, 0.5 * q - 4.0)
+    assert np.array_equal(O.dequant_np(codes, s, b, 1, 64, 4), w)
+
+
+@pytest.mark.parametrize("bits,sym", [(0, False), (8, False), (4, False), (8, True)])
+def test_c_oracle_matches_numpy(bits, sym):
+    rng = np.random.default_rng(5 + bits)
+    n, k, m = 96, 192, 17
+    if bits == 0:
+        pw = P.synthetic_dense(rng, n, k)
+    elif sym:
+        pw = P.synthetic_symmetric_w8(rng, n, k)
+    else:
+        pw = P.synthetic_affine(rng, n, k, bits)
+    x = P.f32_to_bf16_bits(rng.normal(size=(m, k)).astype(np.float32))
+    slots = []
+    for r, s in ((4, 0.7), (8, 0.0), (16, -1.1)):
+        a, b = P.synthetic_lora(rng, n, k, r)
+        slots.append((a, b, s))
+    yc = O.projection(x, pw.data, pw.scales, pw.biases, n, k, bits, sym, slots)
+    yn = O.projection_np(x, pw.data, pw.scales, pw.biases, n, k, bits, sym, slots)
+    assert np.allclose(yc, yn, rtol=1e-12, atol=1e-12)
+
+
+def test_pure_python_loop_agrees_on_tiny_case():
+    rng = np.random.default_rng(9)
+    n, k, m = 3, 64, 2
+    pw = P.synthetic_affine(rng, n, k, 8)
+    x = P.f32_to_bf16_bits(rng.normal(size=(m, k)).astype(np.float32))
+    a, b = P.synthetic_lora(rng, n, k, 2)
+    q = O.unpack_codes_np(pw.data, k, 8)
+    xs = O.bf16_to_f64(x)
+    sc, bi = O.bf16_to_f64(pw.scales), O.bf16_to_f64(pw.biases)
+    af, bf = O.bf16_to_f64(a), O.bf16_to_f64(b)
+    want = np.zeros((m, n))
+    for r in range(m):
+        for c in range(n):
+            acc = 0.0
+            for i in range(k):
+                acc += xs[r, i] * (sc[c, i // 64] * q[c, i] + bi[c, i // 64])
+            for j in range(2):
+                t = sum(xs[r, i] * af[j, i] for i in range(k))
+                acc += 0.5 * t * bf[c, j]
+            want[r, c] = acc
+    got = O.projection(x, pw.data, pw.scales, pw.biases, n, k, 8, False, [(a, b, 0.5)])
+    assert np.allclose(got, want, rtol=1e-12, atol=1e-12)
+
+
+def test_detection_rule():
+    # src/ming-dit.cc:1115-1135 on the pinned pack shapes
+    H = 3840
+    assert P.detect_bits((3840, 960), (3840, 60), H) == (8, 64)
+    assert P.detect_bits((3840, 480), (3840, 60), H) == (4, 64)
+    assert P.detect_bits((10240, 960), (10240, 60), H) == (8, 64)
+    # detection reads block 0's to_q (K = hidden); w2's K = 10240 then follows
+    # from the detected group, per tensor
+    assert P.tensor_bits((3840, 2560), (3840, 160), 64) == 8
+    assert P.tensor_bits((3840, 1280), (3840, 160), 64) == 4
+    assert P.detect_bits((3840, 700), (3840, 60), H)[0] == 0       # neither 4 nor 8: dense
+
+
+def test_selection_counts_match_reference_pin():
+    # tests/ming-quant-test.cc:547-551: 32*(7+adaLN) + 2*7 quantized, 7 model-level dense
+    names = []
+    for pre, n, ada in (("context_refiner", 2, False), ("noise_refiner", 2, True),
+                        ("layers", 30, True)):
+        for i in range(n):
+            for p in P.PROJ_NAMES + (("adaLN_modulation.0",) if ada else ()):
+                names += [f"{pre}.{i}.{p}.weight", f"{pre}.{i}.{p}.scales",
+                          f"{pre}.{i}.{p}.biases"]
+            names += [f"{pre}.{i}.attention_norm1.weight"]
+    names += ["all_x_embedder.2-1.weight", "cap_embedder.0.weight", "cap_embedder.1.weight",
+              "t_embedder.mlp.0.weight", "t_embedder.mlp.2.weight",
+              "all_final_layer.2-1.adaLN_modulation.1.weight",
+              "all_final_layer.2-1.linear.weight"]
+    c = P.selection_counts(names)
+    assert c["quantized"] == 32 * 8 + 2 * 7
+    assert c["dense_model"] == 7
+
+
+def test_rel_l2_matches_reference_definition():
+    a = np.array([1.0, 2.0, 3.0])
+    b = np.array([1.0, 2.0, 4.0])
+    assert abs(O.rel_l2(a, b) - np.sqrt(1.0 / 21.0)) < 1e-15
+    assert O.rel_l2(a, a) == 0.0
+    assert O.rel_l2(a, b[:2]) == 1.0
+
+
+def test_bf16_rounding_matches_torch():
+    import torch
+    rng = np.random.default_rng(3)
+    f = rng.normal(size=4096).astype(np.float32) * 10.0 ** rng.integers(-5, 5, size=4096)
+    mine = P.f32_to_bf16_bits(f)
+    ref = torch.from_numpy(f).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(mine, ref)
+    assert np.array_equal(O.f32_to_bf16(f), ref)

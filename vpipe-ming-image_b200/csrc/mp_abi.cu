@@ -1,0 +1,820 @@
+// Host side of the mingproj C-ABI (include/mingproj.h): contexts, weight
+// upload, LoRA slot binding and the stacked-adapter cache, launch assembly
+// for the projection and modulation kernels, engagement counters.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <climits>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/mingproj.h"
+#include "mp_kernels.h"
+
+namespace mp {
+cudaError_t launch_proj(const ProjParams& p, cudaStream_t stream);
+cudaError_t launch_mod(const ModParams& p, cudaStream_t stream);
+}  // namespace mp
+
+using mp::ProjParams;
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+  }
+  return fn;
+}
+
+struct Stack {
+  bool valid = false;
+  uint32_t mask = 0;       // live slots the stack was built for
+  uint64_t bind_version = 0;
+  int rpad = 0;            // stacked rank, padded to 64
+  int ranks[mp::kMaxSlots] = {};
+  uint16_t* a = nullptr;   // [rpad, k]
+  size_t a_cap = 0;
+  uint16_t* b = nullptr;   // [n, rpad]
+  size_t b_cap = 0;
+  CUtensorMap tm_a;        // box {64, 128}, SW128 (LoRA-down "weight")
+  CUtensorMap tm_b;        // box {64, 128}, SW128 (appended K tiles)
+  uint64_t version = 0;
+};
+
+}  // namespace
+
+struct mp_weight {
+  mp_weight_desc d{};
+  void* w = nullptr;       // codes bytes [n, k*bits/8] or bf16 [n, k]
+  size_t w_bytes = 0;
+  uint32_t* sb = nullptr;  // [n, sb_stride] (bf16 scale | bf16 bias << 16)
+  int sb_stride = 0;
+  CUtensorMap tm_w;
+  int rank[mp::kMaxSlots] = {};
+  uint16_t* la[mp::kMaxSlots] = {};  // [rank, k]
+  uint16_t* lb[mp::kMaxSlots] = {};  // [n, rank]
+  uint64_t bind_version = 1;
+  Stack stack;
+};
+
+struct mp_modset {
+  int n_blocks = 0;
+  int n = 0, k = 0, bits = 0, mode = 0, sb_stride = 0;
+  mp::ModBlock* dev_blocks = nullptr;
+  std::vector<void*> owned;  // bias / gain copies
+};
+
+namespace {
+
+struct SharedStack {
+  std::vector<uint64_t> versions;
+  uint16_t* a = nullptr;
+  size_t a_cap = 0;
+  int rtot = 0;
+  CUtensorMap tm_a;
+};
+
+}  // namespace
+
+struct mp_ctx {
+  int device = 0;
+  std::string err = "";
+  float strength[mp::kMaxSlots];
+  int n_seg = 0;
+  int32_t seg_start[mp::kMaxSegments + 1] = {};
+  float seg_scale[mp::kMaxSegments][mp::kMaxSlots] = {};
+  uint32_t* err_word = nullptr;
+  uint16_t* scratch = nullptr;  // rank-space intermediate
+  size_t scratch_cap = 0;       // elements
+  uint64_t wait_limit_ns = 2000000000ull;
+  mp_engagement eng{};
+  std::map<std::vector<uintptr_t>, SharedStack> shared;
+};
+
+namespace {
+
+int fail(mp_ctx* c, int code, const char* fmt, ...) {
+  if (c != nullptr) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    c->err = buf;
+  }
+  return code;
+}
+
+int cuda_fail(mp_ctx* c, cudaError_t e, const char* what) {
+  return fail(c, e == cudaErrorMemoryAllocation ? MP_ENOMEM : MP_ECUDA, "%s: %s", what,
+              cudaGetErrorString(e));
+}
+
+#define MP_CUDA(ctx, call)                               \
+  do {                                                   \
+    cudaError_t e_ = (call);                             \
+    if (e_ != cudaSuccess) return cuda_fail(ctx, e_, #call); \
+  } while (0)
+
+int use_device(mp_ctx* c) {
+  cudaError_t e = cudaSetDevice(c->device);
+  if (e != cudaSuccess) return cuda_fail(c, e, "cudaSetDevice");
+  return MP_OK;
+}
+
+bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner,
+               uint64_t outer, uint64_t stride_bytes, uint32_t box_inner, uint32_t box_outer,
+               CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Token rows per CTA tile: the widest tile that still fills the GPU, else 64.
+int pick_ntok(int m, int n) {
+  const int ntiles = (n + mp::kBlockN - 1) / mp::kBlockN;
+  for (int nt : {256, 128}) {
+    if (static_cast<long>(ntiles) * ((m + nt - 1) / nt) >= 148) return nt;
+  }
+  return 64;
+}
+
+uint32_t live_mask(const mp_ctx* c, const mp_weight* w) {
+  uint32_t mask = 0;
+  for (int i = 0; i < mp::kMaxSlots; ++i) {
+    if (w->rank[i] <= 0) continue;
+    bool live = false;
+    if (c->n_seg > 0) {
+      for (int g = 0; g < c->n_seg; ++g) live = live || c->seg_scale[g][i] != 0.0f;
+    } else {
+      live = c->strength[i] != 0.0f;
+    }
+    if (live) mask |= 1u << i;
+  }
+  return mask;
+}
+
+template <class T>
+int ensure_buf(mp_ctx* c, T** p, size_t* cap, size_t elems, cudaStream_t stream) {
+  if (*cap >= elems && *p != nullptr) return MP_OK;
+  if (*p != nullptr) {
+    cudaStreamSynchronize(stream);
+    cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+  }
+  void* q = nullptr;
+  cudaError_t e = cudaMalloc(&q, std::max<size_t>(elems, 1) * sizeof(T));
+  if (e != cudaSuccess) return cuda_fail(c, e, "cudaMalloc");
+  *p = static_cast<T*>(q);
+  *cap = elems;
+  return MP_OK;
+}
+
+// Builds (or reuses) the stacked factors of the live slots of `w`, in slot
+// order: A rows [r_0 | r_1 | ...] padded with zero rows to a multiple of 64,
+// B columns in the same order, zero-padded.
+int ensure_stack(mp_ctx* c, mp_weight* w, uint32_t mask, cudaStream_t stream) {
+  Stack& st = w->stack;
+  if (st.valid && st.mask == mask && st.bind_version == w->bind_version) return MP_OK;
+  const int n = w->d.n, k = w->d.k;
+  int rtot = 0;
+  for (int i = 0; i < mp::kMaxSlots; ++i)
+    if (mask & (1u << i)) rtot += w->rank[i];
+  const int rpad = (rtot + 63) / 64 * 64;
+  int rc = ensure_buf(c, &st.a, &st.a_cap, static_cast<size_t>(rpad) * k, stream);
+  if (rc != MP_OK) return rc;
+  rc = ensure_buf(c, &st.b, &st.b_cap, static_cast<size_t>(n) * rpad, stream);
+  if (rc != MP_OK) return rc;
+  MP_CUDA(c, cudaMemsetAsync(st.a, 0, static_cast<size_t>(rpad) * k * 2, stream));
+  MP_CUDA(c, cudaMemsetAsync(st.b, 0, static_cast<size_t>(n) * rpad * 2, stream));
+  int off = 0;
+  for (int i = 0; i < mp::kMaxSlots; ++i) {
+    st.ranks[i] = 0;
+    if (!(mask & (1u << i))) continue;
+    const int r = w->rank[i];
+    st.ranks[i] = r;
+    MP_CUDA(c, cudaMemcpyAsync(st.a + static_cast<size_t>(off) * k, w->la[i],
+                               static_cast<size_t>(r) * k * 2, cudaMemcpyDeviceToDevice, stream));
+    MP_CUDA(c, cudaMemcpy2DAsync(st.b + off, static_cast<size_t>(rpad) * 2, w->lb[i],
+                                 static_cast<size_t>(r) * 2, static_cast<size_t>(r) * 2, n,
+                                 cudaMemcpyDeviceToDevice, stream));
+    off += r;
+  }
+  if (rpad > 0) {
+    if (!encode_2d(&st.tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st.a, k, rpad,
+                   static_cast<uint64_t>(k) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_2d(&st.tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st.b, rpad, n,
+                   static_cast<uint64_t>(rpad) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+      return fail(c, MP_ECUDA, "tensor map encode failed (LoRA stack)");
+  }
+  st.rpad = rpad;
+  st.mask = mask;
+  st.bind_version = w->bind_version;
+  st.valid = true;
+  st.version += 1;
+  return MP_OK;
+}
+
+void fill_scale(const mp_ctx* c, mp::EpilogueScale* es) {
+  es->enabled = 1;
+  if (c->n_seg > 0) {
+    es->n_seg = c->n_seg;
+    for (int g = 0; g <= c->n_seg; ++g) es->seg_start[g] = c->seg_start[g];
+    for (int g = 0; g < c->n_seg; ++g)
+      for (int i = 0; i < mp::kMaxSlots; ++i) es->seg_scale[g][i] = c->seg_scale[g][i];
+  } else {
+    es->n_seg = 1;
+    es->seg_start[0] = 0;
+    es->seg_start[1] = INT_MAX;
+    for (int i = 0; i < mp::kMaxSlots; ++i) es->seg_scale[0][i] = c->strength[i];
+  }
+}
+
+// Appends the slot ranges of one stack starting at rank column `base`.
+bool add_ranges(mp::EpilogueScale* es, const Stack& st, int base) {
+  int off = base;
+  for (int i = 0; i < mp::kMaxSlots; ++i) {
+    if (!(st.mask & (1u << i))) continue;
+    if (es->n_ranges >= mp::kMaxRanges) return false;
+    es->range_start[es->n_ranges] = off;
+    es->range_slot[es->n_ranges] = i;
+    off += st.ranks[i];
+    es->range_start[es->n_ranges + 1] = off;
+    es->n_ranges += 1;
+  }
+  return true;
+}
+
+int check_x(mp_ctx* c, const void* x, int64_t ldx, int k, int m) {
+  if (x == nullptr) return fail(c, MP_EINVAL, "x is NULL");
+  if (m <= 0) return fail(c, MP_EINVAL, "m must be positive (got %d)", m);
+  if (reinterpret_cast<uintptr_t>(x) % 16 != 0)
+    return fail(c, MP_EINVAL, "x must be 16-byte aligned");
+  if (ldx < k || ldx % 8 != 0)
+    return fail(c, MP_EINVAL, "ldx must be >= k and a multiple of 8 (got %lld)",
+                static_cast<long long>(ldx));
+  return MP_OK;
+}
+
+void base_params(const mp_ctx* c, ProjParams* p) {
+  std::memset(p, 0, sizeof(*p));
+  p->wait_limit_ns = c->wait_limit_ns;
+  p->err = c->err_word;
+}
+
+// Rank-space pre-GEMM: T[m, 0:rtot] = scale ⊙ (x · A^T), into ctx scratch.
+int launch_lora_down(mp_ctx* c, const CUtensorMap& tm_a, int rtot, const mp::EpilogueScale& es,
+                     const void* x, int64_t ldx, int k, int m, cudaStream_t stream) {
+  ProjParams p;
+  base_params(c, &p);
+  const int ntok = pick_ntok(m, rtot);
+  if (!encode_2d(&p.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, k, m,
+                 static_cast<uint64_t>(ldx) * 2, 64, ntok, CU_TENSOR_MAP_SWIZZLE_128B))
+    return fail(c, MP_ECUDA, "tensor map encode failed (x)");
+  p.tm_w = tm_a;
+  p.sb = nullptr;
+  p.y = c->scratch;
+  p.ldy = rtot;
+  p.M = m;
+  p.N = rtot;
+  p.K = k;
+  p.bits = 0;
+  p.n_tok = ntok;
+  p.lora_ktiles = 0;
+  p.scale = es;
+  cudaError_t e = mp::launch_proj(p, stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "proj_kernel (lora down)");
+  c->eng.lora_down += 1;
+  c->eng.kernels += 1;
+  return MP_OK;
+}
+
+int launch_base(mp_ctx* c, const mp_weight* w, const void* x, int64_t ldx, void* y, int64_t ldy,
+                int m, const Stack* st, int t_col, int t_ld, cudaStream_t stream) {
+  ProjParams p;
+  base_params(c, &p);
+  const int n = w->d.n, k = w->d.k;
+  const int ntok = pick_ntok(m, n);
+  if (!encode_2d(&p.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, k, m,
+                 static_cast<uint64_t>(ldx) * 2, 64, ntok, CU_TENSOR_MAP_SWIZZLE_128B))
+    return fail(c, MP_ECUDA, "tensor map encode failed (x)");
+  p.tm_w = w->tm_w;
+  p.sb = w->sb;
+  p.sb_stride = w->sb_stride;
+  p.y = y;
+  p.ldy = ldy;
+  p.M = m;
+  p.N = n;
+  p.K = k;
+  p.bits = w->d.bits;
+  const bool sym = w->d.bits == 8 && w->d.mode == MP_QUANT_SYMMETRIC;
+  p.code_xor = sym ? 0x80808080u : 0u;
+  p.code_magic = sym ? 8388736.0f : 8388608.0f;
+  p.n_tok = ntok;
+  if (st != nullptr && st->rpad > 0) {
+    p.lora_ktiles = st->rpad / 64;
+    const uint16_t* tbase = c->scratch + t_col;
+    if (!encode_2d(&p.tm_t, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, tbase, st->rpad, m,
+                   static_cast<uint64_t>(t_ld) * 2, 64, ntok, CU_TENSOR_MAP_SWIZZLE_128B))
+      return fail(c, MP_ECUDA, "tensor map encode failed (rank-space intermediate)");
+    p.tm_b = st->tm_b;
+  }
+  cudaError_t e = mp::launch_proj(p, stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "proj_kernel");
+  c->eng.kernels += 1;
+  c->eng.linear_calls += 1;
+  if (w->d.bits == 8) c->eng.gemm_w8 += 1;
+  else if (w->d.bits == 4) c->eng.gemm_w4 += 1;
+  else c->eng.gemm_dense += 1;
+  double flops = 2.0 * m * n * static_cast<double>(k);
+  double bytes = static_cast<double>(w->w_bytes) + static_cast<double>(n) * (k / 64) * 4.0 +
+                 2.0 * m * k + 2.0 * m * n;
+  if (st != nullptr && st->rpad > 0) {
+    c->eng.lora_proj += 1;
+    for (int i = 0; i < mp::kMaxSlots; ++i) {
+      flops += 2.0 * m * st->ranks[i] * static_cast<double>(k + n);
+      bytes += 2.0 * st->ranks[i] * static_cast<double>(k + n);
+    }
+  }
+  c->eng.flops += flops;
+  c->eng.bytes += bytes;
+  return MP_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mp_status_string(int s) {
+  switch (s) {
+    case MP_OK: return "MP_OK";
+    case MP_EINVAL: return "MP_EINVAL";
+    case MP_ENOMEM: return "MP_ENOMEM";
+    case MP_ECUDA: return "MP_ECUDA";
+    case MP_ETIMEOUT: return "MP_ETIMEOUT";
+    default: return "MP_UNKNOWN";
+  }
+}
+
+int mp_create(int device, mp_ctx** out) {
+  if (out == nullptr) return MP_EINVAL;
+  *out = nullptr;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count <= 0) {
+    cudaGetLastError();
+    return MP_ECUDA;
+  }
+  if (device < 0 || device >= count) return MP_EINVAL;
+  if (cudaSetDevice(device) != cudaSuccess) return MP_ECUDA;
+  if (encode_fn() == nullptr) return MP_ECUDA;
+  mp_ctx* c = new mp_ctx();
+  c->device = device;
+  for (int i = 0; i < mp::kMaxSlots; ++i) c->strength[i] = 1.0f;
+  if (cudaMalloc(&c->err_word, sizeof(uint32_t)) != cudaSuccess ||
+      cudaMemset(c->err_word, 0, sizeof(uint32_t)) != cudaSuccess) {
+    delete c;
+    return MP_ENOMEM;
+  }
+  *out = c;
+  return MP_OK;
+}
+
+int mp_destroy(mp_ctx* c) {
+  if (c == nullptr) return MP_EINVAL;
+  cudaSetDevice(c->device);
+  cudaDeviceSynchronize();
+  cudaFree(c->err_word);
+  cudaFree(c->scratch);
+  for (auto& kv : c->shared) cudaFree(kv.second.a);
+  delete c;
+  return MP_OK;
+}
+
+const char* mp_last_error(const mp_ctx* c) { return c == nullptr ? "null context" : c->err.c_str(); }
+
+int mp_set_wait_limit(mp_ctx* c, uint64_t ns) {
+  if (c == nullptr || ns == 0) return MP_EINVAL;
+  c->wait_limit_ns = ns;
+  return MP_OK;
+}
+
+int mp_sync_check(mp_ctx* c, void* stream) {
+  if (c == nullptr) return MP_EINVAL;
+  int rc = use_device(c);
+  if (rc != MP_OK) return rc;
+  MP_CUDA(c, cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  uint32_t word = 0;
+  MP_CUDA(c, cudaMemcpy(&word, c->err_word, sizeof(word), cudaMemcpyDeviceToHost));
+  if (word != 0) {
+    MP_CUDA(c, cudaMemset(c->err_word, 0, sizeof(uint32_t)));
+    return fail(c, MP_ETIMEOUT, "a kernel gave up a bounded device-side wait (word 0x%x)", word);
+  }
+  return MP_OK;
+}
+
+int mp_weight_upload(mp_ctx* c, const mp_weight_desc* d, const void* data, const uint16_t* scales,
+                     const uint16_t* biases, mp_weight** out) {
+  if (c == nullptr || d == nullptr || data == nullptr || out == nullptr) return MP_EINVAL;
+  *out = nullptr;
+  if (d->n <= 0 || d->k <= 0 || d->k % 64 != 0)
+    return fail(c, MP_EINVAL, "weight shape [%d, %d]: n > 0 and k a multiple of 64 required",
+                d->n, d->k);
+  if (d->bits != 0 && d->bits != 4 && d->bits != 8)
+    return fail(c, MP_EINVAL, "bits must be 0, 4 or 8 (got %d)", d->bits);
+  if (d->bits != 0) {
+    if (d->group != MP_GROUP) return fail(c, MP_EINVAL, "group must be 64 (got %d)", d->group);
+    if (scales == nullptr) return fail(c, MP_EINVAL, "packed weight without scales");
+    if (d->mode == MP_QUANT_AFFINE && biases == nullptr)
+      return fail(c, MP_EINVAL, "affine packed weight without biases");
+    if (d->mode == MP_QUANT_SYMMETRIC && d->bits != 8)
+      return fail(c, MP_EINVAL, "symmetric mode is 8-bit only");
+    if (d->mode != MP_QUANT_AFFINE && d->mode != MP_QUANT_SYMMETRIC)
+      return fail(c, MP_EINVAL, "unknown quant mode %d", d->mode);
+  }
+  int rc = use_device(c);
+  if (rc != MP_OK) return rc;
+  mp_weight* w = new mp_weight();
+  w->d = *d;
+  const size_t n = d->n, k = d->k;
+  w->w_bytes = d->bits == 0 ? n * k * 2 : n * k * d->bits / 8;
+  auto cleanup = [&](int code) {
+    cudaFree(w->w);
+    cudaFree(w->sb);
+    delete w;
+    return code;
+  };
+  cudaError_t e = cudaMalloc(&w->w, w->w_bytes);
+  if (e != cudaSuccess) return cleanup(cuda_fail(c, e, "cudaMalloc(weight)"));
+  e = cudaMemcpy(w->w, data, w->w_bytes, cudaMemcpyDefault);
+  if (e != cudaSuccess) return cleanup(cuda_fail(c, e, "cudaMemcpy(weight)"));
+  if (d->bits != 0) {
+    const int g = d->k / 64;
+    w->sb_stride = (g + 3) / 4 * 4;
+    std::vector<uint16_t> hs(n * g), hb(n * g, 0);
+    e = cudaMemcpy(hs.data(), scales, n * g * 2, cudaMemcpyDefault);
+    if (e == cudaSuccess && biases != nullptr)
+      e = cudaMemcpy(hb.data(), biases, n * g * 2, cudaMemcpyDefault);
+    if (e != cudaSuccess) return cleanup(cuda_fail(c, e, "cudaMemcpy(scales/biases)"));
+    std::vector<uint32_t> sb(n * w->sb_stride, 0);
+    for (size_t r = 0; r < n; ++r)
+      for (int j = 0; j < g; ++j)
+        sb[r * w->sb_stride + j] =
+            static_cast<uint32_t>(hs[r * g + j]) | (static_cast<uint32_t>(hb[r * g + j]) << 16);
+    e = cudaMalloc(&w->sb, sb.size() * 4);
+    if (e == cudaSuccess) e = cudaMemcpy(w->sb, sb.data(), sb.size() * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cleanup(cuda_fail(c, e, "sb upload"));
+    const uint64_t row_bytes = k * d->bits / 8;
+    const uint32_t box_inner = 64 * d->bits / 8;
+    if (!encode_2d(&w->tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->w, row_bytes, n, row_bytes,
+                   box_inner, 128,
+                   d->bits == 8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B))
+      return cleanup(fail(c, MP_ECUDA, "tensor map encode failed (codes)"));
+  } else {
+    if (!encode_2d(&w->tm_w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w->w, k, n, k * 2, 64, 128,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+      return cleanup(fail(c, MP_ECUDA, "tensor map encode failed (dense weight)"));
+  }
+  *out = w;
+  return MP_OK;
+}
+
+int mp_weight_free(mp_ctx* c, mp_weight* w) {
+  if (c == nullptr || w == nullptr) return MP_EINVAL;
+  cudaSetDevice(c->device);
+  cudaDeviceSynchronize();
+  cudaFree(w->w);
+  cudaFree(w->sb);
+  for (int i = 0; i < mp::kMaxSlots; ++i) {
+    cudaFree(w->la[i]);
+    cudaFree(w->lb[i]);
+  }
+  cudaFree(w->stack.a);
+  cudaFree(w->stack.b);
+  delete w;
+  return MP_OK;
+}
+
+int mp_weight_read_codes(mp_ctx* c, const mp_weight* w, void* dst, size_t bytes) {
+  if (c == nullptr || w == nullptr || dst == nullptr) return MP_EINVAL;
+  if (bytes != w->w_bytes)
+    return fail(c, MP_EINVAL, "read_codes: %zu bytes requested, weight holds %zu", bytes,
+                w->w_bytes);
+  int rc = use_device(c);
+  if (rc != MP_OK) return rc;
+  MP_CUDA(c, cudaMemcpy(dst, w->w, bytes, cudaMemcpyDefault));
+  return MP_OK;
+}
+
+int mp_lora_bind(mp_ctx* c, mp_weight* w, int slot, const uint16_t* a, const uint16_t* b,
+                 int rank) {
+  if (c == nullptr || w == nullptr) return MP_EINVAL;
+  if (slot < 0 || slot >= mp::kMaxSlots)
+    return fail(c, MP_EINVAL, "slot %d outside [0, %d)", slot, mp::kMaxSlots);
+  if (a == nullptr || b == nullptr) return fail(c, MP_EINVAL, "LoRA factor is NULL");
+  if (rank <= 0 || rank > 1024) return fail(c, MP_EINVAL, "rank %d outside [1, 1024]", rank);
+  int rc = use_device(c);
+  if (rc != MP_OK) return rc;
+  cudaDeviceSynchronize();
+  cudaFree(w->la[slot]);
+  cudaFree(w->lb[slot]);
+  w->la[slot] = w->lb[slot] = nullptr;
+  w->rank[slot] = 0;
+  const size_t na = static_cast<size_t>(rank) * w->d.k, nb = static_cast<size_t>(w->d.n) * rank;
+  MP_CUDA(c, cudaMalloc(&w->la[slot], na * 2));
+  MP_CUDA(c, cudaMalloc(&w->lb[slot], nb * 2));
+  MP_CUDA(c, cudaMemcpy(w->la[slot], a, na * 2, cudaMemcpyDefault));
+  MP_CUDA(c, cudaMemcpy(w->lb[slot], b, nb * 2, cudaMemcpyDefault));
+  w->rank[slot] = rank;
+  w->bind_version += 1;
+  return MP_OK;
+}
+
+int mp_lora_unbind(mp_ctx* c, mp_weight* w, int slot) {
+  if (c == nullptr || w == nullptr) return MP_EINVAL;
+  if (slot < 0 || slot >= mp::kMaxSlots)
+    return fail(c, MP_EINVAL, "slot %d outside [0, %d)", slot, mp::kMaxSlots);
+  int rc = use_device(c);
+  if (rc != MP_OK) return rc;
+  cudaDeviceSynchronize();
+  cudaFree(w->la[slot]);
+  cudaFree(w->lb[slot]);
+  w->la[slot] = w->lb[slot] = nullptr;
+  w->rank[slot] = 0;
+  w->bind_version += 1;
+  return MP_OK;
+}
+
+int mp_set_strength(mp_ctx* c, int slot, float s) {
+  if (c == nullptr) return MP_EINVAL;
+  if (slot < 0 || slot >= mp::kMaxSlots)
+    return fail(c, MP_EINVAL, "slot %d outside [0, %d)", slot, mp::kMaxSlots);
+  c->strength[slot] = s;
+  return MP_OK;
+}
+
+int mp_get_strength(const mp_ctx* c, int slot, float* s) {
+  if (c == nullptr || s == nullptr || slot < 0 || slot >= mp::kMaxSlots) return MP_EINVAL;
+  *s = c->strength[slot];
+  return MP_OK;
+}
+
+int mp_set_strengths_rows(mp_ctx* c, const float* s, const int32_t* row_starts, int batch) {
+  if (c == nullptr) return MP_EINVAL;
+  if (batch == 0) {
+    c->n_seg = 0;
+    return MP_OK;
+  }
+  if (batch < 0 || batch > mp::kMaxSegments || s == nullptr || row_starts == nullptr)
+    return fail(c, MP_EINVAL, "batch %d outside [0, %d] or NULL arrays", batch,
+                mp::kMaxSegments);
+  for (int g = 0; g < batch; ++g)
+    if (row_starts[g + 1] < row_starts[g])
+      return fail(c, MP_EINVAL, "row_starts must be non-decreasing");
+  c->n_seg = batch;
+  for (int g = 0; g <= batch; ++g) c->seg_start[g] = row_starts[g];
+  for (int g = 0; g < batch; ++g)
+    for (int i = 0; i < mp::kMaxSlots; ++i) c->seg_scale[g][i] = s[g * mp::kMaxSlots + i];
+  return MP_OK;
+}
+
+int mp_linear(mp_ctx* c, const mp_weight* wc, const void* x, int64_t ldx, void* y, int64_t ldy,
+              int m, void* stream) {
+  if (c == nullptr || wc == nullptr) return MP_EINVAL;
+  mp_weight* w = const_cast<mp_weight*>(wc);
+  int rc = check_x(c, x, ldx, w->d.k, m);
+  if (rc != MP_OK) return rc;
+  if (y == nullptr || ldy < w->d.n) return fail(c, MP_EINVAL, "y is NULL or ldy < n");
+  rc = use_device(c);
+  if (rc != MP_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint32_t mask = live_mask(c, w);
+  const Stack* st = nullptr;
+  if (mask != 0) {
+    rc = ensure_stack(c, w, mask, s);
+    if (rc != MP_OK) return rc;
+    st = &w->stack;
+    rc = ensure_buf(c, &c->scratch, &c->scratch_cap, static_cast<size_t>(m) * st->rpad, s);
+    if (rc != MP_OK) return rc;
+    mp::EpilogueScale es;
+    std::memset(&es, 0, sizeof(es));
+    fill_scale(c, &es);
+    add_ranges(&es, *st, 0);
+    rc = launch_lora_down(c, st->tm_a, st->rpad, es, x, ldx, w->d.k, m, s);
+    if (rc != MP_OK) return rc;
+  }
+  return launch_base(c, w, x, ldx, y, ldy, m, st, 0, st != nullptr ? st->rpad : 0, s);
+}
+
+int mp_linear_shared(mp_ctx* c, const mp_weight* const* ws, void* const* ys, const int64_t* ldys,
+                     int count, const void* x, int64_t ldx, int m, void* stream) {
+  if (c == nullptr || ws == nullptr || ys == nullptr || ldys == nullptr) return MP_EINVAL;
+  if (count <= 0 || count > 4) return fail(c, MP_EINVAL, "count %d outside [1, 4]", count);
+  const int k = ws[0]->d.k;
+  for (int i = 0; i < count; ++i) {
+    if (ws[i] == nullptr || ws[i]->d.k != k)
+      return fail(c, MP_EINVAL, "shared projections need the same k");
+    if (ys[i] == nullptr || ldys[i] < ws[i]->d.n) return fail(c, MP_EINVAL, "y[%d] bad", i);
+  }
+  int rc = check_x(c, x, ldx, k, m);
+  if (rc != MP_OK) return rc;
+  rc = use_device(c);
+  if (rc != MP_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  std::vector<uintptr_t> key;
+  std::vector<uint64_t> versions;
+  int rtot = 0;
+  int col[4] = {0, 0, 0, 0};
+  mp::EpilogueScale es;
+  std::memset(&es, 0, sizeof(es));
+  fill_scale(c, &es);
+  for (int i = 0; i < count; ++i) {
+    mp_weight* w = const_cast<mp_weight*>(ws[i]);
+    const uint32_t mask = live_mask(c, w);
+    key.push_back(reinterpret_cast<uintptr_t>(w));
+    col[i] = rtot;
+    if (mask != 0) {
+      rc = ensure_stack(c, w, mask, s);
+      if (rc != MP_OK) return rc;
+      if (!add_ranges(&es, w->stack, rtot)) return fail(c, MP_EINVAL, "too many slot ranges");
+      rtot += w->stack.rpad;
+      versions.push_back(w->stack.version);
+    } else {
+      versions.push_back(0);
+    }
+  }
+  if (rtot > 0) {
+    SharedStack& sh = c->shared[key];
+    if (sh.versions != versions || sh.rtot != rtot) {
+      rc = ensure_buf(c, &sh.a, &sh.a_cap, static_cast<size_t>(rtot) * k, s);
+      if (rc != MP_OK) return rc;
+      for (int i = 0; i < count; ++i) {
+        const mp_weight* w = ws[i];
+        if (live_mask(c, w) == 0) continue;
+        MP_CUDA(c, cudaMemcpyAsync(sh.a + static_cast<size_t>(col[i]) * k, w->stack.a,
+                                   static_cast<size_t>(w->stack.rpad) * k * 2,
+                                   cudaMemcpyDeviceToDevice, s));
+      }
+      if (!encode_2d(&sh.tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, sh.a, k, rtot,
+                     static_cast<uint64_t>(k) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+        return fail(c, MP_ECUDA, "tensor map encode failed (shared LoRA stack)");
+      sh.versions = versions;
+      sh.rtot = rtot;
+    }
+    rc = ensure_buf(c, &c->scratch, &c->scratch_cap, static_cast<size_t>(m) * rtot, s);
+    if (rc != MP_OK) return rc;
+    rc = launch_lora_down(c, sh.tm_a, rtot, es, x, ldx, k, m, s);
+    if (rc != MP_OK) return rc;
+  }
+  for (int i = 0; i < count; ++i) {
+    const mp_weight* w = ws[i];
+    const Stack* st = live_mask(c, w) != 0 ? &w->stack : nullptr;
+    rc = launch_base(c, w, x, ldx, ys[i], ldys[i], m, st, col[i], rtot, s);
+    if (rc != MP_OK) return rc;
+  }
+  return MP_OK;
+}
+
+int mp_modulation_create(mp_ctx* c, int n_blocks, const mp_weight* const* ada,
+                         const uint16_t* const* ada_bias, const uint16_t* const* an1,
+                         const uint16_t* const* fn1, mp_modset** out) {
+  if (c == nullptr || ada == nullptr || ada_bias == nullptr || out == nullptr) return MP_EINVAL;
+  *out = nullptr;
+  if (n_blocks <= 0) return fail(c, MP_EINVAL, "n_blocks must be positive");
+  const mp_weight_desc& d0 = ada[0]->d;
+  if (d0.n % 4 != 0) return fail(c, MP_EINVAL, "modulation n must be 4*H");
+  for (int i = 0; i < n_blocks; ++i) {
+    const mp_weight_desc& d = ada[i]->d;
+    if (d.n != d0.n || d.k != d0.k || d.bits != d0.bits || d.mode != d0.mode)
+      return fail(c, MP_EINVAL, "modulation weights must share shape and format");
+    if (ada_bias[i] == nullptr) return fail(c, MP_EINVAL, "modulation bias %d is NULL", i);
+  }
+  int rc = use_device(c);
+  if (rc != MP_OK) return rc;
+  mp_modset* set = new mp_modset();
+  set->n_blocks = n_blocks;
+  set->n = d0.n;
+  set->k = d0.k;
+  set->bits = d0.bits;
+  set->mode = d0.mode;
+  set->sb_stride = ada[0]->sb_stride;
+  const int H = d0.n / 4;
+  std::vector<mp::ModBlock> hb(n_blocks);
+  auto copy_vec = [&](const uint16_t* src, size_t elems, const uint16_t** dst) -> int {
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, elems * 2);
+    if (e == cudaSuccess) e = cudaMemcpy(p, src, elems * 2, cudaMemcpyDefault);
+    if (e != cudaSuccess) return cuda_fail(c, e, "modulation vector upload");
+    set->owned.push_back(p);
+    *dst = static_cast<const uint16_t*>(p);
+    return MP_OK;
+  };
+  for (int i = 0; i < n_blocks; ++i) {
+    hb[i].w = static_cast<const uint8_t*>(ada[i]->w);
+    hb[i].sb = ada[i]->sb;
+    hb[i].an1 = nullptr;
+    hb[i].fn1 = nullptr;
+    int r = copy_vec(ada_bias[i], d0.n, &hb[i].bias);
+    if (r == MP_OK && an1 != nullptr && an1[i] != nullptr) r = copy_vec(an1[i], H, &hb[i].an1);
+    if (r == MP_OK && fn1 != nullptr && fn1[i] != nullptr) r = copy_vec(fn1[i], H, &hb[i].fn1);
+    if (r != MP_OK) {
+      for (void* p : set->owned) cudaFree(p);
+      delete set;
+      return r;
+    }
+  }
+  cudaError_t e = cudaMalloc(&set->dev_blocks, sizeof(mp::ModBlock) * n_blocks);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(set->dev_blocks, hb.data(), sizeof(mp::ModBlock) * n_blocks,
+                   cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    for (void* p : set->owned) cudaFree(p);
+    delete set;
+    return cuda_fail(c, e, "modulation table upload");
+  }
+  *out = set;
+  return MP_OK;
+}
+
+int mp_modulation_free(mp_ctx* c, mp_modset* set) {
+  if (c == nullptr || set == nullptr) return MP_EINVAL;
+  cudaSetDevice(c->device);
+  cudaDeviceSynchronize();
+  for (void* p : set->owned) cudaFree(p);
+  cudaFree(set->dev_blocks);
+  delete set;
+  return MP_OK;
+}
+
+int mp_modulation_all(mp_ctx* c, const mp_modset* set, const void* temb, int m, void* mods,
+                      void* nw1, void* nw3, void* stream) {
+  if (c == nullptr || set == nullptr || temb == nullptr || mods == nullptr) return MP_EINVAL;
+  if (m <= 0 || m > mp::kModMaxTok)
+    return fail(c, MP_EINVAL, "modulation m %d outside [1, %d]", m, mp::kModMaxTok);
+  int rc = use_device(c);
+  if (rc != MP_OK) return rc;
+  mp::ModParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.blocks = set->dev_blocks;
+  p.n_blocks = set->n_blocks;
+  p.N = set->n;
+  p.K = set->k;
+  p.H = set->n / 4;
+  p.bits = set->bits;
+  const bool sym = set->bits == 8 && set->mode == MP_QUANT_SYMMETRIC;
+  p.code_xor = sym ? 0x80808080u : 0u;
+  p.code_magic = sym ? 8388736.0f : 8388608.0f;
+  p.sb_stride = set->sb_stride;
+  p.M = m;
+  p.temb = static_cast<const uint16_t*>(temb);
+  p.mods = static_cast<uint16_t*>(mods);
+  p.nw1 = static_cast<uint16_t*>(nw1);
+  p.nw3 = static_cast<uint16_t*>(nw3);
+  cudaError_t e = mp::launch_mod(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(c, e, "mod_kernel");
+  c->eng.modulation += 1;
+  c->eng.kernels += 1;
+  const double wbytes = set->bits == 0 ? 2.0 * set->n * set->k : set->n * set->k * set->bits / 8.0;
+  c->eng.flops += 2.0 * m * set->n * static_cast<double>(set->k) * set->n_blocks;
+  c->eng.bytes += set->n_blocks * (wbytes + (set->bits ? set->n * (set->k / 64) * 4.0 : 0.0) +
+                                   2.0 * set->n * (1 + m));
+  return MP_OK;
+}
+
+int mp_engagement_get(const mp_ctx* c, mp_engagement* out) {
+  if (c == nullptr || out == nullptr) return MP_EINVAL;
+  *out = c->eng;
+  return MP_OK;
+}
+
+int mp_engagement_reset(mp_ctx* c) {
+  if (c == nullptr) return MP_EINVAL;
+  c->eng = mp_engagement{};
+  return MP_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,97 @@
+// Launch parameters shared by the host side of the C-ABI and the sm_100a
+// kernels. Everything a launch needs is passed BY VALUE in these structs, so
+// the strengths in force when a projection is enqueued are the ones it uses
+// (a strength re-set between forwards never races a launch in flight).
+#pragma once
+
+#include <cuda.h>
+#include <stdint.h>
+
+namespace mp {
+
+constexpr int kMaxSlots = 8;       // LoRA slots (the reference's lora::Stack::kMax)
+constexpr int kMaxSegments = 16;   // row segments with their own strength vector
+constexpr int kMaxRanges = 32;     // rank-space column ranges (slot runs) per launch
+
+// Pipeline geometry of the projection kernel.
+constexpr int kBlockN = 128;       // output features per CTA tile (MMA M)
+constexpr int kBlockK = 64;        // K per stage == one quantization group
+constexpr int kMaxTok = 256;       // token rows per CTA tile (MMA N), at most
+constexpr int kStages = 4;
+constexpr int kXStageBytes = kMaxTok * 128;   // activation tile, SW128
+constexpr int kWStageBytes = kBlockN * 128;   // weight tile: codes or bf16, SW128 / SW64 / SW32
+constexpr int kStageBytes = kXStageBytes + kWStageBytes;
+constexpr int kProjThreads = 192;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 dequant + epilogue
+constexpr int kTmemCols = 512;
+constexpr int kAccCol = 0;         // f32 accumulator: columns [0, n_tok)
+constexpr int kACol = 256;         // dequantized weight stages: 32 columns each
+
+constexpr uint32_t kSmemBarrierBytes = 256;
+constexpr uint32_t kProjSmemBytes = kStages * kStageBytes + 1024 + kSmemBarrierBytes;
+
+// Device-side error word bits (OR-ed by kernels, read by mp_sync_check).
+constexpr uint32_t kErrTimeout = 1u;
+
+// Optional epilogue scaling of the rank-space intermediate: the value in
+// token row t and rank column j is multiplied by
+//   seg_scale[segment(t)][range_slot[range(j)]].
+struct EpilogueScale {
+  int32_t enabled;
+  int32_t n_seg;
+  int32_t seg_start[kMaxSegments + 1];     // token row boundaries
+  float seg_scale[kMaxSegments][kMaxSlots];
+  int32_t n_ranges;
+  int32_t range_start[kMaxRanges + 1];     // rank column boundaries
+  int32_t range_slot[kMaxRanges];          // slot whose strength scales the range
+};
+
+struct ProjParams {
+  CUtensorMap tm_x;   // activations [M, K] bf16, box {64, n_tok}, SW128
+  CUtensorMap tm_w;   // packed codes [N, K*bits/8] u8 (box {64*bits/8, 128}) or bf16 [N, K] (SW128)
+  CUtensorMap tm_t;   // rank-space intermediate [M, R] bf16, box {64, n_tok}, SW128
+  CUtensorMap tm_b;   // stacked LoRA B [N, R] bf16, box {64, 128}, SW128
+  const uint32_t* sb; // per row, per group: bf16 scale (low half) | bf16 bias (high half)
+  void* y;            // output [M, ldy] bf16
+  int64_t ldy;
+  int32_t M, N, K;
+  int32_t bits;       // 0 dense bf16, 4 or 8 packed codes
+  uint32_t code_xor;  // 0x80808080 turns signed 8-bit codes into offset-binary
+  float code_magic;   // float(2^23 + code) - magic == code value
+  int32_t sb_stride;  // u32 per row of `sb` (multiple of 4)
+  int32_t n_tok;      // token rows per tile: 64, 128 or 256
+  int32_t lora_ktiles;  // extra 64-wide K tiles taken from (tm_t, tm_b)
+  uint64_t wait_limit_ns;
+  uint32_t* err;      // device error word
+  EpilogueScale scale;
+};
+
+// Batched adaLN modulation: for every block b and token m,
+//   mods[b, m, :] = bf16(W_b · temb[m] + bias_b)
+//   nw1[b, m, i] = bf16(an1_b[i] · (1 + mods[b, m, i]))          (chunk 0)
+//   nw3[b, m, i] = bf16(fn1_b[i] · (1 + mods[b, m, 2H + i]))     (chunk 2)
+struct ModBlock {
+  const uint8_t* w;      // codes [N, K*bits/8] or bf16 [N, K]
+  const uint32_t* sb;    // (scale | bias << 16) per group, stride sb_stride
+  const uint16_t* bias;  // bf16 [N]
+  const uint16_t* an1;   // bf16 [H] or null
+  const uint16_t* fn1;   // bf16 [H] or null
+};
+
+struct ModParams {
+  const ModBlock* blocks;  // device array [n_blocks]
+  int32_t n_blocks;
+  int32_t N, K, H;         // N == 4 * H
+  int32_t bits;
+  uint32_t code_xor;
+  float code_magic;
+  int32_t sb_stride;
+  int32_t M;               // tokens (<= 4)
+  const uint16_t* temb;    // bf16 [M, K]
+  uint16_t* mods;          // bf16 [n_blocks, M, N]
+  uint16_t* nw1;           // bf16 [n_blocks, M, H] or null
+  uint16_t* nw3;           // bf16 [n_blocks, M, H] or null
+};
+
+constexpr int kModMaxTok = 4;
+
+}  // namespace mp

@@ -1,0 +1,277 @@
+"""Projection API over the mingproj C-ABI — the host-side mirror of the
+reference's per-projection surface.
+
+  reference (vpipe-ming-image)                      here
+  -----------------------------------------------   --------------------------------
+  QWeight + load_qw_ (src/ming-dit.cc:446-452,      Context.upload() -> Weight
+    :802-831)
+  Adapter::bind per projection (:2954-2968)         Weight.bind(slot, A, B)
+  set_lora_scale / lora_scale (:3024-3039)          Context.set_strength / strength
+  lin(x, xe, w, y, ye, M, N, K, lora::Stack)        Context.linear(w, x, out=y)
+    (:1763-1771)
+  q/k/v (w1/w3) lin calls on one `nrm`              Context.linear_shared(ws, x)
+    (:2078-2080, :2155-2156)
+  fill_mod (:2266-2273), all blocks at once         Context.modulation(set, temb)
+  DitEngagement (src/ming-dit.h:55-103)             Context.engagement()
+
+Device memory, streams and tensors are torch's; every computation is a call
+into libmingproj.so. There is no CPU path here.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import (MP_GROUP, MP_MAX_SEGMENTS, MP_MAX_SLOTS, MP_OK, MP_QUANT_AFFINE,
+                   MP_QUANT_SYMMETRIC, MPError)
+
+
+def _ptr(t) -> C.c_void_p | None:
+    if t is None:
+        return None
+    if isinstance(t, torch.Tensor):
+        return C.c_void_p(t.data_ptr())
+    if isinstance(t, np.ndarray):
+        return t.ctypes.data_as(C.c_void_p)
+    raise TypeError(f"unsupported buffer type {type(t)}")
+
+
+def _contig(t):
+    if t is None:
+        return None
+    if isinstance(t, torch.Tensor):
+        return t.contiguous()
+    return np.ascontiguousarray(t)
+
+
+def _stream_handle(stream) -> C.c_void_p:
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return C.c_void_p(stream.cuda_stream)
+
+
+@dataclass
+class WeightInfo:
+    n: int
+    k: int
+    bits: int
+    mode: int
+
+
+class Weight:
+    """One uploaded projection weight (a QWeight) and its LoRA slots."""
+
+    def __init__(self, ctx: "Context", handle: C.c_void_p, info: WeightInfo):
+        self.ctx = ctx
+        self.handle = handle
+        self.info = info
+        self.ranks = [0] * MP_MAX_SLOTS
+
+    @property
+    def n(self) -> int:
+        return self.info.n
+
+    @property
+    def k(self) -> int:
+        return self.info.k
+
+    @property
+    def bits(self) -> int:
+        return self.info.bits
+
+    def bind(self, slot: int, a, b) -> None:
+        """a: bf16 [rank, k] (alpha folded in), b: bf16 [n, rank]; torch bf16
+        tensors or uint16 numpy arrays, host or device."""
+        a = _as_bf16_bits(a)
+        b = _as_bf16_bits(b)
+        rank = a.shape[0]
+        if tuple(a.shape) != (rank, self.k) or tuple(b.shape) != (self.n, rank):
+            raise MPError(_lib.MP_EINVAL,
+                          f"LoRA factors {tuple(a.shape)} / {tuple(b.shape)} do not fit "
+                          f"[{self.n}, {self.k}]")
+        self.ctx._check(self.ctx.lib.mp_lora_bind(self.ctx.h, self.handle, slot, _ptr(a),
+                                                   _ptr(b), rank))
+        self.ranks[slot] = rank
+
+    def unbind(self, slot: int) -> None:
+        self.ctx._check(self.ctx.lib.mp_lora_unbind(self.ctx.h, self.handle, slot))
+        self.ranks[slot] = 0
+
+    def read_codes(self) -> np.ndarray:
+        """The stored codes (or dense weight) bytes, read back from the device."""
+        nbytes = self.n * self.k * (2 if self.bits == 0 else self.bits) // (1 if self.bits == 0 else 8)
+        out = np.empty(nbytes, dtype=np.uint8)
+        self.ctx._check(self.ctx.lib.mp_weight_read_codes(self.ctx.h, self.handle, _ptr(out),
+                                                           nbytes))
+        return out
+
+    def free(self) -> None:
+        if self.handle:
+            self.ctx.lib.mp_weight_free(self.ctx.h, self.handle)
+            self.handle = None
+
+
+def _as_bf16_bits(t):
+    """torch bf16 tensor -> same tensor (contiguous); numpy uint16 -> contiguous."""
+    if isinstance(t, torch.Tensor):
+        if t.dtype not in (torch.bfloat16, torch.int16, torch.uint16):
+            raise TypeError(f"expected bf16 tensor, got {t.dtype}")
+        return t.contiguous()
+    a = np.ascontiguousarray(t)
+    if a.dtype != np.uint16:
+        raise TypeError(f"expected uint16 (bf16 bits), got {a.dtype}")
+    return a
+
+
+class ModSet:
+    def __init__(self, ctx: "Context", handle: C.c_void_p, n_blocks: int, n: int, k: int):
+        self.ctx, self.handle, self.n_blocks, self.n, self.k = ctx, handle, n_blocks, n, k
+
+    def free(self):
+        if self.handle:
+            self.ctx.lib.mp_modulation_free(self.ctx.h, self.handle)
+            self.handle = None
+
+
+class Context:
+    """One mingproj context bound to a CUDA device."""
+
+    def __init__(self, device: int = 0):
+        self.lib = _lib.load()
+        self.device = device
+        h = C.c_void_p()
+        rc = self.lib.mp_create(device, C.byref(h))
+        if rc != MP_OK:
+            raise MPError(rc, f"mp_create({device}) failed: {_lib.status_name(rc)}")
+        self.h = h
+
+    # -- plumbing --------------------------------------------------------
+    def _check(self, rc: int) -> None:
+        if rc != MP_OK:
+            msg = self.lib.mp_last_error(self.h).decode()
+            raise MPError(rc, f"{_lib.status_name(rc)}: {msg}")
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.mp_destroy(self.h)
+            self.h = None
+
+    def sync_check(self, stream=None) -> None:
+        """Synchronizes and raises MPError(MP_ETIMEOUT) if a kernel gave up a
+        bounded device-side wait."""
+        self._check(self.lib.mp_sync_check(self.h, _stream_handle(stream)))
+
+    def set_wait_limit(self, ns: int) -> None:
+        self._check(self.lib.mp_set_wait_limit(self.h, int(ns)))
+
+    # -- weights -----------------------------------------------------------
+    def upload(self, n: int, k: int, bits: int, data, scales=None, biases=None,
+               mode: int = MP_QUANT_AFFINE) -> Weight:
+        """data: U32 codes [n, k*bits/32] (numpy uint32 or torch int32) for
+        bits 4/8, or bf16 [n, k] for bits 0. Host or device."""
+        desc = _lib.WeightDesc(n, k, bits, MP_GROUP if bits else 0, mode)
+        data = _contig(data)
+        scales = _contig(scales)
+        biases = _contig(biases)
+        h = C.c_void_p()
+        self._check(self.lib.mp_weight_upload(self.h, C.byref(desc), _ptr(data), _ptr(scales),
+                                              _ptr(biases), C.byref(h)))
+        return Weight(self, h, WeightInfo(n, k, bits, mode))
+
+    # -- strengths ---------------------------------------------------------
+    def set_strength(self, slot: int, s: float) -> None:
+        self._check(self.lib.mp_set_strength(self.h, slot, float(s)))
+
+    def strength(self, slot: int) -> float:
+        v = C.c_float()
+        self._check(self.lib.mp_get_strength(self.h, slot, C.byref(v)))
+        return float(v.value)
+
+    def set_strengths_rows(self, strengths, row_starts) -> None:
+        """strengths: [batch, 8] floats; row_starts: [batch + 1] token rows.
+        Pass batch 0 (empty) to return to per-slot strengths."""
+        s = np.ascontiguousarray(strengths, dtype=np.float32).reshape(-1, MP_MAX_SLOTS)
+        r = np.ascontiguousarray(row_starts, dtype=np.int32)
+        batch = s.shape[0]
+        if batch > MP_MAX_SEGMENTS:
+            raise MPError(_lib.MP_EINVAL, f"at most {MP_MAX_SEGMENTS} segments")
+        self._check(self.lib.mp_set_strengths_rows(
+            self.h, s.ctypes.data_as(C.POINTER(C.c_float)),
+            r.ctypes.data_as(C.POINTER(C.c_int32)), batch))
+
+    def clear_strengths_rows(self) -> None:
+        self._check(self.lib.mp_set_strengths_rows(self.h, None, None, 0))
+
+    # -- projections -------------------------------------------------------
+    def linear(self, w: Weight, x: torch.Tensor, out: torch.Tensor | None = None,
+               stream=None) -> torch.Tensor:
+        """y = x · deq(W)^T + sum_live s_i (x A_i^T) B_i^T; x bf16 [m, k] on the
+        context's device (row stride a multiple of 8)."""
+        m = x.shape[0]
+        if out is None:
+            out = torch.empty((m, w.n), dtype=torch.bfloat16, device=x.device)
+        self._check(self.lib.mp_linear(self.h, w.handle, _ptr(x), x.stride(0), _ptr(out),
+                                       out.stride(0), m, _stream_handle(stream)))
+        return out
+
+    def linear_shared(self, ws: list[Weight], x: torch.Tensor, outs=None, stream=None):
+        m = x.shape[0]
+        if outs is None:
+            outs = [torch.empty((m, w.n), dtype=torch.bfloat16, device=x.device) for w in ws]
+        n = len(ws)
+        W = (C.c_void_p * n)(*[w.handle.value for w in ws])
+        Y = (C.c_void_p * n)(*[o.data_ptr() for o in outs])
+        L = (C.c_int64 * n)(*[o.stride(0) for o in outs])
+        self._check(self.lib.mp_linear_shared(self.h, W, Y, L, n, _ptr(x), x.stride(0), m,
+                                              _stream_handle(stream)))
+        return outs
+
+    # -- modulation ----------------------------------------------------------
+    def modulation_set(self, ada: list[Weight], biases, an1=None, fn1=None) -> ModSet:
+        nb = len(ada)
+        biases = [_as_bf16_bits(b) for b in biases]
+        an1 = [_as_bf16_bits(a) for a in an1] if an1 is not None else None
+        fn1 = [_as_bf16_bits(a) for a in fn1] if fn1 is not None else None
+        W = (C.c_void_p * nb)(*[w.handle.value for w in ada])
+        Bp = (C.c_void_p * nb)(*[_ptr(b).value for b in biases])
+        A1 = (C.c_void_p * nb)(*[_ptr(a).value for a in an1]) if an1 is not None else None
+        F1 = (C.c_void_p * nb)(*[_ptr(a).value for a in fn1]) if fn1 is not None else None
+        h = C.c_void_p()
+        self._check(self.lib.mp_modulation_create(self.h, nb, W, Bp, A1, F1, C.byref(h)))
+        return ModSet(self, h, nb, ada[0].n, ada[0].k)
+
+    def modulation(self, mset: ModSet, temb: torch.Tensor, fold: bool = True, stream=None):
+        """Returns (mods [n_blocks, m, 4H], nw1 [n_blocks, m, H] | None,
+        nw3 [n_blocks, m, H] | None), all bf16."""
+        m = temb.shape[0]
+        H = mset.n // 4
+        dev = temb.device
+        mods = torch.empty((mset.n_blocks, m, mset.n), dtype=torch.bfloat16, device=dev)
+        nw1 = torch.empty((mset.n_blocks, m, H), dtype=torch.bfloat16, device=dev) if fold else None
+        nw3 = torch.empty((mset.n_blocks, m, H), dtype=torch.bfloat16, device=dev) if fold else None
+        self._check(self.lib.mp_modulation_all(self.h, mset.handle, _ptr(temb.contiguous()), m,
+                                               _ptr(mods), _ptr(nw1), _ptr(nw3),
+                                               _stream_handle(stream)))
+        return mods, nw1, nw3
+
+    # -- engagement --------------------------------------------------------
+    def engagement(self) -> dict:
+        e = _lib.Engagement()
+        self._check(self.lib.mp_engagement_get(self.h, C.byref(e)))
+        return e.as_dict()
+
+    def reset_engagement(self) -> None:
+        self._check(self.lib.mp_engagement_reset(self.h))
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+__all__ = ["Context", "Weight", "ModSet", "MPError", "MP_QUANT_AFFINE", "MP_QUANT_SYMMETRIC"]
