@@ -1,0 +1,342 @@
+"""Benchmark of the fused quant + 8-slot-LoRA DiT projection path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One STEP is one pass of the hot path over one image's batch: the full 34-block
+projection set of a 1024x1024 Ming-Image DiT forward (
+4096 image rows + 256 caption rows, joint 4352; hidden 3840, FFN 10240; w8
+affine group-64 packs; eight LoRA slots of ranks {4,8,8,16,16,32,32,64} with
+strengths ~U(-1, 1.5)) plus the batched adaLN modulation of the 32 modulated
+blocks. Inputs are seeded synthetic tensors of those shapes (the reference's
+checkpoint and prompts are not available); every block streams its own
+weights (6.2 GB of codes per step, far larger than L2).
+
+Under torchrun (N > 1) every rank runs one image of its own (image sharding,
+no collective on the data path: weak scaling); the JSON line reports the
+whole-job TFLOP/s over the max-over-ranks device time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "vpipe-ming-image_b200"))
+
+METRIC = "fused quant+8-LoRA DiT-projection TFLOP/s & % TC peak at 1/2/4/8 B200"
+RANKS = (4, 8, 8, 16, 16, 32, 32, 64)
+WORKLOAD = ("config2: full 34-block projection set of one 1024x1024 DiT forward "
+            "(IMG 4096 + CAP 256 rows, joint 4352; H 3840, FFN 10240; w8 affine g64; "
+            "8 LoRA slots r={4,8,8,16,16,32,32,64}, s~U(-1,1.5)) + batched adaLN modulation "
+            "of 32 blocks")
+
+
+def load_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = Path(tempfile.mkstemp(prefix="mp_clocks_", suffix=".csv")[1])
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in self.path.read_text().splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 7:
+                    rows.append(parts)
+        except OSError:
+            pass
+        finally:
+            try:
+                self.path.unlink()
+            except OSError:
+                pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = sorted(float(r[0]) for r in rows if r[0].replace(".", "").isdigit())
+        smax = max(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i] == "Active"})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": smax,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_baseline(sample_rows: int = 4352) -> dict:
+    from oracle import cpu_ref
+    r = cpu_ref.time_block(sample_rows, reps=1)
+    return {"value": r["tflops"], "unit": "TFLOP/s", "cores": r["threads"], "kind": "port",
+            "sample": (f"one main-layer block's 7 projections (w8 dequantized once, 8 LoRA "
+                       f"slots) at {r['rows']} rows, torch fp32 CPU, {r['seconds']:.1f} s; "
+                       "TFLOP/s of that sample")}
+
+
+def run_reference(args) -> None:
+    """The reference arm: the CPU port of the path (the reference itself is
+    Metal-only), one bounded sample per step, all host threads, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import cpu_ref
+    rows = 1088  # a quarter of the joint sequence per step keeps K + W steps within minutes
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_ref.time_block(rows, reps=1, seed=i)
+        if i >= args.warmup:
+            vals.append(r)
+    flops = sum(v["flops"] for v in vals)
+    secs = sum(v["seconds"] for v in vals)
+    value = flops / secs / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": secs / len(vals) * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample": f"one main-layer block at {rows} rows per step"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": vals[0]["threads"],
+                         "kind": "port",
+                         "sample": f"one main-layer block's 7 projections at {rows} rows per step "
+                                   "(torch fp32 CPU restatement; the reference is Metal-only)"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from mingproj.dit import (DitDims, DitProjectionSet, Layout, alloc_outputs,
+                              modulation_flops, projection_flops)
+    from mingproj.proj import Context
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    peaks = load_peaks()
+
+    dims = DitDims()
+    layout = Layout(img=4096, cap=256)
+    ctx = Context(local)
+    pset = DitProjectionSet.synthetic(ctx, dims, bits=8, seed=1 + rank, device=dev)
+    for i, r in enumerate(RANKS):
+        pset.bind_synthetic(i, r, seed=100 + 10 * rank + i, device=dev)
+    rng = np.random.default_rng(2 + rank)
+    for i, s in enumerate(rng.uniform(-1.0, 1.5, size=8)):
+        ctx.set_strength(i, float(s))
+
+    gen = torch.Generator(device=dev).manual_seed(3 + rank)
+    JT = layout.joint
+    nrm = torch.randn((JT, dims.dim), device=dev, generator=gen).to(torch.bfloat16)
+    ao = torch.randn((JT, dims.dim), device=dev, generator=gen).to(torch.bfloat16)
+    ffi = torch.randn((JT, dims.ffn), device=dev, generator=gen).to(torch.bfloat16)
+    temb = torch.randn((1, dims.adaln), device=dev, generator=gen).to(torch.bfloat16)
+    outs = alloc_outputs(dims, JT, dev)
+    stream = torch.cuda.current_stream(dev)
+
+    base_f, lora_f = projection_flops(dims, layout, RANKS)
+    mod_f = modulation_flops(dims, 1)
+    step_flops = base_f + lora_f + mod_f
+
+    def step():
+        pset.forward_projections(layout, nrm, ao, ffi, outs, temb=temb)
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync_check()
+
+    # ---- timed region: inputs resident in HBM --------------------------------
+    ctx.reset_engagement()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    mod_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        ev[0].record(stream)
+        for i in range(args.steps):
+            mod_ev[i][0].record(stream)
+            ctx.modulation(pset.modset, temb)
+            mod_ev[i][1].record(stream)
+            for b in range(dims.n_blocks):
+                m = layout.rows(dims.block_kind(b))
+                pset.block_projections(b, nrm[:m], ao[:m], ffi[:m], outs)
+        ev[1].record(stream)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+    ctx.sync_check()
+    eng = ctx.engagement()
+    elapsed_ms = ev[0].elapsed_time(ev[1])
+    mod_ms = sum(a.elapsed_time(b) for a, b in mod_ev)
+    t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    value = world * step_flops * args.steps / (max_ms / 1e3) / 1e12
+    clocks = clk.summary()
+
+    # Roofline of the dominant kernel (proj_kernel: every projection launch).
+    proj_launches = eng["kernels"] - eng["modulation"]
+    proj_ms = elapsed_ms - mod_ms
+    proj_flops = (base_f + lora_f) * args.steps
+    achieved = proj_flops / (proj_ms / 1e3) / 1e12
+    roofline = {
+        "kernel": "proj_kernel", "bound": "tensor", "achieved": achieved,
+        "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+        "frac": achieved / peaks["bf16_tflops_sustained"],
+        "frac_of_burst": achieved / peaks["bf16_tflops"],
+        "peak_kind": f"{peaks['source']} sustained bf16 (kernel timed inside a long step)",
+        "launches_per_step": proj_launches / args.steps,
+        "avg_launch_us": proj_ms * 1e3 / max(proj_launches, 1),
+        "flops_per_launch": proj_flops / max(proj_launches, 1),
+        "traffic": None,
+        "modulation": {"kernel": "mod_kernel", "bound": "hbm",
+                       "achieved_gbs": None,
+                       "us_per_launch": mod_ms * 1e3 / args.steps},
+    }
+    # modulation: minimal bytes per launch = 32 packed adaLN weights + params
+    mod_bytes = dims.n_modulated * (4 * dims.dim * dims.adaln * 1.0 +
+                                    4 * dims.dim * (dims.adaln // 64) * 4.0 + 4 * dims.dim * 4.0)
+    roofline["modulation"]["achieved_gbs"] = mod_bytes / (mod_ms / args.steps / 1e3) / 1e9
+    roofline["modulation"]["peak_gbs"] = peaks["hbm_gbs"]
+    roofline["modulation"]["frac"] = roofline["modulation"]["achieved_gbs"] / peaks["hbm_gbs"]
+    traffic_file = ROOT / "profiles" / "traffic.json"
+    if traffic_file.exists():
+        try:
+            roofline["traffic"] = json.loads(traffic_file.read_text()).get("proj_kernel_bytes_per_launch")
+        except (ValueError, OSError):
+            pass
+
+    # ---- e2e: through the public API with host buffers ------------------------
+    e2e = None
+    if not args.no_e2e:
+        h_nrm = nrm.cpu().pin_memory()
+        h_ao = ao.cpu().pin_memory()
+        h_ffi = ffi.cpu().pin_memory()
+        h_out = {k: torch.empty_like(v, device="cpu").pin_memory() for k, v in outs.items()}
+        h2d = (h_nrm.numel() + h_ao.numel() + h_ffi.numel()) * 2
+        d2h = sum(v.numel() for v in outs.values()) * 2
+
+        def e2e_step():
+            nrm.copy_(h_nrm, non_blocking=True)
+            ao.copy_(h_ao, non_blocking=True)
+            ffi.copy_(h_ffi, non_blocking=True)
+            step()
+            for k, v in outs.items():
+                h_out[k].copy_(v, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        ev[0].record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        ev[1].record(stream)
+        torch.cuda.synchronize(dev)
+        e_ms = torch.tensor([ev[0].elapsed_time(ev[1])], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.barrier()
+            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        e2e = {"value": world * step_flops * args.steps / (float(e_ms.item()) / 1e3) / 1e12,
+               "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "ms_per_step": float(e_ms.item()) / args.steps,
+               "what": "C-ABI calls with pinned-host inputs copied in and every projection "
+                       "output of the last block copied out each step"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline()
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": max_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD,
+                       "l2": "inputs larger than L2: each step streams 6.2 GB of packed weights",
+                       "flops_per_step": step_flops, "lora_flops_per_step": lora_f,
+                       "parallelism": f"image-sharded x{world} (no data-path collective)"},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": int(eng["kernels"]),
+            "clocks": clocks,
+            "engagement": {k: eng[k] for k in ("linear_calls", "lora_proj", "gemm_w8",
+                                               "lora_down", "modulation", "kernels")},
+        }
+        print(json.dumps(line), flush=True)
+    pset.free()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
