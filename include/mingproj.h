@@ -138,7 +138,8 @@ int mp_get_strength(const mp_ctx* ctx, int slot, float* s);
  * vectors): `s` = float [batch][MP_MAX_SLOTS], `row_starts` = int32
  * [batch + 1] token-row boundaries of the x passed to the next launches.
  * batch = 0 returns to the per-slot strengths. No counterpart in the
- * reference (one strength per slot there); it extends a6 to batches. */
+ * reference, which has one strength per slot; a batch of images with their
+ * own strength vectors uses it. */
 int mp_set_strengths_rows(mp_ctx* ctx, const float* s, const int32_t* row_starts, int batch);
 
 /* ---- projections ------------------------------------------------------ */
@@ -177,6 +178,29 @@ int mp_modulation_free(mp_ctx* ctx, mp_modset* set);
  * (src/ming-dit.cc:2266-2273) for every modulated block at once. */
 int mp_modulation_all(mp_ctx* ctx, const mp_modset* set, const void* temb, int m, void* mods,
                       void* nw1, void* nw3, void* stream);
+
+/* ---- allocation-free projection ---------------------------------------- */
+
+/* No counterpart in the reference. For callers that cannot call cudaMalloc —
+ * a host whose memory planner owns every device allocation, or a serving loop
+ * where an allocation or free could synchronize the device — this runs one
+ * adapter's fused projection, y = x · deq(W)^T + strength · (x a^T) b^T, with
+ * the rank-space intermediate in a fixed 4 MiB device array of this library
+ * (2 Mi bf16 elements; every GPU that loads the library holds it until the
+ * process exits) instead of context scratch. It allocates nothing.
+ *   a: device bf16 [rank, k] (alpha folded in), b: device bf16 [n, rank],
+ *      both 16-byte aligned; rank a multiple of 8 in [8, 256];
+ *   m * roundup(rank, 64) must not exceed 2 Mi elements (else MP_EINVAL);
+ *   the slots bound to `w` with mp_lora_bind are NOT applied here;
+ *   strength 0 runs the base projection alone.
+ * The first call on a device looks up the array's device address (once per
+ * device); make that first call before any stream capture. Every call shares
+ * the one array and it keeps the last call's contents: calls whose kernels
+ * overlap on the GPU (other streams, other contexts on the same device) race
+ * on it — order them on one stream. */
+int mp_linear_lora_static(mp_ctx* ctx, const mp_weight* w, const void* x, int64_t ldx,
+                          const uint16_t* a, const uint16_t* b, int rank, float strength,
+                          void* y, int64_t ldy, int m, void* stream);
 
 /* ---- engagement -------------------------------------------------------- */
 

@@ -818,3 +818,137 @@ int mp_engagement_reset(mp_ctx* c) {
 }
 
 }  // extern "C"
+
+// ---- allocation-free entry point ---------------------------------------------
+//
+// Some callers cannot call cudaMalloc: a host whose memory planner owns every
+// device allocation up front (the plugin's host hands out pooled buffers and
+// budgets device memory per session), and latency-critical serving loops in
+// which an allocation or a free could synchronize the device. For them,
+// mp_linear_lora_static runs one adapter's fused projection with its
+// rank-space intermediate held in a fixed, file-scope device array instead of
+// context scratch. Every GPU that loads this library holds the array (4 MiB)
+// until the process exits.
+
+// Elements (bf16) of the shared rank-space scratch: m * roundup(rank, 64) must fit.
+#define MP_STATIC_RANK_SCRATCH_ELEMS (static_cast<size_t>(2) << 20)
+
+static __device__ __align__(256) uint16_t g_static_rank_scratch[MP_STATIC_RANK_SCRATCH_ELEMS];
+
+namespace {
+
+// Device address of g_static_rank_scratch, looked up once per device with that
+// device current (host code only has a host-side stand-in for the symbol).
+uint16_t* g_static_rank_scratch_dev[64] = {};
+
+int static_rank_scratch(mp_ctx* c, uint16_t** out) {
+  if (c->device < 0 || c->device >= 64) return fail(c, MP_EINVAL, "device index out of range");
+  if (g_static_rank_scratch_dev[c->device] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_static_rank_scratch);
+    if (e != cudaSuccess) return cuda_fail(c, e, "cudaGetSymbolAddress(g_static_rank_scratch)");
+    g_static_rank_scratch_dev[c->device] = static_cast<uint16_t*>(p);
+  }
+  *out = g_static_rank_scratch_dev[c->device];
+  return MP_OK;
+}
+
+}  // namespace
+
+extern "C" int mp_linear_lora_static(mp_ctx* c, const mp_weight* w, const void* x, int64_t ldx,
+                                     const uint16_t* a, const uint16_t* b, int rank,
+                                     float strength, void* y, int64_t ldy, int m, void* stream) {
+  if (c == nullptr || w == nullptr) return MP_EINVAL;
+  int rc = check_x(c, x, ldx, w->d.k, m);
+  if (rc != MP_OK) return rc;
+  if (y == nullptr || ldy < w->d.n) return fail(c, MP_EINVAL, "y is NULL or ldy < n");
+  if (a == nullptr || b == nullptr) return fail(c, MP_EINVAL, "LoRA factor is NULL");
+  if (rank <= 0 || rank > 256 || rank % 8 != 0)
+    return fail(c, MP_EINVAL, "rank %d: must be a multiple of 8 in [8, 256]", rank);
+  if (reinterpret_cast<uintptr_t>(a) % 16 != 0 || reinterpret_cast<uintptr_t>(b) % 16 != 0)
+    return fail(c, MP_EINVAL, "LoRA factors must be 16-byte aligned device memory");
+  const int rpad = (rank + 63) / 64 * 64;
+  if (static_cast<size_t>(m) * rpad > MP_STATIC_RANK_SCRATCH_ELEMS)
+    return fail(c, MP_EINVAL,
+                "m * roundup(rank, 64) = %lld exceeds the static scratch of %zu elements",
+                static_cast<long long>(m) * rpad, static_cast<size_t>(MP_STATIC_RANK_SCRATCH_ELEMS));
+  rc = use_device(c);
+  if (rc != MP_OK) return rc;
+  uint16_t* scratch = nullptr;
+  rc = static_rank_scratch(c, &scratch);
+  if (rc != MP_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int n = w->d.n, k = w->d.k;
+  if (strength == 0.0f) return launch_base(c, w, x, ldx, y, ldy, m, nullptr, 0, 0, s);
+
+  // Rank-space pre-GEMM into the static array: all rpad columns are written
+  // (rows of `a` past `rank` read as zeros), so nothing left from an earlier
+  // call survives into this one.
+  ProjParams p;
+  base_params(c, &p);
+  const int ntok_down = pick_ntok(m, rpad);
+  if (!encode_2d(&p.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, k, m,
+                 static_cast<uint64_t>(ldx) * 2, 64, ntok_down, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&p.tm_w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a, k, rank,
+                 static_cast<uint64_t>(k) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return fail(c, MP_ECUDA, "tensor map encode failed (static LoRA pre-GEMM)");
+  p.y = scratch;
+  p.ldy = rpad;
+  p.M = m;
+  p.N = rpad;
+  p.K = k;
+  p.bits = 0;
+  p.n_tok = ntok_down;
+  p.scale.enabled = 1;
+  p.scale.n_seg = 1;
+  p.scale.seg_start[0] = 0;
+  p.scale.seg_start[1] = INT_MAX;
+  p.scale.seg_scale[0][0] = strength;
+  p.scale.n_ranges = 1;
+  p.scale.range_start[0] = 0;
+  p.scale.range_start[1] = rank;
+  p.scale.range_slot[0] = 0;
+  cudaError_t e = mp::launch_proj(p, s);
+  if (e != cudaSuccess) return cuda_fail(c, e, "proj_kernel (static LoRA pre-GEMM)");
+  c->eng.lora_down += 1;
+  c->eng.kernels += 1;
+
+  // The fused projection with the adapter appended as extra K tiles; `b`'s
+  // columns past `rank` read as zeros.
+  ProjParams q;
+  base_params(c, &q);
+  const int ntok = pick_ntok(m, n);
+  if (!encode_2d(&q.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, k, m,
+                 static_cast<uint64_t>(ldx) * 2, 64, ntok, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&q.tm_t, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, scratch, rpad, m,
+                 static_cast<uint64_t>(rpad) * 2, 64, ntok, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&q.tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, rank, n,
+                 static_cast<uint64_t>(rank) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return fail(c, MP_ECUDA, "tensor map encode failed (static LoRA projection)");
+  q.tm_w = w->tm_w;
+  q.sb = w->sb;
+  q.sb_stride = w->sb_stride;
+  q.y = y;
+  q.ldy = ldy;
+  q.M = m;
+  q.N = n;
+  q.K = k;
+  q.bits = w->d.bits;
+  const bool sym = w->d.bits == 8 && w->d.mode == MP_QUANT_SYMMETRIC;
+  q.code_xor = sym ? 0x80808080u : 0u;
+  q.code_magic = sym ? 8388736.0f : 8388608.0f;
+  q.n_tok = ntok;
+  q.lora_ktiles = rpad / 64;
+  e = mp::launch_proj(q, s);
+  if (e != cudaSuccess) return cuda_fail(c, e, "proj_kernel (static LoRA projection)");
+  c->eng.kernels += 1;
+  c->eng.linear_calls += 1;
+  c->eng.lora_proj += 1;
+  if (w->d.bits == 8) c->eng.gemm_w8 += 1;
+  else if (w->d.bits == 4) c->eng.gemm_w4 += 1;
+  else c->eng.gemm_dense += 1;
+  c->eng.flops += 2.0 * m * n * static_cast<double>(k) + 2.0 * m * rank * static_cast<double>(k + n);
+  c->eng.bytes += static_cast<double>(w->w_bytes) + 2.0 * m * k + 2.0 * m * n +
+                  2.0 * rank * static_cast<double>(k + n);
+  return MP_OK;
+}

@@ -61,6 +61,8 @@ SIGNATURES = {
                                        C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_vp)]),
     "mp_modulation_free": (C.c_int, [_vp, _vp]),
     "mp_modulation_all": (C.c_int, [_vp, _vp, _vp, C.c_int, _vp, _vp, _vp, _vp]),
+    "mp_linear_lora_static": (C.c_int, [_vp, _vp, _vp, _i64, _vp, _vp, C.c_int, C.c_float, _vp,
+                                        _i64, C.c_int, _vp]),
     "mp_engagement_get": (C.c_int, [_vp, C.POINTER(Engagement)]),
     "mp_engagement_reset": (C.c_int, [_vp]),
 }

@@ -230,6 +230,23 @@ class Context:
                                               _stream_handle(stream)))
         return outs
 
+    def linear_lora_static(self, w: Weight, x: torch.Tensor, a: torch.Tensor, b: torch.Tensor,
+                           strength: float, out: torch.Tensor | None = None,
+                           stream=None) -> torch.Tensor:
+        """One adapter's fused projection without any device allocation in the
+        library: the rank-space intermediate lives in the library's fixed
+        device array (see mp_linear_lora_static). a: bf16 [rank, k], b: bf16
+        [n, rank], both on the device; the slots bound to `w` are not applied."""
+        m = x.shape[0]
+        if out is None:
+            out = torch.empty((m, w.n), dtype=torch.bfloat16, device=x.device)
+        a = a.contiguous()
+        b = b.contiguous()
+        self._check(self.lib.mp_linear_lora_static(
+            self.h, w.handle, _ptr(x), x.stride(0), _ptr(a), _ptr(b), a.shape[0],
+            float(strength), _ptr(out), out.stride(0), m, _stream_handle(stream)))
+        return out
+
     # -- modulation ----------------------------------------------------------
     def modulation_set(self, ada: list[Weight], biases, an1=None, fn1=None) -> ModSet:
         nb = len(ada)
