@@ -147,7 +147,7 @@ int mp_set_strengths_rows(mp_ctx* ctx, const float* s, const int32_t* row_starts
 /* y[m, n] = x[m, k] · deq(W)^T + sum over live slots s_i · (x A_i^T) B_i^T,
  * bf16 in / bf16 out, f32 accumulation, one pass over K with the adapters
  * appended as extra K tiles. x: device bf16, 16-byte aligned, ldx a
- * multiple of 8 elements. y: device bf16, ldy >= n.
+ * multiple of 8 elements. y: device bf16, 16-byte aligned, ldy >= n and a multiple of 8.
  * Replaces: lin (src/ming-dit.cc:1763-1771). */
 int mp_linear(mp_ctx* ctx, const mp_weight* w, const void* x, int64_t ldx, void* y, int64_t ldy,
               int m, void* stream);

@@ -8,6 +8,7 @@
 #include <climits>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <string>
@@ -17,7 +18,8 @@
 #include "mp_kernels.h"
 
 namespace mp {
-cudaError_t launch_proj(const ProjParams& p, cudaStream_t stream);
+cudaError_t launch_proj_pair(const ProjParams& p, cudaStream_t stream);
+int pick_ntok_pair(int m, int pairs);
 cudaError_t launch_mod(const ModParams& p, cudaStream_t stream);
 }  // namespace mp
 
@@ -154,14 +156,16 @@ bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Token rows per CTA tile: the widest tile that still fills the GPU, else 64.
-int pick_ntok(int m, int n) {
-  const int ntiles = (n + mp::kBlockN - 1) / mp::kBlockN;
-  for (int nt : {256, 128}) {
-    if (static_cast<long>(ntiles) * ((m + nt - 1) / nt) >= 148) return nt;
-  }
-  return 64;
+// Output map for the pair kernel's bulk stores: [m, n] bf16 rows of ldy,
+// box = 64 features x one pair token tile, 128-byte swizzle.
+bool encode_y(CUtensorMap* m, const void* y, int64_t ldy, int n, int rows, int ntok) {
+  return encode_2d(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, y, static_cast<uint64_t>(n),
+                   static_cast<uint64_t>(rows), static_cast<uint64_t>(ldy) * 2, 64,
+                   static_cast<uint32_t>(ntok), CU_TENSOR_MAP_SWIZZLE_128B);
 }
+
+// Feature pairs (256 output rows) a projection of n outputs occupies.
+int pairs_of(int n) { return (n + 2 * mp::kBlockN - 1) / (2 * mp::kBlockN); }
 
 uint32_t live_mask(const mp_ctx* c, const mp_weight* w) {
   uint32_t mask = 0;
@@ -270,6 +274,16 @@ bool add_ranges(mp::EpilogueScale* es, const Stack& st, int base) {
   return true;
 }
 
+int check_y(mp_ctx* c, const void* y, int64_t ldy, int n) {
+  if (y == nullptr) return fail(c, MP_EINVAL, "y is NULL");
+  if (reinterpret_cast<uintptr_t>(y) % 16 != 0)
+    return fail(c, MP_EINVAL, "y must be 16-byte aligned");
+  if (ldy < n || ldy % 8 != 0)
+    return fail(c, MP_EINVAL, "ldy must be >= n and a multiple of 8 (got %lld)",
+                static_cast<long long>(ldy));
+  return MP_OK;
+}
+
 int check_x(mp_ctx* c, const void* x, int64_t ldx, int k, int m) {
   if (x == nullptr) return fail(c, MP_EINVAL, "x is NULL");
   if (m <= 0) return fail(c, MP_EINVAL, "m must be positive (got %d)", m);
@@ -287,66 +301,75 @@ void base_params(const mp_ctx* c, ProjParams* p) {
   p->err = c->err_word;
 }
 
-// Rank-space pre-GEMM: T[m, 0:rtot] = scale ⊙ (x · A^T), into ctx scratch.
-int launch_lora_down(mp_ctx* c, const CUtensorMap& tm_a, int rtot, const mp::EpilogueScale& es,
-                     const void* x, int64_t ldx, int k, int m, cudaStream_t stream) {
-  ProjParams p;
-  base_params(c, &p);
-  const int ntok = pick_ntok(m, rtot);
-  if (!encode_2d(&p.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, k, m,
-                 static_cast<uint64_t>(ldx) * 2, 64, ntok, CU_TENSOR_MAP_SWIZZLE_128B))
+// The appended LoRA K tiles of one member: `rpad` rank columns of the
+// rank-space intermediate at `tbase` (row stride t_ld), against `tm_b`.
+struct LoraTiles {
+  int rpad = 0;
+  const uint16_t* tbase = nullptr;
+  int t_ld = 0;
+  const CUtensorMap* tm_b = nullptr;
+};
+
+// One projection (weight `w`, or a dense bf16 "weight" map for the
+// rank-space pre-GEMM) as member `i` of a launch.
+int fill_member(mp_ctx* c, ProjParams* p, int i, const CUtensorMap& tm_w, const uint32_t* sb,
+                int sb_stride, int n, int bits, int mode, void* y, int64_t ldy,
+                const LoraTiles& lt) {
+  mp::ProjMember& mb = p->mem[i];
+  mb.tm_w = tm_w;
+  mb.sb = sb;
+  mb.sb_stride = sb_stride;
+  mb.N = n;
+  mb.bits = bits;
+  const bool sym = bits == 8 && mode == MP_QUANT_SYMMETRIC;
+  mb.code_xor = sym ? 0x80808080u : 0u;
+  mb.code_magic = sym ? 8388736.0f : 8388608.0f;
+  if (!encode_y(&mb.tm_y, y, ldy, n, p->M, p->n_tok))
+    return fail(c, MP_ECUDA, "tensor map encode failed (output)");
+  mb.lora_ktiles = 0;
+  if (lt.rpad > 0) {
+    mb.lora_ktiles = lt.rpad / 64;
+    if (!encode_2d(&mb.tm_t, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lt.tbase, lt.rpad, p->M,
+                   static_cast<uint64_t>(lt.t_ld) * 2, 64, static_cast<uint32_t>(p->n_tok / 2),
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+      return fail(c, MP_ECUDA, "tensor map encode failed (rank-space intermediate)");
+    mb.tm_b = *lt.tm_b;
+  }
+  return MP_OK;
+}
+
+// Sets the launch-wide fields for `count` members whose output widths are
+// `ns`, choosing the token tile from the total pair count.
+int begin_launch(mp_ctx* c, ProjParams* p, const void* x, int64_t ldx, int k, int m,
+                 const int* ns, int count) {
+  base_params(c, p);
+  int pairs = 0;
+  for (int i = 0; i < count; ++i) {
+    p->mem[i].pair_begin = pairs;
+    pairs += pairs_of(ns[i]);
+  }
+  p->n_members = count;
+  p->n_pairs = pairs;
+  p->M = m;
+  p->K = k;
+  p->n_tok = mp::pick_ntok_pair(m, pairs);
+  if (!encode_2d(&p->tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, k, m,
+                 static_cast<uint64_t>(ldx) * 2, 64, static_cast<uint32_t>(p->n_tok / 2),
+                 CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(c, MP_ECUDA, "tensor map encode failed (x)");
-  p.tm_w = tm_a;
-  p.sb = nullptr;
-  p.y = c->scratch;
-  p.ldy = rtot;
-  p.M = m;
-  p.N = rtot;
-  p.K = k;
-  p.bits = 0;
-  p.n_tok = ntok;
-  p.lora_ktiles = 0;
-  p.scale = es;
-  cudaError_t e = mp::launch_proj(p, stream);
-  if (e != cudaSuccess) return cuda_fail(c, e, "proj_kernel (lora down)");
-  c->eng.lora_down += 1;
+  return MP_OK;
+}
+
+int run_launch(mp_ctx* c, const ProjParams& p, cudaStream_t stream, const char* what) {
+  cudaError_t e = mp::launch_proj_pair(p, stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, what);
   c->eng.kernels += 1;
   return MP_OK;
 }
 
-int launch_base(mp_ctx* c, const mp_weight* w, const void* x, int64_t ldx, void* y, int64_t ldy,
-                int m, const Stack* st, int t_col, int t_ld, cudaStream_t stream) {
-  ProjParams p;
-  base_params(c, &p);
+// Engagement of one projection launched as a member.
+void count_projection(mp_ctx* c, const mp_weight* w, int m, const int* ranks) {
   const int n = w->d.n, k = w->d.k;
-  const int ntok = pick_ntok(m, n);
-  if (!encode_2d(&p.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, k, m,
-                 static_cast<uint64_t>(ldx) * 2, 64, ntok, CU_TENSOR_MAP_SWIZZLE_128B))
-    return fail(c, MP_ECUDA, "tensor map encode failed (x)");
-  p.tm_w = w->tm_w;
-  p.sb = w->sb;
-  p.sb_stride = w->sb_stride;
-  p.y = y;
-  p.ldy = ldy;
-  p.M = m;
-  p.N = n;
-  p.K = k;
-  p.bits = w->d.bits;
-  const bool sym = w->d.bits == 8 && w->d.mode == MP_QUANT_SYMMETRIC;
-  p.code_xor = sym ? 0x80808080u : 0u;
-  p.code_magic = sym ? 8388736.0f : 8388608.0f;
-  p.n_tok = ntok;
-  if (st != nullptr && st->rpad > 0) {
-    p.lora_ktiles = st->rpad / 64;
-    const uint16_t* tbase = c->scratch + t_col;
-    if (!encode_2d(&p.tm_t, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, tbase, st->rpad, m,
-                   static_cast<uint64_t>(t_ld) * 2, 64, ntok, CU_TENSOR_MAP_SWIZZLE_128B))
-      return fail(c, MP_ECUDA, "tensor map encode failed (rank-space intermediate)");
-    p.tm_b = st->tm_b;
-  }
-  cudaError_t e = mp::launch_proj(p, stream);
-  if (e != cudaSuccess) return cuda_fail(c, e, "proj_kernel");
-  c->eng.kernels += 1;
   c->eng.linear_calls += 1;
   if (w->d.bits == 8) c->eng.gemm_w8 += 1;
   else if (w->d.bits == 4) c->eng.gemm_w4 += 1;
@@ -354,15 +377,63 @@ int launch_base(mp_ctx* c, const mp_weight* w, const void* x, int64_t ldx, void*
   double flops = 2.0 * m * n * static_cast<double>(k);
   double bytes = static_cast<double>(w->w_bytes) + static_cast<double>(n) * (k / 64) * 4.0 +
                  2.0 * m * k + 2.0 * m * n;
-  if (st != nullptr && st->rpad > 0) {
-    c->eng.lora_proj += 1;
+  bool lora = false;
+  if (ranks != nullptr) {
     for (int i = 0; i < mp::kMaxSlots; ++i) {
-      flops += 2.0 * m * st->ranks[i] * static_cast<double>(k + n);
-      bytes += 2.0 * st->ranks[i] * static_cast<double>(k + n);
+      if (ranks[i] <= 0) continue;
+      lora = true;
+      flops += 2.0 * m * ranks[i] * static_cast<double>(k + n);
+      bytes += 2.0 * ranks[i] * static_cast<double>(k + n);
     }
   }
+  if (lora) c->eng.lora_proj += 1;
   c->eng.flops += flops;
   c->eng.bytes += bytes;
+}
+
+// Rank-space pre-GEMM: T[m, 0:rtot] = scale ⊙ (x · A^T), into ctx scratch.
+int launch_lora_down(mp_ctx* c, const CUtensorMap& tm_a, int rtot, const mp::EpilogueScale& es,
+                     const void* x, int64_t ldx, int k, int m, cudaStream_t stream) {
+  ProjParams p;
+  int rc = begin_launch(c, &p, x, ldx, k, m, &rtot, 1);
+  if (rc != MP_OK) return rc;
+  p.scale = es;
+  rc = fill_member(c, &p, 0, tm_a, nullptr, 0, rtot, 0, 0, c->scratch, rtot, LoraTiles{});
+  if (rc != MP_OK) return rc;
+  rc = run_launch(c, p, stream, "proj_pair_kernel (rank-space pre-GEMM)");
+  if (rc != MP_OK) return rc;
+  c->eng.lora_down += 1;
+  return MP_OK;
+}
+
+// `count` projections of one x in one launch; sts[i] (nullable) is member
+// i's live stack, whose intermediate starts at column t_cols[i] of the
+// scratch (row stride t_ld).
+int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
+                       const int64_t* ldys, const Stack* const* sts, const int* t_cols, int t_ld,
+                       int count, const void* x, int64_t ldx, int m, cudaStream_t stream) {
+  ProjParams p;
+  int ns[mp::kMaxMembers] = {0, 0, 0, 0};
+  for (int i = 0; i < count; ++i) ns[i] = ws[i]->d.n;
+  int rc = begin_launch(c, &p, x, ldx, ws[0]->d.k, m, ns, count);
+  if (rc != MP_OK) return rc;
+  for (int i = 0; i < count; ++i) {
+    const mp_weight* w = ws[i];
+    LoraTiles lt;
+    if (sts[i] != nullptr && sts[i]->rpad > 0) {
+      lt.rpad = sts[i]->rpad;
+      lt.tbase = c->scratch + t_cols[i];
+      lt.t_ld = t_ld;
+      lt.tm_b = &sts[i]->tm_b;
+    }
+    rc = fill_member(c, &p, i, w->tm_w, w->sb, w->sb_stride, w->d.n, w->d.bits, w->d.mode, ys[i],
+                     ldys[i], lt);
+    if (rc != MP_OK) return rc;
+  }
+  rc = run_launch(c, p, stream, "proj_pair_kernel");
+  if (rc != MP_OK) return rc;
+  for (int i = 0; i < count; ++i)
+    count_projection(c, ws[i], m, sts[i] != nullptr && sts[i]->rpad > 0 ? sts[i]->ranks : nullptr);
   return MP_OK;
 }
 
@@ -608,7 +679,8 @@ int mp_linear(mp_ctx* c, const mp_weight* wc, const void* x, int64_t ldx, void* 
   mp_weight* w = const_cast<mp_weight*>(wc);
   int rc = check_x(c, x, ldx, w->d.k, m);
   if (rc != MP_OK) return rc;
-  if (y == nullptr || ldy < w->d.n) return fail(c, MP_EINVAL, "y is NULL or ldy < n");
+  rc = check_y(c, y, ldy, w->d.n);
+  if (rc != MP_OK) return rc;
   rc = use_device(c);
   if (rc != MP_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -627,18 +699,25 @@ int mp_linear(mp_ctx* c, const mp_weight* wc, const void* x, int64_t ldx, void* 
     rc = launch_lora_down(c, st->tm_a, st->rpad, es, x, ldx, w->d.k, m, s);
     if (rc != MP_OK) return rc;
   }
-  return launch_base(c, w, x, ldx, y, ldy, m, st, 0, st != nullptr ? st->rpad : 0, s);
+  const mp_weight* wl[1] = {w};
+  void* yl[1] = {y};
+  const int64_t ll[1] = {ldy};
+  const Stack* sl[1] = {st};
+  const int cl[1] = {0};
+  return launch_projections(c, wl, yl, ll, sl, cl, st != nullptr ? st->rpad : 0, 1, x, ldx, m, s);
 }
 
 int mp_linear_shared(mp_ctx* c, const mp_weight* const* ws, void* const* ys, const int64_t* ldys,
                      int count, const void* x, int64_t ldx, int m, void* stream) {
   if (c == nullptr || ws == nullptr || ys == nullptr || ldys == nullptr) return MP_EINVAL;
-  if (count <= 0 || count > 4) return fail(c, MP_EINVAL, "count %d outside [1, 4]", count);
+  if (count <= 0 || count > mp::kMaxMembers)
+    return fail(c, MP_EINVAL, "count %d outside [1, %d]", count, mp::kMaxMembers);
   const int k = ws[0]->d.k;
   for (int i = 0; i < count; ++i) {
     if (ws[i] == nullptr || ws[i]->d.k != k)
       return fail(c, MP_EINVAL, "shared projections need the same k");
-    if (ys[i] == nullptr || ldys[i] < ws[i]->d.n) return fail(c, MP_EINVAL, "y[%d] bad", i);
+    int yrc = check_y(c, ys[i], ldys[i], ws[i]->d.n);
+    if (yrc != MP_OK) return yrc;
   }
   int rc = check_x(c, x, ldx, k, m);
   if (rc != MP_OK) return rc;
@@ -690,13 +769,9 @@ int mp_linear_shared(mp_ctx* c, const mp_weight* const* ws, void* const* ys, con
     rc = launch_lora_down(c, sh.tm_a, rtot, es, x, ldx, k, m, s);
     if (rc != MP_OK) return rc;
   }
-  for (int i = 0; i < count; ++i) {
-    const mp_weight* w = ws[i];
-    const Stack* st = live_mask(c, w) != 0 ? &w->stack : nullptr;
-    rc = launch_base(c, w, x, ldx, ys[i], ldys[i], m, st, col[i], rtot, s);
-    if (rc != MP_OK) return rc;
-  }
-  return MP_OK;
+  const Stack* sts[mp::kMaxMembers];
+  for (int i = 0; i < count; ++i) sts[i] = live_mask(c, ws[i]) != 0 ? &ws[i]->stack : nullptr;
+  return launch_projections(c, ws, ys, ldys, sts, col, rtot, count, x, ldx, m, s);
 }
 
 int mp_modulation_create(mp_ctx* c, int n_blocks, const mp_weight* const* ada,
@@ -861,7 +936,8 @@ extern "C" int mp_linear_lora_static(mp_ctx* c, const mp_weight* w, const void* 
   if (c == nullptr || w == nullptr) return MP_EINVAL;
   int rc = check_x(c, x, ldx, w->d.k, m);
   if (rc != MP_OK) return rc;
-  if (y == nullptr || ldy < w->d.n) return fail(c, MP_EINVAL, "y is NULL or ldy < n");
+  rc = check_y(c, y, ldy, w->d.n);
+  if (rc != MP_OK) return rc;
   if (a == nullptr || b == nullptr) return fail(c, MP_EINVAL, "LoRA factor is NULL");
   if (rank <= 0 || rank > 256 || rank % 8 != 0)
     return fail(c, MP_EINVAL, "rank %d: must be a multiple of 8 in [8, 256]", rank);
@@ -879,26 +955,25 @@ extern "C" int mp_linear_lora_static(mp_ctx* c, const mp_weight* w, const void* 
   if (rc != MP_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int n = w->d.n, k = w->d.k;
-  if (strength == 0.0f) return launch_base(c, w, x, ldx, y, ldy, m, nullptr, 0, 0, s);
+  const mp_weight* wl[1] = {w};
+  void* yl[1] = {y};
+  const int64_t ll[1] = {ldy};
+  if (strength == 0.0f) {
+    const Stack* none[1] = {nullptr};
+    const int cols[1] = {0};
+    return launch_projections(c, wl, yl, ll, none, cols, 0, 1, x, ldx, m, s);
+  }
 
   // Rank-space pre-GEMM into the static array: all rpad columns are written
   // (rows of `a` past `rank` read as zeros), so nothing left from an earlier
   // call survives into this one.
-  ProjParams p;
-  base_params(c, &p);
-  const int ntok_down = pick_ntok(m, rpad);
-  if (!encode_2d(&p.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, k, m,
-                 static_cast<uint64_t>(ldx) * 2, 64, ntok_down, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_2d(&p.tm_w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a, k, rank,
+  CUtensorMap tm_a;
+  if (!encode_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a, k, rank,
                  static_cast<uint64_t>(k) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
-    return fail(c, MP_ECUDA, "tensor map encode failed (static LoRA pre-GEMM)");
-  p.y = scratch;
-  p.ldy = rpad;
-  p.M = m;
-  p.N = rpad;
-  p.K = k;
-  p.bits = 0;
-  p.n_tok = ntok_down;
+    return fail(c, MP_ECUDA, "tensor map encode failed (static LoRA A)");
+  ProjParams p;
+  rc = begin_launch(c, &p, x, ldx, k, m, &rpad, 1);
+  if (rc != MP_OK) return rc;
   p.scale.enabled = 1;
   p.scale.n_seg = 1;
   p.scale.seg_start[0] = 0;
@@ -908,47 +983,31 @@ extern "C" int mp_linear_lora_static(mp_ctx* c, const mp_weight* w, const void* 
   p.scale.range_start[0] = 0;
   p.scale.range_start[1] = rank;
   p.scale.range_slot[0] = 0;
-  cudaError_t e = mp::launch_proj(p, s);
-  if (e != cudaSuccess) return cuda_fail(c, e, "proj_kernel (static LoRA pre-GEMM)");
+  rc = fill_member(c, &p, 0, tm_a, nullptr, 0, rpad, 0, 0, scratch, rpad, LoraTiles{});
+  if (rc != MP_OK) return rc;
+  rc = run_launch(c, p, s, "proj_pair_kernel (static rank-space pre-GEMM)");
+  if (rc != MP_OK) return rc;
   c->eng.lora_down += 1;
-  c->eng.kernels += 1;
 
   // The fused projection with the adapter appended as extra K tiles; `b`'s
   // columns past `rank` read as zeros.
-  ProjParams q;
-  base_params(c, &q);
-  const int ntok = pick_ntok(m, n);
-  if (!encode_2d(&q.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, k, m,
-                 static_cast<uint64_t>(ldx) * 2, 64, ntok, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_2d(&q.tm_t, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, scratch, rpad, m,
-                 static_cast<uint64_t>(rpad) * 2, 64, ntok, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_2d(&q.tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, rank, n,
+  CUtensorMap tm_bl;
+  if (!encode_2d(&tm_bl, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, rank, n,
                  static_cast<uint64_t>(rank) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
-    return fail(c, MP_ECUDA, "tensor map encode failed (static LoRA projection)");
-  q.tm_w = w->tm_w;
-  q.sb = w->sb;
-  q.sb_stride = w->sb_stride;
-  q.y = y;
-  q.ldy = ldy;
-  q.M = m;
-  q.N = n;
-  q.K = k;
-  q.bits = w->d.bits;
-  const bool sym = w->d.bits == 8 && w->d.mode == MP_QUANT_SYMMETRIC;
-  q.code_xor = sym ? 0x80808080u : 0u;
-  q.code_magic = sym ? 8388736.0f : 8388608.0f;
-  q.n_tok = ntok;
-  q.lora_ktiles = rpad / 64;
-  e = mp::launch_proj(q, s);
-  if (e != cudaSuccess) return cuda_fail(c, e, "proj_kernel (static LoRA projection)");
-  c->eng.kernels += 1;
-  c->eng.linear_calls += 1;
-  c->eng.lora_proj += 1;
-  if (w->d.bits == 8) c->eng.gemm_w8 += 1;
-  else if (w->d.bits == 4) c->eng.gemm_w4 += 1;
-  else c->eng.gemm_dense += 1;
-  c->eng.flops += 2.0 * m * n * static_cast<double>(k) + 2.0 * m * rank * static_cast<double>(k + n);
-  c->eng.bytes += static_cast<double>(w->w_bytes) + 2.0 * m * k + 2.0 * m * n +
-                  2.0 * rank * static_cast<double>(k + n);
+    return fail(c, MP_ECUDA, "tensor map encode failed (static LoRA B)");
+  ProjParams q;
+  rc = begin_launch(c, &q, x, ldx, k, m, &n, 1);
+  if (rc != MP_OK) return rc;
+  LoraTiles lt;
+  lt.rpad = rpad;
+  lt.tbase = scratch;
+  lt.t_ld = rpad;
+  lt.tm_b = &tm_bl;
+  rc = fill_member(c, &q, 0, w->tm_w, w->sb, w->sb_stride, n, w->d.bits, w->d.mode, y, ldy, lt);
+  if (rc != MP_OK) return rc;
+  rc = run_launch(c, q, s, "proj_pair_kernel (static LoRA projection)");
+  if (rc != MP_OK) return rc;
+  int ranks[mp::kMaxSlots] = {rank};
+  count_projection(c, w, m, ranks);
   return MP_OK;
 }

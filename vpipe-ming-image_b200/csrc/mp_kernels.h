@@ -13,21 +13,13 @@ constexpr int kMaxSlots = 8;       // LoRA slots (the reference's lora::Stack::k
 constexpr int kMaxSegments = 16;   // row segments with their own strength vector
 constexpr int kMaxRanges = 32;     // rank-space column ranges (slot runs) per launch
 
-// Pipeline geometry of the projection kernel.
-constexpr int kBlockN = 128;       // output features per CTA tile (MMA M)
+// Pipeline geometry of the projection kernel (CTA pairs, mp_proj.cu).
+constexpr int kBlockN = 128;       // output features per CTA (a pair covers 256: MMA M)
 constexpr int kBlockK = 64;        // K per stage == one quantization group
-constexpr int kMaxTok = 256;       // token rows per CTA tile (MMA N), at most
-constexpr int kStages = 4;
-constexpr int kXStageBytes = kMaxTok * 128;   // activation tile, SW128
-constexpr int kWStageBytes = kBlockN * 128;   // weight tile: codes or bf16, SW128 / SW64 / SW32
-constexpr int kStageBytes = kXStageBytes + kWStageBytes;
-constexpr int kProjThreads = 192;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 dequant + epilogue
+constexpr int kMaxTok = 256;       // token rows per pair tile (MMA N), at most
+constexpr int kWStageBytes = kBlockN * 128;   // weight tile: codes or bf16
 constexpr int kTmemCols = 512;
-constexpr int kAccCol = 0;         // f32 accumulator: columns [0, n_tok)
-constexpr int kACol = 256;         // dequantized weight stages: 32 columns each
-
-constexpr uint32_t kSmemBarrierBytes = 256;
-constexpr uint32_t kProjSmemBytes = kStages * kStageBytes + 1024 + kSmemBarrierBytes;
+constexpr int kMaxMembers = 4;     // projections of one input in one launch (q/k/v, w1/w3)
 
 // Device-side error word bits (OR-ed by kernels, read by mp_sync_check).
 constexpr uint32_t kErrTimeout = 1u;
@@ -45,24 +37,34 @@ struct EpilogueScale {
   int32_t range_slot[kMaxRanges];          // slot whose strength scales the range
 };
 
-struct ProjParams {
-  CUtensorMap tm_x;   // activations [M, K] bf16, box {64, n_tok}, SW128
-  CUtensorMap tm_w;   // packed codes [N, K*bits/8] u8 (box {64*bits/8, 128}) or bf16 [N, K] (SW128)
-  CUtensorMap tm_t;   // rank-space intermediate [M, R] bf16, box {64, n_tok}, SW128
-  CUtensorMap tm_b;   // stacked LoRA B [N, R] bf16, box {64, 128}, SW128
+// One projection of a launch: its weight, output and appended LoRA K tiles.
+// A launch covers the pairs [pair_begin, next member's pair_begin) for it.
+struct ProjMember {
+  CUtensorMap tm_w;   // packed codes [N, K*bits/8] u8 (box {64*bits/8, 128}, SW64/SW32)
+                      // or bf16 [N, K] (box {64, 128}, SW128)
+  CUtensorMap tm_t;   // rank-space intermediate [M, R] bf16 (box {64, n_tok/2}, SW128)
+  CUtensorMap tm_b;   // stacked LoRA B [N, R] bf16 (box {64, 128}, SW128)
+  CUtensorMap tm_y;   // output [M, N] bf16 (box {64, n_tok}, SW128)
   const uint32_t* sb; // per row, per group: bf16 scale (low half) | bf16 bias (high half)
-  void* y;            // output [M, ldy] bf16
-  int64_t ldy;
-  int32_t M, N, K;
+  int32_t N;
   int32_t bits;       // 0 dense bf16, 4 or 8 packed codes
+  int32_t sb_stride;  // u32 per row of `sb` (multiple of 4)
+  int32_t lora_ktiles;  // extra 64-wide K tiles taken from (tm_t, tm_b)
   uint32_t code_xor;  // 0x80808080 turns signed 8-bit codes into offset-binary
   float code_magic;   // float(2^23 + code) - magic == code value
-  int32_t sb_stride;  // u32 per row of `sb` (multiple of 4)
-  int32_t n_tok;      // token rows per tile: 64, 128 or 256
-  int32_t lora_ktiles;  // extra 64-wide K tiles taken from (tm_t, tm_b)
+  int32_t pair_begin;
+};
+
+struct ProjParams {
+  CUtensorMap tm_x;   // activations [M, K] bf16 (box {64, n_tok/2}, SW128), shared by all members
+  int32_t M, K;
+  int32_t n_tok;      // token rows per pair tile: 64, 128, 192 or 256
+  int32_t n_members;
+  int32_t n_pairs;    // total pairs of the launch (grid.x = 2 * n_pairs)
   uint64_t wait_limit_ns;
   uint32_t* err;      // device error word
-  EpilogueScale scale;
+  EpilogueScale scale;  // rank-space pre-GEMM only
+  ProjMember mem[kMaxMembers];
 };
 
 // Batched adaLN modulation: for every block b and token m,
