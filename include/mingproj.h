@@ -61,7 +61,7 @@ typedef struct mp_modset mp_modset;
 /* One projection weight, torch Linear layout [n out, k in]. */
 typedef struct {
   int32_t n;     /* output features */
-  int32_t k;     /* input features; multiple of 64 */
+  int32_t k;     /* input features; a multiple of 64 when packed (dense: any) */
   int32_t bits;  /* 0 = dense bf16, 8 or 4 = packed codes */
   int32_t group; /* must be MP_GROUP for packed weights */
   int32_t mode;  /* mp_quant_mode, packed weights only */
@@ -107,7 +107,9 @@ int mp_set_wait_limit(mp_ctx* ctx, uint64_t ns);
  *   packed: `data` = U32 codes [n, k*bits/32] exactly as the pack stores
  *           them (code j of a word at bits [j*bits, (j+1)*bits)), `scales`
  *           and `biases` = bf16 [n, k/64] (`biases` NULL for symmetric);
- *   dense:  `data` = bf16 [n, k]; scales/biases NULL.
+ *   dense:  `data` = bf16 [n, k]; scales/biases NULL. Any k: rows are stored
+ *           at a pitch padded to 8 elements and a ragged last K tile reads
+ *           zeros.
  * All pointers host or device. */
 int mp_weight_upload(mp_ctx* ctx, const mp_weight_desc* desc, const void* data,
                      const uint16_t* scales, const uint16_t* biases, mp_weight** out);

@@ -257,3 +257,26 @@ def test_config1_full_size_sampled_rows(ctx):
     w.free()
     err = O.rel_l2(got, ref)
     assert err <= TOL, f"config 1 sampled rel-L2 {err:.3e}"
+
+
+@pytest.mark.parametrize("m,n,k", [(357, 1024, 2730), (100, 2730, 1024)])
+def test_dense_ragged_k_with_lora(ctx, m, n, k):
+    """Dense weights of any width (the small DiT's FFN is 2730 wide): rows are
+    stored at a padded pitch and the last K tile reads zeros."""
+    rng = np.random.default_rng(m + n + k)
+    pw = P.synthetic_dense(rng, n, k)
+    w = _upload(ctx, pw)
+    a, b = P.synthetic_lora(rng, n, k, 8, b_std=0.05)
+    w.bind(2, a, b)
+    ctx.set_strength(2, 0.6)
+    ld = (k + 7) // 8 * 8
+    x = _x(rng, m, k, ld)
+    xd = _to_dev(x)[:, :k]
+    y = ctx.linear(w, xd)
+    ctx.sync_check()
+    ctx.set_strength(2, 1.0)
+    ref = O.projection(np.ascontiguousarray(x[:, :k]), pw.data, None, None, n, k, 0, False,
+                       [(a, b, 0.6)])
+    assert np.array_equal(w.read_codes().view(np.uint16).reshape(n, k), pw.data)
+    w.free()
+    assert O.rel_l2(_host(y), ref) <= TOL

@@ -65,8 +65,9 @@ struct Stack {
 
 struct mp_weight {
   mp_weight_desc d{};
-  void* w = nullptr;       // codes bytes [n, k*bits/8] or bf16 [n, k]
-  size_t w_bytes = 0;
+  void* w = nullptr;       // codes bytes [n, k*bits/8] or bf16 [n, kp]
+  size_t w_bytes = 0;      // algorithmic bytes (no padding)
+  int kp = 0;              // row pitch in elements of dense weights / LoRA A rows: k rounded up to 8
   uint32_t* sb = nullptr;  // [n, sb_stride] (bf16 scale | bf16 bias << 16)
   int sb_stride = 0;
   CUtensorMap tm_w;
@@ -205,16 +206,16 @@ int ensure_buf(mp_ctx* c, T** p, size_t* cap, size_t elems, cudaStream_t stream)
 int ensure_stack(mp_ctx* c, mp_weight* w, uint32_t mask, cudaStream_t stream) {
   Stack& st = w->stack;
   if (st.valid && st.mask == mask && st.bind_version == w->bind_version) return MP_OK;
-  const int n = w->d.n, k = w->d.k;
+  const int n = w->d.n, k = w->d.k, kp = w->kp;
   int rtot = 0;
   for (int i = 0; i < mp::kMaxSlots; ++i)
     if (mask & (1u << i)) rtot += w->rank[i];
   const int rpad = (rtot + 63) / 64 * 64;
-  int rc = ensure_buf(c, &st.a, &st.a_cap, static_cast<size_t>(rpad) * k, stream);
+  int rc = ensure_buf(c, &st.a, &st.a_cap, static_cast<size_t>(rpad) * kp, stream);
   if (rc != MP_OK) return rc;
   rc = ensure_buf(c, &st.b, &st.b_cap, static_cast<size_t>(n) * rpad, stream);
   if (rc != MP_OK) return rc;
-  MP_CUDA(c, cudaMemsetAsync(st.a, 0, static_cast<size_t>(rpad) * k * 2, stream));
+  MP_CUDA(c, cudaMemsetAsync(st.a, 0, static_cast<size_t>(rpad) * kp * 2, stream));
   MP_CUDA(c, cudaMemsetAsync(st.b, 0, static_cast<size_t>(n) * rpad * 2, stream));
   int off = 0;
   for (int i = 0; i < mp::kMaxSlots; ++i) {
@@ -222,8 +223,10 @@ int ensure_stack(mp_ctx* c, mp_weight* w, uint32_t mask, cudaStream_t stream) {
     if (!(mask & (1u << i))) continue;
     const int r = w->rank[i];
     st.ranks[i] = r;
-    MP_CUDA(c, cudaMemcpyAsync(st.a + static_cast<size_t>(off) * k, w->la[i],
-                               static_cast<size_t>(r) * k * 2, cudaMemcpyDeviceToDevice, stream));
+    MP_CUDA(c, cudaMemcpy2DAsync(st.a + static_cast<size_t>(off) * kp,
+                                 static_cast<size_t>(kp) * 2, w->la[i],
+                                 static_cast<size_t>(k) * 2, static_cast<size_t>(k) * 2, r,
+                                 cudaMemcpyDeviceToDevice, stream));
     MP_CUDA(c, cudaMemcpy2DAsync(st.b + off, static_cast<size_t>(rpad) * 2, w->lb[i],
                                  static_cast<size_t>(r) * 2, static_cast<size_t>(r) * 2, n,
                                  cudaMemcpyDeviceToDevice, stream));
@@ -231,7 +234,7 @@ int ensure_stack(mp_ctx* c, mp_weight* w, uint32_t mask, cudaStream_t stream) {
   }
   if (rpad > 0) {
     if (!encode_2d(&st.tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st.a, k, rpad,
-                   static_cast<uint64_t>(k) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+                   static_cast<uint64_t>(kp) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_2d(&st.tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st.b, rpad, n,
                    static_cast<uint64_t>(rpad) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
       return fail(c, MP_ECUDA, "tensor map encode failed (LoRA stack)");
@@ -512,8 +515,9 @@ int mp_weight_upload(mp_ctx* c, const mp_weight_desc* d, const void* data, const
                      const uint16_t* biases, mp_weight** out) {
   if (c == nullptr || d == nullptr || data == nullptr || out == nullptr) return MP_EINVAL;
   *out = nullptr;
-  if (d->n <= 0 || d->k <= 0 || d->k % 64 != 0)
-    return fail(c, MP_EINVAL, "weight shape [%d, %d]: n > 0 and k a multiple of 64 required",
+  if (d->n <= 0 || d->k <= 0 || (d->bits != 0 && d->k % 64 != 0))
+    return fail(c, MP_EINVAL,
+                "weight shape [%d, %d]: n > 0 and k > 0 required, k a multiple of 64 when packed",
                 d->n, d->k);
   if (d->bits != 0 && d->bits != 4 && d->bits != 8)
     return fail(c, MP_EINVAL, "bits must be 0, 4 or 8 (got %d)", d->bits);
@@ -533,15 +537,24 @@ int mp_weight_upload(mp_ctx* c, const mp_weight_desc* d, const void* data, const
   w->d = *d;
   const size_t n = d->n, k = d->k;
   w->w_bytes = d->bits == 0 ? n * k * 2 : n * k * d->bits / 8;
+  w->kp = (d->k + 7) / 8 * 8;
+  const size_t stored = d->bits == 0 ? n * static_cast<size_t>(w->kp) * 2 : w->w_bytes;
   auto cleanup = [&](int code) {
     cudaFree(w->w);
     cudaFree(w->sb);
     delete w;
     return code;
   };
-  cudaError_t e = cudaMalloc(&w->w, w->w_bytes);
+  cudaError_t e = cudaMalloc(&w->w, stored);
   if (e != cudaSuccess) return cleanup(cuda_fail(c, e, "cudaMalloc(weight)"));
-  e = cudaMemcpy(w->w, data, w->w_bytes, cudaMemcpyDefault);
+  if (d->bits == 0 && w->kp != d->k) {
+    e = cudaMemset(w->w, 0, stored);
+    if (e == cudaSuccess)
+      e = cudaMemcpy2D(w->w, static_cast<size_t>(w->kp) * 2, data, k * 2, k * 2, n,
+                       cudaMemcpyDefault);
+  } else {
+    e = cudaMemcpy(w->w, data, stored, cudaMemcpyDefault);
+  }
   if (e != cudaSuccess) return cleanup(cuda_fail(c, e, "cudaMemcpy(weight)"));
   if (d->bits != 0) {
     const int g = d->k / 64;
@@ -566,7 +579,8 @@ int mp_weight_upload(mp_ctx* c, const mp_weight_desc* d, const void* data, const
                    d->bits == 8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B))
       return cleanup(fail(c, MP_ECUDA, "tensor map encode failed (codes)"));
   } else {
-    if (!encode_2d(&w->tm_w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w->w, k, n, k * 2, 64, 128,
+    if (!encode_2d(&w->tm_w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w->w, k, n,
+                   static_cast<uint64_t>(w->kp) * 2, 64, 128,
                    CU_TENSOR_MAP_SWIZZLE_128B))
       return cleanup(fail(c, MP_ECUDA, "tensor map encode failed (dense weight)"));
   }
@@ -597,7 +611,13 @@ int mp_weight_read_codes(mp_ctx* c, const mp_weight* w, void* dst, size_t bytes)
                 w->w_bytes);
   int rc = use_device(c);
   if (rc != MP_OK) return rc;
-  MP_CUDA(c, cudaMemcpy(dst, w->w, bytes, cudaMemcpyDefault));
+  if (w->d.bits == 0 && w->kp != w->d.k) {
+    MP_CUDA(c, cudaMemcpy2D(dst, static_cast<size_t>(w->d.k) * 2, w->w,
+                            static_cast<size_t>(w->kp) * 2, static_cast<size_t>(w->d.k) * 2,
+                            w->d.n, cudaMemcpyDefault));
+  } else {
+    MP_CUDA(c, cudaMemcpy(dst, w->w, bytes, cudaMemcpyDefault));
+  }
   return MP_OK;
 }
 
@@ -748,18 +768,19 @@ int mp_linear_shared(mp_ctx* c, const mp_weight* const* ws, void* const* ys, con
   }
   if (rtot > 0) {
     SharedStack& sh = c->shared[key];
+    const int kp = ws[0]->kp;
     if (sh.versions != versions || sh.rtot != rtot) {
-      rc = ensure_buf(c, &sh.a, &sh.a_cap, static_cast<size_t>(rtot) * k, s);
+      rc = ensure_buf(c, &sh.a, &sh.a_cap, static_cast<size_t>(rtot) * kp, s);
       if (rc != MP_OK) return rc;
       for (int i = 0; i < count; ++i) {
         const mp_weight* w = ws[i];
         if (live_mask(c, w) == 0) continue;
-        MP_CUDA(c, cudaMemcpyAsync(sh.a + static_cast<size_t>(col[i]) * k, w->stack.a,
-                                   static_cast<size_t>(w->stack.rpad) * k * 2,
+        MP_CUDA(c, cudaMemcpyAsync(sh.a + static_cast<size_t>(col[i]) * kp, w->stack.a,
+                                   static_cast<size_t>(w->stack.rpad) * kp * 2,
                                    cudaMemcpyDeviceToDevice, s));
       }
       if (!encode_2d(&sh.tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, sh.a, k, rtot,
-                     static_cast<uint64_t>(k) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+                     static_cast<uint64_t>(kp) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
         return fail(c, MP_ECUDA, "tensor map encode failed (shared LoRA stack)");
       sh.versions = versions;
       sh.rtot = rtot;
@@ -787,6 +808,7 @@ int mp_modulation_create(mp_ctx* c, int n_blocks, const mp_weight* const* ada,
     if (d.n != d0.n || d.k != d0.k || d.bits != d0.bits || d.mode != d0.mode)
       return fail(c, MP_EINVAL, "modulation weights must share shape and format");
     if (ada_bias[i] == nullptr) return fail(c, MP_EINVAL, "modulation bias %d is NULL", i);
+    if (d.k % 8 != 0) return fail(c, MP_EINVAL, "modulation k must be a multiple of 8");
   }
   int rc = use_device(c);
   if (rc != MP_OK) return rc;
@@ -943,6 +965,7 @@ extern "C" int mp_linear_lora_static(mp_ctx* c, const mp_weight* w, const void* 
     return fail(c, MP_EINVAL, "rank %d: must be a multiple of 8 in [8, 256]", rank);
   if (reinterpret_cast<uintptr_t>(a) % 16 != 0 || reinterpret_cast<uintptr_t>(b) % 16 != 0)
     return fail(c, MP_EINVAL, "LoRA factors must be 16-byte aligned device memory");
+  if (w->d.k % 8 != 0) return fail(c, MP_EINVAL, "k must be a multiple of 8 here");
   const int rpad = (rank + 63) / 64 * 64;
   if (static_cast<size_t>(m) * rpad > MP_STATIC_RANK_SCRATCH_ELEMS)
     return fail(c, MP_EINVAL,

@@ -394,7 +394,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   const int f0 = (pair - mb.pair_begin) * (2 * kBlockN) + static_cast<int>(rank) * kBlockN;
   const int t0 = blockIdx.y * p.n_tok;
   const int tx0 = t0 + static_cast<int>(rank) * (p.n_tok / 2);
-  const int base_kt = p.K / kBlockK;
+  const int base_kt = (p.K + kBlockK - 1) / kBlockK;  // a ragged last tile (dense only) reads zeros
   const int total_kt = base_kt + mb.lora_ktiles;
 
   if (threadIdx.x == 0) {

@@ -1,0 +1,248 @@
+"""The Ming-Image DiT forward on one GPU, with every block projection and the
+batched adaLN modulation running through the mingproj kernels, and the rest
+of the block (norms, q/k RMSNorm, RoPE, attention, SwiGLU, gated residuals),
+the embedders and the final layer in torch bf16 — the DiT driver around the
+hot path.
+
+Follows the reference's MingDitMetal::forward (vpipe-ming-image,
+src/ming-dit.cc:1490-2642): one forward over the REAL rows [image | caption]
+with pads dropped and positions keeping the padded offsets
+(src/ming-layout.cc:19-60); precision as the reference's map
+(docs/MING-IMAGE.md:786-799): bf16 activations, f32 norm statistics and
+RoPE, timestep sinusoid f32 then bf16.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from .dit import DitDims, DitProjectionSet
+from .pack import PROJ_NAMES, PackedWeight, bf16_bits_to_f32
+from .proj import Context
+
+X_EMBEDDER = "all_x_embedder.2-1"
+FINAL = "all_final_layer.2-1"
+SEQ_MULTIPLE = 32
+
+
+@dataclass
+class DitModelConfig:
+    """The DiT's structural dimensions (ming::DitConfig, src/ming-config.h:34-56)."""
+    dim: int = 3840
+    n_heads: int = 30
+    n_refiner: int = 2
+    n_layers: int = 30
+    cap_feat_dim: int = 2560
+    patch_dim: int = 64
+    time_freq: int = 256
+    time_mid: int = 1024
+    adaln: int = 256
+    norm_eps: float = 1e-5
+    rope_theta: float = 256.0
+    t_scale: float = 1000.0
+    axes: tuple = (32, 48, 48)
+
+    @property
+    def head_dim(self) -> int:
+        return self.dim // self.n_heads
+
+    @property
+    def ffn(self) -> int:
+        return int(self.dim / 3 * 8)
+
+    def proj_dims(self) -> DitDims:
+        return DitDims(dim=self.dim, n_heads=self.n_heads, n_refiner=self.n_refiner,
+                       n_layers=self.n_layers, adaln=self.adaln)
+
+
+def _bf16(a) -> torch.Tensor:
+    """uint16 bf16 bits (numpy) or float array -> torch bf16 (CPU)."""
+    if isinstance(a, torch.Tensor):
+        return a.to(torch.bfloat16)
+    a = np.asarray(a)
+    if a.dtype == np.uint16:
+        return torch.from_numpy(a.view(np.int16).copy()).view(torch.bfloat16)
+    return torch.from_numpy(np.asarray(a, dtype=np.float32)).to(torch.bfloat16)
+
+
+def rope_tables(positions: np.ndarray, head_dim: int, axes, theta: float):
+    """cos / sin [rows, head_dim / 2] for interleaved pairs (f64 angles -> f32),
+    as build_rope_ (src/ming-dit.cc:1443-1486)."""
+    freqs, axis_of = [], []
+    for a, d in enumerate(axes):
+        for j in range(d // 2):
+            freqs.append(1.0 / theta ** (2.0 * j / d))
+            axis_of.append(a)
+    freqs = np.array(freqs[: head_dim // 2], dtype=np.float64)
+    axis_of = np.array(axis_of[: head_dim // 2])
+    ang = positions[:, axis_of].astype(np.float64) * freqs[None, :]
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+def layout_positions(grid_h: int, grid_w: int, cap_len: int) -> np.ndarray:
+    """[joint, 3] positions (build_layout, src/ming-layout.cc:19-60): the image
+    sits at axis-0 position roundup32(cap_len) + 1; caption row i at i + 1."""
+    img = grid_h * grid_w
+    cap_total = (cap_len + SEQ_MULTIPLE - 1) // SEQ_MULTIPLE * SEQ_MULTIPLE
+    pos = np.zeros((img + cap_len, 3), dtype=np.int64)
+    hh, ww = np.meshgrid(np.arange(grid_h), np.arange(grid_w), indexing="ij")
+    pos[:img, 0] = cap_total + 1
+    pos[:img, 1] = hh.reshape(-1)
+    pos[:img, 2] = ww.reshape(-1)
+    pos[img:, 0] = np.arange(cap_len) + 1
+    return pos
+
+
+class DitForward:
+    """One DiT on one device. `weights` maps checkpoint names to bf16 bit
+    arrays (uint16) for dense tensors, and block projections may instead be
+    PackedWeight (a w8/w4 pack)."""
+
+    def __init__(self, ctx: Context, cfg: DitModelConfig, weights: dict, device):
+        self.ctx, self.cfg, self.dev = ctx, cfg, device
+        dims = cfg.proj_dims()
+        self.dims = dims
+        self.proj = DitProjectionSet(ctx, dims)
+        for b in range(dims.n_blocks):
+            pre = dims.block_prefix(b)
+            for name in PROJ_NAMES:
+                v = weights[pre + name + ".weight"] if (pre + name + ".weight") in weights else \
+                    weights[pre + name]
+                if isinstance(v, PackedWeight):
+                    w = ctx.upload(v.n, v.k, v.bits, v.data, v.scales, v.biases, mode=v.mode)
+                else:
+                    t = _bf16(v)
+                    w = ctx.upload(t.shape[0], t.shape[1], 0, t.contiguous())
+                self.proj.blocks[b].proj[name] = w
+        # adaLN of the modulated blocks, in the order noise_refiner..., layers...
+        ada, biases, an1, fn1 = [], [], [], []
+        for b in range(cfg.n_refiner, dims.n_blocks):
+            pre = dims.block_prefix(b)
+            v = weights[pre + "adaLN_modulation.0.weight"]
+            if isinstance(v, PackedWeight):
+                ada.append(ctx.upload(v.n, v.k, v.bits, v.data, v.scales, v.biases, mode=v.mode))
+            else:
+                t = _bf16(v)
+                ada.append(ctx.upload(t.shape[0], t.shape[1], 0, t.contiguous()))
+            biases.append(_bf16(weights[pre + "adaLN_modulation.0.bias"]).to(device))
+            an1.append(_bf16(weights[pre + "attention_norm1.weight"]).to(device))
+            fn1.append(_bf16(weights[pre + "ffn_norm1.weight"]).to(device))
+        self.ada = ada
+        self.modset = ctx.modulation_set(ada, biases, an1, fn1)
+        self._keep = (biases, an1, fn1)
+        # every other tensor as a device bf16 tensor
+        self.t = {}
+        for k, v in weights.items():
+            if isinstance(v, PackedWeight):
+                continue
+            if any(k.startswith(dims.block_prefix(b) + n) for b in range(dims.n_blocks)
+                   for n in PROJ_NAMES + ("adaLN_modulation.0",)):
+                continue
+            self.t[k] = _bf16(v).to(device)
+
+    # ---- pieces ------------------------------------------------------------
+    def _rms(self, x: torch.Tensor, w: torch.Tensor | None, eps: float | None = None):
+        eps = self.cfg.norm_eps if eps is None else eps
+        xf = x.float()
+        y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+        if w is not None:
+            y = y * w.float()
+        return y.to(torch.bfloat16)
+
+    def _rope(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        xf = x.float()
+        x0, x1 = xf[..., 0::2], xf[..., 1::2]
+        c, s = cos[:, None, :], sin[:, None, :]
+        out = torch.empty_like(xf)
+        out[..., 0::2] = x0 * c - x1 * s
+        out[..., 1::2] = x0 * s + x1 * c
+        return out.to(torch.bfloat16)
+
+    def _linear(self, x: torch.Tensor, name: str) -> torch.Tensor:
+        return F.linear(x, self.t[name + ".weight"], self.t.get(name + ".bias"))
+
+    def _block(self, b: int, x: torch.Tensor, cos, sin, mod_idx: int | None, mods, nw1, nw3):
+        cfg, pre = self.cfg, self.dims.block_prefix(b)
+        t = self.t
+        R = x.shape[0]
+        H, nh, hd, FF = cfg.dim, cfg.n_heads, cfg.head_dim, cfg.ffn
+        p = self.proj.blocks[b].proj
+        modulated = mod_idx is not None
+        gain1 = nw1[mod_idx, 0] if modulated else t[pre + "attention_norm1.weight"]
+        nrm = self._rms(x, gain1)
+        q, k, v = self.ctx.linear_shared([p["attention.to_q"], p["attention.to_k"],
+                                          p["attention.to_v"]], nrm)
+        q = self._rope(self._rms(q.view(R, nh, hd), t[pre + "attention.norm_q.weight"]), cos, sin)
+        k = self._rope(self._rms(k.view(R, nh, hd), t[pre + "attention.norm_k.weight"]), cos, sin)
+        v = v.view(R, nh, hd)
+        att = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
+                                             v.transpose(0, 1)[None])
+        a = att[0].transpose(0, 1).reshape(R, H).contiguous()
+        o = self.ctx.linear(p["attention.to_out.0"], a)
+        o2 = self._rms(o, t[pre + "attention_norm2.weight"]).float()
+        if modulated:
+            x = (x.float() + torch.tanh(mods[mod_idx, 0, H:2 * H].float()) * o2).to(torch.bfloat16)
+        else:
+            x = (x.float() + o2).to(torch.bfloat16)
+        gain3 = nw3[mod_idx, 0] if modulated else t[pre + "ffn_norm1.weight"]
+        nrm = self._rms(x, gain3)
+        g, u = self.ctx.linear_shared([p["feed_forward.w1"], p["feed_forward.w3"]], nrm)
+        ld = (FF + 7) // 8 * 8
+        h = torch.empty((R, ld), dtype=torch.bfloat16, device=x.device)
+        h[:, :FF] = (F.silu(g.float()) * u.float()).to(torch.bfloat16)
+        f = self.ctx.linear(p["feed_forward.w2"], h[:, :FF])
+        f2 = self._rms(f, t[pre + "ffn_norm2.weight"]).float()
+        if modulated:
+            return (x.float() + torch.tanh(mods[mod_idx, 0, 3 * H:].float()) * f2).to(torch.bfloat16)
+        return (x.float() + f2).to(torch.bfloat16)
+
+    # ---- the forward -------------------------------------------------------
+    @torch.no_grad()
+    def forward(self, latents: torch.Tensor, cap: torch.Tensor, query_rows: int, grid_h: int,
+                grid_w: int, sigma: float) -> torch.Tensor:
+        """latents bf16 [img, patch_dim]; cap bf16 [cap_len, >= dim] (stream A in
+        rows [0, query_rows) x columns [0, cap_feat_dim)). Returns bf16
+        [img, patch_dim], the model output before the pipeline's negation."""
+        cfg, dev = self.cfg, self.dev
+        img = grid_h * grid_w
+        cap_len = cap.shape[0]
+        c, s = rope_tables(layout_positions(grid_h, grid_w, cap_len), cfg.head_dim, cfg.axes,
+                           cfg.rope_theta)
+        cos = torch.from_numpy(c).to(dev)
+        sin = torch.from_numpy(s).to(dev)
+        half = cfg.time_freq // 2
+        tt = cfg.t_scale * (1.0 - sigma)
+        f = np.exp(-math.log(10000.0) * np.arange(half, dtype=np.float64) / half)
+        emb = np.concatenate([np.cos(tt * f), np.sin(tt * f)]).astype(np.float32)
+        emb = torch.from_numpy(emb).to(dev).to(torch.bfloat16)[None]
+        temb = self._linear(F.silu(self._linear(emb, "t_embedder.mlp.0")), "t_embedder.mlp.2")
+        mods, nw1, nw3 = self.ctx.modulation(self.modset, temb.contiguous())
+        x = self._linear(latents.to(dev), X_EMBEDDER)
+        nref = cfg.n_refiner
+        for i in range(nref):
+            x = self._block(nref + i, x, cos[:img], sin[:img], i, mods, nw1, nw3)
+        ca = self._rms(cap[:query_rows, : cfg.cap_feat_dim].to(dev), self.t["cap_embedder.0.weight"])
+        ca = self._linear(ca, "cap_embedder.1")
+        cj = torch.cat([ca, cap[query_rows:, : cfg.dim].to(dev)], dim=0)
+        for i in range(nref):
+            cj = self._block(i, cj, cos[img:], sin[img:], None, mods, nw1, nw3)
+        j = torch.cat([x, cj], dim=0).contiguous()
+        for i in range(cfg.n_layers):
+            j = self._block(2 * nref + i, j, cos, sin, nref + i, mods, nw1, nw3)
+        scale = self._linear(F.silu(temb), FINAL + ".adaLN_modulation.1")[0]
+        xi = F.layer_norm(j[:img].float(), (cfg.dim,), eps=1e-6)
+        xi = (xi * (1.0 + scale.float())).to(torch.bfloat16)
+        return self._linear(xi, FINAL + ".linear")
+
+    def free(self) -> None:
+        self.proj.free()
+        for w in self.ada:
+            w.free()
+        self.modset.free()
+
+
+__all__ = ["DitForward", "DitModelConfig", "layout_positions", "rope_tables"]

@@ -48,6 +48,13 @@ def _contig(t):
     return np.ascontiguousarray(t)
 
 
+def _alloc_out(m: int, n: int, device) -> torch.Tensor:
+    """bf16 [m, n] output view whose row pitch is rounded up to 8 elements (the
+    kernels store rows with TMA, which wants 16-byte row strides)."""
+    ld = (n + 7) // 8 * 8
+    return torch.empty((m, ld), dtype=torch.bfloat16, device=device)[:, :n]
+
+
 def _stream_handle(stream) -> C.c_void_p:
     if stream is None:
         stream = torch.cuda.current_stream()
@@ -213,7 +220,7 @@ class Context:
         context's device (row stride a multiple of 8)."""
         m = x.shape[0]
         if out is None:
-            out = torch.empty((m, w.n), dtype=torch.bfloat16, device=x.device)
+            out = _alloc_out(m, w.n, x.device)
         self._check(self.lib.mp_linear(self.h, w.handle, _ptr(x), x.stride(0), _ptr(out),
                                        out.stride(0), m, _stream_handle(stream)))
         return out
@@ -221,7 +228,7 @@ class Context:
     def linear_shared(self, ws: list[Weight], x: torch.Tensor, outs=None, stream=None):
         m = x.shape[0]
         if outs is None:
-            outs = [torch.empty((m, w.n), dtype=torch.bfloat16, device=x.device) for w in ws]
+            outs = [_alloc_out(m, w.n, x.device) for w in ws]
         n = len(ws)
         W = (C.c_void_p * n)(*[w.handle.value for w in ws])
         Y = (C.c_void_p * n)(*[o.data_ptr() for o in outs])
@@ -239,7 +246,7 @@ class Context:
         [n, rank], both on the device; the slots bound to `w` are not applied."""
         m = x.shape[0]
         if out is None:
-            out = torch.empty((m, w.n), dtype=torch.bfloat16, device=x.device)
+            out = _alloc_out(m, w.n, x.device)
         a = a.contiguous()
         b = b.contiguous()
         self._check(self.lib.mp_linear_lora_static(
