@@ -1,0 +1,53 @@
+"""Batched adaLN modulation (mp_modulation_all) against the fp64 oracle: the
+reference's fill_mod (src/ming-dit.cc:2266-2273) for several blocks at once,
+mods = W temb + b, nw1 = an1 (1 + mods[0:H]), nw3 = fn1 (1 + mods[2H:3H])."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from mingproj import pack as P
+
+pytestmark = pytest.mark.gpu
+
+TOL = 5e-3
+
+
+def _dev(bits):
+    return torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16).cuda()
+
+
+@pytest.mark.parametrize("bits", [8, 4, 0])
+@pytest.mark.parametrize("m", [1, 2, 4])
+@pytest.mark.parametrize("H,K", [(256, 256), (384, 3840)])
+def test_modulation_matches_oracle(ctx, bits, m, H, K):
+    rng = np.random.default_rng(bits * 100 + m * 10 + H)
+    nb = 3
+    ws, pws, biases, an1, fn1 = [], [], [], [], []
+    for _ in range(nb):
+        pw = (P.synthetic_affine(rng, 4 * H, K, bits) if bits else
+              P.synthetic_dense(rng, 4 * H, K, std=0.05))
+        pws.append(pw)
+        ws.append(ctx.upload(pw.n, pw.k, pw.bits, pw.data, pw.scales, pw.biases))
+        biases.append(P.f32_to_bf16_bits(rng.normal(0, 0.02, 4 * H).astype(np.float32)))
+        an1.append(P.f32_to_bf16_bits((1 + 0.1 * rng.normal(size=H)).astype(np.float32)))
+        fn1.append(P.f32_to_bf16_bits((1 + 0.1 * rng.normal(size=H)).astype(np.float32)))
+    mset = ctx.modulation_set(ws, biases, an1, fn1)
+    temb = P.f32_to_bf16_bits(rng.normal(size=(m, K)).astype(np.float32))
+    mods, nw1, nw3 = ctx.modulation(mset, _dev(temb))
+    ctx.sync_check()
+    mods = mods.float().cpu().numpy()
+    nw1 = nw1.float().cpu().numpy()
+    nw3 = nw3.float().cpu().numpy()
+    mset.free()
+    for w in ws:
+        w.free()
+    for b in range(nb):
+        ref = O.modulation(temb, pws[b].data, pws[b].scales, pws[b].biases, biases[b], 4 * H, K,
+                           bits)
+        assert O.rel_l2(mods[b], ref) <= TOL
+        # the fold reads the bf16-rounded mods, as the reference's modulate does
+        mb = O.bf16_to_f64(P.f32_to_bf16_bits(mods[b].astype(np.float32)))
+        want1 = O.bf16_to_f64(an1[b])[None, :] * (1.0 + mb[:, :H])
+        want3 = O.bf16_to_f64(fn1[b])[None, :] * (1.0 + mb[:, 2 * H:3 * H])
+        assert O.rel_l2(nw1[b], want1) <= 4e-3 and O.rel_l2(nw3[b], want3) <= 4e-3

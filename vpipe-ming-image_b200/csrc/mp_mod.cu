@@ -8,9 +8,11 @@
 // pass here: the work is reading the packed adaLN weights once (HBM-bound),
 // with M <= 4 tokens riding along in registers.
 //
-// Grid: (ceil(N / 64), n_blocks), 256 threads. A half-warp owns one output
-// row at a time and walks its codes in 16-byte chunks (16 w8 codes, 32 w4
-// codes or 8 bf16 weights per lane per step).
+// Grid: (ceil(N / 128), n_blocks), 256 threads. A half-warp owns 8 output
+// rows and walks them together in 16-byte chunks (16 w8 codes, 32 w4 codes
+// or 8 bf16 weights per lane per row per step), so every lane has 8
+// independent loads in flight; the temb slice of a chunk is loaded once and
+// reused across the 8 rows.
 #include <cuda_runtime.h>
 
 #include "mp_device.cuh"
@@ -21,99 +23,109 @@ namespace mp {
 namespace {
 
 constexpr int kModThreads = 256;
-constexpr int kModRowsPerCta = 64;
+constexpr int kRowsPerHalfWarp = 8;
+constexpr int kModRowsPerCta = 16 * kRowsPerHalfWarp;
 
-__device__ __forceinline__ float dot_tok(const float* t, int k) { return t[k]; }
-
-}  // namespace
-
-__global__ void __launch_bounds__(kModThreads) mod_kernel(const __grid_constant__ ModParams p) {
-  extern __shared__ float temb_s[];  // [M][K] fp32
-  const ModBlock blk = p.blocks[blockIdx.y];
-  for (int i = threadIdx.x; i < p.M * p.K; i += blockDim.x) {
-    temb_s[i] = bf16_bits_to_f32(p.temb[i]);
-  }
-  __syncthreads();
-
-  const int hw = threadIdx.x >> 4;  // half-warp 0..15
-  const int hl = threadIdx.x & 15;
-  const int row_bytes = p.bits == 0 ? p.K * 2 : p.K * p.bits / 8;
-  const int nchunks = row_bytes / 16;
-
-  for (int rr = 0; rr < kModRowsPerCta / 16; ++rr) {
-    const int n = blockIdx.x * kModRowsPerCta + rr * 16 + hw;
-    const bool row_ok = n < p.N;
-    float acc[kModMaxTok] = {0.f, 0.f, 0.f, 0.f};
-    if (row_ok) {
-      const uint8_t* wrow = blk.w + static_cast<size_t>(n) * row_bytes;
-      const uint32_t* sbrow = blk.sb + static_cast<size_t>(n) * p.sb_stride;
-      for (int ch = hl; ch < nchunks; ch += 16) {
-        const uint4 c = ld_global_nc_v4(wrow + static_cast<size_t>(ch) * 16);
-        uint32_t words[4];
-        words[0] = c.x; words[1] = c.y; words[2] = c.z; words[3] = c.w;
-        if (p.bits == 0) {
-          const int k0 = ch * 8;
+// Weights of one 16-byte chunk (`per` of them) -> fp32, for chunk starting at k0.
+template <int BITS>
+__device__ __forceinline__ void chunk_weights(const uint4& c, uint32_t sbw, uint32_t code_xor,
+                                              float magic, float* wv) {
+  const uint32_t words[4] = {c.x, c.y, c.z, c.w};
+  if constexpr (BITS == 0) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float w0 = bf16_bits_to_f32(words[i] & 0xFFFFu);
-            const float w1 = bf16_bits_to_f32(words[i] >> 16);
+    for (int i = 0; i < 4; ++i) {
+      wv[2 * i] = bf16_bits_to_f32(words[i] & 0xFFFFu);
+      wv[2 * i + 1] = bf16_bits_to_f32(words[i] >> 16);
+    }
+  } else {
+    const float sc = bf16_bits_to_f32(sbw & 0xFFFFu);
+    const float bi = bf16_bits_to_f32(sbw >> 16);
+    if constexpr (BITS == 8) {
 #pragma unroll
-            for (int m = 0; m < kModMaxTok; ++m) {
-              if (m < p.M) {
-                acc[m] = fmaf(w0, dot_tok(temb_s + m * p.K, k0 + 2 * i), acc[m]);
-                acc[m] = fmaf(w1, dot_tok(temb_s + m * p.K, k0 + 2 * i + 1), acc[m]);
-              }
-            }
-          }
-        } else if (p.bits == 8) {
-          const int k0 = ch * 16;
-          const uint32_t sbw = sbrow[k0 / 64];
-          const float sc = bf16_bits_to_f32(sbw & 0xFFFFu);
-          const float bi = bf16_bits_to_f32(sbw >> 16);
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t w = words[i] ^ code_xor;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint32_t w = words[i] ^ p.code_xor;
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-              const float qv =
-                  __uint_as_float(__byte_perm(w, 0x4Bu, 0x4550u | static_cast<uint32_t>(b))) -
-                  p.code_magic;
-              const float wv = fmaf(qv, sc, bi);
-#pragma unroll
-              for (int m = 0; m < kModMaxTok; ++m)
-                if (m < p.M) acc[m] = fmaf(wv, temb_s[m * p.K + k0 + 4 * i + b], acc[m]);
-            }
-          }
-        } else {
-          const int k0 = ch * 32;
-          const uint32_t sbw = sbrow[k0 / 64];
-          const float sc = bf16_bits_to_f32(sbw & 0xFFFFu);
-          const float bi = bf16_bits_to_f32(sbw >> 16);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint32_t w = words[i];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float qv = static_cast<float>((w >> (4 * j)) & 0xFu);
-              const float wv = fmaf(qv, sc, bi);
-#pragma unroll
-              for (int m = 0; m < kModMaxTok; ++m)
-                if (m < p.M) acc[m] = fmaf(wv, temb_s[m * p.K + k0 + 8 * i + j], acc[m]);
-            }
-          }
+        for (int b = 0; b < 4; ++b) {
+          const float q =
+              __uint_as_float(__byte_perm(w, 0x4Bu, 0x4550u | static_cast<uint32_t>(b))) - magic;
+          wv[4 * i + b] = fmaf(q, sc, bi);
         }
       }
-    }
+    } else {
 #pragma unroll
-    for (int m = 0; m < kModMaxTok; ++m) {
+      for (int i = 0; i < 4; ++i) {
 #pragma unroll
-      for (int off = 8; off > 0; off >>= 1) acc[m] += __shfl_xor_sync(0xFFFFFFFFu, acc[m], off);
+        for (int j = 0; j < 8; ++j)
+          wv[8 * i + j] = fmaf(static_cast<float>((words[i] >> (4 * j)) & 0xFu), sc, bi);
+      }
     }
-    if (row_ok && hl == 0) {
+  }
+}
+
+template <int BITS, int MT>
+__device__ void mod_rows(const ModParams& p, const ModBlock& blk, const float* temb_s, int row0,
+                         int hl) {
+  constexpr int per = BITS == 0 ? 8 : (BITS == 8 ? 16 : 32);  // weights per 16-byte chunk
+  const int row_bytes = BITS == 0 ? p.K * 2 : p.K * BITS / 8;
+  const int nchunks = row_bytes / 16;
+  float acc[kRowsPerHalfWarp][MT];
+#pragma unroll
+  for (int r = 0; r < kRowsPerHalfWarp; ++r)
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[r][m] = 0.0f;
+
+  for (int ch = hl; ch < nchunks; ch += 16) {
+    const int k0 = ch * per;
+    uint4 c[kRowsPerHalfWarp];
+    uint32_t sbw[kRowsPerHalfWarp];
+#pragma unroll
+    for (int r = 0; r < kRowsPerHalfWarp; ++r) {
+      const int n = min(row0 + r, p.N - 1);
+      c[r] = ld_global_nc_v4(blk.w + static_cast<size_t>(n) * row_bytes +
+                             static_cast<size_t>(ch) * 16);
+      sbw[r] = BITS == 0 ? 0u : blk.sb[static_cast<size_t>(n) * p.sb_stride + k0 / 64];
+    }
+    float t[MT][per];
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int i = 0; i < per; ++i) t[m][i] = m < p.M ? temb_s[m * p.K + k0 + i] : 0.0f;
+#pragma unroll
+    for (int r = 0; r < kRowsPerHalfWarp; ++r) {
+      float wv[per];
+      chunk_weights<BITS>(c[r], sbw[r], p.code_xor, p.code_magic, wv);
+#pragma unroll
+      for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int i = 0; i < per; ++i) acc[r][m] = fmaf(wv[i], t[m][i], acc[r][m]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kRowsPerHalfWarp; ++r)
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1)
+        acc[r][m] += __shfl_xor_sync(0xFFFFFFFFu, acc[r][m], off);
+
+  if (hl < kRowsPerHalfWarp) {
+    // lane hl of the half-warp writes row row0 + hl
+    float a[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      a[m] = acc[0][m];
+#pragma unroll
+      for (int r = 1; r < kRowsPerHalfWarp; ++r) a[m] = (hl == r) ? acc[r][m] : a[m];
+    }
+    const int n = row0 + hl;
+    if (n < p.N) {
       const float bias = bf16_bits_to_f32(blk.bias[n]);
       for (int m = 0; m < p.M; ++m) {
+        float v = a[0];
+#pragma unroll
+        for (int mm = 1; mm < MT; ++mm) v = (m == mm) ? a[mm] : v;
         const size_t bm = static_cast<size_t>(blockIdx.y) * p.M + m;
-        const __nv_bfloat16 mv = __float2bfloat16_rn(acc[m] + bias);
+        const __nv_bfloat16 mv = __float2bfloat16_rn(v + bias);
         reinterpret_cast<__nv_bfloat16*>(p.mods)[bm * p.N + n] = mv;
         const float scale1 = 1.0f + __bfloat162float(mv);
         if (p.nw1 != nullptr && blk.an1 != nullptr && n < p.H) {
@@ -129,16 +141,48 @@ __global__ void __launch_bounds__(kModThreads) mod_kernel(const __grid_constant_
   }
 }
 
-cudaError_t launch_mod(const ModParams& p, cudaStream_t stream) {
+}  // namespace
+
+template <int BITS, int MT>
+__global__ void __launch_bounds__(kModThreads) mod_kernel(const __grid_constant__ ModParams p) {
+  extern __shared__ float temb_s[];  // [M][K] fp32
+  const ModBlock blk = p.blocks[blockIdx.y];
+  for (int i = threadIdx.x; i < p.M * p.K; i += blockDim.x) {
+    temb_s[i] = bf16_bits_to_f32(p.temb[i]);
+  }
+  __syncthreads();
+  const int hw = threadIdx.x >> 4;  // half-warp 0..15
+  const int hl = threadIdx.x & 15;
+  const int row0 = blockIdx.x * kModRowsPerCta + hw * kRowsPerHalfWarp;
+  mod_rows<BITS, MT>(p, blk, temb_s, row0, hl);
+}
+
+template <int BITS, int MT>
+cudaError_t launch_mod_t(const ModParams& p, cudaStream_t stream) {
   const size_t smem = static_cast<size_t>(p.M) * p.K * sizeof(float);
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(mod_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(mod_kernel<BITS, MT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
   dim3 grid((p.N + kModRowsPerCta - 1) / kModRowsPerCta, p.n_blocks);
-  mod_kernel<<<grid, kModThreads, smem, stream>>>(p);
+  mod_kernel<BITS, MT><<<grid, kModThreads, smem, stream>>>(p);
   return cudaGetLastError();
+}
+
+// Token count rounded up to 1, 2 or 4: registers scale with it.
+template <int BITS>
+cudaError_t launch_mod_bits(const ModParams& p, cudaStream_t stream) {
+  if (p.M == 1) return launch_mod_t<BITS, 1>(p, stream);
+  if (p.M == 2) return launch_mod_t<BITS, 2>(p, stream);
+  return launch_mod_t<BITS, 4>(p, stream);
+}
+
+cudaError_t launch_mod(const ModParams& p, cudaStream_t stream) {
+  if (p.bits == 8) return launch_mod_bits<8>(p, stream);
+  if (p.bits == 4) return launch_mod_bits<4>(p, stream);
+  return launch_mod_bits<0>(p, stream);
 }
 
 }  // namespace mp
