@@ -19,6 +19,7 @@
 
 namespace mp {
 cudaError_t launch_proj_pair(const ProjParams& p, cudaStream_t stream);
+cudaError_t launch_lora_reduce(const ReduceParams& p, cudaStream_t stream);
 int pick_ntok_pair(int m, int pairs);
 cudaError_t launch_mod(const ModParams& p, cudaStream_t stream);
 }  // namespace mp
@@ -107,6 +108,8 @@ struct mp_ctx {
   uint32_t* err_word = nullptr;
   uint16_t* scratch = nullptr;  // rank-space intermediate
   size_t scratch_cap = 0;       // elements
+  float* part = nullptr;        // split-K partial sums of the rank-space pre-GEMM
+  size_t part_cap = 0;          // elements
   uint64_t wait_limit_ns = 2000000000ull;
   mp_engagement eng{};
   std::map<std::vector<uintptr_t>, SharedStack> shared;
@@ -164,6 +167,10 @@ bool encode_y(CUtensorMap* m, const void* y, int64_t ldy, int n, int rows, int n
                    static_cast<uint64_t>(rows), static_cast<uint64_t>(ldy) * 2, 64,
                    static_cast<uint32_t>(ntok), CU_TENSOR_MAP_SWIZZLE_128B);
 }
+
+// Token rows of one accumulator (MMA N) for a pair tile of `ntok` rows: the
+// TMA boxes of x, the rank-space intermediate and y are sized by it.
+int sub_tok(int ntok) { return std::min(ntok, mp::kMaxTok); }
 
 // Feature pairs (256 output rows) a projection of n outputs occupies.
 int pairs_of(int n) { return (n + 2 * mp::kBlockN - 1) / (2 * mp::kBlockN); }
@@ -326,14 +333,14 @@ int fill_member(mp_ctx* c, ProjParams* p, int i, const CUtensorMap& tm_w, const 
   mb.bits = bits;
   const bool sym = bits == 8 && mode == MP_QUANT_SYMMETRIC;
   mb.code_xor = sym ? 0x80808080u : 0u;
-  mb.code_magic = sym ? 8388736.0f : 8388608.0f;
-  if (!encode_y(&mb.tm_y, y, ldy, n, p->M, p->n_tok))
+  mb.code_offset = sym ? 32896.0f : 32768.0f;
+  if (!encode_y(&mb.tm_y, y, ldy, n, p->M, sub_tok(p->n_tok)))
     return fail(c, MP_ECUDA, "tensor map encode failed (output)");
   mb.lora_ktiles = 0;
   if (lt.rpad > 0) {
     mb.lora_ktiles = lt.rpad / 64;
     if (!encode_2d(&mb.tm_t, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lt.tbase, lt.rpad, p->M,
-                   static_cast<uint64_t>(lt.t_ld) * 2, 64, static_cast<uint32_t>(p->n_tok / 2),
+                   static_cast<uint64_t>(lt.t_ld) * 2, 64, static_cast<uint32_t>(sub_tok(p->n_tok) / 2),
                    CU_TENSOR_MAP_SWIZZLE_128B))
       return fail(c, MP_ECUDA, "tensor map encode failed (rank-space intermediate)");
     mb.tm_b = *lt.tm_b;
@@ -344,7 +351,7 @@ int fill_member(mp_ctx* c, ProjParams* p, int i, const CUtensorMap& tm_w, const 
 // Sets the launch-wide fields for `count` members whose output widths are
 // `ns`, choosing the token tile from the total pair count.
 int begin_launch(mp_ctx* c, ProjParams* p, const void* x, int64_t ldx, int k, int m,
-                 const int* ns, int count) {
+                 const int* ns, int count, int n_tok = 0) {
   base_params(c, p);
   int pairs = 0;
   for (int i = 0; i < count; ++i) {
@@ -355,9 +362,9 @@ int begin_launch(mp_ctx* c, ProjParams* p, const void* x, int64_t ldx, int k, in
   p->n_pairs = pairs;
   p->M = m;
   p->K = k;
-  p->n_tok = mp::pick_ntok_pair(m, pairs);
+  p->n_tok = n_tok > 0 ? n_tok : mp::pick_ntok_pair(m, pairs);
   if (!encode_2d(&p->tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, k, m,
-                 static_cast<uint64_t>(ldx) * 2, 64, static_cast<uint32_t>(p->n_tok / 2),
+                 static_cast<uint64_t>(ldx) * 2, 64, static_cast<uint32_t>(sub_tok(p->n_tok) / 2),
                  CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(c, MP_ECUDA, "tensor map encode failed (x)");
   return MP_OK;
@@ -394,17 +401,76 @@ void count_projection(mp_ctx* c, const mp_weight* w, int m, const int* ranks) {
   c->eng.bytes += bytes;
 }
 
+}  // namespace
+
+namespace mp {
+
+// K splits for a launch of `pairs` feature pairs x 256-token tiles over
+// `base_kt` 64-wide K tiles, whose fp32 partials are [S, m, r]: the S with
+// the least modelled time, counted in K stages. One wave is 74 pairs (one
+// CTA per SM); a CTA adds ~5 stages of set-up and epilogue; a second pass
+// adds ~6 stages plus its partial-sum traffic (~2.25 MB per stage).
+int choose_ksplit(int m, int pairs, int base_kt, int r) {
+  const int tiles = (m + 255) / 256;
+  double best = 1e300;
+  int best_s = 1;
+  for (int s = 1; s <= 16 && s <= base_kt; ++s) {
+    const int kps = (base_kt + s - 1) / s;
+    if ((base_kt + kps - 1) / kps != s) continue;  // every split gets at least one tile
+    const long long units = static_cast<long long>(pairs) * tiles * s;
+    const long long waves = (units + 73) / 74;
+    double cost = static_cast<double>(waves) * (kps + 5.0);
+    if (s > 1) cost += 6.0 + static_cast<double>(s) * m * r * 4.0 / 2.25e6;
+    if (cost < best - 1e-9) {
+      best = cost;
+      best_s = s;
+    }
+  }
+  return best_s;
+}
+
+}  // namespace mp
+
+namespace {
+
 // Rank-space pre-GEMM: T[m, 0:rtot] = scale ⊙ (x · A^T), into ctx scratch.
+// 256-token tiles; when the K loop is split, each split writes fp32 partial
+// sums and lora_reduce_kernel adds them (in split order), scales and rounds.
 int launch_lora_down(mp_ctx* c, const CUtensorMap& tm_a, int rtot, const mp::EpilogueScale& es,
                      const void* x, int64_t ldx, int k, int m, cudaStream_t stream) {
   ProjParams p;
-  int rc = begin_launch(c, &p, x, ldx, k, m, &rtot, 1);
+  int rc = begin_launch(c, &p, x, ldx, k, m, &rtot, 1, mp::kMaxTok);
   if (rc != MP_OK) return rc;
   p.scale = es;
   rc = fill_member(c, &p, 0, tm_a, nullptr, 0, rtot, 0, 0, c->scratch, rtot, LoraTiles{});
   if (rc != MP_OK) return rc;
+  const int base_kt = (k + mp::kBlockK - 1) / mp::kBlockK;
+  const int ks = mp::choose_ksplit(m, p.n_pairs, base_kt, rtot);
+  if (ks > 1) {
+    rc = ensure_buf(c, &c->part, &c->part_cap, static_cast<size_t>(ks) * m * rtot, stream);
+    if (rc != MP_OK) return rc;
+    p.ksplit = ks;
+    p.kt_per_split = (base_kt + ks - 1) / ks;
+    p.part = c->part;
+    p.part_ld = rtot;
+  }
   rc = run_launch(c, p, stream, "proj_pair_kernel (rank-space pre-GEMM)");
   if (rc != MP_OK) return rc;
+  if (ks > 1) {
+    mp::ReduceParams rp;
+    std::memset(&rp, 0, sizeof(rp));
+    rp.part = c->part;
+    rp.ksplit = ks;
+    rp.M = m;
+    rp.R = rtot;
+    rp.part_ld = rtot;
+    rp.out = c->scratch;
+    rp.out_ld = rtot;
+    rp.scale = es;
+    cudaError_t e = mp::launch_lora_reduce(rp, stream);
+    if (e != cudaSuccess) return cuda_fail(c, e, "lora_reduce_kernel");
+    c->eng.kernels += 1;
+  }
   c->eng.lora_down += 1;
   return MP_OK;
 }
@@ -484,6 +550,7 @@ int mp_destroy(mp_ctx* c) {
   cudaDeviceSynchronize();
   cudaFree(c->err_word);
   cudaFree(c->scratch);
+  cudaFree(c->part);
   for (auto& kv : c->shared) cudaFree(kv.second.a);
   delete c;
   return MP_OK;

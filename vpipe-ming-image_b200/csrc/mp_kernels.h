@@ -16,7 +16,8 @@ constexpr int kMaxRanges = 32;     // rank-space column ranges (slot runs) per l
 // Pipeline geometry of the projection kernel (CTA pairs, mp_proj.cu).
 constexpr int kBlockN = 128;       // output features per CTA (a pair covers 256: MMA M)
 constexpr int kBlockK = 64;        // K per stage == one quantization group
-constexpr int kMaxTok = 256;       // token rows per pair tile (MMA N), at most
+constexpr int kMaxTok = 256;       // token rows of one accumulator (MMA N), at most
+constexpr int kMaxTileTok = 512;   // token rows per pair tile (two accumulators), at most
 constexpr int kWStageBytes = kBlockN * 128;   // weight tile: codes or bf16
 constexpr int kTmemCols = 512;
 constexpr int kMaxMembers = 4;     // projections of one input in one launch (q/k/v, w1/w3)
@@ -42,29 +43,50 @@ struct EpilogueScale {
 struct ProjMember {
   CUtensorMap tm_w;   // packed codes [N, K*bits/8] u8 (box {64*bits/8, 128}, SW64/SW32)
                       // or bf16 [N, K] (box {64, 128}, SW128)
-  CUtensorMap tm_t;   // rank-space intermediate [M, R] bf16 (box {64, n_tok/2}, SW128)
+  CUtensorMap tm_t;   // rank-space intermediate [M, R] bf16 (box {64, sub/2}, SW128)
   CUtensorMap tm_b;   // stacked LoRA B [N, R] bf16 (box {64, 128}, SW128)
-  CUtensorMap tm_y;   // output [M, N] bf16 (box {64, n_tok}, SW128)
+  CUtensorMap tm_y;   // output [M, N] bf16 (box {64, sub}, SW128); sub = min(n_tok, 256)
   const uint32_t* sb; // per row, per group: bf16 scale (low half) | bf16 bias (high half)
   int32_t N;
   int32_t bits;       // 0 dense bf16, 4 or 8 packed codes
   int32_t sb_stride;  // u32 per row of `sb` (multiple of 4)
   int32_t lora_ktiles;  // extra 64-wide K tiles taken from (tm_t, tm_b)
   uint32_t code_xor;  // 0x80808080 turns signed 8-bit codes into offset-binary
-  float code_magic;   // float(2^23 + code) - magic == code value
+  float code_offset;  // 32768 + the codes' zero point (128 for signed 8-bit codes, else 0)
   int32_t pair_begin;
 };
 
 struct ProjParams {
-  CUtensorMap tm_x;   // activations [M, K] bf16 (box {64, n_tok/2}, SW128), shared by all members
+  CUtensorMap tm_x;   // activations [M, K] bf16 (box {64, sub/2}, SW128), shared by all members
   int32_t M, K;
-  int32_t n_tok;      // token rows per pair tile: 64, 128, 192 or 256
+  int32_t n_tok;      // token rows per pair tile: 64, 128, 256 or 512 (two accumulators)
   int32_t n_members;
   int32_t n_pairs;    // total pairs of the launch (grid.x = 2 * n_pairs)
   uint64_t wait_limit_ns;
   uint32_t* err;      // device error word
   EpilogueScale scale;  // rank-space pre-GEMM only
+  // Split-K (grid.z = ksplit > 1, a single member): split z runs the K tiles
+  // [z * kt_per_split, min((z + 1) * kt_per_split, K tiles)) (the last split
+  // also takes the member's LoRA K tiles) and writes its fp32 partial sums,
+  // unscaled, to part[z][t][f] (row stride part_ld) instead of the bf16
+  // output; lora_reduce_kernel adds the splits in z order.
+  int32_t ksplit;
+  int32_t kt_per_split;
+  float* part;
+  int32_t part_ld;
   ProjMember mem[kMaxMembers];
+};
+
+// Second pass of a split-K launch: out[t, j] = bf16(scale(t, j) * sum_z
+// part[z][t][j]) for t < M, j < R, the splits added in z order (the result
+// does not depend on launch timing). `scale` as in EpilogueScale; with
+// enabled == 0 the sum is stored unscaled.
+struct ReduceParams {
+  const float* part;
+  int32_t ksplit, M, R, part_ld;
+  uint16_t* out;
+  int32_t out_ld;
+  EpilogueScale scale;
 };
 
 // Batched adaLN modulation: for every block b and token m,
