@@ -405,28 +405,36 @@ void count_projection(mp_ctx* c, const mp_weight* w, int m, const int* ranks) {
 
 namespace mp {
 
-// K splits for a launch of `pairs` feature pairs x 256-token tiles over
-// `base_kt` 64-wide K tiles, whose fp32 partials are [S, m, r]: the S with
-// the least modelled time, counted in K stages. One wave is 74 pairs (one
-// CTA per SM); a CTA adds ~5 stages of set-up and epilogue; a second pass
-// adds ~6 stages plus its partial-sum traffic (~2.25 MB per stage).
-int choose_ksplit(int m, int pairs, int base_kt, int r) {
-  const int tiles = (m + 255) / 256;
-  double best = 1e300;
-  int best_s = 1;
-  for (int s = 1; s <= 16 && s <= base_kt; ++s) {
-    const int kps = (base_kt + s - 1) / s;
-    if ((base_kt + kps - 1) / kps != s) continue;  // every split gets at least one tile
-    const long long units = static_cast<long long>(pairs) * tiles * s;
-    const long long waves = (units + 73) / 74;
-    double cost = static_cast<double>(waves) * (kps + 5.0);
-    if (s > 1) cost += 6.0 + static_cast<double>(s) * m * r * 4.0 / 2.25e6;
-    if (cost < best - 1e-9) {
-      best = cost;
-      best_s = s;
+struct SplitChoice {
+  int n_tok;
+  int ksplit;
+};
+
+// Token tile and K splits of a rank-space pre-GEMM of `pairs` feature pairs
+// over m rows and `base_kt` 64-wide K tiles (r rank columns): the pair with
+// the least modelled time. A 64-wide K stage takes ~800 cycles on a
+// 256-token tile and ~1150 on a 512-token tile, a CTA adds ~6000 cycles of
+// set-up and epilogue, 74 pairs run at once (one CTA per SM), and the second
+// pass of a split launch costs ~2 us plus its traffic at ~4 TB/s.
+SplitChoice choose_ksplit(int m, int pairs, int base_kt, int r) {
+  SplitChoice best{kMaxTok, 1};
+  double best_us = 1e300;
+  for (int nt : {kMaxTileTok, kMaxTok}) {
+    const double stage_cycles = nt > kMaxTok ? 1150.0 : 800.0;
+    const long long tiles = (m + nt - 1) / nt;
+    for (int s = 1; s <= kMaxSplits && s <= base_kt; ++s) {
+      const int kps = (base_kt + s - 1) / s;
+      if ((base_kt + kps - 1) / kps != s) continue;  // every split gets at least one tile
+      const long long waves = (pairs * tiles * s + 73) / 74;
+      double us = static_cast<double>(waves) * (kps * stage_cycles + 6000.0) / 1900.0;
+      if (s > 1) us += 2.0 + (static_cast<double>(s) * 4.0 + 2.0) * m * r / 4.0e6;
+      if (us < best_us - 1e-9) {
+        best_us = us;
+        best = SplitChoice{nt, s};
+      }
     }
   }
-  return best_s;
+  return best;
 }
 
 }  // namespace mp
@@ -434,18 +442,19 @@ int choose_ksplit(int m, int pairs, int base_kt, int r) {
 namespace {
 
 // Rank-space pre-GEMM: T[m, 0:rtot] = scale ⊙ (x · A^T), into ctx scratch.
-// 256-token tiles; when the K loop is split, each split writes fp32 partial
-// sums and lora_reduce_kernel adds them (in split order), scales and rounds.
+// When the K loop is split, each split writes fp32 partial sums and
+// lora_reduce_kernel adds them (in split order), scales and rounds.
 int launch_lora_down(mp_ctx* c, const CUtensorMap& tm_a, int rtot, const mp::EpilogueScale& es,
                      const void* x, int64_t ldx, int k, int m, cudaStream_t stream) {
+  const int base_kt = (k + mp::kBlockK - 1) / mp::kBlockK;
+  const mp::SplitChoice sc = mp::choose_ksplit(m, pairs_of(rtot), base_kt, rtot);
+  const int ks = sc.ksplit;
   ProjParams p;
-  int rc = begin_launch(c, &p, x, ldx, k, m, &rtot, 1, mp::kMaxTok);
+  int rc = begin_launch(c, &p, x, ldx, k, m, &rtot, 1, sc.n_tok);
   if (rc != MP_OK) return rc;
   p.scale = es;
   rc = fill_member(c, &p, 0, tm_a, nullptr, 0, rtot, 0, 0, c->scratch, rtot, LoraTiles{});
   if (rc != MP_OK) return rc;
-  const int base_kt = (k + mp::kBlockK - 1) / mp::kBlockK;
-  const int ks = mp::choose_ksplit(m, p.n_pairs, base_kt, rtot);
   if (ks > 1) {
     rc = ensure_buf(c, &c->part, &c->part_cap, static_cast<size_t>(ks) * m * rtot, stream);
     if (rc != MP_OK) return rc;

@@ -21,6 +21,7 @@ constexpr int kMaxTileTok = 512;   // token rows per pair tile (two accumulators
 constexpr int kWStageBytes = kBlockN * 128;   // weight tile: codes or bf16
 constexpr int kTmemCols = 512;
 constexpr int kMaxMembers = 4;     // projections of one input in one launch (q/k/v, w1/w3)
+constexpr int kMaxSplits = 16;     // K splits of a split-K launch
 
 // Device-side error word bits (OR-ed by kernels, read by mp_sync_check).
 constexpr uint32_t kErrTimeout = 1u;

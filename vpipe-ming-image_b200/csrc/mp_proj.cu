@@ -374,7 +374,7 @@ __device__ void pair_epilogue(const ProjParams& p, const ProjMember& mb, const P
         const int col = g * cols + c * 32;
         uint32_t v[32];
         MP_TMEM_LD_32X32B_X32(tmem + lane_base + static_cast<uint32_t>(j * tg.sub + col), v);
-        tmem_wait_ld();
+        MP_TMEM_WAIT_LD_REGS32(v);
         if (f < mb.N) {
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) {
@@ -394,35 +394,41 @@ __device__ void pair_epilogue(const ProjParams& p, const ProjMember& mb, const P
     // word (2 features) index within a staging row of 64 features
     const uint32_t wi = static_cast<uint32_t>(16 * (q & 1) + (lane >> 1));
     const uint32_t chunk = wi >> 2, in_chunk = (wi & 3u) << 2;
-    for (int j = 0; j < tg.n_sub; ++j) {
+    // Chunks of 32 token columns, in (accumulator, column) order.
+    const int nck = cols / 32;
+    const int total = tg.n_sub * nck;
+    auto col_of = [&](int i) { return (i / nck) * tg.sub + g * cols + (i % nck) * 32; };
+    auto convert = [&](int i, uint32_t(&v)[32]) {
+      const int j = i / nck;
+      const int col = g * cols + (i % nck) * 32;  // within accumulator j
       // staging half tile of features [64h, 64h + 64) of accumulator j
       const uint32_t stage =
           smem_u32(sm.tiles) + static_cast<uint32_t>(2 * j + (q >> 1)) * half_bytes;
-      for (int c = 0; c < cols / 32; ++c) {
-        const int col = g * cols + c * 32;
-        uint32_t v[32];
-        MP_TMEM_LD_32X32B_X32(tmem + lane_base + static_cast<uint32_t>(j * tg.sub + col), v);
-        tmem_wait_ld();
-        if (p.scale.enabled) {
+      if (p.scale.enabled) {
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const float sc =
-                slot >= 0 ? pair_scale(p.scale, t0 + j * tg.sub + col + jj, slot) : 0.0f;
-            v[jj] = __float_as_uint(__uint_as_float(v[jj]) * sc);
-          }
-        }
-#pragma unroll
-        for (int jj = 0; jj < 32; jj += 2) {
-          const float mine_even = __uint_as_float(v[jj]);
-          const float mine_odd = __uint_as_float(v[jj + 1]);
-          const float give = odd ? mine_even : mine_odd;
-          const float got = __shfl_xor_sync(0xFFFFFFFFu, give, 1);
-          const uint32_t word = odd ? pack_bf16x2(got, mine_odd) : pack_bf16x2(mine_even, got);
-          const uint32_t r = static_cast<uint32_t>(col + jj + (odd ? 1 : 0));
-          const uint32_t addr = stage + r * 128u + (((chunk ^ (r & 7u)) << 4) | in_chunk);
-          asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(word) : "memory");
+        for (int jj = 0; jj < 32; ++jj) {
+          const float sc =
+              slot >= 0 ? pair_scale(p.scale, t0 + j * tg.sub + col + jj, slot) : 0.0f;
+          v[jj] = __float_as_uint(__uint_as_float(v[jj]) * sc);
         }
       }
+#pragma unroll
+      for (int jj = 0; jj < 32; jj += 2) {
+        const float mine_even = __uint_as_float(v[jj]);
+        const float mine_odd = __uint_as_float(v[jj + 1]);
+        const float give = odd ? mine_even : mine_odd;
+        const float got = __shfl_xor_sync(0xFFFFFFFFu, give, 1);
+        const uint32_t word = odd ? pack_bf16x2(got, mine_odd) : pack_bf16x2(mine_even, got);
+        const uint32_t r = static_cast<uint32_t>(col + jj + (odd ? 1 : 0));
+        const uint32_t addr = stage + r * 128u + (((chunk ^ (r & 7u)) << 4) | in_chunk);
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(word) : "memory");
+      }
+    };
+    for (int i = 0; i < total; ++i) {
+      uint32_t v[32];
+      MP_TMEM_LD_32X32B_X32(tmem + lane_base + static_cast<uint32_t>(col_of(i)), v);
+      MP_TMEM_WAIT_LD_REGS32(v);
+      convert(i, v);
     }
   }
   // Every epilogue thread passes this barrier (also on the abort path).
@@ -552,13 +558,20 @@ __global__ void __launch_bounds__(256) lora_reduce_kernel(const __grid_constant_
   const int j = static_cast<int>(idx % cols4) * 4;
   const size_t split_stride = static_cast<size_t>(p.M) * p.part_ld;
   const float* src = p.part + static_cast<size_t>(t) * p.part_ld + j;
-  float4 a = *reinterpret_cast<const float4*>(src);
-  for (int z = 1; z < p.ksplit; ++z) {
-    const float4 b = *reinterpret_cast<const float4*>(src + z * split_stride);
-    a.x += b.x;
-    a.y += b.y;
-    a.z += b.z;
-    a.w += b.w;
+  // all splits' loads in flight at once, then the sum in split order
+  float4 part[kMaxSplits];
+#pragma unroll
+  for (int z = 0; z < kMaxSplits; ++z)
+    if (z < p.ksplit) part[z] = *reinterpret_cast<const float4*>(src + z * split_stride);
+  float4 a = part[0];
+#pragma unroll
+  for (int z = 1; z < kMaxSplits; ++z) {
+    if (z < p.ksplit) {
+      a.x += part[z].x;
+      a.y += part[z].y;
+      a.z += part[z].z;
+      a.w += part[z].w;
+    }
   }
   float sc[4] = {1.0f, 1.0f, 1.0f, 1.0f};
   if (p.scale.enabled) {
