@@ -334,7 +334,7 @@ int fill_member(mp_ctx* c, ProjParams* p, int i, const CUtensorMap& tm_w, const 
   const bool sym = bits == 8 && mode == MP_QUANT_SYMMETRIC;
   mb.code_xor = sym ? 0x80808080u : 0u;
   mb.code_offset = sym ? 32896.0f : 32768.0f;
-  if (!encode_y(&mb.tm_y, y, ldy, n, p->M, sub_tok(p->n_tok)))
+  if (!encode_y(&mb.tm_y, y, ldy, n, p->M, mp::kEpiRows))
     return fail(c, MP_ECUDA, "tensor map encode failed (output)");
   mb.lora_ktiles = 0;
   if (lt.rpad > 0) {

@@ -18,6 +18,7 @@ constexpr int kBlockN = 128;       // output features per CTA (a pair covers 256
 constexpr int kBlockK = 64;        // K per stage == one quantization group
 constexpr int kMaxTok = 256;       // token rows of one accumulator (MMA N), at most
 constexpr int kMaxTileTok = 512;   // token rows per pair tile (two accumulators), at most
+constexpr int kEpiRows = 64;       // token rows per epilogue store (the output map's box)
 constexpr int kWStageBytes = kBlockN * 128;   // weight tile: codes or bf16
 constexpr int kTmemCols = 512;
 constexpr int kMaxMembers = 4;     // projections of one input in one launch (q/k/v, w1/w3)
@@ -46,7 +47,7 @@ struct ProjMember {
                       // or bf16 [N, K] (box {64, 128}, SW128)
   CUtensorMap tm_t;   // rank-space intermediate [M, R] bf16 (box {64, sub/2}, SW128)
   CUtensorMap tm_b;   // stacked LoRA B [N, R] bf16 (box {64, 128}, SW128)
-  CUtensorMap tm_y;   // output [M, N] bf16 (box {64, sub}, SW128); sub = min(n_tok, 256)
+  CUtensorMap tm_y;   // output [M, N] bf16 (box {64, kEpiRows}, SW128)
   const uint32_t* sb; // per row, per group: bf16 scale (low half) | bf16 bias (high half)
   int32_t N;
   int32_t bits;       // 0 dense bf16, 4 or 8 packed codes
@@ -62,11 +63,13 @@ struct ProjParams {
   int32_t M, K;
   int32_t n_tok;      // token rows per pair tile: 64, 128, 256 or 512 (two accumulators)
   int32_t n_members;
-  int32_t n_pairs;    // total pairs of the launch (grid.x = 2 * n_pairs)
+  int32_t n_pairs;    // feature pairs of the launch (all members)
+  int32_t n_ttiles;   // token tiles: ceil(M / n_tok)
+  int32_t n_tiles;    // n_pairs * n_ttiles * max(ksplit, 1): the persistent grid's work list
   uint64_t wait_limit_ns;
   uint32_t* err;      // device error word
   EpilogueScale scale;  // rank-space pre-GEMM only
-  // Split-K (grid.z = ksplit > 1, a single member): split z runs the K tiles
+  // Split-K (ksplit > 1, a single member): the tiles of split z run the K tiles
   // [z * kt_per_split, min((z + 1) * kt_per_split, K tiles)) (the last split
   // also takes the member's LoRA K tiles) and writes its fp32 partial sums,
   // unscaled, to part[z][t][f] (row stride part_ld) instead of the bf16

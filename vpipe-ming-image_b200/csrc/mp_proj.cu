@@ -1,26 +1,27 @@
-// The fused projection kernel on CTA PAIRS (cluster of 2, tcgen05 cta_group::2):
+// The fused projection kernel: PERSISTENT CTA pairs (cluster of 2,
+// tcgen05 cta_group::2) over a static list of output tiles:
 //
 //   y[M, N] = x[M, K] · deq(W)[N, K]^T  +  T[M, R] · Bstack[N, R]^T
 //
 // the reference's `lin` (src/ming-dit.cc:1763-1771) as one pass over K with
-// the live LoRA slots appended as extra K tiles, on a tile of 256 output
-// features x up to 512 tokens per pair of SMs. One launch may cover up to
-// four projections of the same input (q/k/v, w1/w3): each pair maps to the
-// member whose feature range it falls in.
-//   * each CTA owns 128 of the pair's features (MMA M = 256 across the pair)
-//     and loads HALF of every 256-token sub-tile (MMA N is split across the
-//     pair); a 512-token tile keeps two f32 accumulators of 256 columns in
-//     TMEM, so every dequantized weight stage feeds two MMAs;
-//   * each CTA dequantizes its own 128 feature rows per 64-wide K stage (two
-//     warpgroups, each converting half of the stage's columns with packed
-//     f32x2 arithmetic) into a bf16 tile in shared memory laid out exactly as
-//     a 128-byte-swizzled TMA load would lay it out, and the leader's single
-//     MMA thread issues tcgen05.mma.cta_group::2 with both operands in
-//     shared memory;
-//   * activation / dense-weight / LoRA tiles complete on the LEADER's full
-//     barrier (cta_group::2 TMA); the codes tile of each CTA completes on
-//     that CTA's own barrier, where its dequantizers wait; the MMA commit
-//     multicasts stage release and accumulator-ready to both CTAs.
+// the live LoRA slots appended as extra K tiles. A tile is 256 output features
+// x up to 512 tokens; one launch may cover up to four projections of the same
+// input (q/k/v, w1/w3), each feature pair mapping to the member whose feature
+// range it falls in. Every pair walks the tiles pair_id, pair_id + pairs, ...
+//   * each CTA owns 128 of a tile's features (MMA M = 256 across the pair)
+//     and loads half of every 256-token sub-tile (MMA N is split across the
+//     pair); a 512-token tile keeps two f32 accumulators of 256 TMEM columns,
+//     so every dequantized weight stage feeds two MMAs;
+//   * warp 0 issues TMA (x sub-tiles and dense / LoRA-B tiles as cta_group::2
+//     loads completing on the LEADER's barrier; the codes tile on the CTA's
+//     own barrier); warps 2-9 dequantize each CTA's 128 feature rows per
+//     64-wide K stage into a bf16 tile in shared memory laid out exactly as a
+//     128-byte-swizzled TMA load would lay it out; the leader's warp 1 issues
+//     tcgen05.mma.cta_group::2 with both operands in shared memory;
+//   * warps 10-13 drain the accumulators of tile i (TMEM -> bf16 -> swizzled
+//     staging -> TMA bulk stores) while warps 0-9 already run tile i + 1: the
+//     MMAs of tile i + 1 into accumulator j wait only until accumulator j of
+//     tile i has been read out.
 #include <cuda_runtime.h>
 
 #include "mp_device.cuh"
@@ -31,33 +32,39 @@ namespace mp {
 namespace {
 
 #ifndef MP_PAIR_STAGES
-#define MP_PAIR_STAGES 4
+#define MP_PAIR_STAGES 3
 #endif
-constexpr int kPairStages = MP_PAIR_STAGES;
+constexpr int kStages = MP_PAIR_STAGES;
 constexpr int kSubTok = kMaxTok;       // tokens of one accumulator (MMA N): 256
 constexpr int kTileTok = kMaxTileTok;  // tokens of a pair tile: two accumulators
-constexpr uint32_t kPairXBytes = (kTileTok / 2) * 128;    // x: this CTA's token rows, 32 KB
-constexpr uint32_t kPairABytes = kWStageBytes;            // A: 128 feature rows bf16, 16 KB
-constexpr uint32_t kPairCodesBytes = kBlockN * kBlockK;   // codes: 8-bit at most, 8 KB
-constexpr uint32_t kPairStageBytes = kPairXBytes + kPairABytes + kPairCodesBytes;  // 56 KB
+constexpr uint32_t kXBytes = (kTileTok / 2) * 128;    // x: this CTA's token rows, 32 KB
+constexpr uint32_t kABytes = kWStageBytes;            // A: 128 feature rows bf16, 16 KB
+constexpr uint32_t kCodesBytes = kBlockN * kBlockK;   // codes: 8-bit at most, 8 KB
+constexpr uint32_t kStageBytes = kXBytes + kABytes + kCodesBytes;  // 56 KB
+constexpr uint32_t kEpiHalfBytes = kEpiRows * 128;    // [64 tokens][64 features] bf16, 8 KB
+constexpr uint32_t kEpiBufBytes = 2 * kEpiHalfBytes;  // both feature halves of a CTA
+constexpr uint32_t kStagesBytes = kStages * kStageBytes;
+constexpr uint32_t kTileBytes = kStagesBytes + 2 * kEpiBufBytes;
 
 // Stage s: [x (MMA B operand) | A (MMA A operand: a dense weight or LoRA B
-// tile by TMA, or the dequantized codes) | codes], from the 1024-byte-aligned
-// tile base.
-__device__ __forceinline__ uint32_t off_x(int s) { return s * kPairStageBytes; }
-__device__ __forceinline__ uint32_t off_a(int s) { return s * kPairStageBytes + kPairXBytes; }
-__device__ __forceinline__ uint32_t off_c(int s) {
-  return s * kPairStageBytes + kPairXBytes + kPairABytes;
-}
-constexpr uint32_t kPairTileBytes = kPairStages * kPairStageBytes;
+// tile by TMA, or the dequantized codes) | codes]; then two epilogue staging
+// buffers. Offsets from the 1024-byte-aligned tile base.
+__device__ __forceinline__ uint32_t off_x(int s) { return s * kStageBytes; }
+__device__ __forceinline__ uint32_t off_a(int s) { return s * kStageBytes + kXBytes; }
+__device__ __forceinline__ uint32_t off_c(int s) { return s * kStageBytes + kXBytes + kABytes; }
+__device__ __forceinline__ uint32_t off_epi(int b) { return kStagesBytes + b * kEpiBufBytes; }
 
-// warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 dequant + epilogue
-constexpr int kPairThreads = 320;
+// warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 dequant, warps 10-13 epilogue
+constexpr int kDeqWarp0 = 2;
 constexpr int kDeqThreads = 256;
-constexpr uint32_t kPairSmemBytes = kPairTileBytes + 1024 + 512;
+constexpr int kEpiWarp0 = 10;
+constexpr int kEpiThreads = 128;
+constexpr int kPairThreads = 32 * kEpiWarp0 + kEpiThreads;
+constexpr uint32_t kEpiBarrier = 1;  // named barrier of the epilogue warps
+constexpr uint32_t kPairSmemBytes = kTileBytes + 1024 + 512;
 static_assert(kPairSmemBytes <= 232448, "shared memory per CTA");
-static_assert(kPairTileBytes >= 2 * 2 * kSubTok * 128, "epilogue staging of two accumulators");
 static_assert(2 * kSubTok <= kTmemCols, "two accumulators in TMEM");
+static_assert(kStages <= 8, "per-slot parity bit masks");
 
 enum : uint32_t {
   kSiteEmpty = 0x1100u,
@@ -66,6 +73,7 @@ enum : uint32_t {
   kSiteCodes = 0x1400u,
   kSiteEpi = 0x1500u,
   kSiteDrain = 0x1600u,
+  kSiteTmem = 0x1700u,
 };
 
 // Per-stage timeline of the first CTA pair, only in builds compiled with
@@ -89,7 +97,8 @@ struct PairSmem {
   uint64_t* empty;   // [stages] each CTA: stage released by the MMA
   uint64_t* cfull;   // [stages] each CTA: its own codes tile landed
   uint64_t* afull;   // [stages] leader: both CTAs' dequantized A tile written
-  uint64_t* tfull;   // each CTA: accumulators complete
+  uint64_t* tfull;   // each CTA: the tile's accumulators complete
+  uint64_t* tempty;  // [2] leader: accumulator j read out by both CTAs' epilogues
   uint64_t* drain;   // leader: every MMA issued has completed
   uint32_t* tmem_slot;
   volatile uint32_t* abort;
@@ -99,13 +108,14 @@ __device__ __forceinline__ PairSmem carve_pair(uint8_t* raw) {
   PairSmem s;
   const uintptr_t base = (reinterpret_cast<uintptr_t>(raw) + 1023u) & ~uintptr_t(1023u);
   s.tiles = reinterpret_cast<uint8_t*>(base);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s.tiles + kPairTileBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s.tiles + kTileBytes);
   s.full = bars;
-  s.empty = bars + kPairStages;
-  s.cfull = bars + 2 * kPairStages;
-  s.afull = bars + 3 * kPairStages;
-  s.tfull = bars + 4 * kPairStages;
-  s.drain = s.tfull + 1;
+  s.empty = bars + kStages;
+  s.cfull = bars + 2 * kStages;
+  s.afull = bars + 3 * kStages;
+  s.tfull = bars + 4 * kStages;
+  s.tempty = s.tfull + 1;
+  s.drain = s.tempty + 2;
   s.tmem_slot = reinterpret_cast<uint32_t*>(s.drain + 1);
   s.abort = s.tmem_slot + 1;
   return s;
@@ -149,111 +159,182 @@ __device__ __forceinline__ uint32_t pick4p(const uint4& v, int i) {
   return r;
 }
 
-// Token geometry of one pair tile at token row t0: `n_sub` accumulators of
-// `sub` tokens each (a second accumulator whose rows all lie past M is
-// dropped), every CTA holding `half` rows of each sub-tile.
-struct TileGeom {
-  int n_sub;
-  int sub;
-  int half;
+// One output tile of a launch, as seen by one CTA of the pair.
+struct Tile {
+  int mi;        // member
+  int f0;        // this CTA's first feature row (member-relative)
+  int t0;        // first token row
+  int z;         // K split
+  int n_sub;     // accumulators in use (a second one whose rows all lie past M is dropped)
+  int sub;       // tokens per accumulator
+  int half;      // token rows of each sub-tile this CTA loads
+  int kt_begin;  // K tiles [kt_begin, kt_end); those >= base_kt are appended LoRA tiles
+  int kt_end;
 };
 
-__device__ __forceinline__ TileGeom tile_geom(const ProjParams& p, int t0) {
-  TileGeom g;
+__device__ __forceinline__ Tile decode_tile(const ProjParams& p, int tile, int rank, int base_kt) {
+  Tile t;
+  const int per_split = p.n_pairs * p.n_ttiles;
+  t.z = tile / per_split;
+  const int rem = tile - t.z * per_split;
+  const int tt = rem / p.n_pairs;
+  const int pair = rem - tt * p.n_pairs;
+  int mi = 0;
+  while (mi + 1 < p.n_members && pair >= p.mem[mi + 1].pair_begin) ++mi;
+  t.mi = mi;
+  t.f0 = (pair - p.mem[mi].pair_begin) * (2 * kBlockN) + rank * kBlockN;
+  t.t0 = tt * p.n_tok;
   const int most = p.n_tok > kSubTok ? 2 : 1;
-  g.sub = p.n_tok / most;
-  g.half = g.sub / 2;
-  g.n_sub = (most == 2 && t0 + g.sub >= p.M) ? 1 : most;
-  return g;
+  t.sub = p.n_tok / most;
+  t.half = t.sub / 2;
+  t.n_sub = (most == 2 && t.t0 + t.sub >= p.M) ? 1 : most;
+  t.kt_begin = 0;
+  t.kt_end = base_kt + p.mem[mi].lora_ktiles;
+  if (p.ksplit > 1) {
+    t.kt_begin = t.z * p.kt_per_split;
+    if (t.z + 1 < p.ksplit) t.kt_end = min(base_kt, t.kt_begin + p.kt_per_split);
+  }
+  return t;
 }
 
-// K tiles [kt_begin, kt_end): tiles below base_kt are the base weight's,
-// the rest are appended LoRA tiles. Stage i of the loop holds tile kt_begin + i.
-__device__ void pair_producer(const ProjParams& p, const ProjMember& mb, const PairSmem& sm,
-                              const TileGeom& tg, bool leader, int f0, int t0, int rank,
-                              int kt_begin, int base_kt, int kt_end) {
-  const bool quant = mb.bits != 0;
-  const uint32_t sub_bytes = static_cast<uint32_t>(tg.half) * 128u;  // one sub-tile, one CTA
-  const uint32_t xbytes_pair = 2u * static_cast<uint32_t>(tg.n_sub) * sub_bytes;
-  const uint32_t codes_bytes = static_cast<uint32_t>(kBlockN * kBlockK * mb.bits / 8);
-  const int n_kt = kt_end - kt_begin;
-  int issued = 0;
-  for (int i = 0; i < n_kt; ++i) {
-    const int kt = kt_begin + i;
-    const int s = i % kPairStages;
-    const uint32_t ph = static_cast<uint32_t>(i / kPairStages) & 1u;
-    if (i >= kPairStages &&
-        !mbar_wait(smem_u32(&sm.empty[s]), ph ^ 1u, sm.abort, kSiteEmpty | s, p.wait_limit_ns))
-      break;
-    MP_TRACE_MARK(kTrProducer, i);
-    const uint32_t xb = smem_u32(sm.tiles) + off_x(s);
-    const uint32_t wb = smem_u32(sm.tiles) + off_a(s);
-    const uint32_t full_local = smem_u32(&sm.full[s]);
-    const uint32_t full_leader = mapa_shared(full_local, 0);
-    const bool lora = kt >= base_kt;
-    const CUtensorMap* xmap = lora ? &mb.tm_t : &p.tm_x;
-    const int xk = (lora ? kt - base_kt : kt) * kBlockK;
-    if (!lora && quant) {
-      if (leader) mbar_arrive_expect_tx(full_local, xbytes_pair);
-      const uint32_t cbar = smem_u32(&sm.cfull[s]);
-      mbar_arrive_expect_tx(cbar, codes_bytes);
-      tma_load_2d(smem_u32(sm.tiles) + off_c(s), &mb.tm_w, cbar, kt * kBlockK * mb.bits / 8, f0);
-    } else {
-      if (leader) mbar_arrive_expect_tx(full_local, xbytes_pair + 2u * kWStageBytes);
-      tma_load_2d_pair(wb, lora ? &mb.tm_b : &mb.tm_w, full_leader, xk, f0);
+__device__ __forceinline__ int first_tile() { return static_cast<int>(blockIdx.x >> 1); }
+__device__ __forceinline__ int tile_stride() { return static_cast<int>(gridDim.x >> 1); }
+
+// Warp 0, one thread. Stage iteration `it` runs on across tiles.
+__device__ void pair_producer(const ProjParams& p, const PairSmem& sm, bool leader, int rank,
+                              int base_kt) {
+  uint32_t it = 0;
+  uint32_t cpar = 0;           // per slot: parity of the slot's next codes phase
+  uint32_t pend_codes = 0;     // slots whose codes copy this thread has not seen consumed
+  uint32_t pend_codes_par = 0;
+  uint32_t pend_full = 0;      // slots whose pair copies this thread has not seen consumed
+  uint32_t pend_full_par = 0;
+  bool aborted = false;
+  for (int tile = first_tile(); tile < p.n_tiles && !aborted; tile += tile_stride()) {
+    const Tile t = decode_tile(p, tile, rank, base_kt);
+    const ProjMember& mb = p.mem[t.mi];
+    const bool quant = mb.bits != 0;
+    const uint32_t sub_bytes = static_cast<uint32_t>(t.half) * 128u;  // one sub-tile, one CTA
+    const uint32_t xbytes_pair = 2u * static_cast<uint32_t>(t.n_sub) * sub_bytes;
+    const uint32_t codes_bytes = static_cast<uint32_t>(kBlockN * kBlockK * mb.bits / 8);
+    for (int kt = t.kt_begin; kt < t.kt_end; ++kt, ++it) {
+      const int s = static_cast<int>(it % kStages);
+      const uint32_t ph = (it / kStages) & 1u;
+      const uint32_t bit = 1u << s;
+      if (it >= kStages &&
+          !mbar_wait(smem_u32(&sm.empty[s]), ph ^ 1u, sm.abort, kSiteEmpty | s, p.wait_limit_ns)) {
+        aborted = true;
+        break;
+      }
+      pend_codes &= ~bit;  // the MMA consumed the slot's previous copies
+      pend_full &= ~bit;
+      MP_TRACE_MARK(kTrProducer, static_cast<int>(it));
+      const uint32_t xb = smem_u32(sm.tiles) + off_x(s);
+      const uint32_t wb = smem_u32(sm.tiles) + off_a(s);
+      const uint32_t full_local = smem_u32(&sm.full[s]);
+      const uint32_t full_leader = mapa_shared(full_local, 0);
+      const bool lora = kt >= base_kt;
+      const CUtensorMap* xmap = lora ? &mb.tm_t : &p.tm_x;
+      const int xk = (lora ? kt - base_kt : kt) * kBlockK;
+      if (!lora && quant) {
+        if (leader) mbar_arrive_expect_tx(full_local, xbytes_pair);
+        const uint32_t cbar = smem_u32(&sm.cfull[s]);
+        mbar_arrive_expect_tx(cbar, codes_bytes);
+        tma_load_2d(smem_u32(sm.tiles) + off_c(s), &mb.tm_w, cbar, kt * kBlockK * mb.bits / 8,
+                    t.f0);
+        pend_codes |= bit;
+        pend_codes_par = (pend_codes_par & ~bit) | (cpar & bit);
+        cpar ^= bit;
+      } else {
+        if (leader) mbar_arrive_expect_tx(full_local, xbytes_pair + 2u * kWStageBytes);
+        tma_load_2d_pair(wb, lora ? &mb.tm_b : &mb.tm_w, full_leader, xk, t.f0);
+      }
+      for (int j = 0; j < t.n_sub; ++j)
+        tma_load_2d_pair(xb + j * sub_bytes, xmap, full_leader, xk,
+                         t.t0 + j * t.sub + rank * t.half);
+      pend_full |= bit;
+      pend_full_par = (pend_full_par & ~bit) | ((ph & 1u) << s);
     }
-    for (int j = 0; j < tg.n_sub; ++j)
-      tma_load_2d_pair(xb + j * sub_bytes, xmap, full_leader, xk, t0 + j * tg.sub + rank * tg.half);
-    issued = i + 1;
   }
   if (*sm.abort != 0u) {
-    // Unwind: wait (bounded) for this CTA's own codes copies still in flight;
-    // the pair copies are drained by the teardown cluster barrier, which the
-    // leader passes only after its bounded MMA drain.
-    for (int i = issued - kPairStages < 0 ? 0 : issued - kPairStages; i < issued; ++i) {
-      if (!(kt_begin + i < base_kt && quant)) continue;
-      const int s = i % kPairStages;
-      const uint32_t ph = static_cast<uint32_t>(i / kPairStages) & 1u;
-      const uint64_t t0w = global_timer_ns();
-      while (!mbar_try_wait(smem_u32(&sm.cfull[s]), ph)) {
-        if (global_timer_ns() - t0w > p.wait_limit_ns) break;
+    // Unwind: wait (bounded) until the copies this CTA still has in flight
+    // have landed (the codes on its own barrier; on the leader, both CTAs'
+    // pair copies on its full barriers), so none writes shared memory after
+    // the CTA has left.
+    for (int s = 0; s < kStages; ++s) {
+      const uint32_t bit = 1u << s;
+      const uint64_t t0 = global_timer_ns();
+      if (pend_codes & bit) {
+        while (!mbar_try_wait(smem_u32(&sm.cfull[s]), (pend_codes_par >> s) & 1u))
+          if (global_timer_ns() - t0 > p.wait_limit_ns) break;
+      }
+      if (leader && (pend_full & bit)) {
+        while (!mbar_try_wait(smem_u32(&sm.full[s]), (pend_full_par >> s) & 1u))
+          if (global_timer_ns() - t0 > p.wait_limit_ns) break;
       }
     }
   }
 }
 
-__device__ void pair_mma(const ProjParams& p, const ProjMember& mb, const PairSmem& sm,
-                         const TileGeom& tg, uint32_t tmem, int kt_begin, int base_kt,
-                         int kt_end) {
-  const bool quant = mb.bits != 0;
-  const uint32_t idesc = make_idesc_bf16(2 * kBlockN, static_cast<uint32_t>(tg.sub));
-  const uint32_t sub_bytes = static_cast<uint32_t>(tg.half) * 128u;
-  uint32_t acc = 0;
-  for (int i = 0; i < kt_end - kt_begin; ++i) {
-    const int kt = kt_begin + i;
-    const int s = i % kPairStages;
-    const uint32_t ph = static_cast<uint32_t>(i / kPairStages) & 1u;
-    if (!mbar_wait(smem_u32(&sm.full[s]), ph, sm.abort, kSiteFull | s, p.wait_limit_ns)) break;
-    const bool dequantized = quant && kt < base_kt;
-    if (dequantized &&
-        !mbar_wait(smem_u32(&sm.afull[s]), ph, sm.abort, kSiteDeq | s, p.wait_limit_ns))
-      break;
-    tc_fence_after();
-    MP_TRACE_MARK(kTrMma, i);
-    const uint32_t xaddr = smem_u32(sm.tiles) + off_x(s);
-    const uint32_t waddr = smem_u32(sm.tiles) + off_a(s);
-#pragma unroll
-    for (int kk = 0; kk < kBlockK / 16; ++kk) {
-      const uint64_t adesc = make_sdesc_sw128(waddr + kk * 32);
-      for (int j = 0; j < tg.n_sub; ++j) {
-        const uint64_t bdesc = make_sdesc_sw128(xaddr + j * sub_bytes + kk * 32);
-        umma_ss_pair(tmem + static_cast<uint32_t>(j * tg.sub), adesc, bdesc, idesc, acc);
+// Warp 1 of the leader, one thread.
+__device__ void pair_mma(const ProjParams& p, const PairSmem& sm, uint32_t tmem, int base_kt) {
+  uint32_t it = 0;
+  uint32_t apar = 0;  // per slot: parity of the slot's next dequant phase
+  uint32_t tcount = 0;
+  bool aborted = false;
+  for (int tile = first_tile(); tile < p.n_tiles && !aborted; tile += tile_stride(), ++tcount) {
+    const Tile t = decode_tile(p, tile, 0, base_kt);
+    const ProjMember& mb = p.mem[t.mi];
+    const bool quant = mb.bits != 0;
+    const uint32_t idesc = make_idesc_bf16(2 * kBlockN, static_cast<uint32_t>(t.sub));
+    const uint32_t sub_bytes = static_cast<uint32_t>(t.half) * 128u;
+    uint32_t acc = 0;
+    for (int kt = t.kt_begin; kt < t.kt_end; ++kt, ++it) {
+      const int s = static_cast<int>(it % kStages);
+      const uint32_t ph = (it / kStages) & 1u;
+      if (!mbar_wait(smem_u32(&sm.full[s]), ph, sm.abort, kSiteFull | s, p.wait_limit_ns)) {
+        aborted = true;
+        break;
       }
-      acc = 1;
+      if (quant && kt < base_kt) {
+        if (!mbar_wait(smem_u32(&sm.afull[s]), (apar >> s) & 1u, sm.abort, kSiteDeq | s,
+                       p.wait_limit_ns)) {
+          aborted = true;
+          break;
+        }
+        apar ^= 1u << s;
+      }
+      tc_fence_after();
+      MP_TRACE_MARK(kTrMma, static_cast<int>(it));
+      const uint32_t xaddr = smem_u32(sm.tiles) + off_x(s);
+      const uint32_t waddr = smem_u32(sm.tiles) + off_a(s);
+#pragma unroll
+      for (int kk = 0; kk < kBlockK / 16; ++kk) {
+        const uint64_t adesc = make_sdesc_sw128(waddr + kk * 32);
+        for (int j = 0; j < 2; ++j) {
+          if (acc == 0 && tcount > 0) {
+            // Accumulator j holds the previous tile until its epilogue has read
+            // it out. Both accumulators' phases are waited every tile (also one
+            // this tile leaves unused), so no phase is ever skipped.
+            if (!mbar_wait(smem_u32(&sm.tempty[j]), (tcount - 1) & 1u, sm.abort, kSiteTmem | j,
+                           p.wait_limit_ns)) {
+              aborted = true;
+              break;
+            }
+            tc_fence_after();
+          }
+          if (j >= t.n_sub) continue;
+          const uint64_t bdesc = make_sdesc_sw128(xaddr + j * sub_bytes + kk * 32);
+          umma_ss_pair(tmem + static_cast<uint32_t>(j * t.sub), adesc, bdesc, idesc, acc);
+        }
+        if (aborted) break;
+        acc = 1;
+      }
+      if (aborted) break;
+      umma_commit_pair(smem_u32(&sm.empty[s]), 0x3);
     }
-    umma_commit_pair(smem_u32(&sm.empty[s]), 0x3);
+    if (!aborted) umma_commit_pair(smem_u32(sm.tfull), 0x3);
   }
-  if (*sm.abort == 0u) umma_commit_pair(smem_u32(sm.tfull), 0x3);
   umma_commit_pair(smem_u32(sm.drain), 0x1);
   const uint64_t t0 = global_timer_ns();
   while (!mbar_try_wait(smem_u32(sm.drain), 0)) {
@@ -265,185 +346,226 @@ __device__ void pair_mma(const ProjParams& p, const ProjMember& mb, const PairSm
 }
 
 // Warps 2-9. Warpgroup g converts columns [32g, 32g + 32) of every stage for
-// the 128 feature rows of this CTA: thread (warp % 4, lane) owns row r.
-// The codes tile is 64-byte (w8) or 32-byte (w4) swizzled by its TMA map.
-__device__ void pair_dequant(const ProjParams& p, const ProjMember& mb, const PairSmem& sm,
-                             int f0, int kt_begin, int base_end) {
+// the 128 feature rows of this CTA: thread (warp % 4, lane) owns row r. The
+// codes tile is 64-byte (w8) or 32-byte (w4) swizzled by its TMA map.
+__device__ void pair_dequant(const ProjParams& p, const PairSmem& sm, int rank, int base_kt) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int g = (warp - 2) >> 2;  // K columns [32g, 32g + 32) of every stage
+  const int g = (warp - kDeqWarp0) >> 2;  // K columns [32g, 32g + 32) of every stage
   const int q = warp & 3;
   const int r = q * 32 + lane;
-  const int n = f0 + r;
-  const bool row_ok = n < mb.N;
-  const uint32_t* sbrow = mb.sb + static_cast<size_t>(row_ok ? n : 0) * mb.sb_stride;
-  uint4 sbv = make_uint4(0, 0, 0, 0);
-  int sb_group = -1;  // which 4 groups sbv holds
-  for (int i = 0; i < base_end - kt_begin; ++i) {
-    const int kt = kt_begin + i;
-    const int s = i % kPairStages;
-    const uint32_t ph = static_cast<uint32_t>(i / kPairStages) & 1u;
-    if ((kt >> 2) != sb_group) {
-      sbv = row_ok ? ld_global_nc_v4(sbrow + (kt & ~3)) : make_uint4(0, 0, 0, 0);
-      sb_group = kt >> 2;
+  uint32_t it = 0;
+  uint32_t cpar = 0;  // per slot: parity of the slot's next codes phase
+  bool aborted = false;
+  for (int tile = first_tile(); tile < p.n_tiles && !aborted; tile += tile_stride()) {
+    const Tile t = decode_tile(p, tile, rank, base_kt);
+    const ProjMember& mb = p.mem[t.mi];
+    const int base_end = min(base_kt, t.kt_end);
+    if (mb.bits == 0) {  // no dequant stages: keep the stage count in step
+      it += static_cast<uint32_t>(t.kt_end - t.kt_begin);
+      continue;
     }
-    const uint32_t sbw = pick4p(sbv, kt & 3);
-    const float sc = bf16_bits_to_f32(sbw & 0xFFFFu);
-    const float bi = bf16_bits_to_f32(sbw >> 16);
-    const float bf = fmaf(-sc, mb.code_offset, bi);
-    const uint64_t sc2 = f32x2(sc, sc), bf2 = f32x2(bf, bf);
-    if (!mbar_wait(smem_u32(&sm.cfull[s]), ph, sm.abort, kSiteCodes | s, p.wait_limit_ns)) break;
-    if (threadIdx.x == 64) MP_TRACE_MARK(kTrDeqStart, i);
-    const uint32_t wb = smem_u32(sm.tiles) + off_c(s);
-    uint32_t packed[16];
-    if (mb.bits == 8) {
-      const uint32_t sw = static_cast<uint32_t>((r >> 1) & 3);
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const uint32_t chunk = static_cast<uint32_t>(2 * g + j);
-        const uint4 c = ld_shared_v4(wb + r * 64 + ((chunk ^ sw) << 4));
-        deq8x4(c.x ^ mb.code_xor, sc2, bf2, packed[8 * j + 0], packed[8 * j + 1]);
-        deq8x4(c.y ^ mb.code_xor, sc2, bf2, packed[8 * j + 2], packed[8 * j + 3]);
-        deq8x4(c.z ^ mb.code_xor, sc2, bf2, packed[8 * j + 4], packed[8 * j + 5]);
-        deq8x4(c.w ^ mb.code_xor, sc2, bf2, packed[8 * j + 6], packed[8 * j + 7]);
+    const int n = t.f0 + r;
+    const bool row_ok = n < mb.N;
+    const uint32_t* sbrow = mb.sb + static_cast<size_t>(row_ok ? n : 0) * mb.sb_stride;
+    uint4 sbv = make_uint4(0, 0, 0, 0);
+    int sb_group = -1;  // which 4 groups sbv holds
+    for (int kt = t.kt_begin; kt < base_end; ++kt, ++it) {
+      const int s = static_cast<int>(it % kStages);
+      if ((kt >> 2) != sb_group) {
+        sbv = row_ok ? ld_global_nc_v4(sbrow + (kt & ~3)) : make_uint4(0, 0, 0, 0);
+        sb_group = kt >> 2;
       }
-    } else {
-      const uint32_t sw = static_cast<uint32_t>((r >> 2) & 1);
-      const uint4 c = ld_shared_v4(wb + r * 32 + ((static_cast<uint32_t>(g) ^ sw) << 4));
-      deq4x8(c.x, sc2, bf2, &packed[0]);
-      deq4x8(c.y, sc2, bf2, &packed[4]);
-      deq4x8(c.z, sc2, bf2, &packed[8]);
-      deq4x8(c.w, sc2, bf2, &packed[12]);
-    }
-    if (threadIdx.x == 64) MP_TRACE_MARK(kTrDeqMath, i);
-    // Row r of the stage's A tile, K columns [32g, 32g + 32): four 16-byte
-    // chunks at the 128-byte-swizzled positions a TMA load would use, then a
-    // proxy fence so the tensor core (async proxy) sees the generic stores.
-    const uint32_t arow = smem_u32(sm.tiles) + off_a(s) + r * 128u;
+      const uint32_t sbw = pick4p(sbv, kt & 3);
+      const float sc = bf16_bits_to_f32(sbw & 0xFFFFu);
+      const float bi = bf16_bits_to_f32(sbw >> 16);
+      const float bf = fmaf(-sc, mb.code_offset, bi);
+      const uint64_t sc2 = f32x2(sc, sc), bf2 = f32x2(bf, bf);
+      if (!mbar_wait(smem_u32(&sm.cfull[s]), (cpar >> s) & 1u, sm.abort, kSiteCodes | s,
+                     p.wait_limit_ns)) {
+        aborted = true;
+        break;
+      }
+      cpar ^= 1u << s;
+      if (threadIdx.x == 64) MP_TRACE_MARK(kTrDeqStart, static_cast<int>(it));
+      const uint32_t wb = smem_u32(sm.tiles) + off_c(s);
+      uint32_t packed[16];
+      if (mb.bits == 8) {
+        const uint32_t sw = static_cast<uint32_t>((r >> 1) & 3);
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint32_t chunk = (static_cast<uint32_t>(4 * g + c) ^ static_cast<uint32_t>(r & 7)) << 4;
-      st_shared_v4(arow + chunk, packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
-                   packed[4 * c + 3]);
+        for (int j = 0; j < 2; ++j) {
+          const uint32_t chunk = static_cast<uint32_t>(2 * g + j);
+          const uint4 c = ld_shared_v4(wb + r * 64 + ((chunk ^ sw) << 4));
+          deq8x4(c.x ^ mb.code_xor, sc2, bf2, packed[8 * j + 0], packed[8 * j + 1]);
+          deq8x4(c.y ^ mb.code_xor, sc2, bf2, packed[8 * j + 2], packed[8 * j + 3]);
+          deq8x4(c.z ^ mb.code_xor, sc2, bf2, packed[8 * j + 4], packed[8 * j + 5]);
+          deq8x4(c.w ^ mb.code_xor, sc2, bf2, packed[8 * j + 6], packed[8 * j + 7]);
+        }
+      } else {
+        const uint32_t sw = static_cast<uint32_t>((r >> 2) & 1);
+        const uint4 c = ld_shared_v4(wb + r * 32 + ((static_cast<uint32_t>(g) ^ sw) << 4));
+        deq4x8(c.x, sc2, bf2, &packed[0]);
+        deq4x8(c.y, sc2, bf2, &packed[4]);
+        deq4x8(c.z, sc2, bf2, &packed[8]);
+        deq4x8(c.w, sc2, bf2, &packed[12]);
+      }
+      if (threadIdx.x == 64) MP_TRACE_MARK(kTrDeqMath, static_cast<int>(it));
+      // Row r of the stage's A tile, K columns [32g, 32g + 32): four 16-byte
+      // chunks at the 128-byte-swizzled positions a TMA load would use, then a
+      // proxy fence so the tensor core (async proxy) sees the generic stores.
+      const uint32_t arow = smem_u32(sm.tiles) + off_a(s) + r * 128u;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t chunk =
+            (static_cast<uint32_t>(4 * g + c) ^ static_cast<uint32_t>(r & 7)) << 4;
+        st_shared_v4(arow + chunk, packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
+                     packed[4 * c + 3]);
+      }
+      fence_proxy_async_shared();
+      if (threadIdx.x == 64) MP_TRACE_MARK(kTrDeqStored, static_cast<int>(it));
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&sm.afull[s]), 0));
+      if (threadIdx.x == 64) MP_TRACE_MARK(kTrDeqEnd, static_cast<int>(it));
     }
-    fence_proxy_async_shared();
-    if (threadIdx.x == 64) MP_TRACE_MARK(kTrDeqStored, i);
-    __syncwarp();
-    if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&sm.afull[s]), 0));
-    if (threadIdx.x == 64) MP_TRACE_MARK(kTrDeqEnd, i);
+    it += static_cast<uint32_t>(t.kt_end - base_end);  // appended LoRA stages: nothing to do
   }
 }
 
-__device__ __forceinline__ float pair_scale(const EpilogueScale& es, int t, int slot) {
+// Row segment of token row t (segments are few; the boundaries are uniform
+// across the warp, so these are broadcast parameter loads).
+__device__ __forceinline__ int row_segment(const EpilogueScale& es, int t) {
   int g = 0;
   while (g + 1 < es.n_seg && t >= es.seg_start[g + 1]) ++g;
-  return es.seg_scale[g][slot];
+  return g;
 }
 
-// Warps 2-9: for each accumulator j, warpgroup g reads token columns
-// [g * sub / 2, (g + 1) * sub / 2) of this CTA's 128 feature rows out of TMEM
-// and rounds them to bf16. Lanes pair up (features 2i, 2i+1) with one shuffle
-// per token pair, so each lane writes one bf16x2 word of a [sub][64]-feature
-// staging half tile laid out with the 128-byte swizzle (conflict-free). One
-// thread then stores the halves with TMA bulk stores, which clip rows past M
-// and columns past N. In split-K mode the fp32 sums go straight to the
-// partial-sum array instead.
-__device__ void pair_epilogue(const ProjParams& p, const ProjMember& mb, const PairSmem& sm,
-                              const TileGeom& tg, uint32_t tmem, int f0, int t0) {
+// Tells the leader's MMA thread that this warp has read accumulator j out.
+__device__ __forceinline__ void release_accumulator(const PairSmem& sm, int j) {
+  tc_fence_before();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive_remote(mapa_shared(smem_u32(&sm.tempty[j]), 0));
+}
+
+// Warps 10-13 (TMEM lane quarter q = warp % 4: features 32q .. 32q + 31 of the
+// CTA's 128). Per accumulator, rounds of 64 tokens: two 32-column TMEM loads,
+// lane-pair shuffles into bf16x2 words (features 2i, 2i+1), a [64][64]-feature
+// staging half tile per feature half laid out with the 128-byte swizzle, then
+// one thread stores both halves with TMA bulk stores (they clip rows past M
+// and columns past N). Two staging buffers alternate. In split-K mode the fp32
+// sums go straight to the partial-sum array instead.
+__device__ void pair_epilogue(const ProjParams& p, const PairSmem& sm, uint32_t tmem, int rank,
+                              int base_kt) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int g = (warp - 2) >> 2;
   const int q = warp & 3;
   const int fl = q * 32 + lane;  // feature row within this CTA's 128
-  const int f = f0 + fl;
   const bool odd = (lane & 1) != 0;
-  const bool ok = mbar_wait(smem_u32(sm.tfull), 0, sm.abort, kSiteEpi, p.wait_limit_ns);
-  const uint32_t half_bytes = static_cast<uint32_t>(tg.sub) * 128u;  // one staging half tile
+  const bool issuer = threadIdx.x == 32 * kEpiWarp0;
   const bool split = p.part != nullptr;
   const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-  const int cols = tg.sub / 2;  // per warpgroup and accumulator
-  if (ok) {
+  // word (2 features) index within a staging row of 64 features
+  const uint32_t wi = static_cast<uint32_t>(16 * (q & 1) + (lane >> 1));
+  const uint32_t chunk = wi >> 2, in_chunk = (wi & 3u) << 2;
+  uint32_t tcount = 0;
+  uint32_t round = 0;
+  for (int tile = first_tile(); tile < p.n_tiles; tile += tile_stride(), ++tcount) {
+    const Tile t = decode_tile(p, tile, rank, base_kt);
+    const ProjMember& mb = p.mem[t.mi];
+    const int f = t.f0 + fl;
+    const bool ok_mine =
+        mbar_wait(smem_u32(sm.tfull), tcount & 1u, sm.abort, kSiteEpi, p.wait_limit_ns);
+    if (!named_barrier_and(kEpiBarrier, kEpiThreads, ok_mine)) break;
     tc_fence_after();
-    if (threadIdx.x == 64) MP_TRACE_MARK(kTrEpiStart, 0);
-  }
-  if (ok && split) {
-    // Lanes own consecutive features, so every warp store is 128 contiguous bytes.
-    float* prow = p.part + static_cast<size_t>(blockIdx.z) * p.M * p.part_ld + f;
-    for (int j = 0; j < tg.n_sub; ++j) {
-      for (int c = 0; c < cols / 32; ++c) {
-        const int col = g * cols + c * 32;
-        uint32_t v[32];
-        MP_TMEM_LD_32X32B_X32(tmem + lane_base + static_cast<uint32_t>(j * tg.sub + col), v);
-        MP_TMEM_WAIT_LD_REGS32(v);
-        if (f < mb.N) {
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const int t = t0 + j * tg.sub + col + jj;
-            if (t < p.M) prow[static_cast<size_t>(t) * p.part_ld] = __uint_as_float(v[jj]);
-          }
-        }
-      }
-    }
-  } else if (ok) {
+    if (threadIdx.x == 32 * kEpiWarp0) MP_TRACE_MARK(kTrEpiStart, static_cast<int>(tcount));
     int slot = -1;
-    if (p.scale.enabled) {
+    if (!split && p.scale.enabled) {
       for (int i = 0; i < p.scale.n_ranges; ++i)
         if (f >= p.scale.range_start[i] && f < p.scale.range_start[i + 1])
           slot = p.scale.range_slot[i];
     }
-    // word (2 features) index within a staging row of 64 features
-    const uint32_t wi = static_cast<uint32_t>(16 * (q & 1) + (lane >> 1));
-    const uint32_t chunk = wi >> 2, in_chunk = (wi & 3u) << 2;
-    // Chunks of 32 token columns, in (accumulator, column) order.
-    const int nck = cols / 32;
-    const int total = tg.n_sub * nck;
-    auto col_of = [&](int i) { return (i / nck) * tg.sub + g * cols + (i % nck) * 32; };
-    auto convert = [&](int i, uint32_t(&v)[32]) {
-      const int j = i / nck;
-      const int col = g * cols + (i % nck) * 32;  // within accumulator j
-      // staging half tile of features [64h, 64h + 64) of accumulator j
-      const uint32_t stage =
-          smem_u32(sm.tiles) + static_cast<uint32_t>(2 * j + (q >> 1)) * half_bytes;
-      if (p.scale.enabled) {
+    for (int j = 0; j < 2; ++j) {
+      if (j >= t.n_sub) {
+        release_accumulator(sm, j);
+        continue;
+      }
+      // rounds of this accumulator with at least one token row below M (a
+      // store box never starts past the output)
+      const int rows_left = p.M - (t.t0 + j * t.sub);
+      const int rounds = min(t.sub, rows_left) / kEpiRows + (min(t.sub, rows_left) % kEpiRows != 0);
+      for (int rr = 0; rr < rounds; ++rr) {
+        const int tr0 = t.t0 + j * t.sub + rr * kEpiRows;  // first token row of the round
+        if (split) {
+          float* prow = p.part + static_cast<size_t>(t.z) * p.M * p.part_ld + f;
+          for (int c = 0; c < 2; ++c) {
+            uint32_t v[32];
+            MP_TMEM_LD_32X32B_X32(
+                tmem + lane_base + static_cast<uint32_t>(j * t.sub + rr * kEpiRows + c * 32), v);
+            MP_TMEM_WAIT_LD_REGS32(v);
+            if (rr + 1 == rounds && c == 1) release_accumulator(sm, j);
+            if (f < mb.N) {
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const float sc =
-              slot >= 0 ? pair_scale(p.scale, t0 + j * tg.sub + col + jj, slot) : 0.0f;
-          v[jj] = __float_as_uint(__uint_as_float(v[jj]) * sc);
+              for (int jj = 0; jj < 32; ++jj) {
+                const int tok = tr0 + c * 32 + jj;
+                if (tok < p.M) prow[static_cast<size_t>(tok) * p.part_ld] = __uint_as_float(v[jj]);
+              }
+            }
+          }
+          continue;
         }
-      }
+        const uint32_t buf = smem_u32(sm.tiles) + off_epi(static_cast<int>(round & 1u));
+        // the stores that last read this buffer have finished reading (issuer waited)
+        named_barrier(kEpiBarrier, kEpiThreads);
+        const uint32_t stage = buf + static_cast<uint32_t>(q >> 1) * kEpiHalfBytes;
+        for (int c = 0; c < 2; ++c) {
+          uint32_t v[32];
+          MP_TMEM_LD_32X32B_X32(
+              tmem + lane_base + static_cast<uint32_t>(j * t.sub + rr * kEpiRows + c * 32), v);
+          MP_TMEM_WAIT_LD_REGS32(v);
+          if (rr + 1 == rounds && c == 1) release_accumulator(sm, j);
+          if (p.scale.enabled) {
+            // one strength per 32-token chunk unless a row-segment boundary
+            // falls inside it (the per-lane slot makes each lookup divergent)
+            const int tc = tr0 + c * 32;
+            const int g_lo = row_segment(p.scale, tc);
+            if (g_lo == row_segment(p.scale, tc + 31)) {
+              const float sc = slot >= 0 ? p.scale.seg_scale[g_lo][slot] : 0.0f;
 #pragma unroll
-      for (int jj = 0; jj < 32; jj += 2) {
-        const float mine_even = __uint_as_float(v[jj]);
-        const float mine_odd = __uint_as_float(v[jj + 1]);
-        const float give = odd ? mine_even : mine_odd;
-        const float got = __shfl_xor_sync(0xFFFFFFFFu, give, 1);
-        const uint32_t word = odd ? pack_bf16x2(got, mine_odd) : pack_bf16x2(mine_even, got);
-        const uint32_t r = static_cast<uint32_t>(col + jj + (odd ? 1 : 0));
-        const uint32_t addr = stage + r * 128u + (((chunk ^ (r & 7u)) << 4) | in_chunk);
-        asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(word) : "memory");
+              for (int jj = 0; jj < 32; ++jj) v[jj] = __float_as_uint(__uint_as_float(v[jj]) * sc);
+            } else {
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj) {
+                const float sc =
+                    slot >= 0 ? p.scale.seg_scale[row_segment(p.scale, tc + jj)][slot] : 0.0f;
+                v[jj] = __float_as_uint(__uint_as_float(v[jj]) * sc);
+              }
+            }
+          }
+#pragma unroll
+          for (int jj = 0; jj < 32; jj += 2) {
+            const float mine_even = __uint_as_float(v[jj]);
+            const float mine_odd = __uint_as_float(v[jj + 1]);
+            const float give = odd ? mine_even : mine_odd;
+            const float got = __shfl_xor_sync(0xFFFFFFFFu, give, 1);
+            const uint32_t word = odd ? pack_bf16x2(got, mine_odd) : pack_bf16x2(mine_even, got);
+            const uint32_t row = static_cast<uint32_t>(c * 32 + jj + (odd ? 1 : 0));
+            const uint32_t addr = stage + row * 128u + (((chunk ^ (row & 7u)) << 4) | in_chunk);
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(word) : "memory");
+          }
+        }
+        fence_proxy_async_shared();
+        named_barrier(kEpiBarrier, kEpiThreads);
+        if (issuer) {
+          tma_store_2d(&mb.tm_y, buf, t.f0, tr0);
+          tma_store_2d(&mb.tm_y, buf + kEpiHalfBytes, t.f0 + 64, tr0);
+          tma_store_commit();
+          tma_store_wait_read_1();  // the other buffer is free again
+        }
+        ++round;
       }
-    };
-    for (int i = 0; i < total; ++i) {
-      uint32_t v[32];
-      MP_TMEM_LD_32X32B_X32(tmem + lane_base + static_cast<uint32_t>(col_of(i)), v);
-      MP_TMEM_WAIT_LD_REGS32(v);
-      convert(i, v);
     }
+    if (threadIdx.x == 32 * kEpiWarp0) MP_TRACE_MARK(kTrEpiEnd, static_cast<int>(tcount));
   }
-  // Every epilogue thread passes this barrier (also on the abort path).
-  fence_proxy_async_shared();
-  named_barrier(1, kDeqThreads);
-  if (ok && !split && threadIdx.x == 64 && *sm.abort == 0u) {
-    for (int j = 0; j < tg.n_sub; ++j) {
-      const uint32_t st = smem_u32(sm.tiles) + static_cast<uint32_t>(2 * j) * half_bytes;
-      tma_store_2d(&mb.tm_y, st, f0, t0 + j * tg.sub);
-      tma_store_2d(&mb.tm_y, st + half_bytes, f0 + 64, t0 + j * tg.sub);
-    }
-    tma_store_commit();
-    tma_store_wait_read();
-    MP_TRACE_MARK(kTrEpiEnd, 0);
-  }
+  if (issuer) tma_store_wait_all();
 }
 
 }  // namespace
@@ -462,42 +584,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   const PairSmem sm = carve_pair(smem_raw);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_ctarank();
+  const int rank = static_cast<int>(cluster_ctarank());
   const bool leader = rank == 0;
-  const int pair = blockIdx.x >> 1;
-  int mi = 0;
-  while (mi + 1 < p.n_members && pair >= p.mem[mi + 1].pair_begin) ++mi;
-  const ProjMember& mb = p.mem[mi];
-  const int f0 = (pair - mb.pair_begin) * (2 * kBlockN) + static_cast<int>(rank) * kBlockN;
-  const int t0 = blockIdx.y * p.n_tok;
-  const TileGeom tg = tile_geom(p, t0);
   const int base_kt = (p.K + kBlockK - 1) / kBlockK;  // a ragged last tile (dense only) reads zeros
-  int kt_begin = 0, kt_end = base_kt + mb.lora_ktiles;
-  if (p.ksplit > 1) {
-    kt_begin = static_cast<int>(blockIdx.z) * p.kt_per_split;
-    if (static_cast<int>(blockIdx.z) + 1 < p.ksplit) kt_end = min(base_kt, kt_begin + p.kt_per_split);
-  }
-  const int base_end = min(base_kt, kt_end);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kPairStages; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(smem_u32(&sm.full[s]), 1);
       mbar_init(smem_u32(&sm.empty[s]), 1);
       mbar_init(smem_u32(&sm.cfull[s]), 1);
       mbar_init(smem_u32(&sm.afull[s]), 2 * kDeqThreads / 32);  // one arrive per dequant warp
     }
     mbar_init(smem_u32(sm.tfull), 1);
+    mbar_init(smem_u32(&sm.tempty[0]), 2 * kEpiThreads / 32);  // one arrive per epilogue warp
+    mbar_init(smem_u32(&sm.tempty[1]), 2 * kEpiThreads / 32);
     mbar_init(smem_u32(sm.drain), 1);
     *sm.abort = 0u;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_map(&p.tm_x);
-    tma_prefetch_map(&mb.tm_w);
-    tma_prefetch_map(&mb.tm_y);
-    if (mb.lora_ktiles > 0) {
-      tma_prefetch_map(&mb.tm_t);
-      tma_prefetch_map(&mb.tm_b);
+    for (int i = 0; i < p.n_members; ++i) {
+      tma_prefetch_map(&p.mem[i].tm_w);
+      tma_prefetch_map(&p.mem[i].tm_y);
+      if (p.mem[i].lora_ktiles > 0) {
+        tma_prefetch_map(&p.mem[i].tm_t);
+        tma_prefetch_map(&p.mem[i].tm_b);
+      }
     }
   }
   if (warp == 1) {
@@ -510,14 +623,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   const uint32_t tmem = *sm.tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0)
-      pair_producer(p, mb, sm, tg, leader, f0, t0, static_cast<int>(rank), kt_begin, base_kt,
-                    kt_end);
+    if (lane == 0) pair_producer(p, sm, leader, rank, base_kt);
   } else if (warp == 1) {
-    if (lane == 0 && leader) pair_mma(p, mb, sm, tg, tmem, kt_begin, base_kt, kt_end);
+    if (lane == 0 && leader) pair_mma(p, sm, tmem, base_kt);
+  } else if (warp < kEpiWarp0) {
+    pair_dequant(p, sm, rank, base_kt);
   } else {
-    if (mb.bits != 0) pair_dequant(p, mb, sm, f0, kt_begin, base_end);
-    pair_epilogue(p, mb, sm, tg, tmem, f0, t0);
+    pair_epilogue(p, sm, tmem, rank, base_kt);
   }
 
   tc_fence_before();
@@ -539,68 +651,86 @@ int pick_ntok_pair(int m, int pairs) {
   return MP_FORCE_NTOK;
 #else
   const long long slots = 74;  // pairs resident at once: one CTA per SM
-  auto waves = [&](int nt) { return (pairs * static_cast<long long>((m + nt - 1) / nt) + slots - 1) / slots; };
+  auto waves = [&](int nt) {
+    return (pairs * static_cast<long long>((m + nt - 1) / nt) + slots - 1) / slots;
+  };
   if (pairs * static_cast<long long>((m + 255) / 256) >= slots) {
-    return 0.85 * 2.0 * static_cast<double>(waves(512)) <= static_cast<double>(waves(256)) ? 512 : 256;
+    return 0.85 * 2.0 * static_cast<double>(waves(512)) <= static_cast<double>(waves(256)) ? 512
+                                                                                           : 256;
   }
   if (pairs * static_cast<long long>((m + 127) / 128) >= slots) return 128;
   return 64;
 #endif
 }
 
-// Second pass of a split-K launch (ReduceParams): one thread per 4
-// consecutive columns of one token row; the splits are added in z order.
-__global__ void __launch_bounds__(256) lora_reduce_kernel(const __grid_constant__ ReduceParams p) {
+// Second pass of a split-K launch (ReduceParams). Thread i owns the 4
+// consecutive columns (i mod R/4) and walks the rows i / (R/4), + rows_step,
+// ...: the column scale slots are looked up once per thread; every row's
+// split loads are in flight together and added in split order.
+__global__ void __launch_bounds__(256) lora_reduce_kernel(const __grid_constant__ ReduceParams p,
+                                                          int rows_step) {
   const int cols4 = p.R / 4;
-  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int t = static_cast<int>(idx / cols4);
-  if (t >= p.M) return;
-  const int j = static_cast<int>(idx % cols4) * 4;
-  const size_t split_stride = static_cast<size_t>(p.M) * p.part_ld;
-  const float* src = p.part + static_cast<size_t>(t) * p.part_ld + j;
-  // all splits' loads in flight at once, then the sum in split order
-  float4 part[kMaxSplits];
-#pragma unroll
-  for (int z = 0; z < kMaxSplits; ++z)
-    if (z < p.ksplit) part[z] = *reinterpret_cast<const float4*>(src + z * split_stride);
-  float4 a = part[0];
-#pragma unroll
-  for (int z = 1; z < kMaxSplits; ++z) {
-    if (z < p.ksplit) {
-      a.x += part[z].x;
-      a.y += part[z].y;
-      a.z += part[z].z;
-      a.w += part[z].w;
-    }
-  }
-  float sc[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+  const int tid = static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x);
+  if (tid >= cols4 * rows_step) return;
+  const int j = (tid % cols4) * 4;
+  int slot[4] = {-1, -1, -1, -1};
   if (p.scale.enabled) {
-    int g = 0;
-    while (g + 1 < p.scale.n_seg && t >= p.scale.seg_start[g + 1]) ++g;
+    for (int i = 0; i < p.scale.n_ranges; ++i) {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      int slot = -1;
-      for (int i = 0; i < p.scale.n_ranges; ++i)
+      for (int e = 0; e < 4; ++e)
         if (j + e >= p.scale.range_start[i] && j + e < p.scale.range_start[i + 1])
-          slot = p.scale.range_slot[i];
-      sc[e] = slot >= 0 ? p.scale.seg_scale[g][slot] : 0.0f;
+          slot[e] = p.scale.range_slot[i];
     }
   }
-  uint2 w;
-  w.x = pack_bf16x2(a.x * sc[0], a.y * sc[1]);
-  w.y = pack_bf16x2(a.z * sc[2], a.w * sc[3]);
-  *reinterpret_cast<uint2*>(p.out + static_cast<size_t>(t) * p.out_ld + j) = w;
+  const size_t split_stride = static_cast<size_t>(p.M) * p.part_ld;
+  int g = 0;  // row segment of t (rows only increase)
+  for (int t = tid / cols4; t < p.M; t += rows_step) {
+    const float* src = p.part + static_cast<size_t>(t) * p.part_ld + j;
+    float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int z0 = 0; z0 < p.ksplit; z0 += 8) {  // 8 splits' loads in flight at a time
+      float4 part[8];
+#pragma unroll
+      for (int z = 0; z < 8; ++z)
+        if (z0 + z < p.ksplit)
+          part[z] = *reinterpret_cast<const float4*>(src + (z0 + z) * split_stride);
+#pragma unroll
+      for (int z = 0; z < 8; ++z) {
+        if (z0 + z < p.ksplit) {
+          a.x = (z0 + z == 0) ? part[z].x : a.x + part[z].x;
+          a.y = (z0 + z == 0) ? part[z].y : a.y + part[z].y;
+          a.z = (z0 + z == 0) ? part[z].z : a.z + part[z].z;
+          a.w = (z0 + z == 0) ? part[z].w : a.w + part[z].w;
+        }
+      }
+    }
+    float sc[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+    if (p.scale.enabled) {
+      while (g + 1 < p.scale.n_seg && t >= p.scale.seg_start[g + 1]) ++g;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[e] = slot[e] >= 0 ? p.scale.seg_scale[g][slot[e]] : 0.0f;
+    }
+    uint2 w;
+    w.x = pack_bf16x2(a.x * sc[0], a.y * sc[1]);
+    w.y = pack_bf16x2(a.z * sc[2], a.w * sc[3]);
+    *reinterpret_cast<uint2*>(p.out + static_cast<size_t>(t) * p.out_ld + j) = w;
+  }
 }
 
 cudaError_t launch_lora_reduce(const ReduceParams& p, cudaStream_t stream) {
-  const long long threads = static_cast<long long>(p.M) * (p.R / 4);
+  // one pass of resident threads (about 1024 per SM) covers rows_step rows
+  const int cols4 = p.R / 4;
+  int rows_step = (148 * 1024) / cols4;
+  if (rows_step > p.M) rows_step = p.M;
+  if (rows_step < 1) rows_step = 1;
+  const long long threads = static_cast<long long>(cols4) * rows_step;
   const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
-  lora_reduce_kernel<<<blocks, 256, 0, stream>>>(p);
+  lora_reduce_kernel<<<blocks, 256, 0, stream>>>(p, rows_step);
   return cudaGetLastError();
 }
 
 cudaError_t launch_proj_pair(const ProjParams& p, cudaStream_t stream) {
   static bool configured[64] = {};
+  static int max_pairs[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -609,10 +739,27 @@ cudaError_t launch_proj_pair(const ProjParams& p, cudaStream_t stream) {
     e = cudaFuncSetAttribute(proj_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kPairSmemBytes));
     if (e != cudaSuccess) return e;
+    // pairs resident at once (one CTA per SM), which the persistent grid fills
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(kPairThreads, 1, 1);
+    cfg.dynamicSmemBytes = kPairSmemBytes;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, proj_pair_kernel, &cfg) != cudaSuccess ||
+        clusters <= 0) {
+      (void)cudaGetLastError();
+      int sms = 0;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      clusters = sms > 1 ? sms / 2 : 1;
+    }
+    max_pairs[dev] = clusters;
     configured[dev] = true;
   }
-  dim3 grid(2 * p.n_pairs, (p.M + p.n_tok - 1) / p.n_tok, p.ksplit > 1 ? p.ksplit : 1);
-  proj_pair_kernel<<<grid, kPairThreads, kPairSmemBytes, stream>>>(p);
+  ProjParams q = p;
+  q.n_ttiles = (p.M + p.n_tok - 1) / p.n_tok;
+  q.n_tiles = q.n_pairs * q.n_ttiles * (p.ksplit > 1 ? p.ksplit : 1);
+  const int pairs = q.n_tiles < max_pairs[dev] ? q.n_tiles : max_pairs[dev];
+  proj_pair_kernel<<<dim3(2 * pairs, 1, 1), kPairThreads, kPairSmemBytes, stream>>>(q);
   return cudaGetLastError();
 }
 
