@@ -540,16 +540,22 @@ __device__ void pair_epilogue(const ProjParams& p, const PairSmem& sm, uint32_t 
               }
             }
           }
+          // The even lane of a pair writes token je, the odd lane token je + 4:
+          // rows 4 apart land in opposite halves of the swizzled row, so one
+          // store instruction touches 32 distinct banks.
 #pragma unroll
-          for (int jj = 0; jj < 32; jj += 2) {
-            const float mine_even = __uint_as_float(v[jj]);
-            const float mine_odd = __uint_as_float(v[jj + 1]);
-            const float give = odd ? mine_even : mine_odd;
-            const float got = __shfl_xor_sync(0xFFFFFFFFu, give, 1);
-            const uint32_t word = odd ? pack_bf16x2(got, mine_odd) : pack_bf16x2(mine_even, got);
-            const uint32_t row = static_cast<uint32_t>(c * 32 + jj + (odd ? 1 : 0));
-            const uint32_t addr = stage + row * 128u + (((chunk ^ (row & 7u)) << 4) | in_chunk);
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(word) : "memory");
+          for (int jb = 0; jb < 32; jb += 8) {
+#pragma unroll
+            for (int d = 0; d < 4; ++d) {
+              const int je = jb + d, jo = jb + d + 4;
+              const float give = __uint_as_float(odd ? v[je] : v[jo]);
+              const float got = __shfl_xor_sync(0xFFFFFFFFu, give, 1);
+              const uint32_t word = odd ? pack_bf16x2(got, __uint_as_float(v[jo]))
+                                        : pack_bf16x2(__uint_as_float(v[je]), got);
+              const uint32_t row = static_cast<uint32_t>(c * 32 + (odd ? jo : je));
+              const uint32_t addr = stage + row * 128u + (((chunk ^ (row & 7u)) << 4) | in_chunk);
+              asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(word) : "memory");
+            }
           }
         }
         fence_proxy_async_shared();
