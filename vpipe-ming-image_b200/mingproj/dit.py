@@ -234,17 +234,29 @@ class DitProjectionSet:
     # ---- the projections of one block ------------------------------------------
     def block_projections(self, b: int, nrm: torch.Tensor, attn_out: torch.Tensor,
                           ffn_in: torch.Tensor, outs: dict[str, torch.Tensor],
-                          stream=None) -> None:
+                          stream=None, around=None) -> None:
         """The seven projections of block b, in run_block's order: q/k/v on
         `nrm` (one shared rank-space pass), to_out on `attn_out`, w1/w3 on
         `nrm`, w2 on `ffn_in`. `outs` maps projection name -> output tensor
-        (rows >= nrm.shape[0])."""
+        (rows >= nrm.shape[0]). `around(i, call)` (optional) runs call i (0-3)
+        of the block, e.g. between two CUDA events."""
         p = self.blocks[b].proj
         m = nrm.shape[0]
-        self.ctx.linear_shared([p[n] for n in QKV], nrm, [outs[n][:m] for n in QKV], stream)
-        self.ctx.linear(p["attention.to_out.0"], attn_out, outs["attention.to_out.0"][:m], stream)
-        self.ctx.linear_shared([p[n] for n in FF13], nrm, [outs[n][:m] for n in FF13], stream)
-        self.ctx.linear(p["feed_forward.w2"], ffn_in, outs["feed_forward.w2"][:m], stream)
+        calls = (
+            lambda: self.ctx.linear_shared([p[n] for n in QKV], nrm, [outs[n][:m] for n in QKV],
+                                           stream),
+            lambda: self.ctx.linear(p["attention.to_out.0"], attn_out,
+                                    outs["attention.to_out.0"][:m], stream),
+            lambda: self.ctx.linear_shared([p[n] for n in FF13], nrm, [outs[n][:m] for n in FF13],
+                                           stream),
+            lambda: self.ctx.linear(p["feed_forward.w2"], ffn_in, outs["feed_forward.w2"][:m],
+                                    stream),
+        )
+        for i, call in enumerate(calls):
+            if around is None:
+                call()
+            else:
+                around(i, call)
 
     def forward_projections(self, layout: Layout, nrm: torch.Tensor, attn_out: torch.Tensor,
                             ffn_in: torch.Tensor, outs: dict[str, torch.Tensor],
