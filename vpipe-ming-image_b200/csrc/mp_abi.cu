@@ -20,6 +20,7 @@
 namespace mp {
 cudaError_t launch_proj_pair(const ProjParams& p, cudaStream_t stream);
 cudaError_t launch_lora_reduce(const ReduceParams& p, cudaStream_t stream);
+int resident_pairs();
 int pick_ntok_pair(int m, int pairs);
 cudaError_t launch_mod(const ModParams& p, cudaStream_t stream);
 }  // namespace mp
@@ -110,6 +111,10 @@ struct mp_ctx {
   size_t scratch_cap = 0;       // elements
   float* part = nullptr;        // split-K partial sums of the rank-space pre-GEMM
   size_t part_cap = 0;          // elements
+  uint32_t* flags = nullptr;    // fused-prologue ready flags (zeroed on allocation)
+  size_t flags_cap = 0;         // entries
+  uint32_t epoch = 0;           // value of a flag that is set, per fused launch
+  bool fuse_off = false;        // cooperative launches refused on this device
   uint64_t wait_limit_ns = 2000000000ull;
   mp_engagement eng{};
   std::map<std::vector<uintptr_t>, SharedStack> shared;
@@ -204,6 +209,16 @@ int ensure_buf(mp_ctx* c, T** p, size_t* cap, size_t elems, cudaStream_t stream)
   if (e != cudaSuccess) return cuda_fail(c, e, "cudaMalloc");
   *p = static_cast<T*>(q);
   *cap = elems;
+  return MP_OK;
+}
+
+// Ready flags of fused prologues: at least `n` entries, zeroed when (re)allocated.
+int ensure_flags(mp_ctx* c, size_t n, cudaStream_t stream) {
+  if (c->flags_cap >= n && c->flags != nullptr) return MP_OK;
+  const size_t cap = std::max<size_t>(n, 1024);
+  int rc = ensure_buf(c, &c->flags, &c->flags_cap, cap, stream);
+  if (rc != MP_OK) return rc;
+  MP_CUDA(c, cudaMemsetAsync(c->flags, 0, cap * sizeof(uint32_t), stream));
   return MP_OK;
 }
 
@@ -408,19 +423,20 @@ namespace mp {
 struct SplitChoice {
   int n_tok;
   int ksplit;
+  double us;  // modelled time, pre-GEMM and reduce
 };
 
 // Token tile and K splits of a rank-space pre-GEMM of `pairs` feature pairs
 // over m rows and `base_kt` 64-wide K tiles (r rank columns): the pair with
-// the least modelled time. A 64-wide K stage takes ~800 cycles on a
-// 256-token tile and ~1150 on a 512-token tile, a CTA adds ~6000 cycles of
+// the least modelled time. A 64-wide K stage takes ~890 cycles on a
+// 256-token tile and ~1250 on a 512-token tile, a CTA adds ~6000 cycles of
 // set-up and epilogue, 74 pairs run at once (one CTA per SM), and the second
 // pass of a split launch costs ~2 us plus its traffic at ~4 TB/s.
 SplitChoice choose_ksplit(int m, int pairs, int base_kt, int r) {
-  SplitChoice best{kMaxTok, 1};
+  SplitChoice best{kMaxTok, 1, 0.0};
   double best_us = 1e300;
   for (int nt : {kMaxTileTok, kMaxTok}) {
-    const double stage_cycles = nt > kMaxTok ? 1150.0 : 800.0;
+    const double stage_cycles = nt > kMaxTok ? 1250.0 : 890.0;
     const long long tiles = (m + nt - 1) / nt;
     for (int s = 1; s <= kMaxSplits && s <= base_kt; ++s) {
       const int kps = (base_kt + s - 1) / s;
@@ -430,7 +446,7 @@ SplitChoice choose_ksplit(int m, int pairs, int base_kt, int r) {
       if (s > 1) us += 2.0 + (static_cast<double>(s) * 4.0 + 2.0) * m * r / 4.0e6;
       if (us < best_us - 1e-9) {
         best_us = us;
-        best = SplitChoice{nt, s};
+        best = SplitChoice{nt, s, us};
       }
     }
   }
@@ -484,17 +500,57 @@ int launch_lora_down(mp_ctx* c, const CUtensorMap& tm_a, int rtot, const mp::Epi
   return MP_OK;
 }
 
+// The rank-space pre-GEMM a projection launch may run as its own prologue:
+// the stacked A of every live member (rtot rank rows) and the strengths.
+struct Prologue {
+  const CUtensorMap* tm_a = nullptr;
+  int rtot = 0;
+  const mp::EpilogueScale* es = nullptr;
+};
+
+constexpr int kFallback = -1;  // fused launch not possible: run the pre-GEMM separately
+
 // `count` projections of one x in one launch; sts[i] (nullable) is member
 // i's live stack, whose intermediate starts at column t_cols[i] of the
-// scratch (row stride t_ld).
+// scratch (row stride t_ld). With `pro`, the launch computes that
+// intermediate itself (fused prologue, cooperative launch); it returns
+// kFallback, having launched nothing, when that is not possible here.
 int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
                        const int64_t* ldys, const Stack* const* sts, const int* t_cols, int t_ld,
-                       int count, const void* x, int64_t ldx, int m, cudaStream_t stream) {
+                       int count, const void* x, int64_t ldx, int m, cudaStream_t stream,
+                       const Prologue* pro = nullptr) {
   ProjParams p;
   int ns[mp::kMaxMembers] = {0, 0, 0, 0};
   for (int i = 0; i < count; ++i) ns[i] = ws[i]->d.n;
   int rc = begin_launch(c, &p, x, ldx, ws[0]->d.k, m, ns, count);
   if (rc != MP_OK) return rc;
+  if (pro != nullptr && (c->fuse_off || p.n_tok < mp::kPreTok)) return kFallback;
+  if (pro != nullptr) {
+    // Fuse when the prologue units, on the pairs that run one member tile
+    // fewer, lengthen the launch by less than a separate pre-GEMM would take
+    // (cycle model: ~1300 / 1150 cycles per 512-token quantized / dense stage,
+    // ~890 per 256-token prologue stage, ~6000-8000 per tile of set-up and
+    // epilogue; 1900 cycles per microsecond).
+    const int P = mp::resident_pairs();
+    const long long n_main = static_cast<long long>(p.n_pairs) * ((m + p.n_tok - 1) / p.n_tok);
+    const long long light_pairs = P - n_main % P;
+    const int base_kt = (ws[0]->d.k + mp::kBlockK - 1) / mp::kBlockK;
+    int lora_kt = 0;
+    for (int i = 0; i < count; ++i)
+      if (sts[i] != nullptr) lora_kt = std::max(lora_kt, sts[i]->rpad / mp::kBlockK);
+    const double c_stage = (ws[0]->d.bits != 0 ? 1300.0 : 1150.0) * (p.n_tok > mp::kMaxTok ? 1.0 : 0.6);
+    const double t_main = (base_kt + lora_kt) * c_stage + 6000.0;
+    const double t_pre = base_kt * 890.0 + 8000.0;
+    const long long n_pre = static_cast<long long>((m + mp::kPreTok - 1) / mp::kPreTok) *
+                            pairs_of(pro->rtot);
+    const double heavy = static_cast<double>((n_main + P - 1) / P) * t_main;
+    const double light = static_cast<double>((n_pre + light_pairs - 1) / light_pairs) * t_pre +
+                         static_cast<double>(n_main / P) * t_main;
+    const double fused_extra = std::max(0.0, light - heavy);
+    const double separate = (mp::choose_ksplit(m, pairs_of(pro->rtot), base_kt, pro->rtot).us + 3.0) *
+                            1900.0;
+    if (fused_extra >= separate) return kFallback;
+  }
   for (int i = 0; i < count; ++i) {
     const mp_weight* w = ws[i];
     LoraTiles lt;
@@ -507,9 +563,39 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
     rc = fill_member(c, &p, i, w->tm_w, w->sb, w->sb_stride, w->d.n, w->d.bits, w->d.mode, ys[i],
                      ldys[i], lt);
     if (rc != MP_OK) return rc;
+    p.mem[i].t_col = lt.rpad > 0 ? t_cols[i] : 0;
   }
-  rc = run_launch(c, p, stream, "proj_pair_kernel");
-  if (rc != MP_OK) return rc;
+  if (pro != nullptr) {
+    p.pre_ttiles = (m + mp::kPreTok - 1) / mp::kPreTok;
+    p.pre_rpairs = pairs_of(pro->rtot);
+    p.n_pre = p.pre_ttiles * p.pre_rpairs;
+    rc = ensure_flags(c, static_cast<size_t>(p.n_pre) * 2, stream);
+    if (rc != MP_OK) return rc;
+    c->epoch = c->epoch + 1 == 0 ? 1 : c->epoch + 1;
+    p.flags = c->flags;
+    p.epoch = c->epoch;
+    p.scale = *pro->es;
+    mp::ProjMember& pre = p.pre;
+    pre.tm_w = *pro->tm_a;
+    pre.N = pro->rtot;
+    pre.bits = 0;
+    pre.sb = nullptr;
+    pre.lora_ktiles = 0;
+    if (!encode_y(&pre.tm_y, c->scratch, t_ld, pro->rtot, m, mp::kEpiRows))
+      return fail(c, MP_ECUDA, "tensor map encode failed (rank-space intermediate)");
+    cudaError_t e = mp::launch_proj_pair(p, stream);
+    if (e != cudaSuccess) {
+      // a cooperative launch this device refuses: nothing ran; never try again
+      (void)cudaGetLastError();
+      c->fuse_off = true;
+      return kFallback;
+    }
+    c->eng.kernels += 1;
+    c->eng.lora_down += 1;
+  } else {
+    rc = run_launch(c, p, stream, "proj_pair_kernel");
+    if (rc != MP_OK) return rc;
+  }
   for (int i = 0; i < count; ++i)
     count_projection(c, ws[i], m, sts[i] != nullptr && sts[i]->rpad > 0 ? sts[i]->ranks : nullptr);
   return MP_OK;
@@ -560,6 +646,7 @@ int mp_destroy(mp_ctx* c) {
   cudaFree(c->err_word);
   cudaFree(c->scratch);
   cudaFree(c->part);
+  cudaFree(c->flags);
   for (auto& kv : c->shared) cudaFree(kv.second.a);
   delete c;
   return MP_OK;
@@ -792,6 +879,17 @@ int mp_linear(mp_ctx* c, const mp_weight* wc, const void* x, int64_t ldx, void* 
     std::memset(&es, 0, sizeof(es));
     fill_scale(c, &es);
     add_ranges(&es, *st, 0);
+    const mp_weight* wl[1] = {w};
+    void* yl[1] = {y};
+    const int64_t ll[1] = {ldy};
+    const Stack* sl[1] = {st};
+    const int cl[1] = {0};
+    Prologue pro;
+    pro.tm_a = &st->tm_a;
+    pro.rtot = st->rpad;
+    pro.es = &es;
+    rc = launch_projections(c, wl, yl, ll, sl, cl, st->rpad, 1, x, ldx, m, s, &pro);
+    if (rc != kFallback) return rc;
     rc = launch_lora_down(c, st->tm_a, st->rpad, es, x, ldx, w->d.k, m, s);
     if (rc != MP_OK) return rc;
   }
@@ -863,6 +961,14 @@ int mp_linear_shared(mp_ctx* c, const mp_weight* const* ws, void* const* ys, con
     }
     rc = ensure_buf(c, &c->scratch, &c->scratch_cap, static_cast<size_t>(m) * rtot, s);
     if (rc != MP_OK) return rc;
+    const Stack* sts[mp::kMaxMembers];
+    for (int i = 0; i < count; ++i) sts[i] = live_mask(c, ws[i]) != 0 ? &ws[i]->stack : nullptr;
+    Prologue pro;
+    pro.tm_a = &sh.tm_a;
+    pro.rtot = rtot;
+    pro.es = &es;
+    rc = launch_projections(c, ws, ys, ldys, sts, col, rtot, count, x, ldx, m, s, &pro);
+    if (rc != kFallback) return rc;
     rc = launch_lora_down(c, sh.tm_a, rtot, es, x, ldx, k, m, s);
     if (rc != MP_OK) return rc;
   }

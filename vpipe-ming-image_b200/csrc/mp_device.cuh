@@ -393,6 +393,20 @@ __device__ __forceinline__ void tma_store_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
+// Generic-proxy / async-proxy ordering of global memory (TMA loads and stores
+// on one side of it, ordinary loads and stores on the other).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Waits until at most one committed bulk-store group is still reading shared memory.
 __device__ __forceinline__ void tma_store_wait_read_1() {
   asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");

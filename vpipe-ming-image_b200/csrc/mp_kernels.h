@@ -56,6 +56,7 @@ struct ProjMember {
   uint32_t code_xor;  // 0x80808080 turns signed 8-bit codes into offset-binary
   float code_offset;  // 32768 + the codes' zero point (128 for signed 8-bit codes, else 0)
   int32_t pair_begin;
+  int32_t t_col;      // first column of this member's ranks in the rank-space intermediate
 };
 
 struct ProjParams {
@@ -68,7 +69,7 @@ struct ProjParams {
   int32_t n_tiles;    // n_pairs * n_ttiles * max(ksplit, 1): the persistent grid's work list
   uint64_t wait_limit_ns;
   uint32_t* err;      // device error word
-  EpilogueScale scale;  // rank-space pre-GEMM only
+  EpilogueScale scale;  // rank-space pre-GEMM / prologue only
   // Split-K (ksplit > 1, a single member): the tiles of split z run the K tiles
   // [z * kt_per_split, min((z + 1) * kt_per_split, K tiles)) (the last split
   // also takes the member's LoRA K tiles) and writes its fp32 partial sums,
@@ -78,8 +79,24 @@ struct ProjParams {
   int32_t kt_per_split;
   float* part;
   int32_t part_ld;
+  // Fused rank-space prologue (n_pre > 0): before their member tiles, the
+  // pairs with the fewest member tiles run n_pre prologue units, each the
+  // full-K product of 256 token rows x 256 rank rows of T = scale ⊙ (x ·
+  // A_stack^T) (member `pre`: the stacked A as a dense weight, tm_y = T),
+  // stored scaled in bf16; each CTA of the unit then sets its flag
+  // flags[(rank_pair * pre_ttiles + token_tile) * 2 + cta] = epoch. A member
+  // tile waits for the flags of its T rows before its appended LoRA K tiles.
+  // The launch is cooperative (every pair resident), so the waits end.
+  int32_t n_pre;
+  int32_t pre_ttiles;     // 256-token tiles of the prologue: ceil(M / 256)
+  int32_t pre_rpairs;     // 256-row rank pairs: ceil(R / 256)
+  uint32_t* flags;
+  uint32_t epoch;
+  ProjMember pre;
   ProjMember mem[kMaxMembers];
 };
+
+constexpr int kPreTok = 256;  // token rows of a prologue unit
 
 // Second pass of a split-K launch: out[t, j] = bf16(scale(t, j) * sum_z
 // part[z][t][j]) for t < M, j < R, the splits added in z order (the result

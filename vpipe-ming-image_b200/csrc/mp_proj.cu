@@ -74,6 +74,7 @@ enum : uint32_t {
   kSiteEpi = 0x1500u,
   kSiteDrain = 0x1600u,
   kSiteTmem = 0x1700u,
+  kSitePrologue = 0x1800u,
 };
 
 // Per-stage timeline of the first CTA pair, only in builds compiled with
@@ -197,8 +198,97 @@ __device__ __forceinline__ Tile decode_tile(const ProjParams& p, int tile, int r
   return t;
 }
 
-__device__ __forceinline__ int first_tile() { return static_cast<int>(blockIdx.x >> 1); }
-__device__ __forceinline__ int tile_stride() { return static_cast<int>(gridDim.x >> 1); }
+// A prologue unit v (fused rank-space pre-GEMM): 256 rank rows x 256 tokens
+// of T over the full K, the stacked A as a dense weight.
+__device__ __forceinline__ Tile decode_pre(const ProjParams& p, int v, int rank, int base_kt) {
+  Tile t;
+  const int rp = v % p.pre_rpairs;
+  const int tt = v / p.pre_rpairs;
+  t.mi = -1;
+  t.f0 = rp * (2 * kBlockN) + rank * kBlockN;
+  t.t0 = tt * kPreTok;
+  t.z = 0;
+  t.n_sub = 1;
+  t.sub = kPreTok;
+  t.half = kPreTok / 2;
+  t.kt_begin = 0;
+  t.kt_end = base_kt;
+  return t;
+}
+
+// The units a pair runs, in order: its prologue units, then its member tiles
+// p, p + pairs, ... . Prologue units go round-robin to the pairs that run
+// the fewest member tiles (those past n_tiles % pairs), filling the idle end
+// of the member-tile schedule.
+struct UnitIter {
+  int pre_next, pre_step, main_next, main_step;
+};
+
+__device__ __forceinline__ UnitIter units_begin(const ProjParams& p) {
+  const int pairs = static_cast<int>(gridDim.x >> 1);
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int light0 = p.n_tiles % pairs;
+  UnitIter u;
+  u.main_next = pair;
+  u.main_step = pairs;
+  u.pre_step = pairs - light0;
+  u.pre_next = (p.n_pre > 0 && pair >= light0) ? pair - light0 : p.n_pre;
+  return u;
+}
+
+// Next unit: -1 - v for prologue unit v, the tile index for a member tile,
+// or kNoUnit.
+constexpr int kNoUnit = -0x7FFFFFFF;
+__device__ __forceinline__ int units_next(const ProjParams& p, UnitIter& u) {
+  if (u.pre_next < p.n_pre) {
+    const int v = u.pre_next;
+    u.pre_next += u.pre_step;
+    return -1 - v;
+  }
+  if (u.main_next < p.n_tiles) {
+    const int t = u.main_next;
+    u.main_next += u.main_step;
+    return t;
+  }
+  return kNoUnit;
+}
+
+__device__ __forceinline__ Tile decode_unit(const ProjParams& p, int unit, int rank, int base_kt) {
+  return unit < 0 ? decode_pre(p, -1 - unit, rank, base_kt) : decode_tile(p, unit, rank, base_kt);
+}
+
+__device__ __forceinline__ const ProjMember& unit_member(const ProjParams& p, const Tile& t) {
+  return t.mi < 0 ? p.pre : p.mem[t.mi];
+}
+
+// Fused prologue: bounded wait until every prologue unit holding T rows of
+// member tile t has stored them (both CTAs' flags of the needed rank pairs
+// and 256-token tiles), then order the coming TMA reads of T after that.
+__device__ bool wait_prologue(const ProjParams& p, const ProjMember& mb, const Tile& t,
+                              volatile uint32_t* abort) {
+  const int rp_lo = mb.t_col / (2 * kBlockN);
+  const int rp_hi = (mb.t_col + mb.lora_ktiles * kBlockK - 1) / (2 * kBlockN);
+  const int rows_end = min(p.M, t.t0 + t.n_sub * t.sub);
+  const int tt_lo = t.t0 / kPreTok;
+  const int tt_hi = (rows_end - 1) / kPreTok;
+  const uint64_t t0 = global_timer_ns();
+  for (int rp = rp_lo; rp <= rp_hi; ++rp) {
+    for (int tt = tt_lo; tt <= tt_hi; ++tt) {
+      for (int c = 0; c < 2; ++c) {
+        const uint32_t* f = p.flags + (static_cast<size_t>(rp) * p.pre_ttiles + tt) * 2 + c;
+        while (ld_acquire_gpu(f) != p.epoch) {
+          if (*abort != 0u) return false;
+          if (global_timer_ns() - t0 > p.wait_limit_ns) {
+            atomicCAS(const_cast<uint32_t*>(abort), 0u, kSitePrologue);
+            return false;
+          }
+        }
+      }
+    }
+  }
+  fence_proxy_async_global();
+  return true;
+}
 
 // Warp 0, one thread. Stage iteration `it` runs on across tiles.
 __device__ void pair_producer(const ProjParams& p, const PairSmem& sm, bool leader, int rank,
@@ -210,9 +300,10 @@ __device__ void pair_producer(const ProjParams& p, const PairSmem& sm, bool lead
   uint32_t pend_full = 0;      // slots whose pair copies this thread has not seen consumed
   uint32_t pend_full_par = 0;
   bool aborted = false;
-  for (int tile = first_tile(); tile < p.n_tiles && !aborted; tile += tile_stride()) {
-    const Tile t = decode_tile(p, tile, rank, base_kt);
-    const ProjMember& mb = p.mem[t.mi];
+  UnitIter units = units_begin(p);
+  for (int unit = units_next(p, units); unit != kNoUnit && !aborted; unit = units_next(p, units)) {
+    const Tile t = decode_unit(p, unit, rank, base_kt);
+    const ProjMember& mb = unit_member(p, t);
     const bool quant = mb.bits != 0;
     const uint32_t sub_bytes = static_cast<uint32_t>(t.half) * 128u;  // one sub-tile, one CTA
     const uint32_t xbytes_pair = 2u * static_cast<uint32_t>(t.n_sub) * sub_bytes;
@@ -234,6 +325,10 @@ __device__ void pair_producer(const ProjParams& p, const PairSmem& sm, bool lead
       const uint32_t full_local = smem_u32(&sm.full[s]);
       const uint32_t full_leader = mapa_shared(full_local, 0);
       const bool lora = kt >= base_kt;
+      if (lora && kt == base_kt && p.n_pre > 0 && !wait_prologue(p, mb, t, sm.abort)) {
+        aborted = true;
+        break;
+      }
       const CUtensorMap* xmap = lora ? &mb.tm_t : &p.tm_x;
       const int xk = (lora ? kt - base_kt : kt) * kBlockK;
       if (!lora && quant) {
@@ -282,9 +377,11 @@ __device__ void pair_mma(const ProjParams& p, const PairSmem& sm, uint32_t tmem,
   uint32_t apar = 0;  // per slot: parity of the slot's next dequant phase
   uint32_t tcount = 0;
   bool aborted = false;
-  for (int tile = first_tile(); tile < p.n_tiles && !aborted; tile += tile_stride(), ++tcount) {
-    const Tile t = decode_tile(p, tile, 0, base_kt);
-    const ProjMember& mb = p.mem[t.mi];
+  UnitIter units = units_begin(p);
+  for (int unit = units_next(p, units); unit != kNoUnit && !aborted;
+       unit = units_next(p, units), ++tcount) {
+    const Tile t = decode_unit(p, unit, 0, base_kt);
+    const ProjMember& mb = unit_member(p, t);
     const bool quant = mb.bits != 0;
     const uint32_t idesc = make_idesc_bf16(2 * kBlockN, static_cast<uint32_t>(t.sub));
     const uint32_t sub_bytes = static_cast<uint32_t>(t.half) * 128u;
@@ -357,9 +454,10 @@ __device__ void pair_dequant(const ProjParams& p, const PairSmem& sm, int rank, 
   uint32_t it = 0;
   uint32_t cpar = 0;  // per slot: parity of the slot's next codes phase
   bool aborted = false;
-  for (int tile = first_tile(); tile < p.n_tiles && !aborted; tile += tile_stride()) {
-    const Tile t = decode_tile(p, tile, rank, base_kt);
-    const ProjMember& mb = p.mem[t.mi];
+  UnitIter units = units_begin(p);
+  for (int unit = units_next(p, units); unit != kNoUnit && !aborted; unit = units_next(p, units)) {
+    const Tile t = decode_unit(p, unit, rank, base_kt);
+    const ProjMember& mb = unit_member(p, t);
     const int base_end = min(base_kt, t.kt_end);
     if (mb.bits == 0) {  // no dequant stages: keep the stage count in step
       it += static_cast<uint32_t>(t.kt_end - t.kt_begin);
@@ -468,17 +566,20 @@ __device__ void pair_epilogue(const ProjParams& p, const PairSmem& sm, uint32_t 
   const uint32_t chunk = wi >> 2, in_chunk = (wi & 3u) << 2;
   uint32_t tcount = 0;
   uint32_t round = 0;
-  for (int tile = first_tile(); tile < p.n_tiles; tile += tile_stride(), ++tcount) {
-    const Tile t = decode_tile(p, tile, rank, base_kt);
-    const ProjMember& mb = p.mem[t.mi];
+  UnitIter units = units_begin(p);
+  for (int unit = units_next(p, units); unit != kNoUnit; unit = units_next(p, units), ++tcount) {
+    const Tile t = decode_unit(p, unit, rank, base_kt);
+    const ProjMember& mb = unit_member(p, t);
     const int f = t.f0 + fl;
+    // strengths apply to a rank-space pre-GEMM launch and to prologue units
+    const bool scaled = p.scale.enabled && (p.n_pre == 0 || t.mi < 0);
     const bool ok_mine =
         mbar_wait(smem_u32(sm.tfull), tcount & 1u, sm.abort, kSiteEpi, p.wait_limit_ns);
     if (!named_barrier_and(kEpiBarrier, kEpiThreads, ok_mine)) break;
     tc_fence_after();
     if (threadIdx.x == 32 * kEpiWarp0) MP_TRACE_MARK(kTrEpiStart, static_cast<int>(tcount));
     int slot = -1;
-    if (!split && p.scale.enabled) {
+    if (!split && scaled) {
       for (int i = 0; i < p.scale.n_ranges; ++i)
         if (f >= p.scale.range_start[i] && f < p.scale.range_start[i + 1])
           slot = p.scale.range_slot[i];
@@ -522,7 +623,7 @@ __device__ void pair_epilogue(const ProjParams& p, const PairSmem& sm, uint32_t 
               tmem + lane_base + static_cast<uint32_t>(j * t.sub + rr * kEpiRows + c * 32), v);
           MP_TMEM_WAIT_LD_REGS32(v);
           if (rr + 1 == rounds && c == 1) release_accumulator(sm, j);
-          if (p.scale.enabled) {
+          if (scaled) {
             // one strength per 32-token chunk unless a row-segment boundary
             // falls inside it (the per-lane slot makes each lookup divergent)
             const int tc = tr0 + c * 32;
@@ -568,6 +669,16 @@ __device__ void pair_epilogue(const ProjParams& p, const PairSmem& sm, uint32_t 
         }
         ++round;
       }
+    }
+    if (t.mi < 0 && issuer) {
+      // prologue unit: T rows stored (complete, not just read out of shared
+      // memory), then published to the member tiles waiting for them
+      tma_store_wait_all();
+      fence_proxy_async_global();
+      __threadfence();
+      const int v = -1 - unit;
+      const int rp = v % p.pre_rpairs, tt = v / p.pre_rpairs;
+      st_release_gpu(p.flags + (static_cast<size_t>(rp) * p.pre_ttiles + tt) * 2 + rank, p.epoch);
     }
     if (threadIdx.x == 32 * kEpiWarp0) MP_TRACE_MARK(kTrEpiEnd, static_cast<int>(tcount));
   }
@@ -734,36 +845,72 @@ cudaError_t launch_lora_reduce(const ReduceParams& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-cudaError_t launch_proj_pair(const ProjParams& p, cudaStream_t stream) {
-  static bool configured[64] = {};
-  static int max_pairs[64] = {};
+namespace {
+
+bool g_configured[64] = {};
+int g_max_pairs[64] = {};
+
+// Opts the kernel in to its shared memory and finds the CTA pairs resident at
+// once (one CTA per SM), which the persistent grid fills; once per device.
+cudaError_t configure(int* dev_out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!configured[dev]) {
-    e = cudaFuncSetAttribute(proj_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kPairSmemBytes));
-    if (e != cudaSuccess) return e;
-    // pairs resident at once (one CTA per SM), which the persistent grid fills
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2, 1, 1);
-    cfg.blockDim = dim3(kPairThreads, 1, 1);
-    cfg.dynamicSmemBytes = kPairSmemBytes;
-    int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, proj_pair_kernel, &cfg) != cudaSuccess ||
-        clusters <= 0) {
-      (void)cudaGetLastError();
-      int sms = 0;
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      clusters = sms > 1 ? sms / 2 : 1;
-    }
-    max_pairs[dev] = clusters;
-    configured[dev] = true;
+  *dev_out = dev;
+  if (g_configured[dev]) return cudaSuccess;
+  e = cudaFuncSetAttribute(proj_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(kPairSmemBytes));
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(kPairThreads, 1, 1);
+  cfg.dynamicSmemBytes = kPairSmemBytes;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, proj_pair_kernel, &cfg) != cudaSuccess ||
+      clusters <= 0) {
+    (void)cudaGetLastError();
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    clusters = sms > 1 ? sms / 2 : 1;
   }
+  g_max_pairs[dev] = clusters;
+  g_configured[dev] = true;
+  return cudaSuccess;
+}
+
+}  // namespace
+
+int resident_pairs() {
+  int dev = 0;
+  if (configure(&dev) != cudaSuccess) return 74;
+  return g_max_pairs[dev];
+}
+
+cudaError_t launch_proj_pair(const ProjParams& p, cudaStream_t stream) {
+  int dev = 0;
+  cudaError_t e = configure(&dev);
+  if (e != cudaSuccess) return e;
+  int* max_pairs = g_max_pairs;
   ProjParams q = p;
   q.n_ttiles = (p.M + p.n_tok - 1) / p.n_tok;
   q.n_tiles = q.n_pairs * q.n_ttiles * (p.ksplit > 1 ? p.ksplit : 1);
+  if (q.n_pre > 0) {
+    // Fused prologue: member tiles wait on prologue units of other pairs, so
+    // every pair must be resident at once: a cooperative launch of exactly
+    // the resident pair count (refused, with nothing run, if it cannot be).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * max_pairs[dev], 1, 1);
+    cfg.blockDim = dim3(kPairThreads, 1, 1);
+    cfg.dynamicSmemBytes = kPairSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, proj_pair_kernel, q);
+  }
   const int pairs = q.n_tiles < max_pairs[dev] ? q.n_tiles : max_pairs[dev];
   proj_pair_kernel<<<dim3(2 * pairs, 1, 1), kPairThreads, kPairSmemBytes, stream>>>(q);
   return cudaGetLastError();
