@@ -99,6 +99,11 @@ const char* mp_status_string(int status);
 int mp_sync_check(mp_ctx* ctx, void* stream);
 /* Device-side wait limit in nanoseconds (default 2e9). */
 int mp_set_wait_limit(mp_ctx* ctx, uint64_t ns);
+/* Failure-detection self-test (no reference counterpart): launches one CTA
+ * whose mbarrier wait can never complete, bounded by `limit_ns` exactly as the
+ * projection kernels bound theirs. The next mp_sync_check reports MP_ETIMEOUT
+ * and clears it; the context stays usable. Nothing faults or traps. */
+int mp_selftest_wait(mp_ctx* ctx, uint64_t limit_ns, void* stream);
 
 /* ---- weights ---------------------------------------------------------- */
 

@@ -4,6 +4,9 @@ the plugin's own bar for bf16 against fp32 (README.md:123-125 of the
 reference). Also the pack path, runtime LoRA against fused weights (the
 reference's bars, tests/ming-dit-test.cc:1241-1246) and strength-0 bit
 identity (:1249-1273)."""
+import json
+from pathlib import Path
+
 import numpy as np
 import pytest
 import torch
@@ -17,7 +20,10 @@ from mingproj.lora import Factors, SlotBinding
 
 pytestmark = pytest.mark.gpu
 
-BAR = 0.0158        # bf16 forward vs fp32 forward
+# bf16 forward vs fp32 forward: the reference's own bar (README.md:124, recorded in
+# tests/golden/reference_pins.json)
+BAR = json.loads((Path(__file__).resolve().parent / "golden" /
+                  "reference_pins.json").read_text())["bf16_forward_rel_l2_bar"]["value"]
 K_SMALL_TOL = 0.035  # runtime LoRA vs the fused reference (tests/ming-dit-test.cc:810-815)
 
 CFG = DitModelConfig(dim=fx.DIM, n_heads=fx.HEADS, n_refiner=fx.NREF, n_layers=fx.NLAY,

@@ -1,6 +1,9 @@
 """Adapter key parsing and the slot-binding rules of the reference's
 bind_loras_ (src/ming-dit.cc:2893-3005), restated as the reference's own test
 cases (tests/ming-dit-test.cc:1165-1168, :1196-1225, :1342-1386)."""
+import json
+from pathlib import Path
+
 import numpy as np
 import pytest
 
@@ -45,8 +48,13 @@ def _write(path, mods, spelling, alpha=16.0):
 
 def test_module_capacity():
     # tests/ming-dit-test.cc:1165-1168 (small: 28) and :2026 (real: 238)
-    assert L.module_capacity(1, 2) == 28 == len(L.module_names(1, 2))
-    assert L.module_capacity(2, 30) == 238 == len(L.module_names(2, 30))
+    pins = json.loads((Path(__file__).resolve().parent / "golden" /
+                       "reference_pins.json").read_text())
+    rule = pins["lora_capacity_rule"]
+    assert L.module_capacity(1, 2) == rule["per_block"] * (rule["refiner_stacks"] * 1 + 2) == 28
+    assert L.module_capacity(1, 2) == len(L.module_names(1, 2))
+    assert L.module_capacity(2, 30) == pins["lora_capacity_real_model"]["value"] == 238
+    assert L.module_capacity(2, 30) == len(L.module_names(2, 30))
 
 
 def test_three_spellings_bind_identically(tmp_path):

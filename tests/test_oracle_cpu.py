@@ -1,11 +1,18 @@
 """The oracle itself: its C and numpy restatements agree, the pack code layout
 round-trips bit-exactly, and the structural facts the reference's tests pin
-hold (pack shapes and dtypes, detection rule, FLOP formula)."""
+hold (pack shapes and dtypes, detection rule, FLOP formula), as recorded in
+tests/golden/reference_pins.json (made from the reference's test sources by
+tests/golden/make_reference_pins.py)."""
+import json
+from pathlib import Path
+
 import numpy as np
 import pytest
 
 from oracle import oracle as O
 from mingproj import pack as P
+
+PINS = json.loads((Path(__file__).resolve().parent / "golden" / "reference_pins.json").read_text())
 
 
 @pytest.mark.parametrize("bits", [8, 4])
@@ -119,16 +126,30 @@ def test_selection_counts_match_reference_pin():
               "all_final_layer.2-1.adaLN_modulation.1.weight",
               "all_final_layer.2-1.linear.weight"]
     c = P.selection_counts(names)
-    assert c["quantized"] == 32 * 8 + 2 * 7
-    assert c["dense_model"] == 7
+    assert c["quantized"] == PINS["quantized_block_matrices"]["value"] == 32 * 8 + 2 * 7
+    assert c["dense_model"] == PINS["dense_model_weights"]["value"] == 7
 
 
 def test_rel_l2_matches_reference_definition():
+    assert PINS["rel_l2_definition"]["source"].startswith("tests/ming-test.h")
     a = np.array([1.0, 2.0, 3.0])
     b = np.array([1.0, 2.0, 4.0])
     assert abs(O.rel_l2(a, b) - np.sqrt(1.0 / 21.0)) < 1e-15
     assert O.rel_l2(a, a) == 0.0
     assert O.rel_l2(a, b[:2]) == 1.0
+
+
+def test_pack_shapes_follow_reference_rule():
+    """codes [N, K*bits/32] U32 beside scales [N, K/64] (the pack check of
+    the reference's quant test, pinned in tests/golden/reference_pins.json)."""
+    rule = PINS["pack_shape_rule"]
+    rng = np.random.default_rng(9)
+    for bits in (8, 4):
+        pw = P.synthetic_affine(rng, 128, 512, bits)
+        codes = np.asarray(pw.data)
+        scales = np.asarray(pw.scales)
+        assert codes.dtype == np.uint32
+        assert codes.shape[1] * rule["codes_word_bits"] == scales.shape[1] * rule["group"] * bits
 
 
 def test_bf16_rounding_matches_torch():

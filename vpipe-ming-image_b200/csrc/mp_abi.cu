@@ -22,6 +22,7 @@ cudaError_t launch_proj_pair(const ProjParams& p, cudaStream_t stream);
 cudaError_t launch_lora_reduce(const ReduceParams& p, cudaStream_t stream);
 int resident_pairs();
 int pick_ntok_pair(int m, int pairs);
+cudaError_t launch_wait_selftest(uint64_t limit_ns, uint32_t* err, cudaStream_t stream);
 cudaError_t launch_mod(const ModParams& p, cudaStream_t stream);
 }  // namespace mp
 
@@ -671,6 +672,15 @@ int mp_sync_check(mp_ctx* c, void* stream) {
     MP_CUDA(c, cudaMemset(c->err_word, 0, sizeof(uint32_t)));
     return fail(c, MP_ETIMEOUT, "a kernel gave up a bounded device-side wait (word 0x%x)", word);
   }
+  return MP_OK;
+}
+
+int mp_selftest_wait(mp_ctx* c, uint64_t limit_ns, void* stream) {
+  if (c == nullptr) return MP_EINVAL;
+  int rc = use_device(c);
+  if (rc != MP_OK) return rc;
+  cudaError_t e = mp::launch_wait_selftest(limit_ns, c->err_word, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(c, e, "wait_selftest_kernel");
   return MP_OK;
 }
 

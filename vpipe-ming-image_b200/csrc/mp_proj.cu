@@ -749,6 +749,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     pair_epilogue(p, sm, tmem, rank, base_kt);
   }
 
+  if (*sm.abort != 0u) {
+    // Error path only: let copies issued before the abort land (their
+    // completion may be counted on the other CTA's barrier) before either
+    // CTA of the pair leaves.
+    const uint64_t t_settle = global_timer_ns();
+    while (global_timer_ns() - t_settle < 100000ull) __nanosleep(1000);
+  }
   tc_fence_before();
   cluster_sync();
   tc_fence_after();
@@ -778,6 +785,28 @@ int pick_ntok_pair(int m, int pairs) {
   if (pairs * static_cast<long long>((m + 127) / 128) >= slots) return 128;
   return 64;
 #endif
+}
+
+// Failure-detection self-test: an mbarrier nobody arrives on, waited on with
+// the same bounded wait the projection kernel uses; the CTA reports the
+// timeout through the context's error word and returns.
+__global__ void __launch_bounds__(32) wait_selftest_kernel(uint64_t limit_ns, uint32_t* err) {
+  __shared__ uint64_t bar;
+  __shared__ uint32_t abort_word;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_word = 0u;
+    fence_mbar_init();
+  }
+  __syncwarp();
+  const bool ok = mbar_wait(smem_u32(&bar), 0, &abort_word, 0x1900u, limit_ns);
+  __syncwarp();
+  if (threadIdx.x == 0 && (!ok || abort_word != 0u)) atomicOr(err, kErrTimeout);
+}
+
+cudaError_t launch_wait_selftest(uint64_t limit_ns, uint32_t* err, cudaStream_t stream) {
+  wait_selftest_kernel<<<1, 32, 0, stream>>>(limit_ns, err);
+  return cudaGetLastError();
 }
 
 // Second pass of a split-K launch (ReduceParams). Thread i owns the 4

@@ -172,6 +172,11 @@ class Context:
         bounded device-side wait."""
         self._check(self.lib.mp_sync_check(self.h, _stream_handle(stream)))
 
+    def selftest_wait(self, limit_ns: int, stream=None) -> None:
+        """Launches the failure-detection self-test: one bounded wait that can
+        never complete. The next sync_check raises MPError(MP_ETIMEOUT)."""
+        self._check(self.lib.mp_selftest_wait(self.h, limit_ns, _stream_handle(stream)))
+
     def set_wait_limit(self, ns: int) -> None:
         self._check(self.lib.mp_set_wait_limit(self.h, int(ns)))
 
