@@ -14,6 +14,11 @@ weights (6.2 GB of codes per step, far larger than L2).
 Under torchrun (N > 1) every rank runs one image of its own (image sharding,
 no collective on the data path: weak scaling); the JSON line reports the
 whole-job TFLOP/s over the max-over-ranks device time.
+
+`--shard rows` instead splits ONE image's token rows across the N ranks
+(128-row-aligned slices, configs 2-4): every rank projects its slice of every
+block, and each block's K and V are all-gathered over NCCL on a side stream
+while the block's remaining projections run (strong scaling).
 """
 from __future__ import annotations
 
@@ -143,6 +148,117 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_rows(args) -> None:
+    """One image's rows sharded over the ranks (strong scaling): projections of
+    the local 128-row-aligned slice, K and V all-gathered per block on side
+    streams that overlap to_out, w1/w3 and w2; the timed region ends when every
+    gather has landed."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from mingproj.dit import (DitDims, DitProjectionSet, Layout, alloc_outputs,
+                              modulation_flops, projection_flops)
+    from mingproj.parallel import RowGather, row_shards
+    from mingproj.proj import Context
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    peaks = load_peaks()
+    dims = DitDims()
+    layout = Layout(img=4096, cap=256)
+    ctx = Context(local)
+    # one model and one image shared by all ranks: same seeds everywhere
+    pset = DitProjectionSet.synthetic(ctx, dims, bits=8, seed=1, device=dev)
+    for i, r in enumerate(RANKS):
+        pset.bind_synthetic(i, r, seed=100 + i, device=dev)
+    for i, s_ in enumerate(np.random.default_rng(2).uniform(-1.0, 1.5, size=8)):
+        ctx.set_strength(i, float(s_))
+    gen = torch.Generator(device=dev).manual_seed(3)
+    JT = layout.joint
+    nrm = torch.randn((JT, dims.dim), device=dev, generator=gen).to(torch.bfloat16)
+    ao = torch.randn((JT, dims.dim), device=dev, generator=gen).to(torch.bfloat16)
+    ffi = torch.randn((JT, dims.ffn), device=dev, generator=gen).to(torch.bfloat16)
+    temb = torch.randn((1, dims.adaln), device=dev, generator=gen).to(torch.bfloat16)
+    outs = alloc_outputs(dims, JT, dev)
+    stream = torch.cuda.current_stream(dev)
+    base_f, lora_f = projection_flops(dims, layout, RANKS)
+    step_flops = base_f + lora_f + modulation_flops(dims, 1)
+    sizes = sorted({layout.rows(dims.block_kind(b)) for b in range(dims.n_blocks)})
+    gathers = {m: [[RowGather(m, dims.dim, world, rank, dev) for _ in range(2)] for _ in range(2)]
+               for m in sizes} if world > 1 else {}
+
+    def step():
+        ctx.modulation(pset.modset, temb)
+        for b in range(dims.n_blocks):
+            m = layout.rows(dims.block_kind(b))
+            sh = row_shards(m, world)[rank]
+            gk, gv = gathers[m][b % 2] if world > 1 else (None, None)
+
+            def around(i, call, rows=sh.rows, gk=gk, gv=gv):
+                if rows > 0:
+                    call()
+                if i == 0 and gk is not None:  # K and V of the block: gather now
+                    gk.start(outs["attention.to_k"][:rows])
+                    gv.start(outs["attention.to_v"][:rows])
+            pset.block_projections(b, nrm[sh.start:sh.stop], ao[sh.start:sh.stop],
+                                   ffi[sh.start:sh.stop], outs, around=around)
+        for pair in gathers.values():
+            for g2 in pair:
+                for g in g2:
+                    if g.pending:
+                        g.wait()
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync_check()
+    torch.cuda.synchronize(dev)
+    ctx.reset_engagement()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    with ClockSampler(local) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        ev[0].record(stream)
+        for _ in range(args.steps):
+            step()
+        ev[1].record(stream)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+    ctx.sync_check()
+    t = torch.tensor([ev[0].elapsed_time(ev[1])], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    value = step_flops * args.steps / (max_ms / 1e3) / 1e12
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "l2": "inputs larger than L2",
+                       "flops_per_step": step_flops,
+                       "parallelism": f"token-rows x{world} (128-row-aligned slices), NCCL "
+                                      "all-gather of each block's K and V overlapping the "
+                                      "block's remaining projections"},
+            "roofline": None, "cpu_baseline": None, "e2e": None,
+            "gpu_launches": ctx.engagement()["kernels"], "clocks": clk.summary(),
+            "peaks": peaks.get("source"),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -151,9 +267,13 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--shard", choices=["images", "rows"], default="images")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.shard == "rows":
+        run_rows(args)
         return
 
     import numpy as np

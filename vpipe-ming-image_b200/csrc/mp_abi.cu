@@ -525,12 +525,13 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
   for (int i = 0; i < count; ++i) ns[i] = ws[i]->d.n;
   int rc = begin_launch(c, &p, x, ldx, ws[0]->d.k, m, ns, count);
   if (rc != MP_OK) return rc;
-  if (pro != nullptr && (c->fuse_off || p.n_tok < mp::kPreTok)) return kFallback;
+  // the prologue's x tiles share the member tiles' TMA map: 256-token sub-tiles
+  if (pro != nullptr && (c->fuse_off || p.n_tok < mp::kMaxTok)) return kFallback;
   if (pro != nullptr) {
     // Fuse when the prologue units, on the pairs that run one member tile
     // fewer, lengthen the launch by less than a separate pre-GEMM would take
     // (cycle model: ~1300 / 1150 cycles per 512-token quantized / dense stage,
-    // ~890 per 256-token prologue stage, ~6000-8000 per tile of set-up and
+    // the prologue's stages dense, ~6000-8000 per tile of set-up and
     // epilogue; 1900 cycles per microsecond).
     const int P = mp::resident_pairs();
     const long long n_main = static_cast<long long>(p.n_pairs) * ((m + p.n_tok - 1) / p.n_tok);
@@ -541,7 +542,7 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
       if (sts[i] != nullptr) lora_kt = std::max(lora_kt, sts[i]->rpad / mp::kBlockK);
     const double c_stage = (ws[0]->d.bits != 0 ? 1300.0 : 1150.0) * (p.n_tok > mp::kMaxTok ? 1.0 : 0.6);
     const double t_main = (base_kt + lora_kt) * c_stage + 6000.0;
-    const double t_pre = base_kt * 890.0 + 8000.0;
+    const double t_pre = base_kt * 1150.0 + 8000.0;
     const long long n_pre = static_cast<long long>((m + mp::kPreTok - 1) / mp::kPreTok) *
                             pairs_of(pro->rtot);
     const double heavy = static_cast<double>((n_main + P - 1) / P) * t_main;

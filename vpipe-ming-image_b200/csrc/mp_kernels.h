@@ -81,14 +81,14 @@ struct ProjParams {
   int32_t part_ld;
   // Fused rank-space prologue (n_pre > 0): before their member tiles, the
   // pairs with the fewest member tiles run n_pre prologue units, each the
-  // full-K product of 256 token rows x 256 rank rows of T = scale ⊙ (x ·
+  // full-K product of 512 token rows x 256 rank rows of T = scale ⊙ (x ·
   // A_stack^T) (member `pre`: the stacked A as a dense weight, tm_y = T),
   // stored scaled in bf16; each CTA of the unit then sets its flag
   // flags[(rank_pair * pre_ttiles + token_tile) * 2 + cta] = epoch. A member
   // tile waits for the flags of its T rows before its appended LoRA K tiles.
   // The launch is cooperative (every pair resident), so the waits end.
   int32_t n_pre;
-  int32_t pre_ttiles;     // 256-token tiles of the prologue: ceil(M / 256)
+  int32_t pre_ttiles;     // 512-token tiles of the prologue: ceil(M / 512)
   int32_t pre_rpairs;     // 256-row rank pairs: ceil(R / 256)
   uint32_t* flags;
   uint32_t epoch;
@@ -96,7 +96,7 @@ struct ProjParams {
   ProjMember mem[kMaxMembers];
 };
 
-constexpr int kPreTok = 256;  // token rows of a prologue unit
+constexpr int kPreTok = 512;  // token rows of a prologue unit (two accumulators, as member tiles)
 
 // Second pass of a split-K launch: out[t, j] = bf16(scale(t, j) * sum_z
 // part[z][t][j]) for t < M, j < R, the splits added in z order (the result

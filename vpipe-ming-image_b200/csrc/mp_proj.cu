@@ -198,8 +198,9 @@ __device__ __forceinline__ Tile decode_tile(const ProjParams& p, int tile, int r
   return t;
 }
 
-// A prologue unit v (fused rank-space pre-GEMM): 256 rank rows x 256 tokens
-// of T over the full K, the stacked A as a dense weight.
+// A prologue unit v (fused rank-space pre-GEMM): 256 rank rows x 512 tokens
+// of T (two accumulators, as a member tile) over the full K, the stacked A
+// as a dense weight.
 __device__ __forceinline__ Tile decode_pre(const ProjParams& p, int v, int rank, int base_kt) {
   Tile t;
   const int rp = v % p.pre_rpairs;
@@ -208,9 +209,9 @@ __device__ __forceinline__ Tile decode_pre(const ProjParams& p, int v, int rank,
   t.f0 = rp * (2 * kBlockN) + rank * kBlockN;
   t.t0 = tt * kPreTok;
   t.z = 0;
-  t.n_sub = 1;
-  t.sub = kPreTok;
-  t.half = kPreTok / 2;
+  t.sub = kSubTok;
+  t.half = kSubTok / 2;
+  t.n_sub = t.t0 + kSubTok < p.M ? 2 : 1;
   t.kt_begin = 0;
   t.kt_end = base_kt;
   return t;

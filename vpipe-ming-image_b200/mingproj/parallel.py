@@ -92,6 +92,11 @@ class RowGather:
     def local(self) -> Shard:
         return self.shards[self.rank]
 
+    @property
+    def pending(self) -> bool:
+        """A gather has been started and not yet joined."""
+        return self._work is not None
+
     def start(self, y_local: torch.Tensor) -> None:
         """Begin gathering this rank's rows y_local [local.rows, n]."""
         rows = self.local.rows
