@@ -322,12 +322,14 @@ def test_dense_ragged_k_with_lora(ctx, m, n, k):
 
 
 @pytest.mark.parametrize("bits", [8, 4, 0])
-@pytest.mark.parametrize("m", [4400, 4352, 4200])
+@pytest.mark.parametrize("m", [4400, 4352, 4200, 2176, 700])
 def test_512_token_tiles_ragged_tail(ctx, bits, m):
     """Wide launches take 512-token pair tiles (two accumulators per dequantized
     stage): the last tile's second half is partly past M (4400), absent
-    (4352: dropped accumulator) or both halves ragged (4200). Rows sampled from
-    every tile, the tail tile in full, against the oracle; LoRA slots live."""
+    (4352: dropped accumulator) or both halves ragged (4200); narrower ones
+    (2176, 700 rows) take 256- or 128-token tiles with their own stage
+    layouts and a separate rank-space pre-GEMM. Rows sampled from every tile,
+    the tail tile in full, against the oracle; LoRA slots live."""
     rng = np.random.default_rng(m + bits)
     n, k = 3840, 640
     pw = _weight(rng, n, k, bits)

@@ -525,8 +525,9 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
   for (int i = 0; i < count; ++i) ns[i] = ws[i]->d.n;
   int rc = begin_launch(c, &p, x, ldx, ws[0]->d.k, m, ns, count);
   if (rc != MP_OK) return rc;
-  // the prologue's x tiles share the member tiles' TMA map: 256-token sub-tiles
-  if (pro != nullptr && (c->fuse_off || p.n_tok < mp::kMaxTok)) return kFallback;
+  // prologue units are 512-token tiles: they share the member tiles' stage
+  // layout and x map, so the member tiles must be 512-token tiles too
+  if (pro != nullptr && (c->fuse_off || p.n_tok != mp::kMaxTileTok)) return kFallback;
   if (pro != nullptr) {
     // Fuse when the prologue units, on the pairs that run one member tile
     // fewer, lengthen the launch by less than a separate pre-GEMM would take

@@ -31,27 +31,35 @@ namespace mp {
 
 namespace {
 
-#ifndef MP_PAIR_STAGES
-#define MP_PAIR_STAGES 3
-#endif
-constexpr int kStages = MP_PAIR_STAGES;
+constexpr int kMaxStages = 8;          // pipeline stages, at most (per-slot parity bit masks)
 constexpr int kSubTok = kMaxTok;       // tokens of one accumulator (MMA N): 256
-constexpr int kTileTok = kMaxTileTok;  // tokens of a pair tile: two accumulators
-constexpr uint32_t kXBytes = (kTileTok / 2) * 128;    // x: this CTA's token rows, 32 KB
 constexpr uint32_t kABytes = kWStageBytes;            // A: 128 feature rows bf16, 16 KB
 constexpr uint32_t kCodesBytes = kBlockN * kBlockK;   // codes: 8-bit at most, 8 KB
-constexpr uint32_t kStageBytes = kXBytes + kABytes + kCodesBytes;  // 56 KB
 constexpr uint32_t kEpiHalfBytes = kEpiRows * 128;    // [64 tokens][64 features] bf16, 8 KB
 constexpr uint32_t kEpiBufBytes = 2 * kEpiHalfBytes;  // both feature halves of a CTA
-constexpr uint32_t kStagesBytes = kStages * kStageBytes;
+constexpr uint32_t kStagesBytes = 168 * 1024;         // region of the pipeline stages
 constexpr uint32_t kTileBytes = kStagesBytes + 2 * kEpiBufBytes;
 
-// Stage s: [x (MMA B operand) | A (MMA A operand: a dense weight or LoRA B
-// tile by TMA, or the dequantized codes) | codes]; then two epilogue staging
-// buffers. Offsets from the 1024-byte-aligned tile base.
-__device__ __forceinline__ uint32_t off_x(int s) { return s * kStageBytes; }
-__device__ __forceinline__ uint32_t off_a(int s) { return s * kStageBytes + kXBytes; }
-__device__ __forceinline__ uint32_t off_c(int s) { return s * kStageBytes + kXBytes + kABytes; }
+// Stage s: [x (MMA B operand): this CTA's rows of the tile's token sub-tiles |
+// A (MMA A operand: a dense weight or LoRA B tile by TMA, or the dequantized
+// codes) | codes]; as many stages as fit in kStagesBytes for the launch's
+// token tile NT (3 at 512 tokens, 4 at 256, 5 at 128, 6 at 64: smaller tiles
+// finish a stage sooner, so they need more in flight to cover the copy
+// latency); then two epilogue staging buffers. Offsets from the
+// 1024-byte-aligned tile base. The kernel is instantiated per NT, so the
+// stage arithmetic is compile-time.
+template <int NT>
+struct Geo {
+  static constexpr int kSub = NT < kSubTok ? NT : kSubTok;
+  static constexpr uint32_t kX = (NT > kSubTok ? 2u : 1u) * (kSub / 2) * 128u;
+  static constexpr uint32_t kStage = kX + kABytes + kCodesBytes;
+  static constexpr int kStagesFit = static_cast<int>(kStagesBytes / kStage);
+  static constexpr int kStages = kStagesFit < kMaxStages ? kStagesFit : kMaxStages;
+  static_assert(kStage % 1024u == 0u, "stage alignment");
+  __device__ static __forceinline__ uint32_t off_x(int s) { return s * kStage; }
+  __device__ static __forceinline__ uint32_t off_a(int s) { return s * kStage + kX; }
+  __device__ static __forceinline__ uint32_t off_c(int s) { return s * kStage + kX + kABytes; }
+};
 __device__ __forceinline__ uint32_t off_epi(int b) { return kStagesBytes + b * kEpiBufBytes; }
 
 // warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 dequant, warps 10-13 epilogue
@@ -64,7 +72,7 @@ constexpr uint32_t kEpiBarrier = 1;  // named barrier of the epilogue warps
 constexpr uint32_t kPairSmemBytes = kTileBytes + 1024 + 512;
 static_assert(kPairSmemBytes <= 232448, "shared memory per CTA");
 static_assert(2 * kSubTok <= kTmemCols, "two accumulators in TMEM");
-static_assert(kStages <= 8, "per-slot parity bit masks");
+static_assert(kMaxStages <= 8, "per-slot parity bit masks");
 
 enum : uint32_t {
   kSiteEmpty = 0x1100u,
@@ -111,10 +119,10 @@ __device__ __forceinline__ PairSmem carve_pair(uint8_t* raw) {
   s.tiles = reinterpret_cast<uint8_t*>(base);
   uint64_t* bars = reinterpret_cast<uint64_t*>(s.tiles + kTileBytes);
   s.full = bars;
-  s.empty = bars + kStages;
-  s.cfull = bars + 2 * kStages;
-  s.afull = bars + 3 * kStages;
-  s.tfull = bars + 4 * kStages;
+  s.empty = bars + kMaxStages;
+  s.cfull = bars + 2 * kMaxStages;
+  s.afull = bars + 3 * kMaxStages;
+  s.tfull = bars + 4 * kMaxStages;
   s.tempty = s.tfull + 1;
   s.drain = s.tempty + 2;
   s.tmem_slot = reinterpret_cast<uint32_t*>(s.drain + 1);
@@ -292,8 +300,11 @@ __device__ bool wait_prologue(const ProjParams& p, const ProjMember& mb, const T
 }
 
 // Warp 0, one thread. Stage iteration `it` runs on across tiles.
+template <int NT>
 __device__ void pair_producer(const ProjParams& p, const PairSmem& sm, bool leader, int rank,
                               int base_kt) {
+  using G = Geo<NT>;
+  constexpr uint32_t stages = G::kStages;
   uint32_t it = 0;
   uint32_t cpar = 0;           // per slot: parity of the slot's next codes phase
   uint32_t pend_codes = 0;     // slots whose codes copy this thread has not seen consumed
@@ -310,10 +321,10 @@ __device__ void pair_producer(const ProjParams& p, const PairSmem& sm, bool lead
     const uint32_t xbytes_pair = 2u * static_cast<uint32_t>(t.n_sub) * sub_bytes;
     const uint32_t codes_bytes = static_cast<uint32_t>(kBlockN * kBlockK * mb.bits / 8);
     for (int kt = t.kt_begin; kt < t.kt_end; ++kt, ++it) {
-      const int s = static_cast<int>(it % kStages);
-      const uint32_t ph = (it / kStages) & 1u;
+      const int s = static_cast<int>(it % stages);
+      const uint32_t ph = (it / stages) & 1u;
       const uint32_t bit = 1u << s;
-      if (it >= kStages &&
+      if (it >= stages &&
           !mbar_wait(smem_u32(&sm.empty[s]), ph ^ 1u, sm.abort, kSiteEmpty | s, p.wait_limit_ns)) {
         aborted = true;
         break;
@@ -321,8 +332,8 @@ __device__ void pair_producer(const ProjParams& p, const PairSmem& sm, bool lead
       pend_codes &= ~bit;  // the MMA consumed the slot's previous copies
       pend_full &= ~bit;
       MP_TRACE_MARK(kTrProducer, static_cast<int>(it));
-      const uint32_t xb = smem_u32(sm.tiles) + off_x(s);
-      const uint32_t wb = smem_u32(sm.tiles) + off_a(s);
+      const uint32_t xb = smem_u32(sm.tiles) + G::off_x(s);
+      const uint32_t wb = smem_u32(sm.tiles) + G::off_a(s);
       const uint32_t full_local = smem_u32(&sm.full[s]);
       const uint32_t full_leader = mapa_shared(full_local, 0);
       const bool lora = kt >= base_kt;
@@ -336,7 +347,7 @@ __device__ void pair_producer(const ProjParams& p, const PairSmem& sm, bool lead
         if (leader) mbar_arrive_expect_tx(full_local, xbytes_pair);
         const uint32_t cbar = smem_u32(&sm.cfull[s]);
         mbar_arrive_expect_tx(cbar, codes_bytes);
-        tma_load_2d(smem_u32(sm.tiles) + off_c(s), &mb.tm_w, cbar, kt * kBlockK * mb.bits / 8,
+        tma_load_2d(smem_u32(sm.tiles) + G::off_c(s), &mb.tm_w, cbar, kt * kBlockK * mb.bits / 8,
                     t.f0);
         pend_codes |= bit;
         pend_codes_par = (pend_codes_par & ~bit) | (cpar & bit);
@@ -357,7 +368,7 @@ __device__ void pair_producer(const ProjParams& p, const PairSmem& sm, bool lead
     // have landed (the codes on its own barrier; on the leader, both CTAs'
     // pair copies on its full barriers), so none writes shared memory after
     // the CTA has left.
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < static_cast<int>(stages); ++s) {
       const uint32_t bit = 1u << s;
       const uint64_t t0 = global_timer_ns();
       if (pend_codes & bit) {
@@ -373,7 +384,10 @@ __device__ void pair_producer(const ProjParams& p, const PairSmem& sm, bool lead
 }
 
 // Warp 1 of the leader, one thread.
+template <int NT>
 __device__ void pair_mma(const ProjParams& p, const PairSmem& sm, uint32_t tmem, int base_kt) {
+  using G = Geo<NT>;
+  constexpr uint32_t stages = G::kStages;
   uint32_t it = 0;
   uint32_t apar = 0;  // per slot: parity of the slot's next dequant phase
   uint32_t tcount = 0;
@@ -388,8 +402,8 @@ __device__ void pair_mma(const ProjParams& p, const PairSmem& sm, uint32_t tmem,
     const uint32_t sub_bytes = static_cast<uint32_t>(t.half) * 128u;
     uint32_t acc = 0;
     for (int kt = t.kt_begin; kt < t.kt_end; ++kt, ++it) {
-      const int s = static_cast<int>(it % kStages);
-      const uint32_t ph = (it / kStages) & 1u;
+      const int s = static_cast<int>(it % stages);
+      const uint32_t ph = (it / stages) & 1u;
       if (!mbar_wait(smem_u32(&sm.full[s]), ph, sm.abort, kSiteFull | s, p.wait_limit_ns)) {
         aborted = true;
         break;
@@ -404,8 +418,8 @@ __device__ void pair_mma(const ProjParams& p, const PairSmem& sm, uint32_t tmem,
       }
       tc_fence_after();
       MP_TRACE_MARK(kTrMma, static_cast<int>(it));
-      const uint32_t xaddr = smem_u32(sm.tiles) + off_x(s);
-      const uint32_t waddr = smem_u32(sm.tiles) + off_a(s);
+      const uint32_t xaddr = smem_u32(sm.tiles) + G::off_x(s);
+      const uint32_t waddr = smem_u32(sm.tiles) + G::off_a(s);
 #pragma unroll
       for (int kk = 0; kk < kBlockK / 16; ++kk) {
         const uint64_t adesc = make_sdesc_sw128(waddr + kk * 32);
@@ -446,7 +460,10 @@ __device__ void pair_mma(const ProjParams& p, const PairSmem& sm, uint32_t tmem,
 // Warps 2-9. Warpgroup g converts columns [32g, 32g + 32) of every stage for
 // the 128 feature rows of this CTA: thread (warp % 4, lane) owns row r. The
 // codes tile is 64-byte (w8) or 32-byte (w4) swizzled by its TMA map.
+template <int NT>
 __device__ void pair_dequant(const ProjParams& p, const PairSmem& sm, int rank, int base_kt) {
+  using G = Geo<NT>;
+  constexpr uint32_t stages = G::kStages;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int g = (warp - kDeqWarp0) >> 2;  // K columns [32g, 32g + 32) of every stage
@@ -470,7 +487,7 @@ __device__ void pair_dequant(const ProjParams& p, const PairSmem& sm, int rank, 
     uint4 sbv = make_uint4(0, 0, 0, 0);
     int sb_group = -1;  // which 4 groups sbv holds
     for (int kt = t.kt_begin; kt < base_end; ++kt, ++it) {
-      const int s = static_cast<int>(it % kStages);
+      const int s = static_cast<int>(it % stages);
       if ((kt >> 2) != sb_group) {
         sbv = row_ok ? ld_global_nc_v4(sbrow + (kt & ~3)) : make_uint4(0, 0, 0, 0);
         sb_group = kt >> 2;
@@ -487,7 +504,7 @@ __device__ void pair_dequant(const ProjParams& p, const PairSmem& sm, int rank, 
       }
       cpar ^= 1u << s;
       if (threadIdx.x == 64) MP_TRACE_MARK(kTrDeqStart, static_cast<int>(it));
-      const uint32_t wb = smem_u32(sm.tiles) + off_c(s);
+      const uint32_t wb = smem_u32(sm.tiles) + G::off_c(s);
       uint32_t packed[16];
       if (mb.bits == 8) {
         const uint32_t sw = static_cast<uint32_t>((r >> 1) & 3);
@@ -512,7 +529,7 @@ __device__ void pair_dequant(const ProjParams& p, const PairSmem& sm, int rank, 
       // Row r of the stage's A tile, K columns [32g, 32g + 32): four 16-byte
       // chunks at the 128-byte-swizzled positions a TMA load would use, then a
       // proxy fence so the tensor core (async proxy) sees the generic stores.
-      const uint32_t arow = smem_u32(sm.tiles) + off_a(s) + r * 128u;
+      const uint32_t arow = smem_u32(sm.tiles) + G::off_a(s) + r * 128u;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const uint32_t chunk =
@@ -696,6 +713,7 @@ extern "C" int mp_trace_read(long long* host, int n) {
 }
 #endif
 
+template <int NT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     proj_pair_kernel(const __grid_constant__ ProjParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -707,7 +725,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   const int base_kt = (p.K + kBlockK - 1) / kBlockK;  // a ragged last tile (dense only) reads zeros
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kMaxStages; ++s) {
       mbar_init(smem_u32(&sm.full[s]), 1);
       mbar_init(smem_u32(&sm.empty[s]), 1);
       mbar_init(smem_u32(&sm.cfull[s]), 1);
@@ -741,11 +759,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   const uint32_t tmem = *sm.tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) pair_producer(p, sm, leader, rank, base_kt);
+    if (lane == 0) pair_producer<NT>(p, sm, leader, rank, base_kt);
   } else if (warp == 1) {
-    if (lane == 0 && leader) pair_mma(p, sm, tmem, base_kt);
+    if (lane == 0 && leader) pair_mma<NT>(p, sm, tmem, base_kt);
   } else if (warp < kEpiWarp0) {
-    pair_dequant(p, sm, rank, base_kt);
+    pair_dequant<NT>(p, sm, rank, base_kt);
   } else {
     pair_epilogue(p, sm, tmem, rank, base_kt);
   }
@@ -764,27 +782,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   if (threadIdx.x == 0 && *sm.abort != 0u) atomicOr(p.err, kErrTimeout);
 }
 
+int resident_pairs();
+
 // Token rows per pair tile for a launch of `pairs` feature pairs over m rows:
-// 512 (two accumulators: every dequantized stage feeds two MMAs) unless 256
-// finishes in fewer modelled waves, where a 512-row tile counts as 0.85 of two
-// 256-row tiles; below one full wave of 256-row tiles, the widest of 128 / 64
-// that still puts a CTA on every SM.
+// the tile with the fewest modelled cycles, rounds of resident pairs x cycles
+// per 64-wide K stage. A 512-token stage is bound by shared-memory bandwidth
+// (~1250 cycles); smaller tiles run more stages in flight and take ~760 /
+// ~570 / ~470 cycles at 256 / 128 / 64 tokens. Ties go to the wider tile.
 int pick_ntok_pair(int m, int pairs) {
 #ifdef MP_FORCE_NTOK
   (void)m;
   (void)pairs;
   return MP_FORCE_NTOK;
 #else
-  const long long slots = 74;  // pairs resident at once: one CTA per SM
-  auto waves = [&](int nt) {
-    return (pairs * static_cast<long long>((m + nt - 1) / nt) + slots - 1) / slots;
-  };
-  if (pairs * static_cast<long long>((m + 255) / 256) >= slots) {
-    return 0.85 * 2.0 * static_cast<double>(waves(512)) <= static_cast<double>(waves(256)) ? 512
-                                                                                           : 256;
+  const long long slots = resident_pairs();
+  const int tiles[4] = {512, 256, 128, 64};
+  const double stage[4] = {1250.0, 760.0, 570.0, 470.0};
+  int best = 512;
+  double best_cost = 1e300;
+  for (int i = 0; i < 4; ++i) {
+    const long long units = pairs * static_cast<long long>((m + tiles[i] - 1) / tiles[i]);
+    const double cost = static_cast<double>((units + slots - 1) / slots) * stage[i];
+    if (cost < best_cost * 0.999) {
+      best_cost = cost;
+      best = tiles[i];
+    }
   }
-  if (pairs * static_cast<long long>((m + 127) / 128) >= slots) return 128;
-  return 64;
+  return best;
 #endif
 }
 
@@ -880,8 +904,15 @@ namespace {
 bool g_configured[64] = {};
 int g_max_pairs[64] = {};
 
-// Opts the kernel in to its shared memory and finds the CTA pairs resident at
-// once (one CTA per SM), which the persistent grid fills; once per device.
+template <int NT>
+cudaError_t opt_in_smem() {
+  return cudaFuncSetAttribute(proj_pair_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(kPairSmemBytes));
+}
+
+// Opts every instantiation in to its shared memory and finds the CTA pairs
+// resident at once (one CTA per SM, the same for every instantiation), which
+// the persistent grid fills; once per device.
 cudaError_t configure(int* dev_out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -889,15 +920,15 @@ cudaError_t configure(int* dev_out) {
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   *dev_out = dev;
   if (g_configured[dev]) return cudaSuccess;
-  e = cudaFuncSetAttribute(proj_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(kPairSmemBytes));
-  if (e != cudaSuccess) return e;
+  for (cudaError_t r : {opt_in_smem<512>(), opt_in_smem<256>(), opt_in_smem<128>(),
+                        opt_in_smem<64>()})
+    if (r != cudaSuccess) return r;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2, 1, 1);
   cfg.blockDim = dim3(kPairThreads, 1, 1);
   cfg.dynamicSmemBytes = kPairSmemBytes;
   int clusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&clusters, proj_pair_kernel, &cfg) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveClusters(&clusters, proj_pair_kernel<512>, &cfg) != cudaSuccess ||
       clusters <= 0) {
     (void)cudaGetLastError();
     int sms = 0;
@@ -907,6 +938,28 @@ cudaError_t configure(int* dev_out) {
   g_max_pairs[dev] = clusters;
   g_configured[dev] = true;
   return cudaSuccess;
+}
+
+template <int NT>
+cudaError_t launch_nt(const ProjParams& q, int pairs, bool cooperative, cudaStream_t stream) {
+  if (cooperative) {
+    // Fused prologue: member tiles wait on prologue units of other pairs, so
+    // every pair must be resident at once: a cooperative launch of exactly
+    // the resident pair count (refused, with nothing run, if it cannot be).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(kPairThreads, 1, 1);
+    cfg.dynamicSmemBytes = kPairSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, proj_pair_kernel<NT>, q);
+  }
+  proj_pair_kernel<NT><<<dim3(2 * pairs, 1, 1), kPairThreads, kPairSmemBytes, stream>>>(q);
+  return cudaGetLastError();
 }
 
 }  // namespace
@@ -921,29 +974,20 @@ cudaError_t launch_proj_pair(const ProjParams& p, cudaStream_t stream) {
   int dev = 0;
   cudaError_t e = configure(&dev);
   if (e != cudaSuccess) return e;
-  int* max_pairs = g_max_pairs;
   ProjParams q = p;
   q.n_ttiles = (p.M + p.n_tok - 1) / p.n_tok;
   q.n_tiles = q.n_pairs * q.n_ttiles * (p.ksplit > 1 ? p.ksplit : 1);
-  if (q.n_pre > 0) {
-    // Fused prologue: member tiles wait on prologue units of other pairs, so
-    // every pair must be resident at once: a cooperative launch of exactly
-    // the resident pair count (refused, with nothing run, if it cannot be).
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * max_pairs[dev], 1, 1);
-    cfg.blockDim = dim3(kPairThreads, 1, 1);
-    cfg.dynamicSmemBytes = kPairSmemBytes;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, proj_pair_kernel, q);
+  const bool coop = q.n_pre > 0;
+  if (coop && p.n_tok != kMaxTileTok) return cudaErrorInvalidValue;  // prologue units need NT 512
+  const int pairs = coop ? g_max_pairs[dev]
+                         : (q.n_tiles < g_max_pairs[dev] ? q.n_tiles : g_max_pairs[dev]);
+  switch (p.n_tok) {
+    case 512: return launch_nt<512>(q, pairs, coop, stream);
+    case 256: return launch_nt<256>(q, pairs, coop, stream);
+    case 128: return launch_nt<128>(q, pairs, coop, stream);
+    case 64: return launch_nt<64>(q, pairs, coop, stream);
+    default: return cudaErrorInvalidValue;
   }
-  const int pairs = q.n_tiles < max_pairs[dev] ? q.n_tiles : max_pairs[dev];
-  proj_pair_kernel<<<dim3(2 * pairs, 1, 1), kPairThreads, kPairSmemBytes, stream>>>(q);
-  return cudaGetLastError();
 }
 
 }  // namespace mp
