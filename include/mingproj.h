@@ -167,6 +167,15 @@ int mp_linear_shared(mp_ctx* ctx, const mp_weight* const* ws, void* const* ys,
                      const int64_t* ldys, int count, const void* x, int64_t ldx, int m,
                      void* stream);
 
+/* The FFN gate and up projections with the SwiGLU in the epilogue, one launch:
+ *   h[m, n] = bf16(g / (1 + exp(-g)) * u),  g = bf16(lin(x, w1)), u = bf16(lin(x, w3))
+ * each lin with its live LoRA slots (one rank-space pass over x for both).
+ * w1 and w3 share n, k, bits and quant mode; h is 16-byte aligned, ldh >= n
+ * and a multiple of 8. Replaces: the w1 and w3 lin calls and swiglu of
+ * gpu_ff (src/ming-dit.cc:2155-2157; swiglu at src/metal/ming_ops.metal:95-112). */
+int mp_linear_swiglu(mp_ctx* ctx, const mp_weight* w1, const mp_weight* w3, const void* x,
+                     int64_t ldx, void* h, int64_t ldh, int m, void* stream);
+
 /* ---- modulation -------------------------------------------------------- */
 
 /* The adaLN Linears of `n_blocks` modulated blocks, prepared for one

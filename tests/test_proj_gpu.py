@@ -355,3 +355,29 @@ def test_512_token_tiles_ragged_tail(ctx, bits, m):
     assert np.all(np.isfinite(got))
     err = O.rel_l2(got, ref)
     assert err <= TOL, f"rel-L2 {err:.3e} (bits {bits}, m {m})"
+
+
+def test_shared_stack_cache_follows_reuploaded_weights(ctx):
+    """Weights freed and uploaded again (possibly at the same host addresses)
+    with other adapters never reuse the stacked factors cached for the first
+    ones: each shared call matches the oracle."""
+    rng = np.random.default_rng(91)
+    m, n, k = 260, 256, 256
+    x = _x(rng, m, k)
+    xd = _to_dev(x)
+    for rep in range(4):
+        pws = [P.synthetic_dense(rng, n, k, std=0.05) for _ in range(2)]
+        ws = [_upload(ctx, p) for p in pws]
+        slots = []
+        for j, w in enumerate(ws):
+            a, b = P.synthetic_lora(rng, n, k, 16, b_std=0.05)
+            w.bind(j, a, b)
+            slots.append([(a, b, 1.0)])
+        ys = ctx.linear_shared(ws, xd)
+        ctx.sync_check()
+        for j in range(2):
+            ref = O.projection(x, pws[j].data, None, None, n, k, 0, False, slots[j])
+            err = O.rel_l2(_host(ys[j]), ref)
+            assert err <= TOL, f"re-upload {rep}, weight {j}: rel-L2 {err:.3e}"
+        for w in ws:
+            w.free()

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <climits>
 #include <cstdarg>
 #include <cstdio>
@@ -74,6 +75,8 @@ struct mp_weight {
   uint32_t* sb = nullptr;  // [n, sb_stride] (bf16 scale | bf16 bias << 16)
   int sb_stride = 0;
   CUtensorMap tm_w;
+  CUtensorMap tm_w64;      // the same rows with 64-row boxes (SwiGLU pairs), built on first use
+  bool has_w64 = false;
   int rank[mp::kMaxSlots] = {};
   uint16_t* la[mp::kMaxSlots] = {};  // [rank, k]
   uint16_t* lb[mp::kMaxSlots] = {};  // [n, rank]
@@ -96,6 +99,12 @@ struct SharedStack {
   size_t a_cap = 0;
   int rtot = 0;
   CUtensorMap tm_a;
+  // SwiGLU pairs: the two members' B stacks interleaved per 64 features,
+  // [B1 rows 64b.. | 0 ; 0 | B3 rows 64b..] over the ranks [T1 | T3]
+  std::vector<uint64_t> bc_versions;
+  uint16_t* bc = nullptr;
+  size_t bc_cap = 0;
+  CUtensorMap tm_bc;
 };
 
 }  // namespace
@@ -266,7 +275,10 @@ int ensure_stack(mp_ctx* c, mp_weight* w, uint32_t mask, cudaStream_t stream) {
   st.mask = mask;
   st.bind_version = w->bind_version;
   st.valid = true;
-  st.version += 1;
+  // process-wide, never repeated: a weight freed and another uploaded at the
+  // same address can never match a cached shared stack built from the first
+  static std::atomic<uint64_t> g_stack_version{0};
+  st.version = ++g_stack_version;
   return MP_OK;
 }
 
@@ -516,14 +528,26 @@ constexpr int kFallback = -1;  // fused launch not possible: run the pre-GEMM se
 // scratch (row stride t_ld). With `pro`, the launch computes that
 // intermediate itself (fused prologue, cooperative launch); it returns
 // kFallback, having launched nothing, when that is not possible here.
+// With `swi` (count 2: W1 and W3, ys[0] = h), ONE SwiGLU pair member is
+// built from both: h = bf16(silu(g) * u) of their bf16 outputs.
+struct SwiGluLaunch {
+  const CUtensorMap* tm_bc = nullptr;  // interleaved B stack (null without live slots)
+};
+
 int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
                        const int64_t* ldys, const Stack* const* sts, const int* t_cols, int t_ld,
                        int count, const void* x, int64_t ldx, int m, cudaStream_t stream,
-                       const Prologue* pro = nullptr) {
+                       const Prologue* pro = nullptr, const SwiGluLaunch* swi = nullptr) {
   ProjParams p;
   int ns[mp::kMaxMembers] = {0, 0, 0, 0};
   for (int i = 0; i < count; ++i) ns[i] = ws[i]->d.n;
-  int rc = begin_launch(c, &p, x, ldx, ws[0]->d.k, m, ns, count);
+  // a SwiGLU pair covers 128 output features per CTA pair: as a 2N-wide member
+  if (swi != nullptr) ns[0] = 2 * ws[0]->d.n;
+  const int members = swi != nullptr ? 1 : count;
+  // SwiGLU pairs run on 256- or 512-token tiles only (their kernel instantiations)
+  int n_tok = 0;
+  if (swi != nullptr) n_tok = std::max(mp::kMaxTok, mp::pick_ntok_pair(m, pairs_of(ns[0])));
+  int rc = begin_launch(c, &p, x, ldx, ws[0]->d.k, m, ns, members, n_tok);
   if (rc != MP_OK) return rc;
   // prologue units are 512-token tiles: they share the member tiles' stage
   // layout and x map, so the member tiles must be 512-token tiles too
@@ -541,6 +565,7 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
     int lora_kt = 0;
     for (int i = 0; i < count; ++i)
       if (sts[i] != nullptr) lora_kt = std::max(lora_kt, sts[i]->rpad / mp::kBlockK);
+    if (swi != nullptr) lora_kt = t_ld / mp::kBlockK;
     const double c_stage = (ws[0]->d.bits != 0 ? 1300.0 : 1150.0) * (p.n_tok > mp::kMaxTok ? 1.0 : 0.6);
     const double t_main = (base_kt + lora_kt) * c_stage + 6000.0;
     const double t_pre = base_kt * 1150.0 + 8000.0;
@@ -554,19 +579,38 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
                             1900.0;
     if (fused_extra >= separate) return kFallback;
   }
-  for (int i = 0; i < count; ++i) {
-    const mp_weight* w = ws[i];
+  if (swi != nullptr) {
+    const mp_weight* w1 = ws[0];
+    const mp_weight* w3 = ws[1];
     LoraTiles lt;
-    if (sts[i] != nullptr && sts[i]->rpad > 0) {
-      lt.rpad = sts[i]->rpad;
-      lt.tbase = c->scratch + t_cols[i];
+    if (swi->tm_bc != nullptr) {
+      lt.rpad = t_ld;  // [T1 | T3]: both members' ranks
+      lt.tbase = c->scratch;
       lt.t_ld = t_ld;
-      lt.tm_b = &sts[i]->tm_b;
+      lt.tm_b = swi->tm_bc;
     }
-    rc = fill_member(c, &p, i, w->tm_w, w->sb, w->sb_stride, w->d.n, w->d.bits, w->d.mode, ys[i],
-                     ldys[i], lt);
+    rc = fill_member(c, &p, 0, w1->tm_w64, w1->sb, w1->sb_stride, w1->d.n, w1->d.bits, w1->d.mode,
+                     ys[0], ldys[0], lt);
     if (rc != MP_OK) return rc;
-    p.mem[i].t_col = lt.rpad > 0 ? t_cols[i] : 0;
+    p.mem[0].swiglu = 1;
+    p.mem[0].tm_w3 = w3->tm_w64;
+    p.mem[0].sb3 = w3->sb;
+    p.mem[0].t_col = 0;
+  } else {
+    for (int i = 0; i < count; ++i) {
+      const mp_weight* w = ws[i];
+      LoraTiles lt;
+      if (sts[i] != nullptr && sts[i]->rpad > 0) {
+        lt.rpad = sts[i]->rpad;
+        lt.tbase = c->scratch + t_cols[i];
+        lt.t_ld = t_ld;
+        lt.tm_b = &sts[i]->tm_b;
+      }
+      rc = fill_member(c, &p, i, w->tm_w, w->sb, w->sb_stride, w->d.n, w->d.bits, w->d.mode,
+                       ys[i], ldys[i], lt);
+      if (rc != MP_OK) return rc;
+      p.mem[i].t_col = lt.rpad > 0 ? t_cols[i] : 0;
+    }
   }
   if (pro != nullptr) {
     p.pre_ttiles = (m + mp::kPreTok - 1) / mp::kPreTok;
@@ -601,6 +645,111 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
   }
   for (int i = 0; i < count; ++i)
     count_projection(c, ws[i], m, sts[i] != nullptr && sts[i]->rpad > 0 ? sts[i]->ranks : nullptr);
+  return MP_OK;
+}
+
+// The stacked rank-space A over the live slots of `count` weights sharing x
+// (built, or reused while no binding or live set changed), their column
+// offsets col[i] in the intermediate and the strengths' epilogue scale;
+// *out = nullptr and *rtot = 0 when no slot is live.
+int shared_stack(mp_ctx* c, const mp_weight* const* ws, int count, cudaStream_t s,
+                 mp::EpilogueScale* es, int* rtot_out, int* col, SharedStack** out) {
+  std::vector<uintptr_t> key;
+  std::vector<uint64_t> versions;
+  int rtot = 0;
+  std::memset(es, 0, sizeof(*es));
+  fill_scale(c, es);
+  const int k = ws[0]->d.k;
+  for (int i = 0; i < count; ++i) {
+    mp_weight* w = const_cast<mp_weight*>(ws[i]);
+    const uint32_t mask = live_mask(c, w);
+    key.push_back(reinterpret_cast<uintptr_t>(w));
+    col[i] = rtot;
+    if (mask != 0) {
+      int rc = ensure_stack(c, w, mask, s);
+      if (rc != MP_OK) return rc;
+      if (!add_ranges(es, w->stack, rtot)) return fail(c, MP_EINVAL, "too many slot ranges");
+      rtot += w->stack.rpad;
+      versions.push_back(w->stack.version);
+    } else {
+      versions.push_back(0);
+    }
+  }
+  *rtot_out = rtot;
+  *out = nullptr;
+  if (rtot == 0) return MP_OK;
+  SharedStack& sh = c->shared[key];
+  const int kp = ws[0]->kp;
+  if (sh.versions != versions || sh.rtot != rtot) {
+    int rc = ensure_buf(c, &sh.a, &sh.a_cap, static_cast<size_t>(rtot) * kp, s);
+    if (rc != MP_OK) return rc;
+    for (int i = 0; i < count; ++i) {
+      const mp_weight* w = ws[i];
+      if (live_mask(c, w) == 0) continue;
+      MP_CUDA(c, cudaMemcpyAsync(sh.a + static_cast<size_t>(col[i]) * kp, w->stack.a,
+                                 static_cast<size_t>(w->stack.rpad) * kp * 2,
+                                 cudaMemcpyDeviceToDevice, s));
+    }
+    if (!encode_2d(&sh.tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, sh.a, k, rtot,
+                   static_cast<uint64_t>(kp) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+      return fail(c, MP_ECUDA, "tensor map encode failed (shared LoRA stack)");
+    sh.versions = versions;
+    sh.rtot = rtot;
+  }
+  *out = &sh;
+  return MP_OK;
+}
+
+// The row-interleaved LoRA B stack of a SwiGLU pair: per 64-feature block b,
+// rows [128b, 128b + 64) hold W1's B rows 64b.. in the columns of W1's ranks
+// and rows [128b + 64, 128b + 128) W3's in the columns of W3's, zeros
+// elsewhere (a 64-row W1 half and a 64-row W3 half share one MMA).
+int ensure_bc(mp_ctx* c, SharedStack* sh, const mp_weight* w1, const mp_weight* w3,
+              const int* col, cudaStream_t s) {
+  if (sh->bc != nullptr && sh->bc_versions == sh->versions) return MP_OK;
+  const int n = w1->d.n, rtot = sh->rtot;
+  const int nblk = (n + 63) / 64;
+  const size_t rows = static_cast<size_t>(nblk) * 128;
+  int rc = ensure_buf(c, &sh->bc, &sh->bc_cap, rows * rtot, s);
+  if (rc != MP_OK) return rc;
+  MP_CUDA(c, cudaMemsetAsync(sh->bc, 0, rows * rtot * 2, s));
+  const mp_weight* pair[2] = {w1, w3};
+  for (int i = 0; i < 2; ++i) {
+    const mp_weight* w = pair[i];
+    if (live_mask(c, w) == 0) continue;
+    const int rp = w->stack.rpad;
+    for (int b = 0; b < nblk; ++b) {
+      const int nr = std::min(64, n - 64 * b);
+      MP_CUDA(c, cudaMemcpy2DAsync(sh->bc + (static_cast<size_t>(b) * 128 + 64 * i) * rtot + col[i],
+                                   static_cast<size_t>(rtot) * 2,
+                                   w->stack.b + static_cast<size_t>(b) * 64 * rp,
+                                   static_cast<size_t>(rp) * 2, static_cast<size_t>(rp) * 2, nr,
+                                   cudaMemcpyDeviceToDevice, s));
+    }
+  }
+  if (!encode_2d(&sh->tm_bc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, sh->bc, rtot, rows,
+                 static_cast<uint64_t>(rtot) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return fail(c, MP_ECUDA, "tensor map encode failed (SwiGLU LoRA B stack)");
+  sh->bc_versions = sh->versions;
+  return MP_OK;
+}
+
+// The weight's rows with 64-row boxes, for SwiGLU pairs (64 W1 + 64 W3 rows per CTA).
+int ensure_w64(mp_ctx* c, mp_weight* w) {
+  if (w->has_w64) return MP_OK;
+  const int n = w->d.n, k = w->d.k, bits = w->d.bits;
+  bool ok;
+  if (bits != 0) {
+    const uint64_t row_bytes = static_cast<uint64_t>(k) * bits / 8;
+    ok = encode_2d(&w->tm_w64, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->w, row_bytes, n, row_bytes,
+                   64 * bits / 8, 64,
+                   bits == 8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+  } else {
+    ok = encode_2d(&w->tm_w64, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w->w, k, n,
+                   static_cast<uint64_t>(w->kp) * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  if (!ok) return fail(c, MP_ECUDA, "tensor map encode failed (64-row weight boxes)");
+  w->has_w64 = true;
   return MP_OK;
 }
 
@@ -650,7 +799,10 @@ int mp_destroy(mp_ctx* c) {
   cudaFree(c->scratch);
   cudaFree(c->part);
   cudaFree(c->flags);
-  for (auto& kv : c->shared) cudaFree(kv.second.a);
+  for (auto& kv : c->shared) {
+    cudaFree(kv.second.a);
+    cudaFree(kv.second.bc);
+  }
   delete c;
   return MP_OK;
 }
@@ -767,6 +919,17 @@ int mp_weight_free(mp_ctx* c, mp_weight* w) {
   if (c == nullptr || w == nullptr) return MP_EINVAL;
   cudaSetDevice(c->device);
   cudaDeviceSynchronize();
+  // drop the shared stacks built over this weight
+  for (auto it = c->shared.begin(); it != c->shared.end();) {
+    const auto& key = it->first;
+    if (std::find(key.begin(), key.end(), reinterpret_cast<uintptr_t>(w)) != key.end()) {
+      cudaFree(it->second.a);
+      cudaFree(it->second.bc);
+      it = c->shared.erase(it);
+    } else {
+      ++it;
+    }
+  }
   cudaFree(w->w);
   cudaFree(w->sb);
   for (int i = 0; i < mp::kMaxSlots; ++i) {
@@ -930,63 +1093,75 @@ int mp_linear_shared(mp_ctx* c, const mp_weight* const* ws, void* const* ys, con
   rc = use_device(c);
   if (rc != MP_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  std::vector<uintptr_t> key;
-  std::vector<uint64_t> versions;
+  mp::EpilogueScale es;
   int rtot = 0;
   int col[4] = {0, 0, 0, 0};
-  mp::EpilogueScale es;
-  std::memset(&es, 0, sizeof(es));
-  fill_scale(c, &es);
-  for (int i = 0; i < count; ++i) {
-    mp_weight* w = const_cast<mp_weight*>(ws[i]);
-    const uint32_t mask = live_mask(c, w);
-    key.push_back(reinterpret_cast<uintptr_t>(w));
-    col[i] = rtot;
-    if (mask != 0) {
-      rc = ensure_stack(c, w, mask, s);
-      if (rc != MP_OK) return rc;
-      if (!add_ranges(&es, w->stack, rtot)) return fail(c, MP_EINVAL, "too many slot ranges");
-      rtot += w->stack.rpad;
-      versions.push_back(w->stack.version);
-    } else {
-      versions.push_back(0);
-    }
-  }
+  SharedStack* sh = nullptr;
+  rc = shared_stack(c, ws, count, s, &es, &rtot, col, &sh);
+  if (rc != MP_OK) return rc;
+  const Stack* sts[mp::kMaxMembers];
+  for (int i = 0; i < count; ++i) sts[i] = live_mask(c, ws[i]) != 0 ? &ws[i]->stack : nullptr;
   if (rtot > 0) {
-    SharedStack& sh = c->shared[key];
-    const int kp = ws[0]->kp;
-    if (sh.versions != versions || sh.rtot != rtot) {
-      rc = ensure_buf(c, &sh.a, &sh.a_cap, static_cast<size_t>(rtot) * kp, s);
-      if (rc != MP_OK) return rc;
-      for (int i = 0; i < count; ++i) {
-        const mp_weight* w = ws[i];
-        if (live_mask(c, w) == 0) continue;
-        MP_CUDA(c, cudaMemcpyAsync(sh.a + static_cast<size_t>(col[i]) * kp, w->stack.a,
-                                   static_cast<size_t>(w->stack.rpad) * kp * 2,
-                                   cudaMemcpyDeviceToDevice, s));
-      }
-      if (!encode_2d(&sh.tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, sh.a, k, rtot,
-                     static_cast<uint64_t>(kp) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
-        return fail(c, MP_ECUDA, "tensor map encode failed (shared LoRA stack)");
-      sh.versions = versions;
-      sh.rtot = rtot;
-    }
     rc = ensure_buf(c, &c->scratch, &c->scratch_cap, static_cast<size_t>(m) * rtot, s);
     if (rc != MP_OK) return rc;
-    const Stack* sts[mp::kMaxMembers];
-    for (int i = 0; i < count; ++i) sts[i] = live_mask(c, ws[i]) != 0 ? &ws[i]->stack : nullptr;
     Prologue pro;
-    pro.tm_a = &sh.tm_a;
+    pro.tm_a = &sh->tm_a;
     pro.rtot = rtot;
     pro.es = &es;
     rc = launch_projections(c, ws, ys, ldys, sts, col, rtot, count, x, ldx, m, s, &pro);
     if (rc != kFallback) return rc;
-    rc = launch_lora_down(c, sh.tm_a, rtot, es, x, ldx, k, m, s);
+    rc = launch_lora_down(c, sh->tm_a, rtot, es, x, ldx, k, m, s);
     if (rc != MP_OK) return rc;
   }
-  const Stack* sts[mp::kMaxMembers];
-  for (int i = 0; i < count; ++i) sts[i] = live_mask(c, ws[i]) != 0 ? &ws[i]->stack : nullptr;
   return launch_projections(c, ws, ys, ldys, sts, col, rtot, count, x, ldx, m, s);
+}
+
+int mp_linear_swiglu(mp_ctx* c, const mp_weight* w1, const mp_weight* w3, const void* x,
+                     int64_t ldx, void* h, int64_t ldh, int m, void* stream) {
+  if (c == nullptr || w1 == nullptr || w3 == nullptr) return MP_EINVAL;
+  if (w1->d.n != w3->d.n || w1->d.k != w3->d.k || w1->d.bits != w3->d.bits ||
+      w1->d.mode != w3->d.mode)
+    return fail(c, MP_EINVAL, "SwiGLU gate and up weights need the same shape and format");
+  const int n = w1->d.n, k = w1->d.k;
+  int rc = check_x(c, x, ldx, k, m);
+  if (rc != MP_OK) return rc;
+  rc = check_y(c, h, ldh, n);
+  if (rc != MP_OK) return rc;
+  rc = use_device(c);
+  if (rc != MP_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const mp_weight* ws[2] = {w1, w3};
+  for (const mp_weight* w : ws) {
+    rc = ensure_w64(c, const_cast<mp_weight*>(w));
+    if (rc != MP_OK) return rc;
+  }
+  mp::EpilogueScale es;
+  int rtot = 0;
+  int col[4] = {0, 0, 0, 0};
+  SharedStack* sh = nullptr;
+  rc = shared_stack(c, ws, 2, s, &es, &rtot, col, &sh);
+  if (rc != MP_OK) return rc;
+  void* ys[2] = {h, nullptr};
+  const int64_t lds[2] = {ldh, ldh};
+  const Stack* sts[mp::kMaxMembers] = {nullptr, nullptr, nullptr, nullptr};
+  for (int i = 0; i < 2; ++i) sts[i] = live_mask(c, ws[i]) != 0 ? &ws[i]->stack : nullptr;
+  SwiGluLaunch swi;
+  if (rtot > 0) {
+    rc = ensure_bc(c, sh, w1, w3, col, s);
+    if (rc != MP_OK) return rc;
+    swi.tm_bc = &sh->tm_bc;
+    rc = ensure_buf(c, &c->scratch, &c->scratch_cap, static_cast<size_t>(m) * rtot, s);
+    if (rc != MP_OK) return rc;
+    Prologue pro;
+    pro.tm_a = &sh->tm_a;
+    pro.rtot = rtot;
+    pro.es = &es;
+    rc = launch_projections(c, ws, ys, lds, sts, col, rtot, 2, x, ldx, m, s, &pro, &swi);
+    if (rc != kFallback) return rc;
+    rc = launch_lora_down(c, sh->tm_a, rtot, es, x, ldx, k, m, s);
+    if (rc != MP_OK) return rc;
+  }
+  return launch_projections(c, ws, ys, lds, sts, col, rtot, 2, x, ldx, m, s, nullptr, &swi);
 }
 
 int mp_modulation_create(mp_ctx* c, int n_blocks, const mp_weight* const* ada,

@@ -57,6 +57,15 @@ struct ProjMember {
   float code_offset;  // 32768 + the codes' zero point (128 for signed 8-bit codes, else 0)
   int32_t pair_begin;
   int32_t t_col;      // first column of this member's ranks in the rank-space intermediate
+  // SwiGLU pair (swiglu = 1): the member is h = silu(x·W1^T) ⊙ (x·W3^T) with
+  // N = the FFN width. Each CTA holds 64 rows of W1 (tm_w, sb) and the same
+  // 64 rows of W3 (tm_w3, sb3), both maps with 64-row boxes; a pair tile covers
+  // 128 output features; tm_b is the row-interleaved LoRA B stack
+  // [B1 rows 64b.. ‖ 0 ; 0 ‖ B3 rows 64b..] per 64-feature block b, over the
+  // ranks [T1 | T3]; tm_y is h.
+  int32_t swiglu;
+  CUtensorMap tm_w3;
+  const uint32_t* sb3;
 };
 
 struct ProjParams {

@@ -191,7 +191,10 @@ __device__ __forceinline__ Tile decode_tile(const ProjParams& p, int tile, int r
   int mi = 0;
   while (mi + 1 < p.n_members && pair >= p.mem[mi + 1].pair_begin) ++mi;
   t.mi = mi;
-  t.f0 = (pair - p.mem[mi].pair_begin) * (2 * kBlockN) + rank * kBlockN;
+  // a SwiGLU pair member covers 128 output features per pair (64 per CTA,
+  // each with its W1 and W3 rows), any other member 256 (128 per CTA)
+  const int per_cta = p.mem[mi].swiglu ? kBlockN / 2 : kBlockN;
+  t.f0 = (pair - p.mem[mi].pair_begin) * (2 * per_cta) + rank * per_cta;
   t.t0 = tt * p.n_tok;
   const int most = p.n_tok > kSubTok ? 2 : 1;
   t.sub = p.n_tok / most;
@@ -347,14 +350,28 @@ __device__ void pair_producer(const ProjParams& p, const PairSmem& sm, bool lead
         if (leader) mbar_arrive_expect_tx(full_local, xbytes_pair);
         const uint32_t cbar = smem_u32(&sm.cfull[s]);
         mbar_arrive_expect_tx(cbar, codes_bytes);
-        tma_load_2d(smem_u32(sm.tiles) + G::off_c(s), &mb.tm_w, cbar, kt * kBlockK * mb.bits / 8,
-                    t.f0);
+        const int ck = kt * kBlockK * mb.bits / 8;
+        if (mb.swiglu) {  // rows 0-63: W1, rows 64-127: W3, both at features f0..f0+63
+          tma_load_2d(smem_u32(sm.tiles) + G::off_c(s), &mb.tm_w, cbar, ck, t.f0);
+          tma_load_2d(smem_u32(sm.tiles) + G::off_c(s) + codes_bytes / 2, &mb.tm_w3, cbar, ck,
+                      t.f0);
+        } else {
+          tma_load_2d(smem_u32(sm.tiles) + G::off_c(s), &mb.tm_w, cbar, ck, t.f0);
+        }
         pend_codes |= bit;
         pend_codes_par = (pend_codes_par & ~bit) | (cpar & bit);
         cpar ^= bit;
       } else {
         if (leader) mbar_arrive_expect_tx(full_local, xbytes_pair + 2u * kWStageBytes);
-        tma_load_2d_pair(wb, lora ? &mb.tm_b : &mb.tm_w, full_leader, xk, t.f0);
+        if (lora) {
+          // SwiGLU: the interleaved B stack holds 128 rows per 64 features
+          tma_load_2d_pair(wb, &mb.tm_b, full_leader, xk, mb.swiglu ? 2 * t.f0 : t.f0);
+        } else if (mb.swiglu) {
+          tma_load_2d_pair(wb, &mb.tm_w, full_leader, xk, t.f0);
+          tma_load_2d_pair(wb + kWStageBytes / 2, &mb.tm_w3, full_leader, xk, t.f0);
+        } else {
+          tma_load_2d_pair(wb, &mb.tm_w, full_leader, xk, t.f0);
+        }
       }
       for (int j = 0; j < t.n_sub; ++j)
         tma_load_2d_pair(xb + j * sub_bytes, xmap, full_leader, xk,
@@ -481,9 +498,11 @@ __device__ void pair_dequant(const ProjParams& p, const PairSmem& sm, int rank, 
       it += static_cast<uint32_t>(t.kt_end - t.kt_begin);
       continue;
     }
-    const int n = t.f0 + r;
+    // SwiGLU pair: rows 0-63 are W1's features f0.., rows 64-127 W3's same features
+    const int n = mb.swiglu ? t.f0 + (r & 63) : t.f0 + r;
     const bool row_ok = n < mb.N;
-    const uint32_t* sbrow = mb.sb + static_cast<size_t>(row_ok ? n : 0) * mb.sb_stride;
+    const uint32_t* sbase = (mb.swiglu && r >= 64) ? mb.sb3 : mb.sb;
+    const uint32_t* sbrow = sbase + static_cast<size_t>(row_ok ? n : 0) * mb.sb_stride;
     uint4 sbv = make_uint4(0, 0, 0, 0);
     int sb_group = -1;  // which 4 groups sbv holds
     for (int kt = t.kt_begin; kt < base_end; ++kt, ++it) {
@@ -562,6 +581,81 @@ __device__ __forceinline__ void release_accumulator(const PairSmem& sm, int j) {
   if ((threadIdx.x & 31) == 0) mbar_arrive_remote(mapa_shared(smem_u32(&sm.tempty[j]), 0));
 }
 
+// One 64-token epilogue round of a SwiGLU pair member (TMEM lanes 0-63: W1's
+// features f0.., lanes 64-127: W3's same features). The W3 warps (q = 2, 3)
+// round their sums to bf16 (u) into an exchange tile [64 tokens][64 features];
+// the W1 warps (q = 0, 1) round theirs (g) and store bf16(g / (1 + exp(-g)) *
+// u), the reference's swiglu on the bf16 gate and up values
+// (src/metal/ming_ops.metal:95-112), into the 128-byte-swizzled staging tile
+// that one thread stores with a single TMA box. The buffer in use alternates
+// by round; the issuer waited before the first barrier until the store that
+// last read it had done so.
+__device__ void swiglu_round(const ProjMember& mb, const PairSmem& sm, uint32_t tmem,
+                             uint32_t lane_base, const Tile& t, int j, int rr, int rounds,
+                             int tr0, uint32_t round, int q, int lane, bool issuer) {
+  const uint32_t buf = smem_u32(sm.tiles) + off_epi(static_cast<int>(round & 1u));
+  const uint32_t exch = buf + kEpiHalfBytes;  // u, bf16 [64 tokens][64 features], unswizzled
+  const uint32_t col0 = static_cast<uint32_t>(j * t.sub + rr * kEpiRows);
+  const uint32_t fcol = static_cast<uint32_t>(32 * (q & 1) + lane);  // feature within the 64
+  named_barrier(kEpiBarrier, kEpiThreads);
+  if (q >= 2) {
+    for (int c = 0; c < 2; ++c) {
+      uint32_t v[32];
+      MP_TMEM_LD_32X32B_X32(tmem + lane_base + col0 + static_cast<uint32_t>(c * 32), v);
+      MP_TMEM_WAIT_LD_REGS32(v);
+      if (rr + 1 == rounds && c == 1) release_accumulator(sm, j);
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        const uint32_t row = static_cast<uint32_t>(c * 32 + jj);
+        const float u = __uint_as_float(v[jj]);
+        st_shared_b16(exch + (row * 64u + fcol) * 2u,
+                      __bfloat16_as_ushort(__float2bfloat16_rn(u)));
+      }
+    }
+  }
+  named_barrier(kEpiBarrier, kEpiThreads);
+  if (q < 2) {
+    const bool odd = (lane & 1) != 0;
+    const uint32_t wi = static_cast<uint32_t>(16 * q + (lane >> 1));
+    const uint32_t chunk = wi >> 2, in_chunk = (wi & 3u) << 2;
+    for (int c = 0; c < 2; ++c) {
+      uint32_t v[32];
+      MP_TMEM_LD_32X32B_X32(tmem + lane_base + col0 + static_cast<uint32_t>(c * 32), v);
+      MP_TMEM_WAIT_LD_REGS32(v);
+      if (rr + 1 == rounds && c == 1) release_accumulator(sm, j);
+#pragma unroll
+      for (int jb = 0; jb < 32; jb += 8) {
+        // 8 tokens at a time: h for tokens jb..jb+7, then the pair-shuffled stores
+        float h[8];
+#pragma unroll
+        for (int d = 0; d < 8; ++d) {
+          const uint32_t row = static_cast<uint32_t>(c * 32 + jb + d);
+          const float g = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v[jb + d])));
+          uint16_t ub;
+          asm volatile("ld.shared.u16 %0, [%1];" : "=h"(ub) : "r"(exch + (row * 64u + fcol) * 2u));
+          h[d] = g / (1.0f + expf(-g)) * bf16_bits_to_f32(ub);
+        }
+#pragma unroll
+        for (int d = 0; d < 4; ++d) {
+          const float give = odd ? h[d] : h[d + 4];
+          const float got = __shfl_xor_sync(0xFFFFFFFFu, give, 1);
+          const uint32_t word = odd ? pack_bf16x2(got, h[d + 4]) : pack_bf16x2(h[d], got);
+          const uint32_t row = static_cast<uint32_t>(c * 32 + jb + d + (odd ? 4 : 0));
+          const uint32_t addr = buf + row * 128u + (((chunk ^ (row & 7u)) << 4) | in_chunk);
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(word) : "memory");
+        }
+      }
+    }
+  }
+  fence_proxy_async_shared();
+  named_barrier(kEpiBarrier, kEpiThreads);
+  if (issuer) {
+    tma_store_2d(&mb.tm_y, buf, t.f0, tr0);
+    tma_store_commit();
+    tma_store_wait_read_1();  // the other buffer is free again
+  }
+}
+
 // Warps 10-13 (TMEM lane quarter q = warp % 4: features 32q .. 32q + 31 of the
 // CTA's 128). Per accumulator, rounds of 64 tokens: two 32-column TMEM loads,
 // lane-pair shuffles into bf16x2 words (features 2i, 2i+1), a [64][64]-feature
@@ -569,6 +663,7 @@ __device__ __forceinline__ void release_accumulator(const PairSmem& sm, int j) {
 // one thread stores both halves with TMA bulk stores (they clip rows past M
 // and columns past N). Two staging buffers alternate. In split-K mode the fp32
 // sums go straight to the partial-sum array instead.
+template <bool SW>
 __device__ void pair_epilogue(const ProjParams& p, const PairSmem& sm, uint32_t tmem, int rank,
                               int base_kt) {
   const int warp = threadIdx.x >> 5;
@@ -630,6 +725,13 @@ __device__ void pair_epilogue(const ProjParams& p, const PairSmem& sm, uint32_t 
             }
           }
           continue;
+        }
+        if constexpr (SW) {
+          if (mb.swiglu) {
+            swiglu_round(mb, sm, tmem, lane_base, t, j, rr, rounds, tr0, round, q, lane, issuer);
+            ++round;
+            continue;
+          }
         }
         const uint32_t buf = smem_u32(sm.tiles) + off_epi(static_cast<int>(round & 1u));
         // the stores that last read this buffer have finished reading (issuer waited)
@@ -713,7 +815,7 @@ extern "C" int mp_trace_read(long long* host, int n) {
 }
 #endif
 
-template <int NT>
+template <int NT, bool SW>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     proj_pair_kernel(const __grid_constant__ ProjParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -765,7 +867,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   } else if (warp < kEpiWarp0) {
     pair_dequant<NT>(p, sm, rank, base_kt);
   } else {
-    pair_epilogue(p, sm, tmem, rank, base_kt);
+    pair_epilogue<SW>(p, sm, tmem, rank, base_kt);
   }
 
   if (*sm.abort != 0u) {
@@ -904,9 +1006,10 @@ namespace {
 bool g_configured[64] = {};
 int g_max_pairs[64] = {};
 
-template <int NT>
+template <int NT, bool SW>
 cudaError_t opt_in_smem() {
-  return cudaFuncSetAttribute(proj_pair_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  return cudaFuncSetAttribute(proj_pair_kernel<NT, SW>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(kPairSmemBytes));
 }
 
@@ -920,15 +1023,17 @@ cudaError_t configure(int* dev_out) {
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   *dev_out = dev;
   if (g_configured[dev]) return cudaSuccess;
-  for (cudaError_t r : {opt_in_smem<512>(), opt_in_smem<256>(), opt_in_smem<128>(),
-                        opt_in_smem<64>()})
+  for (cudaError_t r : {opt_in_smem<512, false>(), opt_in_smem<256, false>(),
+                        opt_in_smem<128, false>(), opt_in_smem<64, false>(),
+                        opt_in_smem<512, true>(), opt_in_smem<256, true>()})
     if (r != cudaSuccess) return r;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2, 1, 1);
   cfg.blockDim = dim3(kPairThreads, 1, 1);
   cfg.dynamicSmemBytes = kPairSmemBytes;
   int clusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&clusters, proj_pair_kernel<512>, &cfg) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveClusters(&clusters, proj_pair_kernel<512, false>, &cfg) !=
+          cudaSuccess ||
       clusters <= 0) {
     (void)cudaGetLastError();
     int sms = 0;
@@ -940,7 +1045,7 @@ cudaError_t configure(int* dev_out) {
   return cudaSuccess;
 }
 
-template <int NT>
+template <int NT, bool SW>
 cudaError_t launch_nt(const ProjParams& q, int pairs, bool cooperative, cudaStream_t stream) {
   if (cooperative) {
     // Fused prologue: member tiles wait on prologue units of other pairs, so
@@ -956,9 +1061,9 @@ cudaError_t launch_nt(const ProjParams& q, int pairs, bool cooperative, cudaStre
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, proj_pair_kernel<NT>, q);
+    return cudaLaunchKernelEx(&cfg, proj_pair_kernel<NT, SW>, q);
   }
-  proj_pair_kernel<NT><<<dim3(2 * pairs, 1, 1), kPairThreads, kPairSmemBytes, stream>>>(q);
+  proj_pair_kernel<NT, SW><<<dim3(2 * pairs, 1, 1), kPairThreads, kPairSmemBytes, stream>>>(q);
   return cudaGetLastError();
 }
 
@@ -981,11 +1086,20 @@ cudaError_t launch_proj_pair(const ProjParams& p, cudaStream_t stream) {
   if (coop && p.n_tok != kMaxTileTok) return cudaErrorInvalidValue;  // prologue units need NT 512
   const int pairs = coop ? g_max_pairs[dev]
                          : (q.n_tiles < g_max_pairs[dev] ? q.n_tiles : g_max_pairs[dev]);
+  bool swiglu = false;
+  for (int i = 0; i < p.n_members; ++i) swiglu = swiglu || p.mem[i].swiglu != 0;
+  if (swiglu) {  // SwiGLU pair launches: 512- or 256-token tiles
+    switch (p.n_tok) {
+      case 512: return launch_nt<512, true>(q, pairs, coop, stream);
+      case 256: return launch_nt<256, true>(q, pairs, coop, stream);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (p.n_tok) {
-    case 512: return launch_nt<512>(q, pairs, coop, stream);
-    case 256: return launch_nt<256>(q, pairs, coop, stream);
-    case 128: return launch_nt<128>(q, pairs, coop, stream);
-    case 64: return launch_nt<64>(q, pairs, coop, stream);
+    case 512: return launch_nt<512, false>(q, pairs, coop, stream);
+    case 256: return launch_nt<256, false>(q, pairs, coop, stream);
+    case 128: return launch_nt<128, false>(q, pairs, coop, stream);
+    case 64: return launch_nt<64, false>(q, pairs, coop, stream);
     default: return cudaErrorInvalidValue;
   }
 }

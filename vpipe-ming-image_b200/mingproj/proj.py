@@ -242,6 +242,18 @@ class Context:
                                               _stream_handle(stream)))
         return outs
 
+    def linear_swiglu(self, w1: Weight, w3: Weight, x: torch.Tensor,
+                      out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """h = bf16(silu(g) * u) with g = bf16(x W1^T + LoRA), u = bf16(x W3^T + LoRA):
+        the FFN gate/up pair and its SwiGLU in one launch."""
+        m = x.shape[0]
+        if out is None:
+            out = _alloc_out(m, w1.n, x.device)
+        self._check(self.lib.mp_linear_swiglu(self.h, w1.handle, w3.handle, _ptr(x), x.stride(0),
+                                              _ptr(out), out.stride(0), m,
+                                              _stream_handle(stream)))
+        return out
+
     def linear_lora_static(self, w: Weight, x: torch.Tensor, a: torch.Tensor, b: torch.Tensor,
                            strength: float, out: torch.Tensor | None = None,
                            stream=None) -> torch.Tensor:
