@@ -582,69 +582,72 @@ __device__ __forceinline__ void release_accumulator(const PairSmem& sm, int j) {
 }
 
 // One 64-token epilogue round of a SwiGLU pair member (TMEM lanes 0-63: W1's
-// features f0.., lanes 64-127: W3's same features). The W3 warps (q = 2, 3)
-// round their sums to bf16 (u) into an exchange tile [64 tokens][64 features];
-// the W1 warps (q = 0, 1) round theirs (g) and store bf16(g / (1 + exp(-g)) *
-// u), the reference's swiglu on the bf16 gate and up values
+// features f0.., lanes 64-127: W3's same features). Both halves round their
+// sums to bf16 (g from W1, u from W3) and hand the other half the 32 tokens
+// it finishes: the W1 warps (q = 0, 1) compute tokens 0-31 of the round, the
+// W3 warps (q = 2, 3) tokens 32-63, each h = bf16(g / (1 + exp(-g)) * u), the
+// reference's swiglu on the bf16 gate and up values
 // (src/metal/ming_ops.metal:95-112), into the 128-byte-swizzled staging tile
-// that one thread stores with a single TMA box. The buffer in use alternates
-// by round; the issuer waited before the first barrier until the store that
-// last read it had done so.
+// that one thread stores with a single TMA box. Buffer: staging 8 KB, then
+// the exchanged u (tokens 0-31) and g (tokens 32-63), bf16 [32][64] each. The
+// buffer in use alternates by round; the issuer waited before the first
+// barrier until the store that last read it had done so.
 __device__ void swiglu_round(const ProjMember& mb, const PairSmem& sm, uint32_t tmem,
                              uint32_t lane_base, const Tile& t, int j, int rr, int rounds,
                              int tr0, uint32_t round, int q, int lane, bool issuer) {
   const uint32_t buf = smem_u32(sm.tiles) + off_epi(static_cast<int>(round & 1u));
-  const uint32_t exch = buf + kEpiHalfBytes;  // u, bf16 [64 tokens][64 features], unswizzled
+  const uint32_t exch_u = buf + kEpiHalfBytes;         // u of tokens 0-31 (from the W3 half)
+  const uint32_t exch_g = exch_u + kEpiHalfBytes / 2;  // g of tokens 32-63 (from the W1 half)
   const uint32_t col0 = static_cast<uint32_t>(j * t.sub + rr * kEpiRows);
   const uint32_t fcol = static_cast<uint32_t>(32 * (q & 1) + lane);  // feature within the 64
+  const bool gate = q < 2;       // this warp holds W1's sums (g), else W3's (u)
+  const int mine = gate ? 0 : 1;  // the 32-token chunk this warp finishes
   named_barrier(kEpiBarrier, kEpiThreads);
-  if (q >= 2) {
-    for (int c = 0; c < 2; ++c) {
-      uint32_t v[32];
-      MP_TMEM_LD_32X32B_X32(tmem + lane_base + col0 + static_cast<uint32_t>(c * 32), v);
-      MP_TMEM_WAIT_LD_REGS32(v);
-      if (rr + 1 == rounds && c == 1) release_accumulator(sm, j);
+  uint32_t v[32];
+  // 1. the chunk the other half finishes: round to bf16 and hand it over
+  MP_TMEM_LD_32X32B_X32(tmem + lane_base + col0 + static_cast<uint32_t>((1 - mine) * 32), v);
+  MP_TMEM_WAIT_LD_REGS32(v);
+  {
+    const uint32_t dst = gate ? exch_g : exch_u;
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const uint32_t row = static_cast<uint32_t>(c * 32 + jj);
-        const float u = __uint_as_float(v[jj]);
-        st_shared_b16(exch + (row * 64u + fcol) * 2u,
-                      __bfloat16_as_ushort(__float2bfloat16_rn(u)));
-      }
-    }
+    for (int jj = 0; jj < 32; ++jj)
+      st_shared_b16(dst + (static_cast<uint32_t>(jj) * 64u + fcol) * 2u,
+                    __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[jj]))));
   }
+  // 2. this warp's own chunk (the accumulator is read out after this load)
+  MP_TMEM_LD_32X32B_X32(tmem + lane_base + col0 + static_cast<uint32_t>(mine * 32), v);
+  MP_TMEM_WAIT_LD_REGS32(v);
+  if (rr + 1 == rounds) release_accumulator(sm, j);
   named_barrier(kEpiBarrier, kEpiThreads);
-  if (q < 2) {
-    const bool odd = (lane & 1) != 0;
-    const uint32_t wi = static_cast<uint32_t>(16 * q + (lane >> 1));
-    const uint32_t chunk = wi >> 2, in_chunk = (wi & 3u) << 2;
-    for (int c = 0; c < 2; ++c) {
-      uint32_t v[32];
-      MP_TMEM_LD_32X32B_X32(tmem + lane_base + col0 + static_cast<uint32_t>(c * 32), v);
-      MP_TMEM_WAIT_LD_REGS32(v);
-      if (rr + 1 == rounds && c == 1) release_accumulator(sm, j);
+  const bool odd = (lane & 1) != 0;
+  const uint32_t wi = static_cast<uint32_t>(16 * (q & 1) + (lane >> 1));
+  const uint32_t chunk = wi >> 2, in_chunk = (wi & 3u) << 2;
+  const uint32_t src = gate ? exch_u : exch_g;
 #pragma unroll
-      for (int jb = 0; jb < 32; jb += 8) {
-        // 8 tokens at a time: h for tokens jb..jb+7, then the pair-shuffled stores
-        float h[8];
+  for (int jb = 0; jb < 32; jb += 8) {
+    // 8 tokens at a time: h for tokens jb..jb+7 of this warp's chunk, then
+    // the pair-shuffled stores (lanes 2i, 2i+1 hold features 2i, 2i+1)
+    float h[8];
 #pragma unroll
-        for (int d = 0; d < 8; ++d) {
-          const uint32_t row = static_cast<uint32_t>(c * 32 + jb + d);
-          const float g = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v[jb + d])));
-          uint16_t ub;
-          asm volatile("ld.shared.u16 %0, [%1];" : "=h"(ub) : "r"(exch + (row * 64u + fcol) * 2u));
-          h[d] = g / (1.0f + expf(-g)) * bf16_bits_to_f32(ub);
-        }
+    for (int d = 0; d < 8; ++d) {
+      uint16_t ob;
+      asm volatile("ld.shared.u16 %0, [%1];"
+                   : "=h"(ob)
+                   : "r"(src + (static_cast<uint32_t>(jb + d) * 64u + fcol) * 2u));
+      const float own = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v[jb + d])));
+      const float other = bf16_bits_to_f32(ob);
+      const float g = gate ? own : other;
+      const float u = gate ? other : own;
+      h[d] = __fdividef(g, 1.0f + __expf(-g)) * u;
+    }
 #pragma unroll
-        for (int d = 0; d < 4; ++d) {
-          const float give = odd ? h[d] : h[d + 4];
-          const float got = __shfl_xor_sync(0xFFFFFFFFu, give, 1);
-          const uint32_t word = odd ? pack_bf16x2(got, h[d + 4]) : pack_bf16x2(h[d], got);
-          const uint32_t row = static_cast<uint32_t>(c * 32 + jb + d + (odd ? 4 : 0));
-          const uint32_t addr = buf + row * 128u + (((chunk ^ (row & 7u)) << 4) | in_chunk);
-          asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(word) : "memory");
-        }
-      }
+    for (int d = 0; d < 4; ++d) {
+      const float give = odd ? h[d] : h[d + 4];
+      const float got = __shfl_xor_sync(0xFFFFFFFFu, give, 1);
+      const uint32_t word = odd ? pack_bf16x2(got, h[d + 4]) : pack_bf16x2(h[d], got);
+      const uint32_t row = static_cast<uint32_t>(mine * 32 + jb + d + (odd ? 4 : 0));
+      const uint32_t addr = buf + row * 128u + (((chunk ^ (row & 7u)) << 4) | in_chunk);
+      asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(word) : "memory");
     }
   }
   fence_proxy_async_shared();
