@@ -190,10 +190,11 @@ class DitForward:
             x = (x.float() + o2).to(torch.bfloat16)
         gain3 = nw3[mod_idx, 0] if modulated else t[pre + "ffn_norm1.weight"]
         nrm = self._rms(x, gain3)
-        g, u = self.ctx.linear_shared([p["feed_forward.w1"], p["feed_forward.w3"]], nrm)
+        # gate and up projections with the SwiGLU in their epilogue (one launch):
+        # h = bf16(silu(g) * u) of the bf16 gate and up values, as gpu_ff computes it
         ld = (FF + 7) // 8 * 8
         h = torch.empty((R, ld), dtype=torch.bfloat16, device=x.device)
-        h[:, :FF] = (F.silu(g.float()) * u.float()).to(torch.bfloat16)
+        self.ctx.linear_swiglu(p["feed_forward.w1"], p["feed_forward.w3"], nrm, out=h[:, :FF])
         f = self.ctx.linear(p["feed_forward.w2"], h[:, :FF])
         f2 = self._rms(f, t[pre + "ffn_norm2.weight"]).float()
         if modulated:
