@@ -176,6 +176,22 @@ int mp_linear_shared(mp_ctx* ctx, const mp_weight* const* ws, void* const* ys,
 int mp_linear_swiglu(mp_ctx* ctx, const mp_weight* w1, const mp_weight* w3, const void* x,
                      int64_t ldx, void* h, int64_t ldh, int m, void* stream);
 
+/* `count` attention projections of the same input x (q, k, v) in one launch,
+ * each written HEAD-MAJOR: ys[i] is bf16 [n_i / 128][m][128] (16-byte
+ * aligned), head width 128, n_i a multiple of 128. For each i with
+ * norm_w[i] != NULL (q and k) every head row also gets, before the store,
+ *   z = bf16(y * rsqrt(mean(y^2) + eps) * norm_w[i][f])   (y = bf16 projection)
+ *   (out[2j], out[2j+1]) = bf16(z[2j] c - z[2j+1] s, z[2j] s + z[2j+1] c)
+ * with c = rope_cos[t][j], s = rope_sin[t][j] (f32 [m][64], row t = token row
+ * t of x; the caller offsets the tables to the first row). norm_w may be NULL
+ * (no member normed; then the tables may be NULL). Live LoRA slots as in
+ * mp_linear_shared. Replaces: the q/k/v lin calls, the per-head rms, tr_rope
+ * and the v transpose of run_block (src/ming-dit.cc:2078-2088; tr_rope at
+ * :1885-1894). */
+int mp_linear_heads(mp_ctx* ctx, const mp_weight* const* ws, void* const* ys, int count,
+                    const void* x, int64_t ldx, int m, const uint16_t* const* norm_w, float eps,
+                    const float* rope_cos, const float* rope_sin, void* stream);
+
 /* ---- modulation -------------------------------------------------------- */
 
 /* The adaLN Linears of `n_blocks` modulated blocks, prepared for one

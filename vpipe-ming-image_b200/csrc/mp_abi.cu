@@ -183,6 +183,22 @@ bool encode_y(CUtensorMap* m, const void* y, int64_t ldy, int n, int rows, int n
                    static_cast<uint32_t>(ntok), CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// Head-major output map of an attention-head member: [n / 128][rows][128]
+// bf16, box = 64 features x 64 tokens of one head, 128-byte swizzle (the
+// same staging layout as encode_y's boxes).
+bool encode_heads_y(CUtensorMap* m, const void* y, int n, int rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  const uint64_t hd = mp::kHeadDim;
+  cuuint64_t dims[3] = {hd, static_cast<uint64_t>(rows), static_cast<uint64_t>(n) / hd};
+  cuuint64_t strides[2] = {hd * 2, static_cast<uint64_t>(rows) * hd * 2};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(mp::kEpiRows), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(y), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Token rows of one accumulator (MMA N) for a pair tile of `ntok` rows: the
 // TMA boxes of x, the rank-space intermediate and y are sized by it.
 int sub_tok(int ntok) { return std::min(ntok, mp::kMaxTok); }
@@ -534,19 +550,36 @@ struct SwiGluLaunch {
   const CUtensorMap* tm_bc = nullptr;  // interleaved B stack (null without live slots)
 };
 
+// With `hds`, every member is an attention-head member: ys[i] is its
+// head-major output [n / 128][m][128]; norm_w[i] (nullable) turns on the
+// head RMSNorm + rotary embedding for member i.
+struct HeadsLaunch {
+  const uint16_t* const* norm_w = nullptr;
+  float eps = 0.0f;
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
+};
+
 int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
                        const int64_t* ldys, const Stack* const* sts, const int* t_cols, int t_ld,
                        int count, const void* x, int64_t ldx, int m, cudaStream_t stream,
-                       const Prologue* pro = nullptr, const SwiGluLaunch* swi = nullptr) {
+                       const Prologue* pro = nullptr, const SwiGluLaunch* swi = nullptr,
+                       const HeadsLaunch* hds = nullptr) {
   ProjParams p;
   int ns[mp::kMaxMembers] = {0, 0, 0, 0};
   for (int i = 0; i < count; ++i) ns[i] = ws[i]->d.n;
   // a SwiGLU pair covers 128 output features per CTA pair: as a 2N-wide member
   if (swi != nullptr) ns[0] = 2 * ws[0]->d.n;
   const int members = swi != nullptr ? 1 : count;
-  // SwiGLU pairs run on 256- or 512-token tiles only (their kernel instantiations)
+  // SwiGLU pairs and attention-head launches run on 256- or 512-token tiles
+  // only (their kernel instantiations)
   int n_tok = 0;
   if (swi != nullptr) n_tok = std::max(mp::kMaxTok, mp::pick_ntok_pair(m, pairs_of(ns[0])));
+  if (hds != nullptr) {
+    int pairs = 0;
+    for (int i = 0; i < count; ++i) pairs += pairs_of(ns[i]);
+    n_tok = std::max(mp::kMaxTok, mp::pick_ntok_pair(m, pairs));
+  }
   int rc = begin_launch(c, &p, x, ldx, ws[0]->d.k, m, ns, members, n_tok);
   if (rc != MP_OK) return rc;
   // prologue units are 512-token tiles: they share the member tiles' stage
@@ -610,6 +643,17 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
                        ys[i], ldys[i], lt);
       if (rc != MP_OK) return rc;
       p.mem[i].t_col = lt.rpad > 0 ? t_cols[i] : 0;
+      if (hds != nullptr) {
+        mp::ProjMember& mb = p.mem[i];
+        if (!encode_heads_y(&mb.tm_y, ys[i], w->d.n, m))
+          return fail(c, MP_ECUDA, "tensor map encode failed (head-major output)");
+        mb.heads = 1;
+        mb.head_norm = hds->norm_w[i] != nullptr ? 1 : 0;
+        mb.norm_w = hds->norm_w[i];
+        mb.norm_eps = hds->eps;
+        mb.rope_cos = hds->rope_cos;
+        mb.rope_sin = hds->rope_sin;
+      }
     }
   }
   if (pro != nullptr) {
@@ -1114,6 +1158,70 @@ int mp_linear_shared(mp_ctx* c, const mp_weight* const* ws, void* const* ys, con
     if (rc != MP_OK) return rc;
   }
   return launch_projections(c, ws, ys, ldys, sts, col, rtot, count, x, ldx, m, s);
+}
+
+int mp_linear_heads(mp_ctx* c, const mp_weight* const* ws, void* const* ys, int count,
+                    const void* x, int64_t ldx, int m, const uint16_t* const* norm_w, float eps,
+                    const float* rope_cos, const float* rope_sin, void* stream) {
+  if (c == nullptr || ws == nullptr || ys == nullptr) return MP_EINVAL;
+  if (count <= 0 || count > mp::kMaxMembers)
+    return fail(c, MP_EINVAL, "count %d outside [1, %d]", count, mp::kMaxMembers);
+  const int k = ws[0] != nullptr ? ws[0]->d.k : 0;
+  bool any_norm = false;
+  for (int i = 0; i < count; ++i) {
+    if (ws[i] == nullptr || ws[i]->d.k != k)
+      return fail(c, MP_EINVAL, "head projections need the same k");
+    if (ws[i]->d.n % mp::kHeadDim != 0)
+      return fail(c, MP_EINVAL, "n = %d is not a whole number of %d-wide heads", ws[i]->d.n,
+                  mp::kHeadDim);
+    if (ys[i] == nullptr || reinterpret_cast<uintptr_t>(ys[i]) % 16 != 0)
+      return fail(c, MP_EINVAL, "head-major output %d is NULL or not 16-byte aligned", i);
+    any_norm = any_norm || (norm_w != nullptr && norm_w[i] != nullptr);
+  }
+  if (any_norm) {
+    if (rope_cos == nullptr || rope_sin == nullptr ||
+        reinterpret_cast<uintptr_t>(rope_cos) % 4 != 0 ||
+        reinterpret_cast<uintptr_t>(rope_sin) % 4 != 0)
+      return fail(c, MP_EINVAL, "the normed heads need 4-byte aligned rotary tables");
+    if (!(eps > 0.0f)) return fail(c, MP_EINVAL, "eps must be positive");
+  }
+  int rc = check_x(c, x, ldx, k, m);
+  if (rc != MP_OK) return rc;
+  rc = use_device(c);
+  if (rc != MP_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint16_t* nw[mp::kMaxMembers] = {nullptr, nullptr, nullptr, nullptr};
+  for (int i = 0; i < count; ++i) nw[i] = norm_w != nullptr ? norm_w[i] : nullptr;
+  HeadsLaunch hds;
+  hds.norm_w = nw;
+  hds.eps = eps;
+  hds.rope_cos = rope_cos;
+  hds.rope_sin = rope_sin;
+  int64_t lds[mp::kMaxMembers];
+  for (int i = 0; i < count; ++i) lds[i] = ws[i]->d.n;  // token-major stride, unused by the 3-D map
+  mp::EpilogueScale es;
+  int rtot = 0;
+  int col[4] = {0, 0, 0, 0};
+  SharedStack* sh = nullptr;
+  rc = shared_stack(c, ws, count, s, &es, &rtot, col, &sh);
+  if (rc != MP_OK) return rc;
+  const Stack* sts[mp::kMaxMembers] = {nullptr, nullptr, nullptr, nullptr};
+  for (int i = 0; i < count; ++i) sts[i] = live_mask(c, ws[i]) != 0 ? &ws[i]->stack : nullptr;
+  if (rtot > 0) {
+    rc = ensure_buf(c, &c->scratch, &c->scratch_cap, static_cast<size_t>(m) * rtot, s);
+    if (rc != MP_OK) return rc;
+    Prologue pro;
+    pro.tm_a = &sh->tm_a;
+    pro.rtot = rtot;
+    pro.es = &es;
+    rc = launch_projections(c, ws, ys, lds, sts, col, rtot, count, x, ldx, m, s, &pro, nullptr,
+                            &hds);
+    if (rc != kFallback) return rc;
+    rc = launch_lora_down(c, sh->tm_a, rtot, es, x, ldx, k, m, s);
+    if (rc != MP_OK) return rc;
+  }
+  return launch_projections(c, ws, ys, lds, sts, col, rtot, count, x, ldx, m, s, nullptr, nullptr,
+                            &hds);
 }
 
 int mp_linear_swiglu(mp_ctx* c, const mp_weight* w1, const mp_weight* w3, const void* x,

@@ -23,6 +23,7 @@ constexpr int kWStageBytes = kBlockN * 128;   // weight tile: codes or bf16
 constexpr int kTmemCols = 512;
 constexpr int kMaxMembers = 4;     // projections of one input in one launch (q/k/v, w1/w3)
 constexpr int kMaxSplits = 16;     // K splits of a split-K launch
+constexpr int kHeadDim = 128;      // attention head width (one CTA's features)
 
 // Device-side error word bits (OR-ed by kernels, read by mp_sync_check).
 constexpr uint32_t kErrTimeout = 1u;
@@ -66,6 +67,18 @@ struct ProjMember {
   int32_t swiglu;
   CUtensorMap tm_w3;
   const uint32_t* sb3;
+  // Attention-head member (heads = 1; N a multiple of kHeadDim): each CTA's
+  // 128 features are one head, and tm_y is the head-major output
+  // [N / kHeadDim][M][kHeadDim] bf16 (3-D map, box {64, kEpiRows, 1}). With
+  // head_norm = 1 the epilogue first applies the head's RMSNorm (gain
+  // norm_w[kHeadDim] bf16, norm_eps) and the interleaved-pair rotary
+  // embedding (rope_cos / rope_sin f32 [M][kHeadDim / 2], row = token row).
+  int32_t heads;
+  int32_t head_norm;
+  float norm_eps;
+  const uint16_t* norm_w;
+  const float* rope_cos;
+  const float* rope_sin;
 };
 
 struct ProjParams {

@@ -69,7 +69,8 @@ constexpr int kEpiWarp0 = 10;
 constexpr int kEpiThreads = 128;
 constexpr int kPairThreads = 32 * kEpiWarp0 + kEpiThreads;
 constexpr uint32_t kEpiBarrier = 1;  // named barrier of the epilogue warps
-constexpr uint32_t kPairSmemBytes = kTileBytes + 1024 + 512;
+constexpr uint32_t kRedBytes = 2 * 4 * 32 * 4;  // head RMSNorm partial sums [2][4 warps][32 tokens]
+constexpr uint32_t kPairSmemBytes = kTileBytes + 1024 + 512 + kRedBytes;
 static_assert(kPairSmemBytes <= 232448, "shared memory per CTA");
 static_assert(2 * kSubTok <= kTmemCols, "two accumulators in TMEM");
 static_assert(kMaxStages <= 8, "per-slot parity bit masks");
@@ -111,6 +112,7 @@ struct PairSmem {
   uint64_t* drain;   // leader: every MMA issued has completed
   uint32_t* tmem_slot;
   volatile uint32_t* abort;
+  float* red;        // head-norm partial sums of the epilogue warps
 };
 
 __device__ __forceinline__ PairSmem carve_pair(uint8_t* raw) {
@@ -127,6 +129,7 @@ __device__ __forceinline__ PairSmem carve_pair(uint8_t* raw) {
   s.drain = s.tempty + 2;
   s.tmem_slot = reinterpret_cast<uint32_t*>(s.drain + 1);
   s.abort = s.tmem_slot + 1;
+  s.red = reinterpret_cast<float*>(s.tiles + kTileBytes + 512);
   return s;
 }
 
@@ -659,6 +662,141 @@ __device__ void swiglu_round(const ProjMember& mb, const PairSmem& sm, uint32_t 
   }
 }
 
+// Epilogue variants, one kernel instantiation each (they differ in register
+// needs): plain projections, SwiGLU pairs, attention heads.
+enum : int { kEpiPlain = 0, kEpiSwiGlu = 1, kEpiHeads = 2 };
+
+// Sum over the warp's 32 lanes of y[i]^2, for all 32 i at once: a butterfly
+// that halves the values each lane carries at every step (31 shuffles) and
+// leaves lane l with the total of i = l. The squares are rounded before the
+// adds (no contraction), as an unfused square-then-sum computes them.
+__device__ __forceinline__ float lane_sums_of_squares(const float (&y)[32], int lane) {
+  float a[16];
+  {
+    const bool hi = (lane & 16) != 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float lo_sq = __fmul_rn(y[i], y[i]);
+      const float hi_sq = __fmul_rn(y[i + 16], y[i + 16]);
+      const float send = hi ? lo_sq : hi_sq;
+      a[i] = __fadd_rn(hi ? hi_sq : lo_sq, __shfl_xor_sync(0xFFFFFFFFu, send, 16));
+    }
+  }
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1) {
+    const bool hi = (lane & w) != 0;
+#pragma unroll
+    for (int i = 0; i < w; ++i) {
+      const float send = hi ? a[i] : a[i + w];
+      a[i] = __fadd_rn(hi ? a[i + w] : a[i], __shfl_xor_sync(0xFFFFFFFFu, send, w));
+    }
+  }
+  return a[0];
+}
+
+// One 64-token epilogue round of an attention-head member: the CTA's 128
+// features are head f0 / 128 of q, k or v, stored head-major ([heads][M][128],
+// the layout the attention reads; the reference transposes into it,
+// src/ming-dit.cc:2085-2088). For q and k (head_norm) each token's 128 values
+// first get the head's RMSNorm and the rotary embedding, with the roundings of
+// the unfused sequence (projection output, normed value, rotated value, each
+// rounded to bf16; the per-head rms of :2083-2084 and tr_rope of :1885-1894):
+//   y = bf16(acc);  z = bf16(y * rsqrt(sum(y^2) / 128 + eps) * gain[f])
+//   (out[2i], out[2i+1]) = bf16(z[2i] c - z[2i+1] s, z[2i] s + z[2i+1] c)
+// with c, s the tables' entries at (token row, i). A token's sum of squares:
+// the butterfly leaves each warp's partial in lane t, and the four warps'
+// partials meet in shared memory, added in warp order (the result never
+// depends on timing). `hc` counts the chunks normed so far (it alternates the
+// two partial-sum buffers).
+__device__ void head_round(const ProjParams& p, const ProjMember& mb, const PairSmem& sm,
+                           uint32_t tmem, uint32_t lane_base, const Tile& t, int j, int rr,
+                           int rounds, int tr0, uint32_t round, uint32_t& hc, int q, int lane,
+                           bool issuer, float gain) {
+  const bool odd = (lane & 1) != 0;
+  const int fl = q * 32 + lane;  // feature within the head
+  const uint32_t wi = static_cast<uint32_t>(16 * (q & 1) + (lane >> 1));
+  const uint32_t chunk = wi >> 2, in_chunk = (wi & 3u) << 2;
+  const uint32_t buf = smem_u32(sm.tiles) + off_epi(static_cast<int>(round & 1u));
+  const bool norm = mb.head_norm != 0;
+  // the stores that last read this buffer have finished reading (issuer waited)
+  named_barrier(kEpiBarrier, kEpiThreads);
+  const uint32_t stage = buf + static_cast<uint32_t>(q >> 1) * kEpiHalfBytes;
+  for (int c = 0; c < 2; ++c) {
+    const int tc = tr0 + c * 32;
+    // rotary factors of the 16 tokens this lane stores (even lane: tokens
+    // jb + d, odd lane: jb + d + 4), requested before the accumulator read
+    float cs[16], sn[16];
+    if (norm) {
+      const size_t pi = static_cast<size_t>(fl >> 1);
+#pragma unroll
+      for (int g = 0; g < 16; ++g) {
+        const int tok = min(tc + (g >> 2) * 8 + (g & 3) + (odd ? 4 : 0), p.M - 1);
+        cs[g] = __ldg(mb.rope_cos + static_cast<size_t>(tok) * (kHeadDim / 2) + pi);
+        sn[g] = __ldg(mb.rope_sin + static_cast<size_t>(tok) * (kHeadDim / 2) + pi);
+      }
+    }
+    uint32_t v[32];
+    MP_TMEM_LD_32X32B_X32(
+        tmem + lane_base + static_cast<uint32_t>(j * t.sub + rr * kEpiRows + c * 32), v);
+    MP_TMEM_WAIT_LD_REGS32(v);
+    if (rr + 1 == rounds && c == 1) release_accumulator(sm, j);
+    float y[32];
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj)
+      y[jj] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v[jj])));
+    if (norm) {
+      const float part = lane_sums_of_squares(y, lane);
+      float* red = sm.red + (hc & 1u) * (4 * 32);
+      red[q * 32 + lane] = part;
+      named_barrier(kEpiBarrier, kEpiThreads);
+      const float tot =
+          __fadd_rn(__fadd_rn(__fadd_rn(red[lane], red[32 + lane]), red[64 + lane]), red[96 + lane]);
+      const float r = rsqrtf(__fadd_rn(__fmul_rn(tot, 1.0f / kHeadDim), mb.norm_eps));
+      ++hc;
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        const float rj = __shfl_sync(0xFFFFFFFFu, r, jj);
+        y[jj] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(y[jj], rj), gain)));
+      }
+    }
+    // Lane pairs (features 2i, 2i+1) exchange the token the other one stores:
+    // the even lane stores token je, the odd lane token je + 4 (opposite bank
+    // halves of the swizzled rows), each with both features of the pair.
+#pragma unroll
+    for (int jb = 0; jb < 32; jb += 8) {
+#pragma unroll
+      for (int d = 0; d < 4; ++d) {
+        const int je = jb + d, jo = jb + d + 4;
+        const float got = __shfl_xor_sync(0xFFFFFFFFu, odd ? y[je] : y[jo], 1);
+        const float z0 = odd ? got : y[je];
+        const float z1 = odd ? y[jo] : got;
+        float o0 = z0, o1 = z1;
+        if (norm) {
+          const int g = (jb >> 3) * 4 + d;
+          o0 = __fsub_rn(__fmul_rn(z0, cs[g]), __fmul_rn(z1, sn[g]));
+          o1 = __fadd_rn(__fmul_rn(z0, sn[g]), __fmul_rn(z1, cs[g]));
+        }
+        const uint32_t word = pack_bf16x2(o0, o1);
+        const uint32_t row = static_cast<uint32_t>(c * 32 + (odd ? jo : je));
+        const uint32_t addr = stage + row * 128u + (((chunk ^ (row & 7u)) << 4) | in_chunk);
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(word) : "memory");
+      }
+    }
+  }
+  fence_proxy_async_shared();
+  named_barrier(kEpiBarrier, kEpiThreads);
+  if (issuer) {
+    // a CTA past the member's last head (an odd head count) stores nothing
+    if (t.f0 < mb.N) {
+      const int head = t.f0 / kHeadDim;
+      tma_store_3d(&mb.tm_y, buf, 0, tr0, head);
+      tma_store_3d(&mb.tm_y, buf + kEpiHalfBytes, 64, tr0, head);
+    }
+    tma_store_commit();
+    tma_store_wait_read_1();  // the other buffer is free again
+  }
+}
+
 // Warps 10-13 (TMEM lane quarter q = warp % 4: features 32q .. 32q + 31 of the
 // CTA's 128). Per accumulator, rounds of 64 tokens: two 32-column TMEM loads,
 // lane-pair shuffles into bf16x2 words (features 2i, 2i+1), a [64][64]-feature
@@ -666,7 +804,7 @@ __device__ void swiglu_round(const ProjMember& mb, const PairSmem& sm, uint32_t 
 // one thread stores both halves with TMA bulk stores (they clip rows past M
 // and columns past N). Two staging buffers alternate. In split-K mode the fp32
 // sums go straight to the partial-sum array instead.
-template <bool SW>
+template <int EPI>
 __device__ void pair_epilogue(const ProjParams& p, const PairSmem& sm, uint32_t tmem, int rank,
                               int base_kt) {
   const int warp = threadIdx.x >> 5;
@@ -682,6 +820,7 @@ __device__ void pair_epilogue(const ProjParams& p, const PairSmem& sm, uint32_t 
   const uint32_t chunk = wi >> 2, in_chunk = (wi & 3u) << 2;
   uint32_t tcount = 0;
   uint32_t round = 0;
+  uint32_t hc = 0;  // head-norm chunks (kEpiHeads)
   UnitIter units = units_begin(p);
   for (int unit = units_next(p, units); unit != kNoUnit; unit = units_next(p, units), ++tcount) {
     const Tile t = decode_unit(p, unit, rank, base_kt);
@@ -729,9 +868,18 @@ __device__ void pair_epilogue(const ProjParams& p, const PairSmem& sm, uint32_t 
           }
           continue;
         }
-        if constexpr (SW) {
+        if constexpr (EPI == kEpiSwiGlu) {
           if (mb.swiglu) {
             swiglu_round(mb, sm, tmem, lane_base, t, j, rr, rounds, tr0, round, q, lane, issuer);
+            ++round;
+            continue;
+          }
+        }
+        if constexpr (EPI == kEpiHeads) {
+          if (t.mi >= 0 && mb.heads) {
+            const float gain = mb.head_norm ? bf16_bits_to_f32(__ldg(mb.norm_w + fl)) : 1.0f;
+            head_round(p, mb, sm, tmem, lane_base, t, j, rr, rounds, tr0, round, hc, q, lane,
+                       issuer, gain);
             ++round;
             continue;
           }
@@ -818,7 +966,7 @@ extern "C" int mp_trace_read(long long* host, int n) {
 }
 #endif
 
-template <int NT, bool SW>
+template <int NT, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     proj_pair_kernel(const __grid_constant__ ProjParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -870,7 +1018,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   } else if (warp < kEpiWarp0) {
     pair_dequant<NT>(p, sm, rank, base_kt);
   } else {
-    pair_epilogue<SW>(p, sm, tmem, rank, base_kt);
+    pair_epilogue<EPI>(p, sm, tmem, rank, base_kt);
   }
 
   if (*sm.abort != 0u) {
@@ -1009,9 +1157,9 @@ namespace {
 bool g_configured[64] = {};
 int g_max_pairs[64] = {};
 
-template <int NT, bool SW>
+template <int NT, int EPI>
 cudaError_t opt_in_smem() {
-  return cudaFuncSetAttribute(proj_pair_kernel<NT, SW>,
+  return cudaFuncSetAttribute(proj_pair_kernel<NT, EPI>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(kPairSmemBytes));
 }
@@ -1026,16 +1174,17 @@ cudaError_t configure(int* dev_out) {
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   *dev_out = dev;
   if (g_configured[dev]) return cudaSuccess;
-  for (cudaError_t r : {opt_in_smem<512, false>(), opt_in_smem<256, false>(),
-                        opt_in_smem<128, false>(), opt_in_smem<64, false>(),
-                        opt_in_smem<512, true>(), opt_in_smem<256, true>()})
+  for (cudaError_t r : {opt_in_smem<512, kEpiPlain>(), opt_in_smem<256, kEpiPlain>(),
+                        opt_in_smem<128, kEpiPlain>(), opt_in_smem<64, kEpiPlain>(),
+                        opt_in_smem<512, kEpiSwiGlu>(), opt_in_smem<256, kEpiSwiGlu>(),
+                        opt_in_smem<512, kEpiHeads>(), opt_in_smem<256, kEpiHeads>()})
     if (r != cudaSuccess) return r;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2, 1, 1);
   cfg.blockDim = dim3(kPairThreads, 1, 1);
   cfg.dynamicSmemBytes = kPairSmemBytes;
   int clusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&clusters, proj_pair_kernel<512, false>, &cfg) !=
+  if (cudaOccupancyMaxActiveClusters(&clusters, proj_pair_kernel<512, kEpiPlain>, &cfg) !=
           cudaSuccess ||
       clusters <= 0) {
     (void)cudaGetLastError();
@@ -1048,7 +1197,7 @@ cudaError_t configure(int* dev_out) {
   return cudaSuccess;
 }
 
-template <int NT, bool SW>
+template <int NT, int EPI>
 cudaError_t launch_nt(const ProjParams& q, int pairs, bool cooperative, cudaStream_t stream) {
   if (cooperative) {
     // Fused prologue: member tiles wait on prologue units of other pairs, so
@@ -1064,9 +1213,9 @@ cudaError_t launch_nt(const ProjParams& q, int pairs, bool cooperative, cudaStre
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, proj_pair_kernel<NT, SW>, q);
+    return cudaLaunchKernelEx(&cfg, proj_pair_kernel<NT, EPI>, q);
   }
-  proj_pair_kernel<NT, SW><<<dim3(2 * pairs, 1, 1), kPairThreads, kPairSmemBytes, stream>>>(q);
+  proj_pair_kernel<NT, EPI><<<dim3(2 * pairs, 1, 1), kPairThreads, kPairSmemBytes, stream>>>(q);
   return cudaGetLastError();
 }
 
@@ -1089,20 +1238,31 @@ cudaError_t launch_proj_pair(const ProjParams& p, cudaStream_t stream) {
   if (coop && p.n_tok != kMaxTileTok) return cudaErrorInvalidValue;  // prologue units need NT 512
   const int pairs = coop ? g_max_pairs[dev]
                          : (q.n_tiles < g_max_pairs[dev] ? q.n_tiles : g_max_pairs[dev]);
-  bool swiglu = false;
-  for (int i = 0; i < p.n_members; ++i) swiglu = swiglu || p.mem[i].swiglu != 0;
+  bool swiglu = false, heads = false;
+  for (int i = 0; i < p.n_members; ++i) {
+    swiglu = swiglu || p.mem[i].swiglu != 0;
+    heads = heads || p.mem[i].heads != 0;
+  }
+  if (swiglu && heads) return cudaErrorInvalidValue;
   if (swiglu) {  // SwiGLU pair launches: 512- or 256-token tiles
     switch (p.n_tok) {
-      case 512: return launch_nt<512, true>(q, pairs, coop, stream);
-      case 256: return launch_nt<256, true>(q, pairs, coop, stream);
+      case 512: return launch_nt<512, kEpiSwiGlu>(q, pairs, coop, stream);
+      case 256: return launch_nt<256, kEpiSwiGlu>(q, pairs, coop, stream);
+      default: return cudaErrorInvalidValue;
+    }
+  }
+  if (heads) {  // attention-head launches: 512- or 256-token tiles
+    switch (p.n_tok) {
+      case 512: return launch_nt<512, kEpiHeads>(q, pairs, coop, stream);
+      case 256: return launch_nt<256, kEpiHeads>(q, pairs, coop, stream);
       default: return cudaErrorInvalidValue;
     }
   }
   switch (p.n_tok) {
-    case 512: return launch_nt<512, false>(q, pairs, coop, stream);
-    case 256: return launch_nt<256, false>(q, pairs, coop, stream);
-    case 128: return launch_nt<128, false>(q, pairs, coop, stream);
-    case 64: return launch_nt<64, false>(q, pairs, coop, stream);
+    case 512: return launch_nt<512, kEpiPlain>(q, pairs, coop, stream);
+    case 256: return launch_nt<256, kEpiPlain>(q, pairs, coop, stream);
+    case 128: return launch_nt<128, kEpiPlain>(q, pairs, coop, stream);
+    case 64: return launch_nt<64, kEpiPlain>(q, pairs, coop, stream);
     default: return cudaErrorInvalidValue;
   }
 }

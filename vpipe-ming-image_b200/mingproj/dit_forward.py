@@ -174,13 +174,22 @@ class DitForward:
         modulated = mod_idx is not None
         gain1 = nw1[mod_idx, 0] if modulated else t[pre + "attention_norm1.weight"]
         nrm = self._rms(x, gain1)
-        q, k, v = self.ctx.linear_shared([p["attention.to_q"], p["attention.to_k"],
-                                          p["attention.to_v"]], nrm)
-        q = self._rope(self._rms(q.view(R, nh, hd), t[pre + "attention.norm_q.weight"]), cos, sin)
-        k = self._rope(self._rms(k.view(R, nh, hd), t[pre + "attention.norm_k.weight"]), cos, sin)
-        v = v.view(R, nh, hd)
-        att = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
-                                             v.transpose(0, 1)[None])
+        qkv = [p["attention.to_q"], p["attention.to_k"], p["attention.to_v"]]
+        if hd == 128:
+            # one launch: q/k/v head-major, q and k through the head RMSNorm and
+            # the rotary embedding in the projection epilogue
+            q, k, v = self.ctx.linear_heads(
+                qkv, nrm, norm_w=[t[pre + "attention.norm_q.weight"],
+                                  t[pre + "attention.norm_k.weight"], None],
+                eps=cfg.norm_eps, rope_cos=cos, rope_sin=sin)
+        else:
+            q, k, v = self.ctx.linear_shared(qkv, nrm)
+            q = self._rope(self._rms(q.view(R, nh, hd), t[pre + "attention.norm_q.weight"]),
+                           cos, sin).transpose(0, 1)
+            k = self._rope(self._rms(k.view(R, nh, hd), t[pre + "attention.norm_k.weight"]),
+                           cos, sin).transpose(0, 1)
+            v = v.view(R, nh, hd).transpose(0, 1)
+        att = F.scaled_dot_product_attention(q[None], k[None], v[None])
         a = att[0].transpose(0, 1).reshape(R, H).contiguous()
         o = self.ctx.linear(p["attention.to_out.0"], a)
         o2 = self._rms(o, t[pre + "attention_norm2.weight"]).float()

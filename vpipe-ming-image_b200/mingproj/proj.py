@@ -254,6 +254,53 @@ class Context:
                                               _stream_handle(stream)))
         return out
 
+    def linear_heads(self, ws: list[Weight], x: torch.Tensor, norm_w=None, eps: float = 1e-5,
+                     rope_cos: torch.Tensor | None = None, rope_sin: torch.Tensor | None = None,
+                     outs=None, stream=None) -> list[torch.Tensor]:
+        """q/k/v of one input in one launch, each returned head-major
+        [n / 128, m, 128] bf16. norm_w[i] (bf16 [128] on the device, or None)
+        applies member i's per-head RMSNorm and then the interleaved-pair
+        rotary embedding with rope_cos / rope_sin (f32 [m, 64] on the device)."""
+        m = x.shape[0]
+        n = len(ws)
+        if outs is None:
+            outs = [torch.empty((w.n // 128, m, 128), dtype=torch.bfloat16, device=x.device)
+                    for w in ws]
+        W = (C.c_void_p * n)(*[w.handle.value for w in ws])
+        Y = (C.c_void_p * n)(*[o.data_ptr() for o in outs])
+        keep = []
+        NW = None
+        if norm_w is not None:
+            vals = []
+            for g in norm_w:
+                if g is None:
+                    vals.append(None)
+                else:
+                    g = g.to(torch.bfloat16).contiguous()
+                    keep.append(g)
+                    vals.append(g.data_ptr())
+            NW = (C.c_void_p * n)(*vals)
+        tabs = []
+        for tab in (rope_cos, rope_sin):
+            if tab is None:
+                tabs.append(None)
+            else:
+                tab = tab.to(torch.float32).contiguous()
+                if tab.shape != (m, 64):
+                    raise ValueError(f"rotary table shape {tuple(tab.shape)} != ({m}, 64)")
+                keep.append(tab)
+                tabs.append(_ptr(tab))
+        self._check(self.lib.mp_linear_heads(self.h, W, Y, n, _ptr(x), x.stride(0), m, NW,
+                                             float(eps), tabs[0], tabs[1],
+                                             _stream_handle(stream)))
+        if stream is not None:
+            # converted gains and tables: their memory is not reused before the
+            # launch on `stream` has read them (on the current stream the
+            # allocator's stream order already guarantees it)
+            for t in keep:
+                t.record_stream(stream)
+        return outs
+
     def linear_lora_static(self, w: Weight, x: torch.Tensor, a: torch.Tensor, b: torch.Tensor,
                            strength: float, out: torch.Tensor | None = None,
                            stream=None) -> torch.Tensor:
