@@ -183,7 +183,8 @@ int mp_linear_swiglu(mp_ctx* ctx, const mp_weight* w1, const mp_weight* w3, cons
  *   z = bf16(y * rsqrt(mean(y^2) + eps) * norm_w[i][f])   (y = bf16 projection)
  *   (out[2j], out[2j+1]) = bf16(z[2j] c - z[2j+1] s, z[2j] s + z[2j+1] c)
  * with c = rope_cos[t][j], s = rope_sin[t][j] (f32 [m][64], row t = token row
- * t of x; the caller offsets the tables to the first row). norm_w may be NULL
+ * t of x; the caller offsets the tables to the first row; gains and tables
+ * 16-byte aligned). norm_w may be NULL
  * (no member normed; then the tables may be NULL). Live LoRA slots as in
  * mp_linear_shared. Replaces: the q/k/v lin calls, the per-head rms, tr_rope
  * and the v transpose of run_block (src/ming-dit.cc:2078-2088; tr_rope at

@@ -175,6 +175,11 @@ bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Token rows of one epilogue store box: 32 with the token-row accumulators of
+// 256- and 512-token tiles (each epilogue warp stores its own 32 rows), 64
+// with the feature-row accumulators of narrower tiles.
+int epi_box_rows(int ntok) { return ntok >= mp::kMaxTok ? 32 : mp::kEpiRows; }
+
 // Output map for the pair kernel's bulk stores: [m, n] bf16 rows of ldy,
 // box = 64 features x one pair token tile, 128-byte swizzle.
 bool encode_y(CUtensorMap* m, const void* y, int64_t ldy, int n, int rows, int ntok) {
@@ -186,13 +191,13 @@ bool encode_y(CUtensorMap* m, const void* y, int64_t ldy, int n, int rows, int n
 // Head-major output map of an attention-head member: [n / 128][rows][128]
 // bf16, box = 64 features x 64 tokens of one head, 128-byte swizzle (the
 // same staging layout as encode_y's boxes).
-bool encode_heads_y(CUtensorMap* m, const void* y, int n, int rows) {
+bool encode_heads_y(CUtensorMap* m, const void* y, int n, int rows, int ntok) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return false;
   const uint64_t hd = mp::kHeadDim;
   cuuint64_t dims[3] = {hd, static_cast<uint64_t>(rows), static_cast<uint64_t>(n) / hd};
   cuuint64_t strides[2] = {hd * 2, static_cast<uint64_t>(rows) * hd * 2};
-  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(mp::kEpiRows), 1};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(epi_box_rows(ntok)), 1};
   cuuint32_t estr[3] = {1, 1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(y), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -378,7 +383,7 @@ int fill_member(mp_ctx* c, ProjParams* p, int i, const CUtensorMap& tm_w, const 
   const bool sym = bits == 8 && mode == MP_QUANT_SYMMETRIC;
   mb.code_xor = sym ? 0x80808080u : 0u;
   mb.code_offset = sym ? 32896.0f : 32768.0f;
-  if (!encode_y(&mb.tm_y, y, ldy, n, p->M, mp::kEpiRows))
+  if (!encode_y(&mb.tm_y, y, ldy, n, p->M, epi_box_rows(p->n_tok)))
     return fail(c, MP_ECUDA, "tensor map encode failed (output)");
   mb.lora_ktiles = 0;
   if (lt.rpad > 0) {
@@ -645,7 +650,7 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
       p.mem[i].t_col = lt.rpad > 0 ? t_cols[i] : 0;
       if (hds != nullptr) {
         mp::ProjMember& mb = p.mem[i];
-        if (!encode_heads_y(&mb.tm_y, ys[i], w->d.n, m))
+        if (!encode_heads_y(&mb.tm_y, ys[i], w->d.n, m, p.n_tok))
           return fail(c, MP_ECUDA, "tensor map encode failed (head-major output)");
         mb.heads = 1;
         mb.head_norm = hds->norm_w[i] != nullptr ? 1 : 0;
@@ -672,7 +677,7 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
     pre.bits = 0;
     pre.sb = nullptr;
     pre.lora_ktiles = 0;
-    if (!encode_y(&pre.tm_y, c->scratch, t_ld, pro->rtot, m, mp::kEpiRows))
+    if (!encode_y(&pre.tm_y, c->scratch, t_ld, pro->rtot, m, epi_box_rows(p.n_tok)))
       return fail(c, MP_ECUDA, "tensor map encode failed (rank-space intermediate)");
     cudaError_t e = mp::launch_proj_pair(p, stream);
     if (e != cudaSuccess) {
@@ -1176,13 +1181,17 @@ int mp_linear_heads(mp_ctx* c, const mp_weight* const* ws, void* const* ys, int 
                   mp::kHeadDim);
     if (ys[i] == nullptr || reinterpret_cast<uintptr_t>(ys[i]) % 16 != 0)
       return fail(c, MP_EINVAL, "head-major output %d is NULL or not 16-byte aligned", i);
-    any_norm = any_norm || (norm_w != nullptr && norm_w[i] != nullptr);
+    if (norm_w != nullptr && norm_w[i] != nullptr) {
+      if (reinterpret_cast<uintptr_t>(norm_w[i]) % 16 != 0)
+        return fail(c, MP_EINVAL, "norm gain %d must be 16-byte aligned", i);
+      any_norm = true;
+    }
   }
   if (any_norm) {
     if (rope_cos == nullptr || rope_sin == nullptr ||
-        reinterpret_cast<uintptr_t>(rope_cos) % 4 != 0 ||
-        reinterpret_cast<uintptr_t>(rope_sin) % 4 != 0)
-      return fail(c, MP_EINVAL, "the normed heads need 4-byte aligned rotary tables");
+        reinterpret_cast<uintptr_t>(rope_cos) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(rope_sin) % 16 != 0)
+      return fail(c, MP_EINVAL, "the normed heads need 16-byte aligned rotary tables");
     if (!(eps > 0.0f)) return fail(c, MP_EINVAL, "eps must be positive");
   }
   int rc = check_x(c, x, ldx, k, m);

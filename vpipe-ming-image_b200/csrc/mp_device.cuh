@@ -182,6 +182,16 @@ __device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t saddr) {
       : "r"(taddr)                                                                                \
       : "memory")
 
+#define MP_TMEM_LD_32X32B_X16(taddr, r)                                                           \
+  asm volatile(                                                                                   \
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "                                                   \
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"                           \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),       \
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),   \
+        "=r"(r[14]), "=r"(r[15])                                                                  \
+      : "r"(taddr)                                                                                \
+      : "memory")
+
 #define MP_TMEM_ST_32X32B_X32(taddr, r)                                                           \
   asm volatile(                                                                                   \
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "                                             \
@@ -207,6 +217,13 @@ __device__ __forceinline__ void tmem_wait_ld() {
                  "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),    \
                  "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),    \
                  "+r"(r[30]), "+r"(r[31])                                                         \
+               :                                                                                  \
+               : "memory")
+#define MP_TMEM_WAIT_LD_REGS16(r)                                                                 \
+  asm volatile("tcgen05.wait::ld.sync.aligned;"                                                   \
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),          \
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),        \
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])                               \
                :                                                                                  \
                : "memory")
 __device__ __forceinline__ void tmem_wait_st() {
@@ -336,6 +353,26 @@ __device__ __forceinline__ void umma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, u
       "r"(r[15])                                                                                  \
       : "memory")
 
+// ---- asynchronous 16-byte global -> shared copies ---------------------------
+
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 // ---- packed fp32 pairs (sm_100 f32x2 arithmetic) ----------------------------
 
 __device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
@@ -346,6 +383,11 @@ __device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
 __device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
   uint64_t r;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
 __device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {

@@ -62,6 +62,19 @@ struct Geo {
 };
 __device__ __forceinline__ uint32_t off_epi(int b) { return kStagesBytes + b * kEpiBufBytes; }
 
+// Accumulator orientation. 256- and 512-token tiles keep TOKEN-ROW
+// accumulators: TMEM lane = token row (this CTA's half of each 256-token
+// sub-tile), column = feature (all 256 of the pair), so an epilogue thread
+// holds consecutive features of one token. 64- and 128-token tiles (a
+// cta_group::2 MMA with M < 256 puts rows elsewhere in TMEM) keep
+// FEATURE-ROW accumulators: lane = feature (this CTA's 128), column = token.
+template <int NT>
+constexpr bool kTokRows = NT >= kSubTok;
+// Token-row epilogue: each warp stages [32 tokens][64 features] (128-byte
+// swizzled rows, 4 KB) in one of its two buffers and stores it itself.
+constexpr uint32_t kWarpStageBytes = 32 * 128;
+static_assert(4 * 2 * kWarpStageBytes == 2 * kEpiBufBytes, "per-warp staging fits the epilogue region");
+
 // warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 dequant, warps 10-13 epilogue
 constexpr int kDeqWarp0 = 2;
 constexpr int kDeqThreads = 256;
@@ -69,9 +82,17 @@ constexpr int kEpiWarp0 = 10;
 constexpr int kEpiThreads = 128;
 constexpr int kPairThreads = 32 * kEpiWarp0 + kEpiThreads;
 constexpr uint32_t kEpiBarrier = 1;  // named barrier of the epilogue warps
-constexpr uint32_t kRedBytes = 2 * 4 * 32 * 4;  // head RMSNorm partial sums [2][4 warps][32 tokens]
-constexpr uint32_t kPairSmemBytes = kTileBytes + 1024 + 512 + kRedBytes;
-static_assert(kPairSmemBytes <= 232448, "shared memory per CTA");
+// per epilogue warp: the strengths (f32) and slots (int8) of the 256 rank
+// columns of a scaled tile
+constexpr uint32_t kColBytes = 4 * 256 * (4 + 1);
+constexpr uint32_t kPairSmemBytes = kTileBytes + 1024 + 512 + kColBytes;
+// attention-head variant only: per epilogue warp, one 16-pair block of the
+// rotary tables for its 32 token rows (cos, then sin; rows padded to 80 bytes
+// so the row reads are conflict-free)
+constexpr uint32_t kRopeRowBytes = 80;
+constexpr uint32_t kRopeWarpBytes = 2 * 32 * kRopeRowBytes;
+constexpr uint32_t kHeadsSmemBytes = kPairSmemBytes + 4 * kRopeWarpBytes;
+static_assert(kHeadsSmemBytes <= 232448, "shared memory per CTA");
 static_assert(2 * kSubTok <= kTmemCols, "two accumulators in TMEM");
 static_assert(kMaxStages <= 8, "per-slot parity bit masks");
 
@@ -112,7 +133,9 @@ struct PairSmem {
   uint64_t* drain;   // leader: every MMA issued has completed
   uint32_t* tmem_slot;
   volatile uint32_t* abort;
-  float* red;        // head-norm partial sums of the epilogue warps
+  float* colscale;   // [4 warps][256] column strengths of a scaled tile
+  int8_t* colslot;   // [4 warps][256] column slots (-1: no slot)
+  uint8_t* rope;     // [4 warps][kRopeWarpBytes] rotary-table blocks (head variant)
 };
 
 __device__ __forceinline__ PairSmem carve_pair(uint8_t* raw) {
@@ -129,7 +152,9 @@ __device__ __forceinline__ PairSmem carve_pair(uint8_t* raw) {
   s.drain = s.tempty + 2;
   s.tmem_slot = reinterpret_cast<uint32_t*>(s.drain + 1);
   s.abort = s.tmem_slot + 1;
-  s.red = reinterpret_cast<float*>(s.tiles + kTileBytes + 512);
+  s.colscale = reinterpret_cast<float*>(s.tiles + kTileBytes + 512);
+  s.colslot = reinterpret_cast<int8_t*>(s.colscale + 4 * 256);
+  s.rope = reinterpret_cast<uint8_t*>(s.colslot + 4 * 256);
   return s;
 }
 
@@ -418,7 +443,13 @@ __device__ void pair_mma(const ProjParams& p, const PairSmem& sm, uint32_t tmem,
     const Tile t = decode_unit(p, unit, 0, base_kt);
     const ProjMember& mb = unit_member(p, t);
     const bool quant = mb.bits != 0;
-    const uint32_t idesc = make_idesc_bf16(2 * kBlockN, static_cast<uint32_t>(t.sub));
+    // token-row tiles: D[token][feature] (A = the x sub-tile, M = its tokens
+    // across the pair; B = the weight tile, N = the pair's 256 features);
+    // narrower tiles: D[feature][token] (A = weights, B = x)
+    const uint32_t idesc =
+        kTokRows<NT> ? make_idesc_bf16(static_cast<uint32_t>(t.sub), 2 * kBlockN)
+                     : make_idesc_bf16(2 * kBlockN, static_cast<uint32_t>(t.sub));
+    const uint32_t acc_cols = kTokRows<NT> ? 2u * kBlockN : static_cast<uint32_t>(t.sub);
     const uint32_t sub_bytes = static_cast<uint32_t>(t.half) * 128u;
     uint32_t acc = 0;
     for (int kt = t.kt_begin; kt < t.kt_end; ++kt, ++it) {
@@ -442,7 +473,7 @@ __device__ void pair_mma(const ProjParams& p, const PairSmem& sm, uint32_t tmem,
       const uint32_t waddr = smem_u32(sm.tiles) + G::off_a(s);
 #pragma unroll
       for (int kk = 0; kk < kBlockK / 16; ++kk) {
-        const uint64_t adesc = make_sdesc_sw128(waddr + kk * 32);
+        const uint64_t wdesc = make_sdesc_sw128(waddr + kk * 32);
         for (int j = 0; j < 2; ++j) {
           if (acc == 0 && tcount > 0) {
             // Accumulator j holds the previous tile until its epilogue has read
@@ -456,8 +487,11 @@ __device__ void pair_mma(const ProjParams& p, const PairSmem& sm, uint32_t tmem,
             tc_fence_after();
           }
           if (j >= t.n_sub) continue;
-          const uint64_t bdesc = make_sdesc_sw128(xaddr + j * sub_bytes + kk * 32);
-          umma_ss_pair(tmem + static_cast<uint32_t>(j * t.sub), adesc, bdesc, idesc, acc);
+          const uint64_t xdesc = make_sdesc_sw128(xaddr + j * sub_bytes + kk * 32);
+          if constexpr (kTokRows<NT>)
+            umma_ss_pair(tmem + j * acc_cols, xdesc, wdesc, idesc, acc);
+          else
+            umma_ss_pair(tmem + j * acc_cols, wdesc, xdesc, idesc, acc);
         }
         if (aborted) break;
         acc = 1;
@@ -584,219 +618,414 @@ __device__ __forceinline__ void release_accumulator(const PairSmem& sm, int j) {
   if ((threadIdx.x & 31) == 0) mbar_arrive_remote(mapa_shared(smem_u32(&sm.tempty[j]), 0));
 }
 
-// One 64-token epilogue round of a SwiGLU pair member (TMEM lanes 0-63: W1's
-// features f0.., lanes 64-127: W3's same features). Both halves round their
-// sums to bf16 (g from W1, u from W3) and hand the other half the 32 tokens
-// it finishes: the W1 warps (q = 0, 1) compute tokens 0-31 of the round, the
-// W3 warps (q = 2, 3) tokens 32-63, each h = bf16(g / (1 + exp(-g)) * u), the
-// reference's swiglu on the bf16 gate and up values
-// (src/metal/ming_ops.metal:95-112), into the 128-byte-swizzled staging tile
-// that one thread stores with a single TMA box. Buffer: staging 8 KB, then
-// the exchanged u (tokens 0-31) and g (tokens 32-63), bf16 [32][64] each. The
-// buffer in use alternates by round; the issuer waited before the first
-// barrier until the store that last read it had done so.
-__device__ void swiglu_round(const ProjMember& mb, const PairSmem& sm, uint32_t tmem,
-                             uint32_t lane_base, const Tile& t, int j, int rr, int rounds,
-                             int tr0, uint32_t round, int q, int lane, bool issuer) {
-  const uint32_t buf = smem_u32(sm.tiles) + off_epi(static_cast<int>(round & 1u));
-  const uint32_t exch_u = buf + kEpiHalfBytes;         // u of tokens 0-31 (from the W3 half)
-  const uint32_t exch_g = exch_u + kEpiHalfBytes / 2;  // g of tokens 32-63 (from the W1 half)
-  const uint32_t col0 = static_cast<uint32_t>(j * t.sub + rr * kEpiRows);
-  const uint32_t fcol = static_cast<uint32_t>(32 * (q & 1) + lane);  // feature within the 64
-  const bool gate = q < 2;       // this warp holds W1's sums (g), else W3's (u)
-  const int mine = gate ? 0 : 1;  // the 32-token chunk this warp finishes
-  named_barrier(kEpiBarrier, kEpiThreads);
-  uint32_t v[32];
-  // 1. the chunk the other half finishes: round to bf16 and hand it over
-  MP_TMEM_LD_32X32B_X32(tmem + lane_base + col0 + static_cast<uint32_t>((1 - mine) * 32), v);
-  MP_TMEM_WAIT_LD_REGS32(v);
-  {
-    const uint32_t dst = gate ? exch_g : exch_u;
-#pragma unroll
-    for (int jj = 0; jj < 32; ++jj)
-      st_shared_b16(dst + (static_cast<uint32_t>(jj) * 64u + fcol) * 2u,
-                    __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[jj]))));
-  }
-  // 2. this warp's own chunk (the accumulator is read out after this load)
-  MP_TMEM_LD_32X32B_X32(tmem + lane_base + col0 + static_cast<uint32_t>(mine * 32), v);
-  MP_TMEM_WAIT_LD_REGS32(v);
-  if (rr + 1 == rounds) release_accumulator(sm, j);
-  named_barrier(kEpiBarrier, kEpiThreads);
-  const bool odd = (lane & 1) != 0;
-  const uint32_t wi = static_cast<uint32_t>(16 * (q & 1) + (lane >> 1));
-  const uint32_t chunk = wi >> 2, in_chunk = (wi & 3u) << 2;
-  const uint32_t src = gate ? exch_u : exch_g;
-#pragma unroll
-  for (int jb = 0; jb < 32; jb += 8) {
-    // 8 tokens at a time: h for tokens jb..jb+7 of this warp's chunk, then
-    // the pair-shuffled stores (lanes 2i, 2i+1 hold features 2i, 2i+1)
-    float h[8];
-#pragma unroll
-    for (int d = 0; d < 8; ++d) {
-      uint16_t ob;
-      asm volatile("ld.shared.u16 %0, [%1];"
-                   : "=h"(ob)
-                   : "r"(src + (static_cast<uint32_t>(jb + d) * 64u + fcol) * 2u));
-      const float own = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v[jb + d])));
-      const float other = bf16_bits_to_f32(ob);
-      const float g = gate ? own : other;
-      const float u = gate ? other : own;
-      h[d] = __fdividef(g, 1.0f + __expf(-g)) * u;
-    }
-#pragma unroll
-    for (int d = 0; d < 4; ++d) {
-      const float give = odd ? h[d] : h[d + 4];
-      const float got = __shfl_xor_sync(0xFFFFFFFFu, give, 1);
-      const uint32_t word = odd ? pack_bf16x2(got, h[d + 4]) : pack_bf16x2(h[d], got);
-      const uint32_t row = static_cast<uint32_t>(mine * 32 + jb + d + (odd ? 4 : 0));
-      const uint32_t addr = buf + row * 128u + (((chunk ^ (row & 7u)) << 4) | in_chunk);
-      asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(word) : "memory");
-    }
-  }
-  fence_proxy_async_shared();
-  named_barrier(kEpiBarrier, kEpiThreads);
-  if (issuer) {
-    tma_store_2d(&mb.tm_y, buf, t.f0, tr0);
-    tma_store_commit();
-    tma_store_wait_read_1();  // the other buffer is free again
-  }
-}
-
 // Epilogue variants, one kernel instantiation each (they differ in register
 // needs): plain projections, SwiGLU pairs, attention heads.
 enum : int { kEpiPlain = 0, kEpiSwiGlu = 1, kEpiHeads = 2 };
 
-// Sum over the warp's 32 lanes of y[i]^2, for all 32 i at once: a butterfly
-// that halves the values each lane carries at every step (31 shuffles) and
-// leaves lane l with the total of i = l. The squares are rounded before the
-// adds (no contraction), as an unfused square-then-sum computes them.
-__device__ __forceinline__ float lane_sums_of_squares(const float (&y)[32], int lane) {
-  float a[16];
-  {
-    const bool hi = (lane & 16) != 0;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float lo_sq = __fmul_rn(y[i], y[i]);
-      const float hi_sq = __fmul_rn(y[i + 16], y[i + 16]);
-      const float send = hi ? lo_sq : hi_sq;
-      a[i] = __fadd_rn(hi ? hi_sq : lo_sq, __shfl_xor_sync(0xFFFFFFFFu, send, 16));
-    }
-  }
-#pragma unroll
-  for (int w = 8; w >= 1; w >>= 1) {
-    const bool hi = (lane & w) != 0;
-#pragma unroll
-    for (int i = 0; i < w; ++i) {
-      const float send = hi ? a[i] : a[i + w];
-      a[i] = __fadd_rn(hi ? a[i + w] : a[i], __shfl_xor_sync(0xFFFFFFFFu, send, w));
-    }
-  }
-  return a[0];
+
+// ---- token-row epilogue (256- and 512-token tiles) -------------------------
+// Warps 10-13: warp q holds token rows 32q .. 32q + 31 of this CTA's half of a
+// sub-tile (TMEM lane quarter q), each thread one token with the pair's 256
+// feature columns. Per 64 output features a warp packs its 32 rows into
+// bf16x2 words (consecutive features of one token: no shuffles), writes them
+// with 16-byte stores into a [32][64] staging box laid out with the 128-byte
+// swizzle, and its lane 0 stores the box with one TMA bulk store (which clips
+// rows past M and columns past N). Each warp alternates two staging buffers
+// of its own, so the warps never wait for one another.
+
+// Before a warp writes a staging buffer: the store that last read it (two
+// stores ago) has finished reading.
+__device__ __forceinline__ void stage_acquire(int lane) {
+  if (lane == 0) tma_store_wait_read_1();
+  __syncwarp();
 }
 
-// One 64-token epilogue round of an attention-head member: the CTA's 128
-// features are head f0 / 128 of q, k or v, stored head-major ([heads][M][128],
-// the layout the attention reads; the reference transposes into it,
-// src/ming-dit.cc:2085-2088). For q and k (head_norm) each token's 128 values
-// first get the head's RMSNorm and the rotary embedding, with the roundings of
-// the unfused sequence (projection output, normed value, rotated value, each
-// rounded to bf16; the per-head rms of :2083-2084 and tr_rope of :1885-1894):
-//   y = bf16(acc);  z = bf16(y * rsqrt(sum(y^2) / 128 + eps) * gain[f])
-//   (out[2i], out[2i+1]) = bf16(z[2i] c - z[2i+1] s, z[2i] s + z[2i+1] c)
-// with c, s the tables' entries at (token row, i). A token's sum of squares:
-// the butterfly leaves each warp's partial in lane t, and the four warps'
-// partials meet in shared memory, added in warp order (the result never
-// depends on timing). `hc` counts the chunks normed so far (it alternates the
-// two partial-sum buffers).
-__device__ void head_round(const ProjParams& p, const ProjMember& mb, const PairSmem& sm,
-                           uint32_t tmem, uint32_t lane_base, const Tile& t, int j, int rr,
-                           int rounds, int tr0, uint32_t round, uint32_t& hc, int q, int lane,
-                           bool issuer, float gain) {
-  const bool odd = (lane & 1) != 0;
-  const int fl = q * 32 + lane;  // feature within the head
-  const uint32_t wi = static_cast<uint32_t>(16 * (q & 1) + (lane >> 1));
-  const uint32_t chunk = wi >> 2, in_chunk = (wi & 3u) << 2;
-  const uint32_t buf = smem_u32(sm.tiles) + off_epi(static_cast<int>(round & 1u));
-  const bool norm = mb.head_norm != 0;
-  // the stores that last read this buffer have finished reading (issuer waited)
-  named_barrier(kEpiBarrier, kEpiThreads);
-  const uint32_t stage = buf + static_cast<uint32_t>(q >> 1) * kEpiHalfBytes;
-  for (int c = 0; c < 2; ++c) {
-    const int tc = tr0 + c * 32;
-    // rotary factors of the 16 tokens this lane stores (even lane: tokens
-    // jb + d, odd lane: jb + d + 4), requested before the accumulator read
-    float cs[16], sn[16];
-    if (norm) {
-      const size_t pi = static_cast<size_t>(fl >> 1);
+// 16 bf16x2 words = features [32h, 32h + 32) of this thread's token row.
+__device__ __forceinline__ void stage_words(uint32_t buf, int lane, int h, const uint32_t (&w)[16]) {
+  const uint32_t row = buf + static_cast<uint32_t>(lane) * 128u;
 #pragma unroll
-      for (int g = 0; g < 16; ++g) {
-        const int tok = min(tc + (g >> 2) * 8 + (g & 3) + (odd ? 4 : 0), p.M - 1);
-        cs[g] = __ldg(mb.rope_cos + static_cast<size_t>(tok) * (kHeadDim / 2) + pi);
-        sn[g] = __ldg(mb.rope_sin + static_cast<size_t>(tok) * (kHeadDim / 2) + pi);
-      }
-    }
-    uint32_t v[32];
-    MP_TMEM_LD_32X32B_X32(
-        tmem + lane_base + static_cast<uint32_t>(j * t.sub + rr * kEpiRows + c * 32), v);
-    MP_TMEM_WAIT_LD_REGS32(v);
-    if (rr + 1 == rounds && c == 1) release_accumulator(sm, j);
-    float y[32];
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t ch = static_cast<uint32_t>(4 * h + i);
+    st_shared_v4(row + ((ch ^ static_cast<uint32_t>(lane & 7)) << 4), w[4 * i], w[4 * i + 1],
+                 w[4 * i + 2], w[4 * i + 3]);
+  }
+}
+
+__device__ __forceinline__ void pack_words(const uint32_t (&v)[32], uint32_t (&w)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+}
+
+// The warp's staged box: token rows tok0 .. tok0 + 31, output features
+// fcol .. fcol + 63 (member-relative; head-major members: head fcol / 128).
+__device__ __forceinline__ void stage_store(const ProjMember& mb, uint32_t buf, int fcol, int tok0,
+                                            int lane) {
+  fence_proxy_async_shared();
+  __syncwarp();
+  if (lane == 0) {
+    if (mb.heads)
+      tma_store_3d(&mb.tm_y, buf, fcol % kHeadDim, tok0, fcol / kHeadDim);
+    else
+      tma_store_2d(&mb.tm_y, buf, fcol, tok0);
+    tma_store_commit();
+  }
+}
+
+// Scaled tiles (rank-space T): the strength of value (token row t, rank
+// column c) is seg_scale[segment(t)][slot(c)], 0 outside every slot range.
+// Per tile each epilogue warp resolves the slots of the pair's 256 columns
+// once (8 per lane) into its shared-memory table; per sub-tile it tabulates
+// the strengths for the segment of its first row. Rows of that segment (in
+// practice every row: segments are whole images) then read one broadcast
+// shared value per column; a warp straddling a segment boundary looks its
+// other rows up through the slot table.
+__device__ __forceinline__ void column_slots(const EpilogueScale& es, int pf0, int lane,
+                                             int8_t* slots) {
+#pragma unroll 1
+  for (int k = 0; k < 8; ++k) {
+    const int c = 32 * k + lane;
+    const int col = pf0 + c;
+    int slot = -1;
+    for (int i = 0; i < es.n_ranges; ++i)
+      if (col >= es.range_start[i] && col < es.range_start[i + 1]) slot = es.range_slot[i];
+    slots[c] = static_cast<int8_t>(slot);
+  }
+  __syncwarp();
+}
+
+__device__ __forceinline__ void column_scales(const EpilogueScale& es, int g0, int lane,
+                                              const int8_t* slots, float* scales) {
+  __syncwarp();  // the previous sub-tile's reads of the table are done
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int c = 32 * k + lane;
+    const int slot = slots[c];
+    scales[c] = slot >= 0 ? es.seg_scale[g0][slot] : 0.0f;
+  }
+  __syncwarp();
+}
+
+// v[jj] *= strength of (this thread's row, column c0 + jj); c0 relative to the pair.
+__device__ __forceinline__ void scale_columns(const EpilogueScale& es, bool same_seg, int g, int c0,
+                                              const int8_t* slots, const float* scales,
+                                              uint32_t (&v)[32]) {
+  if (same_seg) {
 #pragma unroll
     for (int jj = 0; jj < 32; ++jj)
-      y[jj] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v[jj])));
-    if (norm) {
-      const float part = lane_sums_of_squares(y, lane);
-      float* red = sm.red + (hc & 1u) * (4 * 32);
-      red[q * 32 + lane] = part;
-      named_barrier(kEpiBarrier, kEpiThreads);
-      const float tot =
-          __fadd_rn(__fadd_rn(__fadd_rn(red[lane], red[32 + lane]), red[64 + lane]), red[96 + lane]);
-      const float r = rsqrtf(__fadd_rn(__fmul_rn(tot, 1.0f / kHeadDim), mb.norm_eps));
-      ++hc;
+      v[jj] = __float_as_uint(__uint_as_float(v[jj]) * scales[c0 + jj]);
+  } else {
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const float rj = __shfl_sync(0xFFFFFFFFu, r, jj);
-        y[jj] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(y[jj], rj), gain)));
-      }
+    for (int jj = 0; jj < 32; ++jj) {
+      const int slot = slots[c0 + jj];
+      const float sc = slot >= 0 ? es.seg_scale[g][slot] : 0.0f;
+      v[jj] = __float_as_uint(__uint_as_float(v[jj]) * sc);
     }
-    // Lane pairs (features 2i, 2i+1) exchange the token the other one stores:
-    // the even lane stores token je, the odd lane token je + 4 (opposite bank
-    // halves of the swizzled rows), each with both features of the pair.
-#pragma unroll
-    for (int jb = 0; jb < 32; jb += 8) {
-#pragma unroll
-      for (int d = 0; d < 4; ++d) {
-        const int je = jb + d, jo = jb + d + 4;
-        const float got = __shfl_xor_sync(0xFFFFFFFFu, odd ? y[je] : y[jo], 1);
-        const float z0 = odd ? got : y[je];
-        const float z1 = odd ? y[jo] : got;
-        float o0 = z0, o1 = z1;
-        if (norm) {
-          const int g = (jb >> 3) * 4 + d;
-          o0 = __fsub_rn(__fmul_rn(z0, cs[g]), __fmul_rn(z1, sn[g]));
-          o1 = __fadd_rn(__fmul_rn(z0, sn[g]), __fmul_rn(z1, cs[g]));
-        }
-        const uint32_t word = pack_bf16x2(o0, o1);
-        const uint32_t row = static_cast<uint32_t>(c * 32 + (odd ? jo : je));
-        const uint32_t addr = stage + row * 128u + (((chunk ^ (row & 7u)) << 4) | in_chunk);
-        asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(word) : "memory");
-      }
-    }
-  }
-  fence_proxy_async_shared();
-  named_barrier(kEpiBarrier, kEpiThreads);
-  if (issuer) {
-    // a CTA past the member's last head (an odd head count) stores nothing
-    if (t.f0 < mb.N) {
-      const int head = t.f0 / kHeadDim;
-      tma_store_3d(&mb.tm_y, buf, 0, tr0, head);
-      tma_store_3d(&mb.tm_y, buf + kEpiHalfBytes, 64, tr0, head);
-    }
-    tma_store_commit();
-    tma_store_wait_read_1();  // the other buffer is free again
   }
 }
 
+// Plain member (or prologue unit): features pf0 .. pf0 + 255 of the pair.
+__device__ void rows_plain(const ProjParams& p, const ProjMember& mb, uint32_t acc, uint32_t stg,
+                           int pf0, int tok0, int lane, bool scaled, const int8_t* slots,
+                           float* scales, uint32_t& round) {
+  int g = 0;
+  bool same_seg = true;
+  if (scaled) {
+    g = row_segment(p.scale, min(tok0 + lane, p.M - 1));
+    const int g0 = __shfl_sync(0xFFFFFFFFu, g, 0);
+    same_seg = g == g0;
+    column_scales(p.scale, g0, lane, slots, scales);
+  }
+  for (int r = 0; r < 4; ++r) {
+    const int fcol = pf0 + 64 * r;
+    if (fcol >= mb.N) break;
+    const uint32_t buf = stg + (round & 1u) * kWarpStageBytes;
+    stage_acquire(lane);
+    for (int h = 0; h < 2; ++h) {
+      uint32_t v[32];
+      MP_TMEM_LD_32X32B_X32(acc + static_cast<uint32_t>(64 * r + 32 * h), v);
+      MP_TMEM_WAIT_LD_REGS32(v);
+      if (scaled) scale_columns(p.scale, same_seg, g, 64 * r + 32 * h, slots, scales, v);
+      uint32_t w[16];
+      pack_words(v, w);
+      stage_words(buf, lane, h, w);
+    }
+    stage_store(mb, buf, fcol, tok0, lane);
+    ++round;
+  }
+}
+
+// Split-K: this thread's token row of the fp32 partial sums, 16-byte stores
+// (the rank-space widths split-K runs on are multiples of 64).
+__device__ void rows_split(const ProjParams& p, const ProjMember& mb, const Tile& t, uint32_t acc,
+                           int pf0, int tok) {
+  float* prow = p.part + static_cast<size_t>(t.z) * p.M * p.part_ld + static_cast<size_t>(tok) * p.part_ld;
+  for (int r = 0; r < 8; ++r) {
+    const int c0 = pf0 + 32 * r;
+    if (c0 >= mb.N) break;
+    uint32_t v[32];
+    MP_TMEM_LD_32X32B_X32(acc + static_cast<uint32_t>(32 * r), v);
+    MP_TMEM_WAIT_LD_REGS32(v);
+    if (tok < p.M) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (c0 + 4 * i < mb.N)
+          *reinterpret_cast<float4*>(prow + c0 + 4 * i) =
+              make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                          __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+    }
+  }
+}
+
+// SwiGLU pair member: the pair's columns are [W1 | W3] of CTA 0's 64 features,
+// then [W1 | W3] of CTA 1's, so a thread holds g and u of the same feature:
+// h = bf16(g / (1 + exp(-g)) * u) of the bf16 gate and up values, the
+// reference's swiglu (src/metal/ming_ops.metal:95-112).
+__device__ void rows_swiglu(const ProjMember& mb, uint32_t acc, uint32_t stg, int pf0, int tok0,
+                            int lane, uint32_t& round) {
+  for (int r = 0; r < 2; ++r) {
+    const int fcol = pf0 + 64 * r;
+    if (fcol >= mb.N) break;
+    const uint32_t buf = stg + (round & 1u) * kWarpStageBytes;
+    stage_acquire(lane);
+    const uint32_t row = buf + static_cast<uint32_t>(lane) * 128u;
+    for (int h = 0; h < 4; ++h) {  // 16 features at a time
+      uint32_t gv[16], uv[16];
+      MP_TMEM_LD_32X32B_X16(acc + static_cast<uint32_t>(128 * r + 16 * h), gv);
+      MP_TMEM_LD_32X32B_X16(acc + static_cast<uint32_t>(128 * r + 64 + 16 * h), uv);
+      MP_TMEM_WAIT_LD_REGS16(gv);
+      MP_TMEM_WAIT_LD_REGS16(uv);
+#pragma unroll
+      for (int i4 = 0; i4 < 2; ++i4) {  // one 16-byte chunk (8 features) at a time
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = 8 * i4 + 2 * e;  // features c, c + 1: gate and up rounded as pairs
+          const uint32_t gw = pack_bf16x2(__uint_as_float(gv[c]), __uint_as_float(gv[c + 1]));
+          const uint32_t uw = pack_bf16x2(__uint_as_float(uv[c]), __uint_as_float(uv[c + 1]));
+          const float g[2] = {__uint_as_float(gw << 16), __uint_as_float(gw & 0xFFFF0000u)};
+          const float u[2] = {__uint_as_float(uw << 16), __uint_as_float(uw & 0xFFFF0000u)};
+          float hv[2];
+#pragma unroll
+          for (int b = 0; b < 2; ++b) hv[b] = __fdividef(g[b], 1.0f + __expf(-g[b])) * u[b];
+          w[e] = pack_bf16x2(hv[0], hv[1]);
+        }
+        const uint32_t ch = static_cast<uint32_t>(2 * h + i4);
+        st_shared_v4(row + ((ch ^ static_cast<uint32_t>(lane & 7)) << 4), w[0], w[1], w[2], w[3]);
+      }
+    }
+    stage_store(mb, buf, fcol, tok0, lane);
+    ++round;
+  }
+}
+
+// Attention-head member: the pair's 256 columns are two heads, stored
+// head-major ([heads][M][128], the layout the attention reads; the reference
+// transposes into it, src/ming-dit.cc:2085-2088). For q and k (head_norm)
+// each token's head row first gets the head's RMSNorm and the rotary
+// embedding, with the roundings of the unfused sequence (projection output,
+// normed value and rotated value each rounded to bf16; the per-head rms of
+// :2083-2084 and tr_rope of :1885-1894):
+//   y = bf16(acc);  z = bf16(y * rsqrt(sum(y^2) / 128 + eps) * gain[f])
+//   (out[2i], out[2i+1]) = bf16(z[2i] c - z[2i+1] s, z[2i] s + z[2i+1] c)
+// with c, s the tables' entries at (token row, i). A first pass over the two
+// heads' TMEM columns sums the squares in the thread's own registers
+// (features in order). The second pass walks four blocks of 16 rotary pairs
+// (32 features of each head); a block of the tables for the warp's 32 rows
+// is copied into shared memory with coalesced asynchronous copies (one block
+// ahead), and each thread reads its own row from there.
+
+// Block b of the rotary tables (pairs 16b .. 16b + 15) for token rows tok0 ..
+// tok0 + 31 into the warp's staging rows: 2 x 32 rows x 64 bytes, four
+// 16-byte copies per lane, four lanes per row (rows past M repeat row M - 1).
+__device__ __forceinline__ void rope_block_copy(const ProjMember& mb, uint32_t rope, int M, int tok0,
+                                                int b, int lane) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int piece = lane + 32 * j;  // 0..127: row piece / 4, 16-byte column piece % 4
+    const int row = piece >> 2, col = piece & 3;
+    const size_t src = static_cast<size_t>(min(tok0 + row, M - 1)) * (kHeadDim / 2) + 16 * b + 4 * col;
+    const uint32_t dst = rope + static_cast<uint32_t>(row) * kRopeRowBytes + 16u * col;
+    cp_async_16(dst, mb.rope_cos + src);
+    cp_async_16(dst + 32 * kRopeRowBytes, mb.rope_sin + src);
+  }
+  cp_async_commit();
+}
+
+__device__ void rows_heads(const ProjParams& p, const ProjMember& mb, uint32_t acc, uint32_t stg,
+                           uint32_t rope, int pf0, int tok0, int lane, uint32_t& round) {
+  const bool norm = mb.head_norm != 0;
+  const int nh = pf0 + kHeadDim < mb.N ? 2 : 1;  // heads of the pair inside the member
+  float rn[2] = {1.0f, 1.0f};
+  if (norm) {
+    rope_block_copy(mb, rope, p.M, tok0, 0, lane);  // lands during the first pass
+    float ss[2] = {0.0f, 0.0f};
+    for (int c4 = 0; c4 < 4; ++c4) {
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        if (hh >= nh) break;
+        uint32_t v[32];
+        MP_TMEM_LD_32X32B_X32(acc + static_cast<uint32_t>(kHeadDim * hh + 32 * c4), v);
+        MP_TMEM_WAIT_LD_REGS32(v);
+#pragma unroll
+        for (int jj = 0; jj < 32; jj += 2) {
+          const uint32_t yw = pack_bf16x2(__uint_as_float(v[jj]), __uint_as_float(v[jj + 1]));
+          const float y0 = __uint_as_float(yw << 16), y1 = __uint_as_float(yw & 0xFFFF0000u);
+          ss[hh] = __fadd_rn(ss[hh], __fmul_rn(y0, y0));
+          ss[hh] = __fadd_rn(ss[hh], __fmul_rn(y1, y1));
+        }
+      }
+    }
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh)
+      rn[hh] = rsqrtf(__fadd_rn(__fmul_rn(ss[hh], 1.0f / kHeadDim), mb.norm_eps));
+  }
+  const uint32_t swz = static_cast<uint32_t>(lane & 7);
+  const uint32_t my_row = rope + static_cast<uint32_t>(lane) * kRopeRowBytes;
+  for (int b = 0; b < 4; ++b) {  // 16 rotary pairs = features 32b .. 32b + 31 of each head
+    const int rr = b >> 1;       // the 64-feature box
+    float4 cs[4], sn[4];
+    if (norm) {
+      cp_async_wait_all();
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        cs[i] = ld_shared_f4(my_row + 16u * i);
+        sn[i] = ld_shared_f4(my_row + 32u * kRopeRowBytes + 16u * i);
+      }
+      __syncwarp();  // every lane has its row: the next block may overwrite
+      if (b + 1 < 4) rope_block_copy(mb, rope, p.M, tok0, b + 1, lane);
+    }
+    if ((b & 1) == 0) {
+      // both staging buffers (one box per head): every earlier store has read its buffer
+      if (lane == 0) tma_store_wait_read();
+      __syncwarp();
+    }
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      if (hh >= nh) break;
+      const uint32_t row = stg + static_cast<uint32_t>(hh) * kWarpStageBytes +
+                           static_cast<uint32_t>(lane) * 128u;
+      for (int c2 = 0; c2 < 2; ++c2) {  // 16 features at a time
+        const int k = 2 * b + c2;       // 16-feature chunk of the head
+        uint32_t v[16];
+        MP_TMEM_LD_32X32B_X16(acc + static_cast<uint32_t>(kHeadDim * hh + 16 * k), v);
+        MP_TMEM_WAIT_LD_REGS16(v);
+        uint32_t w[8];
+        if (norm) {
+          // the head's gains (the same address in every lane: cached after the first tile)
+          const uint4* gp = reinterpret_cast<const uint4*>(mb.norm_w) + 2 * k;
+          const uint4 gg[2] = {__ldg(gp), __ldg(gp + 1)};
+          const uint64_t rn2 = f32x2(rn[hh], rn[hh]);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {  // pair i of the chunk: features 2i, 2i + 1
+            const uint4 gq = gg[i >> 2];
+            const uint32_t gw = (i & 3) == 0 ? gq.x : (i & 3) == 1 ? gq.y : (i & 3) == 2 ? gq.z : gq.w;
+            const int pi = 8 * c2 + i;  // pair within the block
+            const float4 cq = cs[pi >> 2], sq = sn[pi >> 2];
+            const float c = (pi & 3) == 0 ? cq.x : (pi & 3) == 1 ? cq.y : (pi & 3) == 2 ? cq.z : cq.w;
+            const float s = (pi & 3) == 0 ? sq.x : (pi & 3) == 1 ? sq.y : (pi & 3) == 2 ? sq.z : sq.w;
+            // packed pairs: y = bf16(acc), z = bf16((y * rn) * gain), then
+            // (z0 c, z0 s) + (-(z1 s), z1 c), each product and sum rounded once
+            const uint32_t yw = pack_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+            const uint64_t y = f32x2(__uint_as_float(yw << 16), __uint_as_float(yw & 0xFFFF0000u));
+            const uint64_t g = f32x2(__uint_as_float(gw << 16), __uint_as_float(gw & 0xFFFF0000u));
+            const uint32_t zw = f32x2_to_bf16x2(mul_f32x2(mul_f32x2(y, rn2), g));
+            const float z0 = __uint_as_float(zw << 16), z1 = __uint_as_float(zw & 0xFFFF0000u);
+            const uint64_t pz = mul_f32x2(f32x2(z0, z0), f32x2(c, s));
+            const uint64_t qz = mul_f32x2(f32x2(z1, z1), f32x2(-s, c));
+            w[i] = f32x2_to_bf16x2(add_f32x2(pz, qz));
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            w[i] = pack_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+        }
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const uint32_t ch = static_cast<uint32_t>(2 * (k & 3) + e);  // 16-byte chunk of the box row
+          st_shared_v4(row + ((ch ^ swz) << 4), w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+        }
+      }
+    }
+    if ((b & 1) == 1) {
+      for (int hh = 0; hh < nh; ++hh)
+        stage_store(mb, stg + static_cast<uint32_t>(hh) * kWarpStageBytes,
+                    pf0 + kHeadDim * hh + 64 * rr, tok0, lane);
+    }
+  }
+  // the warp's next round writes the buffer the NEWEST store did not read
+  // (buffer 1 with two heads, buffer 0 with one): its own wait then only has
+  // to see the older store done
+  round = nh == 2 ? 2u : 1u;
+}
+
+template <int EPI>
+__device__ void pair_epilogue_rows(const ProjParams& p, const PairSmem& sm, uint32_t tmem, int rank,
+                                   int base_kt) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int q = warp & 3;
+  const bool split = p.part != nullptr;
+  const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+  const uint32_t stg = smem_u32(sm.tiles) + kStagesBytes + static_cast<uint32_t>(q) * 2u * kWarpStageBytes;
+  int8_t* const slots = sm.colslot + 256 * q;
+  float* const scales = sm.colscale + 256 * q;
+  uint32_t tcount = 0;
+  uint32_t round = 0;
+  UnitIter units = units_begin(p);
+  for (int unit = units_next(p, units); unit != kNoUnit; unit = units_next(p, units), ++tcount) {
+    const Tile t = decode_unit(p, unit, rank, base_kt);
+    const ProjMember& mb = unit_member(p, t);
+    // strengths apply to a rank-space pre-GEMM launch and to prologue units
+    const bool scaled = p.scale.enabled && (p.n_pre == 0 || t.mi < 0);
+    const bool ok_mine =
+        mbar_wait(smem_u32(sm.tfull), tcount & 1u, sm.abort, kSiteEpi, p.wait_limit_ns);
+    if (!named_barrier_and(kEpiBarrier, kEpiThreads, ok_mine)) break;
+    tc_fence_after();
+    if (threadIdx.x == 32 * kEpiWarp0) MP_TRACE_MARK(kTrEpiStart, static_cast<int>(tcount));
+    const bool swiglu = EPI == kEpiSwiGlu && t.mi >= 0 && mb.swiglu;
+    const bool heads = EPI == kEpiHeads && t.mi >= 0 && mb.heads;
+    const int pf0 = t.f0 - rank * (swiglu ? kBlockN / 2 : kBlockN);  // the pair's first feature
+    if (scaled && !split) column_slots(p.scale, pf0, lane, slots);
+    for (int j = 0; j < 2; ++j) {
+      if (j < t.n_sub) {
+        const int tok0 = t.t0 + j * t.sub + rank * t.half + q * 32;  // this warp's first token row
+        const uint32_t acc = tmem + lane_base + static_cast<uint32_t>(j * 2 * kBlockN);
+        if (tok0 < p.M) {
+          if (split)
+            rows_split(p, mb, t, acc, pf0, tok0 + lane);
+          else if (swiglu)
+            rows_swiglu(mb, acc, stg, pf0, tok0, lane, round);
+          else if (heads)
+            rows_heads(p, mb, acc, stg, smem_u32(sm.rope) + static_cast<uint32_t>(q) * kRopeWarpBytes,
+                       pf0, tok0, lane, round);
+          else
+            rows_plain(p, mb, acc, stg, pf0, tok0, lane, scaled && !split, slots, scales, round);
+        }
+      }
+      release_accumulator(sm, j);
+    }
+    if (t.mi < 0) {
+      // prologue unit: T rows stored (complete, not just read out of shared
+      // memory), then published to the member tiles waiting for them
+      if (lane == 0) {
+        tma_store_wait_all();
+        fence_proxy_async_global();
+      }
+      named_barrier(kEpiBarrier, kEpiThreads);
+      if (threadIdx.x == 32 * kEpiWarp0) {
+        __threadfence();
+        const int v = -1 - unit;
+        const int rp = v % p.pre_rpairs, tt = v / p.pre_rpairs;
+        st_release_gpu(p.flags + (static_cast<size_t>(rp) * p.pre_ttiles + tt) * 2 + rank, p.epoch);
+      }
+    }
+    if (threadIdx.x == 32 * kEpiWarp0) MP_TRACE_MARK(kTrEpiEnd, static_cast<int>(tcount));
+  }
+  if (lane == 0) tma_store_wait_all();
+}
+
+// ---- feature-row epilogue (64- and 128-token tiles, plain members) ---------
 // Warps 10-13 (TMEM lane quarter q = warp % 4: features 32q .. 32q + 31 of the
 // CTA's 128). Per accumulator, rounds of 64 tokens: two 32-column TMEM loads,
 // lane-pair shuffles into bf16x2 words (features 2i, 2i+1), a [64][64]-feature
@@ -804,9 +1033,8 @@ __device__ void head_round(const ProjParams& p, const ProjMember& mb, const Pair
 // one thread stores both halves with TMA bulk stores (they clip rows past M
 // and columns past N). Two staging buffers alternate. In split-K mode the fp32
 // sums go straight to the partial-sum array instead.
-template <int EPI>
-__device__ void pair_epilogue(const ProjParams& p, const PairSmem& sm, uint32_t tmem, int rank,
-                              int base_kt) {
+__device__ void pair_epilogue_cols(const ProjParams& p, const PairSmem& sm, uint32_t tmem,
+                                   int rank, int base_kt) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int q = warp & 3;
@@ -820,7 +1048,6 @@ __device__ void pair_epilogue(const ProjParams& p, const PairSmem& sm, uint32_t 
   const uint32_t chunk = wi >> 2, in_chunk = (wi & 3u) << 2;
   uint32_t tcount = 0;
   uint32_t round = 0;
-  uint32_t hc = 0;  // head-norm chunks (kEpiHeads)
   UnitIter units = units_begin(p);
   for (int unit = units_next(p, units); unit != kNoUnit; unit = units_next(p, units), ++tcount) {
     const Tile t = decode_unit(p, unit, rank, base_kt);
@@ -867,22 +1094,6 @@ __device__ void pair_epilogue(const ProjParams& p, const PairSmem& sm, uint32_t 
             }
           }
           continue;
-        }
-        if constexpr (EPI == kEpiSwiGlu) {
-          if (mb.swiglu) {
-            swiglu_round(mb, sm, tmem, lane_base, t, j, rr, rounds, tr0, round, q, lane, issuer);
-            ++round;
-            continue;
-          }
-        }
-        if constexpr (EPI == kEpiHeads) {
-          if (t.mi >= 0 && mb.heads) {
-            const float gain = mb.head_norm ? bf16_bits_to_f32(__ldg(mb.norm_w + fl)) : 1.0f;
-            head_round(p, mb, sm, tmem, lane_base, t, j, rr, rounds, tr0, round, hc, q, lane,
-                       issuer, gain);
-            ++round;
-            continue;
-          }
         }
         const uint32_t buf = smem_u32(sm.tiles) + off_epi(static_cast<int>(round & 1u));
         // the stores that last read this buffer have finished reading (issuer waited)
@@ -1018,7 +1229,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   } else if (warp < kEpiWarp0) {
     pair_dequant<NT>(p, sm, rank, base_kt);
   } else {
-    pair_epilogue<EPI>(p, sm, tmem, rank, base_kt);
+    if constexpr (kTokRows<NT>)
+      pair_epilogue_rows<EPI>(p, sm, tmem, rank, base_kt);
+    else
+      pair_epilogue_cols(p, sm, tmem, rank, base_kt);
   }
 
   if (*sm.abort != 0u) {
@@ -1157,11 +1371,16 @@ namespace {
 bool g_configured[64] = {};
 int g_max_pairs[64] = {};
 
+template <int EPI>
+constexpr uint32_t smem_bytes() {
+  return EPI == kEpiHeads ? kHeadsSmemBytes : kPairSmemBytes;
+}
+
 template <int NT, int EPI>
 cudaError_t opt_in_smem() {
   return cudaFuncSetAttribute(proj_pair_kernel<NT, EPI>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(kPairSmemBytes));
+                              static_cast<int>(smem_bytes<EPI>()));
 }
 
 // Opts every instantiation in to its shared memory and finds the CTA pairs
@@ -1206,7 +1425,7 @@ cudaError_t launch_nt(const ProjParams& q, int pairs, bool cooperative, cudaStre
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
     cfg.blockDim = dim3(kPairThreads, 1, 1);
-    cfg.dynamicSmemBytes = kPairSmemBytes;
+    cfg.dynamicSmemBytes = smem_bytes<EPI>();
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;
@@ -1215,7 +1434,7 @@ cudaError_t launch_nt(const ProjParams& q, int pairs, bool cooperative, cudaStre
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, proj_pair_kernel<NT, EPI>, q);
   }
-  proj_pair_kernel<NT, EPI><<<dim3(2 * pairs, 1, 1), kPairThreads, kPairSmemBytes, stream>>>(q);
+  proj_pair_kernel<NT, EPI><<<dim3(2 * pairs, 1, 1), kPairThreads, smem_bytes<EPI>(), stream>>>(q);
   return cudaGetLastError();
 }
 
