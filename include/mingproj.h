@@ -193,6 +193,23 @@ int mp_linear_heads(mp_ctx* ctx, const mp_weight* const* ws, void* const* ys, in
                     const void* x, int64_t ldx, int m, const uint16_t* const* norm_w, float eps,
                     const float* rope_cos, const float* rope_sin, void* stream);
 
+/* The sandwich-norm residual step after to_out and after w2, one pass over
+ * the rows:
+ *   s   = bf16(o * rsqrt(mean(o^2) + eps) * o_gain)         (o != NULL)
+ *   x   = bf16(x + tanh(gate) * s)   (gate != NULL)  or  bf16(x + s)
+ *   nrm = bf16(x * rsqrt(mean(x^2) + eps) * nrm_gain)       (nrm != NULL)
+ * With o == NULL only nrm is computed (x is read, not written). x, o, nrm:
+ * device bf16 [m, h], 16-byte aligned, row strides (elements) >= h and
+ * multiples of 8; o_gain, gate, nrm_gain: device bf16 [h], 16-byte aligned;
+ * h a multiple of 8, at most 8192. The mean is the sum times (1/h).
+ * Replaces: rms of the sub-layer output, gated (gated_residual_tanh) or
+ * resid into the joint stream, and rms into the next sub-layer's input
+ * (src/ming-dit.cc:2096-2101 with :2104, :2256-2261 with the next block's
+ * first rms; src/metal/ming_ops.metal:55-93). */
+int mp_rms_residual(mp_ctx* ctx, void* x, int64_t ldx, const void* o, int64_t ldo,
+                    const void* o_gain, const void* gate, void* nrm, int64_t ldn,
+                    const void* nrm_gain, int h, int m, float eps, void* stream);
+
 /* ---- modulation -------------------------------------------------------- */
 
 /* The adaLN Linears of `n_blocks` modulated blocks, prepared for one

@@ -183,6 +183,42 @@ def modulation(temb_bf16, data, scales, biases, bias, n, k, bits, symmetric=Fals
     return out
 
 
+# ---- the sandwich-norm residual step ------------------------------------------
+
+def _bf16_round32(f: np.ndarray) -> np.ndarray:
+    """float32 values rounded to bf16 (ties to even), back as float32."""
+    return (f32_to_bf16(f).astype(np.uint32) << 16).view(np.float32)
+
+
+def rms_residual(x_bf16, o_bf16, o_gain_bf16, gate_bf16, nrm_gain_bf16, eps: float):
+    """The block's norm + residual sequence after to_out / w2, in float32 with
+    bf16 storage between the steps, as the reference chains them
+    (src/ming-dit.cc:2096-2101, :2256-2261): rms of the sub-layer output with
+    its gain (the rms kernel, :1780-1787), the tanh-gated residual into the
+    joint stream (gated_residual_tanh, src/metal/ming_ops.metal:55-93) or the
+    plain residual, then rms of the joint stream with the next gain (:2104).
+    mean = sum * (1/h); products and sums rounded one at a time. Inputs are
+    bf16 bit arrays ([m, h] rows, [h] vectors; o / gate / nrm gain may be
+    None). Returns (x', nrm) as bf16 bit arrays (nrm None without a gain)."""
+    def f(b):
+        return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+    def rms(v, g):
+        inv_h = np.float32(1.0) / np.float32(v.shape[1])
+        ss = np.sum(v.astype(np.float64) * v.astype(np.float64), axis=1).astype(np.float32)
+        r = (np.float32(1.0) / np.sqrt((ss * inv_h + np.float32(eps)).astype(np.float64)))
+        return _bf16_round32((v * r.astype(np.float32)[:, None]) * f(g)[None, :])
+
+    x = f(x_bf16)
+    if o_bf16 is not None:
+        s = rms(f(o_bf16), o_gain_bf16)
+        if gate_bf16 is not None:
+            s = np.tanh(f(gate_bf16).astype(np.float64)).astype(np.float32)[None, :] * s
+        x = _bf16_round32(x + s)
+    nrm = f32_to_bf16(rms(x, nrm_gain_bf16)) if nrm_gain_bf16 is not None else None
+    return f32_to_bf16(x), nrm
+
+
 def rel_l2(a: np.ndarray, b: np.ndarray) -> float:
     """Relative L2 of `a` against `b` — the measure of every numerical bar in the
     reference (tests/ming-test.h:54-67)."""

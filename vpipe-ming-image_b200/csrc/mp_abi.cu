@@ -25,6 +25,7 @@ int resident_pairs();
 int pick_ntok_pair(int m, int pairs);
 cudaError_t launch_wait_selftest(uint64_t limit_ns, uint32_t* err, cudaStream_t stream);
 cudaError_t launch_mod(const ModParams& p, cudaStream_t stream);
+cudaError_t launch_rms_residual(const RmsResidualParams& p, cudaStream_t stream);
 }  // namespace mp
 
 using mp::ProjParams;
@@ -1231,6 +1232,49 @@ int mp_linear_heads(mp_ctx* c, const mp_weight* const* ws, void* const* ys, int 
   }
   return launch_projections(c, ws, ys, lds, sts, col, rtot, count, x, ldx, m, s, nullptr, nullptr,
                             &hds);
+}
+
+int mp_rms_residual(mp_ctx* c, void* x, int64_t ldx, const void* o, int64_t ldo,
+                    const void* o_gain, const void* gate, void* nrm, int64_t ldn,
+                    const void* nrm_gain, int h, int m, float eps, void* stream) {
+  if (c == nullptr) return MP_EINVAL;
+  if (h <= 0 || h % 8 != 0 || h > mp::kNormMaxH)
+    return fail(c, MP_EINVAL, "h = %d must be a positive multiple of 8, at most %d", h,
+                mp::kNormMaxH);
+  if (m <= 0) return fail(c, MP_EINVAL, "m must be positive (got %d)", m);
+  if (!(eps > 0.0f)) return fail(c, MP_EINVAL, "eps must be positive");
+  auto row_ok = [&](const void* ptr, int64_t ld) {
+    return ptr != nullptr && reinterpret_cast<uintptr_t>(ptr) % 16 == 0 && ld >= h && ld % 8 == 0;
+  };
+  auto vec_ok = [&](const void* ptr) {
+    return ptr != nullptr && reinterpret_cast<uintptr_t>(ptr) % 16 == 0;
+  };
+  if (!row_ok(x, ldx)) return fail(c, MP_EINVAL, "x: NULL, not 16-byte aligned or bad ldx");
+  if (o != nullptr && (!row_ok(o, ldo) || !vec_ok(o_gain)))
+    return fail(c, MP_EINVAL, "o: bad rows or o_gain NULL / not 16-byte aligned");
+  if (o == nullptr && gate != nullptr) return fail(c, MP_EINVAL, "gate without o");
+  if (nrm != nullptr && (!row_ok(nrm, ldn) || !vec_ok(nrm_gain)))
+    return fail(c, MP_EINVAL, "nrm: bad rows or nrm_gain NULL / not 16-byte aligned");
+  if (o == nullptr && nrm == nullptr) return fail(c, MP_EINVAL, "nothing to compute");
+  int rc = use_device(c);
+  if (rc != MP_OK) return rc;
+  mp::RmsResidualParams p;
+  p.x = static_cast<uint16_t*>(x);
+  p.ldx = ldx;
+  p.o = static_cast<const uint16_t*>(o);
+  p.ldo = ldo;
+  p.o_gain = static_cast<const uint16_t*>(o_gain);
+  p.gate = static_cast<const uint16_t*>(gate);
+  p.nrm = static_cast<uint16_t*>(nrm);
+  p.ldn = ldn;
+  p.nrm_gain = static_cast<const uint16_t*>(nrm_gain);
+  p.M = m;
+  p.H = h;
+  p.eps = eps;
+  cudaError_t e = mp::launch_rms_residual(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(c, e, "rms_residual_kernel");
+  c->eng.kernels += 1;
+  return MP_OK;
 }
 
 int mp_linear_swiglu(mp_ctx* c, const mp_weight* w1, const mp_weight* w3, const void* x,

@@ -48,7 +48,8 @@ struct ProjMember {
                       // or bf16 [N, K] (box {64, 128}, SW128)
   CUtensorMap tm_t;   // rank-space intermediate [M, R] bf16 (box {64, sub/2}, SW128)
   CUtensorMap tm_b;   // stacked LoRA B [N, R] bf16 (box {64, 128}, SW128)
-  CUtensorMap tm_y;   // output [M, N] bf16 (box {64, kEpiRows}, SW128)
+  CUtensorMap tm_y;   // output [M, N] bf16 (box {64, 32} for 256/512-token tiles, else
+                      // {64, kEpiRows}; SW128)
   const uint32_t* sb; // per row, per group: bf16 scale (low half) | bf16 bias (high half)
   int32_t N;
   int32_t bits;       // 0 dense bf16, 4 or 8 packed codes
@@ -69,7 +70,7 @@ struct ProjMember {
   const uint32_t* sb3;
   // Attention-head member (heads = 1; N a multiple of kHeadDim): each CTA's
   // 128 features are one head, and tm_y is the head-major output
-  // [N / kHeadDim][M][kHeadDim] bf16 (3-D map, box {64, kEpiRows, 1}). With
+  // [N / kHeadDim][M][kHeadDim] bf16 (3-D map, box {64, 32, 1}). With
   // head_norm = 1 the epilogue first applies the head's RMSNorm (gain
   // norm_w[kHeadDim] bf16, norm_eps) and the interleaved-pair rotary
   // embedding (rope_cos / rope_sin f32 [M][kHeadDim / 2], row = token row).
@@ -160,5 +161,25 @@ struct ModParams {
 };
 
 constexpr int kModMaxTok = 4;
+
+// The sandwich-norm residual step (mp_norm.cu), per token row r < M:
+//   s   = bf16(o * rsqrt(mean(o^2) + eps) * o_gain)          (o != null)
+//   x   = bf16(x + tanh(gate) * s)  (gate != null)  or  bf16(x + s)
+//   nrm = bf16(x * rsqrt(mean(x^2) + eps) * nrm_gain)        (nrm != null)
+// bf16 rows of H (a multiple of 8, at most kNormMaxH); row strides in elements.
+constexpr int kNormMaxH = 8192;
+struct RmsResidualParams {
+  uint16_t* x;
+  int64_t ldx;
+  const uint16_t* o;
+  int64_t ldo;
+  const uint16_t* o_gain;
+  const uint16_t* gate;
+  uint16_t* nrm;
+  int64_t ldn;
+  const uint16_t* nrm_gain;
+  int32_t M, H;
+  float eps;
+};
 
 }  // namespace mp

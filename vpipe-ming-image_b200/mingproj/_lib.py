@@ -50,6 +50,8 @@ SIGNATURES = {
     "mp_linear_swiglu": (C.c_int, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _i32, _vp]),
     "mp_linear_heads": (C.c_int, [_vp, C.POINTER(_vp), C.POINTER(_vp), C.c_int, _vp, _i64, _i32,
                                   C.POINTER(_vp), C.c_float, _vp, _vp, _vp]),
+    "mp_rms_residual": (C.c_int, [_vp, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _vp, C.c_int,
+                                  C.c_int, C.c_float, _vp]),
     "mp_weight_upload": (C.c_int, [_vp, C.POINTER(WeightDesc), _vp, _vp, _vp, C.POINTER(_vp)]),
     "mp_weight_free": (C.c_int, [_vp, _vp]),
     "mp_weight_read_codes": (C.c_int, [_vp, _vp, _vp, C.c_size_t]),

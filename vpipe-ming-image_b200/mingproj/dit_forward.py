@@ -1,8 +1,9 @@
-"""The Ming-Image DiT forward on one GPU, with every block projection and the
-batched adaLN modulation running through the mingproj kernels, and the rest
-of the block (norms, q/k RMSNorm, RoPE, attention, SwiGLU, gated residuals),
-the embedders and the final layer in torch bf16 — the DiT driver around the
-hot path.
+"""The Ming-Image DiT forward on one GPU. Through the mingproj kernels: every
+block projection, the batched adaLN modulation, the q/k head RMSNorm + RoPE
+(q/k/v epilogue, head-major outputs), the SwiGLU (w1/w3 epilogue) and the
+sandwich norms with their gated residuals (one pass each after to_out and
+w2). In torch bf16: the attention, the embedders and the final layer — the
+DiT driver around the hot path.
 
 Follows the reference's MingDitMetal::forward (vpipe-ming-image,
 src/ming-dit.cc:1490-2642): one forward over the REAL rows [image | caption]
@@ -173,7 +174,7 @@ class DitForward:
         p = self.proj.blocks[b].proj
         modulated = mod_idx is not None
         gain1 = nw1[mod_idx, 0] if modulated else t[pre + "attention_norm1.weight"]
-        nrm = self._rms(x, gain1)
+        nrm = self.ctx.rms_residual(x, None, nrm_gain=gain1, eps=cfg.norm_eps)
         qkv = [p["attention.to_q"], p["attention.to_k"], p["attention.to_v"]]
         if hd == 128:
             # one launch: q/k/v head-major, q and k through the head RMSNorm and
@@ -192,23 +193,21 @@ class DitForward:
         att = F.scaled_dot_product_attention(q[None], k[None], v[None])
         a = att[0].transpose(0, 1).reshape(R, H).contiguous()
         o = self.ctx.linear(p["attention.to_out.0"], a)
-        o2 = self._rms(o, t[pre + "attention_norm2.weight"]).float()
-        if modulated:
-            x = (x.float() + torch.tanh(mods[mod_idx, 0, H:2 * H].float()) * o2).to(torch.bfloat16)
-        else:
-            x = (x.float() + o2).to(torch.bfloat16)
+        # one pass: x += [tanh(gate_msa) *] rms(o, norm2); nrm = rms(x, ffn norm)
+        # (x is this block's own copy of the stream: updated in place)
         gain3 = nw3[mod_idx, 0] if modulated else t[pre + "ffn_norm1.weight"]
-        nrm = self._rms(x, gain3)
+        nrm = self.ctx.rms_residual(x, o, t[pre + "attention_norm2.weight"],
+                                    mods[mod_idx, 0, H:2 * H] if modulated else None,
+                                    gain3, eps=cfg.norm_eps)
         # gate and up projections with the SwiGLU in their epilogue (one launch):
         # h = bf16(silu(g) * u) of the bf16 gate and up values, as gpu_ff computes it
         ld = (FF + 7) // 8 * 8
         h = torch.empty((R, ld), dtype=torch.bfloat16, device=x.device)
         self.ctx.linear_swiglu(p["feed_forward.w1"], p["feed_forward.w3"], nrm, out=h[:, :FF])
         f = self.ctx.linear(p["feed_forward.w2"], h[:, :FF])
-        f2 = self._rms(f, t[pre + "ffn_norm2.weight"]).float()
-        if modulated:
-            return (x.float() + torch.tanh(mods[mod_idx, 0, 3 * H:].float()) * f2).to(torch.bfloat16)
-        return (x.float() + f2).to(torch.bfloat16)
+        self.ctx.rms_residual(x, f, t[pre + "ffn_norm2.weight"],
+                              mods[mod_idx, 0, 3 * H:] if modulated else None, eps=cfg.norm_eps)
+        return x
 
     # ---- the forward -------------------------------------------------------
     @torch.no_grad()

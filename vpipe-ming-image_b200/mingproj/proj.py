@@ -301,6 +301,34 @@ class Context:
                 t.record_stream(stream)
         return outs
 
+    def rms_residual(self, x: torch.Tensor, o: torch.Tensor | None, o_gain=None, gate=None,
+                     nrm_gain=None, eps: float = 1e-5, nrm: torch.Tensor | None = None,
+                     stream=None) -> torch.Tensor | None:
+        """The sandwich-norm residual step, one kernel: with `o`, x (bf16 [m, h],
+        updated IN PLACE) += [tanh(gate) *] rms(o, o_gain); with `nrm_gain`,
+        returns rms(x, nrm_gain) (into `nrm` when given). Gains and gate: bf16
+        [h] on the device."""
+        m, h = x.shape
+        vecs = []
+        for v in (o_gain, gate, nrm_gain):
+            if v is None:
+                vecs.append(None)
+            else:
+                v = v.to(torch.bfloat16).contiguous()
+                vecs.append(v)
+        if nrm_gain is not None and nrm is None:
+            nrm = _alloc_out(m, h, x.device)
+        self._check(self.lib.mp_rms_residual(
+            self.h, _ptr(x), x.stride(0), _ptr(o), o.stride(0) if o is not None else 0,
+            _ptr(vecs[0]), _ptr(vecs[1]), _ptr(nrm) if nrm_gain is not None else None,
+            nrm.stride(0) if nrm_gain is not None else 0, _ptr(vecs[2]), h, m, float(eps),
+            _stream_handle(stream)))
+        if stream is not None:
+            for v in vecs:
+                if v is not None:
+                    v.record_stream(stream)
+        return nrm if nrm_gain is not None else None
+
     def linear_lora_static(self, w: Weight, x: torch.Tensor, a: torch.Tensor, b: torch.Tensor,
                            strength: float, out: torch.Tensor | None = None,
                            stream=None) -> torch.Tensor:
