@@ -26,6 +26,7 @@ int pick_ntok_pair(int m, int pairs);
 cudaError_t launch_wait_selftest(uint64_t limit_ns, uint32_t* err, cudaStream_t stream);
 cudaError_t launch_mod(const ModParams& p, cudaStream_t stream);
 cudaError_t launch_rms_residual(const RmsResidualParams& p, cudaStream_t stream);
+cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream);
 }  // namespace mp
 
 using mp::ProjParams;
@@ -1232,6 +1233,48 @@ int mp_linear_heads(mp_ctx* c, const mp_weight* const* ws, void* const* ys, int 
   }
   return launch_projections(c, ws, ys, lds, sts, col, rtot, count, x, ldx, m, s, nullptr, nullptr,
                             &hds);
+}
+
+int mp_attention(mp_ctx* c, const void* q, const void* k, const void* v, int s, int nh,
+                 float scale, void* o, int64_t ldo, void* stream) {
+  if (c == nullptr) return MP_EINVAL;
+  if (s <= 0 || nh <= 0) return fail(c, MP_EINVAL, "s and nh must be positive (%d, %d)", s, nh);
+  if (!(scale > 0.0f)) return fail(c, MP_EINVAL, "scale must be positive");
+  for (const void* t : {q, k, v, static_cast<const void*>(o)})
+    if (t == nullptr || reinterpret_cast<uintptr_t>(t) % 16 != 0)
+      return fail(c, MP_EINVAL, "q, k, v and o must be non-NULL and 16-byte aligned");
+  if (ldo < static_cast<int64_t>(nh) * mp::kHeadDim || ldo % 8 != 0)
+    return fail(c, MP_EINVAL, "ldo must be >= 128 * nh and a multiple of 8 (got %lld)",
+                static_cast<long long>(ldo));
+  int rc = use_device(c);
+  if (rc != MP_OK) return rc;
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(c, MP_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  mp::AttnParams p;
+  std::memset(&p, 0, sizeof(p));
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(mp::kHeadDim), static_cast<cuuint64_t>(s),
+                              static_cast<cuuint64_t>(nh)};
+  const cuuint64_t strides[2] = {mp::kHeadDim * 2, static_cast<cuuint64_t>(s) * mp::kHeadDim * 2};
+  const cuuint32_t box[3] = {64, 128, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUtensorMap* maps[3] = {&p.tm_q, &p.tm_k, &p.tm_v};
+  const void* srcs[3] = {q, k, v};
+  for (int i = 0; i < 3; ++i)
+    if (fn(maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(srcs[i]), dims, strides,
+           box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return fail(c, MP_ECUDA, "tensor map encode failed (attention operand %d)", i);
+  p.o = static_cast<uint16_t*>(o);
+  p.ldo = ldo;
+  p.S = s;
+  p.NH = nh;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.wait_limit_ns = c->wait_limit_ns;
+  p.err = c->err_word;
+  cudaError_t e = mp::launch_attention(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(c, e, "attn_kernel");
+  c->eng.kernels += 1;
+  return MP_OK;
 }
 
 int mp_rms_residual(mp_ctx* c, void* x, int64_t ldx, const void* o, int64_t ldo,

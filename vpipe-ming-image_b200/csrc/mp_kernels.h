@@ -168,6 +168,22 @@ constexpr int kModMaxTok = 4;
 //   nrm = bf16(x * rsqrt(mean(x^2) + eps) * nrm_gain)        (nrm != null)
 // bf16 rows of H (a multiple of 8, at most kNormMaxH); row strides in elements.
 constexpr int kNormMaxH = 8192;
+
+// Non-causal attention over head-major q, k, v (mp_attn.cu): for head h and
+// query row i < S,  o[i, 128h .. 128h + 127] = softmax(scale · q_i · K^T) · V.
+// tm_q / tm_k / tm_v: bf16 [NH][S][128] as 3-D maps {128, S, NH}, box
+// {64, 128, 1}, 128-byte swizzle (rows past S read zeros). o: bf16 [S][ldo].
+struct AttnParams {
+  CUtensorMap tm_q;
+  CUtensorMap tm_k;
+  CUtensorMap tm_v;
+  uint16_t* o;
+  int64_t ldo;
+  int32_t S, NH;
+  float scale_log2;  // softmax scale · log2(e)
+  uint64_t wait_limit_ns;
+  uint32_t* err;
+};
 struct RmsResidualParams {
   uint16_t* x;
   int64_t ldx;

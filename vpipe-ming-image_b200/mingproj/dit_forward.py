@@ -1,9 +1,9 @@
 """The Ming-Image DiT forward on one GPU. Through the mingproj kernels: every
 block projection, the batched adaLN modulation, the q/k head RMSNorm + RoPE
-(q/k/v epilogue, head-major outputs), the SwiGLU (w1/w3 epilogue) and the
-sandwich norms with their gated residuals (one pass each after to_out and
-w2). In torch bf16: the attention, the embedders and the final layer — the
-DiT driver around the hot path.
+(q/k/v epilogue, head-major outputs), the attention (head dim 128), the
+SwiGLU (w1/w3 epilogue) and the sandwich norms with their gated residuals
+(one pass each after to_out and w2). In torch bf16: the embedders and the
+final layer — the DiT driver around the hot path.
 
 Follows the reference's MingDitMetal::forward (vpipe-ming-image,
 src/ming-dit.cc:1490-2642): one forward over the REAL rows [image | caption]
@@ -190,8 +190,12 @@ class DitForward:
             k = self._rope(self._rms(k.view(R, nh, hd), t[pre + "attention.norm_k.weight"]),
                            cos, sin).transpose(0, 1)
             v = v.view(R, nh, hd).transpose(0, 1)
-        att = F.scaled_dot_product_attention(q[None], k[None], v[None])
-        a = att[0].transpose(0, 1).reshape(R, H).contiguous()
+        if hd == 128:
+            # the tcgen05 attention kernel, writing the token-major to_out input
+            a = self.ctx.attention(q, k, v)
+        else:
+            att = F.scaled_dot_product_attention(q[None], k[None], v[None])
+            a = att[0].transpose(0, 1).reshape(R, H).contiguous()
         o = self.ctx.linear(p["attention.to_out.0"], a)
         # one pass: x += [tanh(gate_msa) *] rms(o, norm2); nrm = rms(x, ffn norm)
         # (x is this block's own copy of the stream: updated in place)

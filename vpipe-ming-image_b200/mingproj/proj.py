@@ -20,6 +20,7 @@ into libmingproj.so. There is no CPU path here.
 from __future__ import annotations
 
 import ctypes as C
+import math
 from dataclasses import dataclass
 
 import numpy as np
@@ -300,6 +301,23 @@ class Context:
             for t in keep:
                 t.record_stream(stream)
         return outs
+
+    def attention(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                  scale: float | None = None, out: torch.Tensor | None = None,
+                  stream=None) -> torch.Tensor:
+        """Non-causal attention over head-major q, k, v (bf16 [nh, s, 128], as
+        linear_heads returns them); returns token-major bf16 [s, nh * 128]."""
+        nh, s, hd = q.shape
+        if hd != 128 or k.shape != q.shape or v.shape != q.shape:
+            raise ValueError(f"q, k, v must be [nh, s, 128] alike (got {tuple(q.shape)}, "
+                             f"{tuple(k.shape)}, {tuple(v.shape)})")
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        if out is None:
+            out = torch.empty((s, nh * 128), dtype=torch.bfloat16, device=q.device)
+        sc = float(scale) if scale is not None else 1.0 / math.sqrt(hd)
+        self._check(self.lib.mp_attention(self.h, _ptr(q), _ptr(k), _ptr(v), s, nh, sc, _ptr(out),
+                                          out.stride(0), _stream_handle(stream)))
+        return out
 
     def rms_residual(self, x: torch.Tensor, o: torch.Tensor | None, o_gain=None, gate=None,
                      nrm_gain=None, eps: float = 1e-5, nrm: torch.Tensor | None = None,
