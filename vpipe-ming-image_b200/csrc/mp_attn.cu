@@ -6,17 +6,24 @@
 // the reference's run_attn over the joint rows of a block (src/ming-dit.cc:
 // 1905-2039; q, k and v as its tr_rope / transpose leave them). One CTA per
 // (128-query tile, head), single-CTA MMAs (cta_group::1, M = 128):
-//   * warp 0 loads Q once and K_j, V_j (128 keys each) per step with TMA into
-//     two-stage rings (K and V released separately, K as soon as S_j is done);
+//   * warp 0 loads Q once and K_j (128 keys) per step, warp 6 loads V_j, with
+//     TMA into three-stage rings (K released as soon as S_j is done, V once
+//     P_j · V_j is);
 //   * warp 1 issues S_j = Q · K_j^T into one of two TMEM S buffers, then
-//     O_{j-1} = P_{j-1} · V_{j-1} into one of two TMEM O buffers (V as an
-//     MN-major operand straight from its [keys][head dim] tile);
-//   * warps 2-5 (thread = query row, TMEM lane) run the online softmax: a
-//     first pass over S_j for the row maximum, a second for p = 2^(s·c − m)
-//     (c = scale·log2 e), the row sum and P_j in bf16 (the PV operand, stored
-//     128-byte swizzled), and fold each finished O_t into registers
-//     (o = o · 2^(m_{t-1} − m_t) + O_t) once its buffer is complete;
-//   * the epilogue divides by the row sum and stores bf16 rows token-major.
+//     O += P_{j-1} · V_{j-1} into the TMEM accumulator O, with P read from
+//     TMEM and V as an MN-major operand straight from its [keys][head dim]
+//     tile;
+//   * warps 2-5 (thread = query row, TMEM lane) read S_j into registers once
+//     (freeing its buffer for S_{j+2}), and write P_j = 2^(s·c − m) in bf16
+//     (c = scale·log2 e) into one of two TMEM P buffers with the
+//     row sum, in packed f32x2 arithmetic, three of every eight exponential
+//     pairs on the FMA pipe and the rest on the MUFU. The exponent base m is the row maximum seen when it was last
+//     raised: only when a tile's maximum exceeds it by more than 8 (a factor
+//     256) does the warp rescale its rows of O in TMEM (after the previous
+//     P·V has landed) and move m up; otherwise p <= 256 and O, the row sum
+//     and the final quotient stay exact relative to the older m;
+//   * after the last step the rows of O are divided by their sums and stored
+//     bf16 token-major.
 // S and P are double-buffered, so the softmax of tile j overlaps the MMAs
 // of tiles j + 1 (S) and j - 1 (PV). Keys past S are masked (their tiles read
 // zeros); rows past S are computed and not stored. Every wait is bounded;
@@ -33,30 +40,32 @@ namespace {
 constexpr int kAttnTile = 128;                          // query rows per CTA, keys per step
 constexpr uint32_t kAttnBlk = 128 * 64 * 2;             // [128 rows][64 bf16], one TMA box
 constexpr uint32_t kAttnOp = 2 * kAttnBlk;              // 128 rows x 128 bf16
+constexpr int kKvStages = 3;
 constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffK = kOffQ + kAttnOp;             // K ring [2]
-constexpr uint32_t kOffV = kOffK + 2 * kAttnOp;         // V ring [2]
-constexpr uint32_t kOffP = kOffV + 2 * kAttnOp;         // P [2]
-constexpr uint32_t kAttnTiles = kOffP + 2 * kAttnOp;    // 224 KB
+constexpr uint32_t kOffK = kOffQ + kAttnOp;             // K ring
+constexpr uint32_t kOffV = kOffK + kKvStages * kAttnOp; // V ring
+constexpr uint32_t kAttnTiles = kOffV + kKvStages * kAttnOp;  // 224 KB
 constexpr uint32_t kAttnSmem = kAttnTiles + 1024 + 256;
 static_assert(kAttnSmem <= 232448, "shared memory per CTA");
-constexpr int kAttnThreads = 192;
-constexpr uint32_t kAttnCols = 512;                     // S[0] S[1] O[0] O[1], 128 columns each
+constexpr int kAttnThreads = 224;  // warp 0 Q+K, 1 MMA, 2-5 softmax, 6 V
+constexpr uint32_t kAttnCols = 512;  // S[0] S[1] (128 each), O (128), P[0] P[1] (64 each)
+constexpr uint32_t kColO = 256;      // TMEM column of the O accumulator
+constexpr uint32_t kColP = 384;      // TMEM columns of P[0] (P[1] 64 further): bf16 pairs
+constexpr float kRescaleLog2 = 8.0f;                    // move m only when a max exceeds it by this
 
 enum : uint32_t { kAttnSiteWait = 0x2100u, kAttnSiteDrain = 0x2200u };
 
 struct AttnSmem {
   uint8_t* tiles;
   uint64_t* q_full;
-  uint64_t* k_full;   // [2]
-  uint64_t* k_empty;  // [2]
-  uint64_t* v_full;   // [2]
-  uint64_t* v_empty;  // [2]
+  uint64_t* k_full;   // [kKvStages]
+  uint64_t* k_empty;  // [kKvStages]
+  uint64_t* v_full;   // [kKvStages]
+  uint64_t* v_empty;  // [kKvStages]
   uint64_t* s_full;   // [2]
   uint64_t* s_free;   // [2]
   uint64_t* p_full;   // [2]
-  uint64_t* o_full;   // [2]
-  uint64_t* o_free;   // [2]
+  uint64_t* o_done;   // [2] P_t · V_t (t % 2) accumulated: P buffer free, O includes it
   uint64_t* drain;
   uint32_t* tmem_slot;
   volatile uint32_t* abort;
@@ -69,16 +78,15 @@ __device__ __forceinline__ AttnSmem carve_attn(uint8_t* raw) {
   uint64_t* b = reinterpret_cast<uint64_t*>(s.tiles + kAttnTiles);
   s.q_full = b;
   s.k_full = b + 1;
-  s.k_empty = b + 3;
-  s.v_full = b + 5;
-  s.v_empty = b + 7;
-  s.s_full = b + 9;
-  s.s_free = b + 11;
-  s.p_full = b + 13;
-  s.o_full = b + 15;
-  s.o_free = b + 17;
-  s.drain = b + 19;
-  s.tmem_slot = reinterpret_cast<uint32_t*>(b + 20);
+  s.k_empty = b + 4;
+  s.v_full = b + 7;
+  s.v_empty = b + 10;
+  s.s_full = b + 13;
+  s.s_free = b + 15;
+  s.p_full = b + 17;
+  s.o_done = b + 19;
+  s.drain = b + 21;
+  s.tmem_slot = reinterpret_cast<uint32_t*>(b + 22);
   s.abort = s.tmem_slot + 1;
   return s;
 }
@@ -112,30 +120,63 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// 2^x for a packed pair on the FMA pipe (offloads the MUFU): the Cody-Waite
+// split x = i + f with i = round(x) (the 1.5 * 2^23 rounding constant) and
+// f in [-0.5, 0.5], a cubic for 2^f (coefficients fitted for this kernel by
+// minimizing the maximum relative error on [-0.5, 0.5]: 7.5e-5, far below the
+// bf16 rounding of P), and 2^i added to the exponent bits. x is clamped at
+// -126 (2^-126 stands in for smaller values; masked keys never get here).
+__device__ __forceinline__ uint64_t ex2_poly2(float x0, float x1) {
+  const uint64_t x = f32x2(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+  const uint64_t magic = f32x2(12582912.0f, 12582912.0f);
+  const uint64_t t = add_f32x2(x, magic);
+  const uint64_t r = add_f32x2(t, f32x2(-12582912.0f, -12582912.0f));
+  const uint64_t f = fma_f32x2(r, f32x2(-1.0f, -1.0f), x);  // x - r, exact
+  uint64_t q = fma_f32x2(f32x2(0.05517144f, 0.05517144f), f, f32x2(0.24261071f, 0.24261071f));
+  q = fma_f32x2(q, f, f32x2(0.69326097f, 0.69326097f));
+  q = fma_f32x2(q, f, f32x2(0.99992812f, 0.99992812f));
+  const uint32_t lo = static_cast<uint32_t>(q) + (static_cast<uint32_t>(t) << 23);
+  const uint32_t hi = static_cast<uint32_t>(q >> 32) + (static_cast<uint32_t>(t >> 32) << 23);
+  return (static_cast<uint64_t>(hi) << 32) | lo;
+}
+
 __device__ __forceinline__ bool attn_wait(const AttnSmem& sm, uint64_t* bar, uint32_t parity,
                                           uint64_t limit) {
   return mbar_wait(smem_u32(bar), parity, sm.abort, kAttnSiteWait, limit);
 }
 
-// Warp 0, one thread.
-__device__ void attn_producer(const AttnParams& p, const AttnSmem& sm, int q0, int head, int n) {
+// Warp 0, one thread: Q, then the K ring.
+__device__ void attn_producer_k(const AttnParams& p, const AttnSmem& sm, int q0, int head, int n) {
   const uint32_t base = smem_u32(sm.tiles);
   mbar_arrive_expect_tx(smem_u32(sm.q_full), kAttnOp);
   tma_load_3d(base + kOffQ, &p.tm_q, smem_u32(sm.q_full), 0, q0, head);
   tma_load_3d(base + kOffQ + kAttnBlk, &p.tm_q, smem_u32(sm.q_full), 64, q0, head);
   for (int j = 0; j < n; ++j) {
-    const int b = j & 1;
-    const uint32_t free_ph = static_cast<uint32_t>((j - 2) >> 1) & 1u;
-    if (j >= 2 && !attn_wait(sm, &sm.k_empty[b], free_ph, p.wait_limit_ns)) return;
-    const uint32_t kb = base + kOffK + static_cast<uint32_t>(b) * kAttnOp;
-    mbar_arrive_expect_tx(smem_u32(&sm.k_full[b]), kAttnOp);
-    tma_load_3d(kb, &p.tm_k, smem_u32(&sm.k_full[b]), 0, j * kAttnTile, head);
-    tma_load_3d(kb + kAttnBlk, &p.tm_k, smem_u32(&sm.k_full[b]), 64, j * kAttnTile, head);
-    if (j >= 2 && !attn_wait(sm, &sm.v_empty[b], free_ph, p.wait_limit_ns)) return;
-    const uint32_t vb = base + kOffV + static_cast<uint32_t>(b) * kAttnOp;
-    mbar_arrive_expect_tx(smem_u32(&sm.v_full[b]), kAttnOp);
-    tma_load_3d(vb, &p.tm_v, smem_u32(&sm.v_full[b]), 0, j * kAttnTile, head);
-    tma_load_3d(vb + kAttnBlk, &p.tm_v, smem_u32(&sm.v_full[b]), 64, j * kAttnTile, head);
+    const int st = j % kKvStages;
+    if (j >= kKvStages &&
+        !attn_wait(sm, &sm.k_empty[st], static_cast<uint32_t>(j / kKvStages - 1) & 1u,
+                   p.wait_limit_ns))
+      return;
+    const uint32_t kb = base + kOffK + static_cast<uint32_t>(st) * kAttnOp;
+    mbar_arrive_expect_tx(smem_u32(&sm.k_full[st]), kAttnOp);
+    tma_load_3d(kb, &p.tm_k, smem_u32(&sm.k_full[st]), 0, j * kAttnTile, head);
+    tma_load_3d(kb + kAttnBlk, &p.tm_k, smem_u32(&sm.k_full[st]), 64, j * kAttnTile, head);
+  }
+}
+
+// Warp 6, one thread: the V ring.
+__device__ void attn_producer_v(const AttnParams& p, const AttnSmem& sm, int head, int n) {
+  const uint32_t base = smem_u32(sm.tiles);
+  for (int j = 0; j < n; ++j) {
+    const int st = j % kKvStages;
+    if (j >= kKvStages &&
+        !attn_wait(sm, &sm.v_empty[st], static_cast<uint32_t>(j / kKvStages - 1) & 1u,
+                   p.wait_limit_ns))
+      return;
+    const uint32_t vb = base + kOffV + static_cast<uint32_t>(st) * kAttnOp;
+    mbar_arrive_expect_tx(smem_u32(&sm.v_full[st]), kAttnOp);
+    tma_load_3d(vb, &p.tm_v, smem_u32(&sm.v_full[st]), 0, j * kAttnTile, head);
+    tma_load_3d(vb + kAttnBlk, &p.tm_v, smem_u32(&sm.v_full[st]), 64, j * kAttnTile, head);
   }
 }
 
@@ -147,38 +188,38 @@ __device__ void attn_mma(const AttnParams& p, const AttnSmem& sm, uint32_t tmem,
   bool ok = attn_wait(sm, sm.q_full, 0, p.wait_limit_ns);
   auto issue_s = [&](int j) -> bool {
     const int b = j & 1;
-    if (!attn_wait(sm, &sm.k_full[b], static_cast<uint32_t>(j >> 1) & 1u, p.wait_limit_ns))
+    const int st = j % kKvStages;
+    if (!attn_wait(sm, &sm.k_full[st], static_cast<uint32_t>(j / kKvStages) & 1u, p.wait_limit_ns))
       return false;
     if (j >= 2 &&
         !attn_wait(sm, &sm.s_free[b], static_cast<uint32_t>((j - 2) >> 1) & 1u, p.wait_limit_ns))
       return false;
     tc_fence_after();
-    const uint32_t kt = base + kOffK + static_cast<uint32_t>(b) * kAttnOp;
+    const uint32_t kt = base + kOffK + static_cast<uint32_t>(st) * kAttnOp;
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk)
       umma_ss(tmem + static_cast<uint32_t>(b) * 128u, kmajor_desc(base + kOffQ, kk),
               kmajor_desc(kt, kk), idesc_qk, kk > 0 ? 1u : 0u);
     umma_commit(smem_u32(&sm.s_full[b]));
-    umma_commit(smem_u32(&sm.k_empty[b]));
+    umma_commit(smem_u32(&sm.k_empty[st]));
     return true;
   };
   auto issue_pv = [&](int t) -> bool {
     const int b = t & 1;
-    const uint32_t ph = static_cast<uint32_t>(t >> 1) & 1u;
-    if (!attn_wait(sm, &sm.v_full[b], ph, p.wait_limit_ns)) return false;
-    if (!attn_wait(sm, &sm.p_full[b], ph, p.wait_limit_ns)) return false;
-    if (t >= 2 &&
-        !attn_wait(sm, &sm.o_free[b], static_cast<uint32_t>((t - 2) >> 1) & 1u, p.wait_limit_ns))
+    const int st = t % kKvStages;
+    if (!attn_wait(sm, &sm.v_full[st], static_cast<uint32_t>(t / kKvStages) & 1u, p.wait_limit_ns))
+      return false;
+    if (!attn_wait(sm, &sm.p_full[b], static_cast<uint32_t>(t >> 1) & 1u, p.wait_limit_ns))
       return false;
     tc_fence_after();
-    const uint32_t pt = base + kOffP + static_cast<uint32_t>(b) * kAttnOp;
-    const uint32_t vt = base + kOffV + static_cast<uint32_t>(b) * kAttnOp;
+    const uint32_t vt = base + kOffV + static_cast<uint32_t>(st) * kAttnOp;
+    // A = P_t from TMEM: 16 keys (8 columns of bf16 pairs) per step
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk)
-      umma_ss(tmem + 256u + static_cast<uint32_t>(b) * 128u, kmajor_desc(pt, kk), vmn_desc(vt, kk),
-              idesc_pv, kk > 0 ? 1u : 0u);
-    umma_commit(smem_u32(&sm.o_full[b]));
-    umma_commit(smem_u32(&sm.v_empty[b]));
+      umma_ts(tmem + kColO, tmem + kColP + static_cast<uint32_t>(b) * 64u + static_cast<uint32_t>(kk) * 8u,
+              vmn_desc(vt, kk), idesc_pv, (t > 0 || kk > 0) ? 1u : 0u);
+    umma_commit(smem_u32(&sm.o_done[b]));
+    umma_commit(smem_u32(&sm.v_empty[st]));
     return true;
   };
   if (ok) ok = issue_s(0);
@@ -203,116 +244,153 @@ __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t t
   const int quarter = warp & 3;
   const int row = quarter * 32 + lane;
   const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-  const uint32_t swz = static_cast<uint32_t>(row & 7);
-  const uint32_t pbase = smem_u32(sm.tiles) + kOffP + static_cast<uint32_t>(row) * 128u;
   const float c = p.scale_log2;
-  float o[128];
-#pragma unroll
-  for (int d = 0; d < 128; ++d) o[d] = 0.0f;
-  float m_run = -INFINITY, l = 0.0f;
-  float a_m1 = 0.0f, a_m2 = 0.0f;  // alpha of tiles j-1 and j-2
-  bool ok = true;
-  // o = o * alpha + O_t (buffer t % 2)
-  auto fold = [&](int t, float alpha) -> bool {
-    const int b = t & 1;
-    bool w = attn_wait(sm, &sm.o_full[b], static_cast<uint32_t>(t >> 1) & 1u, p.wait_limit_ns);
-    if (!__all_sync(0xFFFFFFFFu, w)) return false;
-    tc_fence_after();
-#pragma unroll
-    for (int c4 = 0; c4 < 4; ++c4) {
-      uint32_t v[32];
-      MP_TMEM_LD_32X32B_X32(tmem + lane_base + 256u + static_cast<uint32_t>(b) * 128u +
-                                static_cast<uint32_t>(32 * c4),
-                            v);
-      MP_TMEM_WAIT_LD_REGS32(v);
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj) o[32 * c4 + jj] = fmaf(o[32 * c4 + jj], alpha, __uint_as_float(v[jj]));
-    }
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(&sm.o_free[b]));
-    return true;
-  };
-  for (int j = 0; j < n && ok; ++j) {
+  float m_used = -INFINITY, l = 0.0f;
+  for (int j = 0; j < n; ++j) {
     const int b = j & 1;
     bool w = attn_wait(sm, &sm.s_full[b], static_cast<uint32_t>(j >> 1) & 1u, p.wait_limit_ns);
-    if (!__all_sync(0xFFFFFFFFu, w)) {
-      ok = false;
-      break;
-    }
+    if (!__all_sync(0xFFFFFFFFu, w)) return;
     tc_fence_after();
     const uint32_t sb = tmem + lane_base + static_cast<uint32_t>(b) * 128u;
-    const int valid = p.S - j * kAttnTile;  // keys of this tile below S (>= 1)
-    // pass 1: the row maximum
-    float mx = -INFINITY;
-#pragma unroll
-    for (int c4 = 0; c4 < 4; ++c4) {
-      uint32_t v[32];
-      MP_TMEM_LD_32X32B_X32(sb + static_cast<uint32_t>(32 * c4), v);
-      MP_TMEM_WAIT_LD_REGS32(v);
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj)
-        if (32 * c4 + jj < valid) mx = fmaxf(mx, __uint_as_float(v[jj]));
-    }
-    const float m_new = fmaxf(m_run, mx * c);
-    const float alpha = ex2(m_run - m_new);
-    m_run = m_new;
-    // P buffer b is free once O_{j-2} is complete; fold it first
-    if (j >= 2 && !fold(j - 2, a_m2)) {
-      ok = false;
-      break;
-    }
-    // pass 2: p = 2^(s c - m), the row sum, P_j in bf16 (128-byte swizzled rows)
-    float sum = 0.0f;
-    const uint32_t prow = pbase + static_cast<uint32_t>(b) * kAttnOp;
-#pragma unroll
-    for (int c4 = 0; c4 < 4; ++c4) {
-      uint32_t v[32];
-      MP_TMEM_LD_32X32B_X32(sb + static_cast<uint32_t>(32 * c4), v);
-      MP_TMEM_WAIT_LD_REGS32(v);
-      uint32_t w16[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int key = 32 * c4 + 2 * i;
-        const float p0 = key < valid ? ex2(fmaf(__uint_as_float(v[2 * i]), c, -m_new)) : 0.0f;
-        const float p1 = key + 1 < valid ? ex2(fmaf(__uint_as_float(v[2 * i + 1]), c, -m_new)) : 0.0f;
-        sum += p0 + p1;
-        w16[i] = pack_bf16x2(p0, p1);
-      }
-      const uint32_t blk = prow + static_cast<uint32_t>(c4 >> 1) * kAttnBlk;
-#pragma unroll
-      for (int i4 = 0; i4 < 4; ++i4) {
-        const uint32_t ch = static_cast<uint32_t>((c4 & 1) * 4 + i4);
-        st_shared_v4(blk + ((ch ^ swz) << 4), w16[4 * i4], w16[4 * i4 + 1], w16[4 * i4 + 2],
-                     w16[4 * i4 + 3]);
-      }
-    }
-    l = l * alpha + sum;
-    tc_fence_before();  // S_j read out
-    fence_proxy_async_shared();
+    uint32_t sv[128];
+    uint32_t* const s1 = sv + 32;
+    uint32_t* const s2 = sv + 64;
+    uint32_t* const s3 = sv + 96;
+    MP_TMEM_LD_32X32B_X32(sb, sv);
+    MP_TMEM_LD_32X32B_X32(sb + 32u, s1);
+    MP_TMEM_LD_32X32B_X32(sb + 64u, s2);
+    MP_TMEM_LD_32X32B_X32(sb + 96u, s3);
+    MP_TMEM_WAIT_LD_REGS32(sv);
+    MP_TMEM_WAIT_LD_REGS32(s1);
+    MP_TMEM_WAIT_LD_REGS32(s2);
+    MP_TMEM_WAIT_LD_REGS32(s3);
+    tc_fence_before();  // S_j is in registers: its buffer may take S_{j+2}
     __syncwarp();
-    if (lane == 0) {
-      mbar_arrive(smem_u32(&sm.s_free[b]));
-      mbar_arrive(smem_u32(&sm.p_full[b]));
+    if (lane == 0) mbar_arrive(smem_u32(&sm.s_free[b]));
+    const int valid = p.S - j * kAttnTile;  // keys of this tile below S (>= 1)
+    const bool full = valid >= kAttnTile;   // the same in every thread of the CTA
+    float mx;
+    if (full) {
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int i = 0; i < 128; i += 8) {
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+          m4[a] = max3_f32(m4[a], __uint_as_float(sv[i + 2 * a]), __uint_as_float(sv[i + 2 * a + 1]));
+      }
+      mx = max3_f32(m4[0], m4[1], fmaxf(m4[2], m4[3]));
+    } else {
+      mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 128; ++i)
+        if (i < valid) mx = fmaxf(mx, __uint_as_float(sv[i]));
     }
-    a_m2 = a_m1;
-    a_m1 = alpha;
+    const float mc = mx * c;
+    if (j == 0) {
+      m_used = mc;
+    } else {
+      const bool need = mc > m_used + kRescaleLog2;
+      if (__any_sync(0xFFFFFFFFu, need)) {
+        // O holds P_0..P_{j-1} · V relative to m_used: once P_{j-1} · V has
+        // landed, scale this warp's rows to the new base (1 for rows that keep it)
+        const int t = j - 1;
+        w = attn_wait(sm, &sm.o_done[t & 1], static_cast<uint32_t>(t >> 1) & 1u, p.wait_limit_ns);
+        if (!__all_sync(0xFFFFFFFFu, w)) return;
+        tc_fence_after();
+        const float alpha = need ? ex2(m_used - mc) : 1.0f;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t ov[32];
+          const uint32_t oa = tmem + lane_base + kColO + static_cast<uint32_t>(32 * c4);
+          MP_TMEM_LD_32X32B_X32(oa, ov);
+          MP_TMEM_WAIT_LD_REGS32(ov);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+          MP_TMEM_ST_32X32B_X32(oa, ov);
+        }
+        tmem_wait_st();
+        l *= alpha;
+        if (need) m_used = mc;
+      }
+    }
+    // P buffer b is free once P_{j-2} · V has been accumulated
+    if (j >= 2) {
+      const int t = j - 2;
+      w = attn_wait(sm, &sm.o_done[b], static_cast<uint32_t>(t >> 1) & 1u, p.wait_limit_ns);
+      if (!__all_sync(0xFFFFFFFFu, w)) return;
+    }
+    float sum = 0.0f;
+    uint64_t acc2[2] = {0ull, 0ull};  // packed partial row sums (full tiles)
+    const uint64_t c2 = f32x2(c, c), nm2 = f32x2(-m_used, -m_used);
+    const uint32_t pcol = tmem + lane_base + kColP + static_cast<uint32_t>(b) * 64u;
+#pragma unroll
+    for (int c4 = 0; c4 < 4; ++c4) {
+      uint32_t w16[16];
+      if (full) {
+        // 3 of every 8 pairs on the FMA pipe, the rest on the MUFU
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int key = 32 * c4 + 2 * i;
+          const uint64_t a = fma_f32x2(f32x2(__uint_as_float(sv[key]), __uint_as_float(sv[key + 1])),
+                                       c2, nm2);
+          uint64_t e;
+          if ((i & 7) < 3)
+            e = ex2_poly2(f32x2_lo(a), f32x2_hi(a));
+          else
+            e = f32x2(ex2(f32x2_lo(a)), ex2(f32x2_hi(a)));
+          acc2[i & 1] = add_f32x2(acc2[i & 1], e);
+          w16[i] = f32x2_to_bf16x2(e);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int key = 32 * c4 + 2 * i;
+          const float p0 = key < valid ? ex2(fmaf(__uint_as_float(sv[key]), c, -m_used)) : 0.0f;
+          const float p1 =
+              key + 1 < valid ? ex2(fmaf(__uint_as_float(sv[key + 1]), c, -m_used)) : 0.0f;
+          sum += p0 + p1;
+          w16[i] = pack_bf16x2(p0, p1);
+        }
+      }
+      MP_TMEM_ST_32X32B_X16(pcol + static_cast<uint32_t>(16 * c4), w16);
+    }
+    if (full) {
+      const uint64_t t2 = add_f32x2(acc2[0], acc2[1]);
+      sum = f32x2_lo(t2) + f32x2_hi(t2);
+    }
+    l += sum;
+    tmem_wait_st();     // P_j (and an O rescale) written to TMEM
+    tc_fence_before();  // ... before P_j · V is issued
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&sm.p_full[b]));
   }
-  if (ok && n >= 2) ok = fold(n - 2, a_m2);
-  if (ok) ok = fold(n - 1, a_m1);
-  if (!ok) return;
+  // all of O: P_{n-1} · V landed
+  {
+    const int t = n - 1;
+    const bool w = attn_wait(sm, &sm.o_done[t & 1], static_cast<uint32_t>(t >> 1) & 1u,
+                             p.wait_limit_ns);
+    if (!__all_sync(0xFFFFFFFFu, w)) return;
+    tc_fence_after();
+  }
   const int q = q0 + row;
-  if (q >= p.S) return;
   const float inv = 1.0f / l;
   uint16_t* dst = p.o + static_cast<size_t>(q) * p.ldo + static_cast<size_t>(head) * 128;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    uint4 w;
-    w.x = pack_bf16x2(o[8 * i] * inv, o[8 * i + 1] * inv);
-    w.y = pack_bf16x2(o[8 * i + 2] * inv, o[8 * i + 3] * inv);
-    w.z = pack_bf16x2(o[8 * i + 4] * inv, o[8 * i + 5] * inv);
-    w.w = pack_bf16x2(o[8 * i + 6] * inv, o[8 * i + 7] * inv);
-    *reinterpret_cast<uint4*>(dst + 8 * i) = w;
+  for (int c4 = 0; c4 < 4; ++c4) {
+    uint32_t ov[32];
+    MP_TMEM_LD_32X32B_X32(tmem + lane_base + kColO + static_cast<uint32_t>(32 * c4), ov);
+    MP_TMEM_WAIT_LD_REGS32(ov);
+    if (q < p.S) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 wv;
+        wv.x = pack_bf16x2(__uint_as_float(ov[8 * i]) * inv, __uint_as_float(ov[8 * i + 1]) * inv);
+        wv.y = pack_bf16x2(__uint_as_float(ov[8 * i + 2]) * inv, __uint_as_float(ov[8 * i + 3]) * inv);
+        wv.z = pack_bf16x2(__uint_as_float(ov[8 * i + 4]) * inv, __uint_as_float(ov[8 * i + 5]) * inv);
+        wv.w = pack_bf16x2(__uint_as_float(ov[8 * i + 6]) * inv, __uint_as_float(ov[8 * i + 7]) * inv);
+        *reinterpret_cast<uint4*>(dst + 32 * c4 + 8 * i) = wv;
+      }
+    }
   }
 }
 
@@ -326,16 +404,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
   const int n = (p.S + kAttnTile - 1) / kAttnTile;
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(sm.q_full), 1);
+    for (int st = 0; st < kKvStages; ++st) {
+      mbar_init(smem_u32(&sm.k_full[st]), 1);
+      mbar_init(smem_u32(&sm.k_empty[st]), 1);
+      mbar_init(smem_u32(&sm.v_full[st]), 1);
+      mbar_init(smem_u32(&sm.v_empty[st]), 1);
+    }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_u32(&sm.k_full[b]), 1);
-      mbar_init(smem_u32(&sm.k_empty[b]), 1);
-      mbar_init(smem_u32(&sm.v_full[b]), 1);
-      mbar_init(smem_u32(&sm.v_empty[b]), 1);
       mbar_init(smem_u32(&sm.s_full[b]), 1);
       mbar_init(smem_u32(&sm.s_free[b]), 4);  // one arrive per softmax warp
       mbar_init(smem_u32(&sm.p_full[b]), 4);
-      mbar_init(smem_u32(&sm.o_full[b]), 1);
-      mbar_init(smem_u32(&sm.o_free[b]), 4);
+      mbar_init(smem_u32(&sm.o_done[b]), 1);
     }
     mbar_init(smem_u32(sm.drain), 1);
     *sm.abort = 0u;
@@ -355,9 +434,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
   tc_fence_after();
   const uint32_t tmem = *sm.tmem_slot;
   if (warp == 0) {
-    if (lane == 0) attn_producer(p, sm, q0, head, n);
+    if (lane == 0) attn_producer_k(p, sm, q0, head, n);
   } else if (warp == 1) {
     if (lane == 0) attn_mma(p, sm, tmem, n);
+  } else if (warp == 6) {
+    if (lane == 0) attn_producer_v(p, sm, head, n);
   } else {
     attn_softmax(p, sm, tmem, q0, head, n);
   }

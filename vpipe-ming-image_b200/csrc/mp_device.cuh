@@ -405,6 +405,17 @@ __device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
   return r;
 }
+__device__ __forceinline__ float max3_f32(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float f32x2_lo(uint64_t v) {
+  return __uint_as_float(static_cast<uint32_t>(v));
+}
+__device__ __forceinline__ float f32x2_hi(uint64_t v) {
+  return __uint_as_float(static_cast<uint32_t>(v >> 32));
+}
 // Rounds a packed fp32 pair to bf16x2 (low half from the low float).
 __device__ __forceinline__ uint32_t f32x2_to_bf16x2(uint64_t v) {
   float lo, hi;
