@@ -6,14 +6,15 @@
 // the reference's run_attn over the joint rows of a block (src/ming-dit.cc:
 // 1905-2039; q, k and v as its tr_rope / transpose leave them). One CTA per
 // (128-query tile, head), single-CTA MMAs (cta_group::1, M = 128):
-//   * warp 0 loads Q once and K_j (128 keys) per step, warp 6 loads V_j, with
-//     TMA into three-stage rings (K released as soon as S_j is done, V once
-//     P_j · V_j is);
+//   * warp 0 loads Q once and K_j (128 keys) per step into a three-stage ring
+//     (released as soon as S_j is done), warp 10 loads V_j into a two-stage
+//     ring (released once P_j · V_j is), with TMA;
 //   * warp 1 issues S_j = Q · K_j^T into one of two TMEM S buffers, then
 //     O += P_{j-1} · V_{j-1} into the TMEM accumulator O, with P read from
 //     TMEM and V as an MN-major operand straight from its [keys][head dim]
 //     tile;
-//   * warps 2-5 (thread = query row, TMEM lane) read S_j into registers once
+//   * warps 2-9 (thread = query row, TMEM lane; two warps per row, one per
+//     64-key half of each tile) read S_j into registers once
 //     (freeing its buffer for S_{j+2}), and write P_j = 2^(s·c − m) in bf16
 //     (c = scale·log2 e) into one of two TMEM P buffers with the
 //     row sum, in packed f32x2 arithmetic, three of every eight exponential
@@ -40,14 +41,17 @@ namespace {
 constexpr int kAttnTile = 128;                          // query rows per CTA, keys per step
 constexpr uint32_t kAttnBlk = 128 * 64 * 2;             // [128 rows][64 bf16], one TMA box
 constexpr uint32_t kAttnOp = 2 * kAttnBlk;              // 128 rows x 128 bf16
-constexpr int kKvStages = 3;
+constexpr int kKStages = 3;
+constexpr int kVStages = 2;
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffK = kOffQ + kAttnOp;             // K ring
-constexpr uint32_t kOffV = kOffK + kKvStages * kAttnOp; // V ring
-constexpr uint32_t kAttnTiles = kOffV + kKvStages * kAttnOp;  // 224 KB
-constexpr uint32_t kAttnSmem = kAttnTiles + 1024 + 256;
+constexpr uint32_t kOffV = kOffK + kKStages * kAttnOp;  // V ring
+constexpr uint32_t kAttnTiles = kOffV + kVStages * kAttnOp;  // 192 KB
+constexpr uint32_t kXchgBytes = 2 * 2 * 128 * 4;        // row maxima [tile parity][half][row]
+constexpr uint32_t kAttnSmem = kAttnTiles + 1024 + 256 + kXchgBytes;
 static_assert(kAttnSmem <= 232448, "shared memory per CTA");
-constexpr int kAttnThreads = 224;  // warp 0 Q+K, 1 MMA, 2-5 softmax, 6 V
+constexpr int kAttnThreads = 352;  // warp 0 Q+K, 1 MMA, 2-9 softmax, 10 V
+constexpr int kSoftWarps = 8;      // two per TMEM lane quarter: keys 0-63 / 64-127 of each row
 constexpr uint32_t kAttnCols = 512;  // S[0] S[1] (128 each), O (128), P[0] P[1] (64 each)
 constexpr uint32_t kColO = 256;      // TMEM column of the O accumulator
 constexpr uint32_t kColP = 384;      // TMEM columns of P[0] (P[1] 64 further): bf16 pairs
@@ -58,10 +62,10 @@ enum : uint32_t { kAttnSiteWait = 0x2100u, kAttnSiteDrain = 0x2200u };
 struct AttnSmem {
   uint8_t* tiles;
   uint64_t* q_full;
-  uint64_t* k_full;   // [kKvStages]
-  uint64_t* k_empty;  // [kKvStages]
-  uint64_t* v_full;   // [kKvStages]
-  uint64_t* v_empty;  // [kKvStages]
+  uint64_t* k_full;   // [kKStages]
+  uint64_t* k_empty;  // [kKStages]
+  uint64_t* v_full;   // [kVStages]
+  uint64_t* v_empty;  // [kVStages]
   uint64_t* s_full;   // [2]
   uint64_t* s_free;   // [2]
   uint64_t* p_full;   // [2]
@@ -69,6 +73,7 @@ struct AttnSmem {
   uint64_t* drain;
   uint32_t* tmem_slot;
   volatile uint32_t* abort;
+  float* xchg;        // [2][2][128] partial row maxima (then the partial row sums)
 };
 
 __device__ __forceinline__ AttnSmem carve_attn(uint8_t* raw) {
@@ -80,14 +85,15 @@ __device__ __forceinline__ AttnSmem carve_attn(uint8_t* raw) {
   s.k_full = b + 1;
   s.k_empty = b + 4;
   s.v_full = b + 7;
-  s.v_empty = b + 10;
-  s.s_full = b + 13;
-  s.s_free = b + 15;
-  s.p_full = b + 17;
-  s.o_done = b + 19;
-  s.drain = b + 21;
-  s.tmem_slot = reinterpret_cast<uint32_t*>(b + 22);
+  s.v_empty = b + 9;
+  s.s_full = b + 11;
+  s.s_free = b + 13;
+  s.p_full = b + 15;
+  s.o_done = b + 17;
+  s.drain = b + 19;
+  s.tmem_slot = reinterpret_cast<uint32_t*>(b + 20);
   s.abort = s.tmem_slot + 1;
+  s.xchg = reinterpret_cast<float*>(s.tiles + kAttnTiles + 256);
   return s;
 }
 
@@ -152,9 +158,9 @@ __device__ void attn_producer_k(const AttnParams& p, const AttnSmem& sm, int q0,
   tma_load_3d(base + kOffQ, &p.tm_q, smem_u32(sm.q_full), 0, q0, head);
   tma_load_3d(base + kOffQ + kAttnBlk, &p.tm_q, smem_u32(sm.q_full), 64, q0, head);
   for (int j = 0; j < n; ++j) {
-    const int st = j % kKvStages;
-    if (j >= kKvStages &&
-        !attn_wait(sm, &sm.k_empty[st], static_cast<uint32_t>(j / kKvStages - 1) & 1u,
+    const int st = j % kKStages;
+    if (j >= kKStages &&
+        !attn_wait(sm, &sm.k_empty[st], static_cast<uint32_t>(j / kKStages - 1) & 1u,
                    p.wait_limit_ns))
       return;
     const uint32_t kb = base + kOffK + static_cast<uint32_t>(st) * kAttnOp;
@@ -164,13 +170,13 @@ __device__ void attn_producer_k(const AttnParams& p, const AttnSmem& sm, int q0,
   }
 }
 
-// Warp 6, one thread: the V ring.
+// Warp 10, one thread: the V ring.
 __device__ void attn_producer_v(const AttnParams& p, const AttnSmem& sm, int head, int n) {
   const uint32_t base = smem_u32(sm.tiles);
   for (int j = 0; j < n; ++j) {
-    const int st = j % kKvStages;
-    if (j >= kKvStages &&
-        !attn_wait(sm, &sm.v_empty[st], static_cast<uint32_t>(j / kKvStages - 1) & 1u,
+    const int st = j % kVStages;
+    if (j >= kVStages &&
+        !attn_wait(sm, &sm.v_empty[st], static_cast<uint32_t>(j / kVStages - 1) & 1u,
                    p.wait_limit_ns))
       return;
     const uint32_t vb = base + kOffV + static_cast<uint32_t>(st) * kAttnOp;
@@ -188,8 +194,8 @@ __device__ void attn_mma(const AttnParams& p, const AttnSmem& sm, uint32_t tmem,
   bool ok = attn_wait(sm, sm.q_full, 0, p.wait_limit_ns);
   auto issue_s = [&](int j) -> bool {
     const int b = j & 1;
-    const int st = j % kKvStages;
-    if (!attn_wait(sm, &sm.k_full[st], static_cast<uint32_t>(j / kKvStages) & 1u, p.wait_limit_ns))
+    const int st = j % kKStages;
+    if (!attn_wait(sm, &sm.k_full[st], static_cast<uint32_t>(j / kKStages) & 1u, p.wait_limit_ns))
       return false;
     if (j >= 2 &&
         !attn_wait(sm, &sm.s_free[b], static_cast<uint32_t>((j - 2) >> 1) & 1u, p.wait_limit_ns))
@@ -206,8 +212,8 @@ __device__ void attn_mma(const AttnParams& p, const AttnSmem& sm, uint32_t tmem,
   };
   auto issue_pv = [&](int t) -> bool {
     const int b = t & 1;
-    const int st = t % kKvStages;
-    if (!attn_wait(sm, &sm.v_full[st], static_cast<uint32_t>(t / kKvStages) & 1u, p.wait_limit_ns))
+    const int st = t % kVStages;
+    if (!attn_wait(sm, &sm.v_full[st], static_cast<uint32_t>(t / kVStages) & 1u, p.wait_limit_ns))
       return false;
     if (!attn_wait(sm, &sm.p_full[b], static_cast<uint32_t>(t >> 1) & 1u, p.wait_limit_ns))
       return false;
@@ -236,44 +242,46 @@ __device__ void attn_mma(const AttnParams& p, const AttnSmem& sm, uint32_t tmem,
   }
 }
 
-// Warps 2-5: thread = query row (TMEM lane).
+// Warps 2-9: two warps per TMEM lane quarter; thread = query row (lane),
+// half = which 64 keys of each 128-key tile (and which 64 columns of O) this
+// warp takes. The two halves of a row exchange their partial maxima through
+// shared memory (one named barrier per quarter pair and tile) and so move
+// the row's exponent base identically; each keeps its own partial row sum,
+// added to the other once at the end.
 __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t tmem, int q0,
                              int head, int n) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int quarter = warp & 3;
+  const int half = (warp - 2) >> 2;
   const int row = quarter * 32 + lane;
+  const uint32_t bar_id = 1u + static_cast<uint32_t>(quarter);  // the quarter's two warps
   const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
   const float c = p.scale_log2;
+  const uint64_t c2 = f32x2(c, c);
   float m_used = -INFINITY, l = 0.0f;
   for (int j = 0; j < n; ++j) {
     const int b = j & 1;
     bool w = attn_wait(sm, &sm.s_full[b], static_cast<uint32_t>(j >> 1) & 1u, p.wait_limit_ns);
     if (!__all_sync(0xFFFFFFFFu, w)) return;
     tc_fence_after();
-    const uint32_t sb = tmem + lane_base + static_cast<uint32_t>(b) * 128u;
-    uint32_t sv[128];
+    const uint32_t sb = tmem + lane_base + static_cast<uint32_t>(b) * 128u + 64u * half;
+    uint32_t sv[64];
     uint32_t* const s1 = sv + 32;
-    uint32_t* const s2 = sv + 64;
-    uint32_t* const s3 = sv + 96;
     MP_TMEM_LD_32X32B_X32(sb, sv);
     MP_TMEM_LD_32X32B_X32(sb + 32u, s1);
-    MP_TMEM_LD_32X32B_X32(sb + 64u, s2);
-    MP_TMEM_LD_32X32B_X32(sb + 96u, s3);
     MP_TMEM_WAIT_LD_REGS32(sv);
     MP_TMEM_WAIT_LD_REGS32(s1);
-    MP_TMEM_WAIT_LD_REGS32(s2);
-    MP_TMEM_WAIT_LD_REGS32(s3);
     tc_fence_before();  // S_j is in registers: its buffer may take S_{j+2}
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(&sm.s_free[b]));
-    const int valid = p.S - j * kAttnTile;  // keys of this tile below S (>= 1)
-    const bool full = valid >= kAttnTile;   // the same in every thread of the CTA
+    const int valid = p.S - j * kAttnTile - 64 * half;  // keys of this half below S (may be <= 0)
+    const bool full = valid >= 64;  // the same in every thread of the warp
     float mx;
     if (full) {
       float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int i = 0; i < 128; i += 8) {
+      for (int i = 0; i < 64; i += 8) {
 #pragma unroll
         for (int a = 0; a < 4; ++a)
           m4[a] = max3_f32(m4[a], __uint_as_float(sv[i + 2 * a]), __uint_as_float(sv[i + 2 * a + 1]));
@@ -282,9 +290,14 @@ __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t t
     } else {
       mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 128; ++i)
+      for (int i = 0; i < 64; ++i)
         if (i < valid) mx = fmaxf(mx, __uint_as_float(sv[i]));
     }
+    // the row's maximum over both halves
+    float* xm = sm.xchg + b * 256;
+    xm[half * 128 + row] = mx;
+    named_barrier(bar_id, 64);
+    mx = fmaxf(mx, xm[(1 - half) * 128 + row]);
     const float mc = mx * c;
     if (j == 0) {
       m_used = mc;
@@ -292,16 +305,16 @@ __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t t
       const bool need = mc > m_used + kRescaleLog2;
       if (__any_sync(0xFFFFFFFFu, need)) {
         // O holds P_0..P_{j-1} · V relative to m_used: once P_{j-1} · V has
-        // landed, scale this warp's rows to the new base (1 for rows that keep it)
+        // landed, scale this warp's half of its rows to the new base
         const int t = j - 1;
         w = attn_wait(sm, &sm.o_done[t & 1], static_cast<uint32_t>(t >> 1) & 1u, p.wait_limit_ns);
         if (!__all_sync(0xFFFFFFFFu, w)) return;
         tc_fence_after();
         const float alpha = need ? ex2(m_used - mc) : 1.0f;
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
+        for (int c2i = 0; c2i < 2; ++c2i) {
           uint32_t ov[32];
-          const uint32_t oa = tmem + lane_base + kColO + static_cast<uint32_t>(32 * c4);
+          const uint32_t oa = tmem + lane_base + kColO + 64u * half + static_cast<uint32_t>(32 * c2i);
           MP_TMEM_LD_32X32B_X32(oa, ov);
           MP_TMEM_WAIT_LD_REGS32(ov);
 #pragma unroll
@@ -320,11 +333,11 @@ __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t t
       if (!__all_sync(0xFFFFFFFFu, w)) return;
     }
     float sum = 0.0f;
-    uint64_t acc2[2] = {0ull, 0ull};  // packed partial row sums (full tiles)
-    const uint64_t c2 = f32x2(c, c), nm2 = f32x2(-m_used, -m_used);
-    const uint32_t pcol = tmem + lane_base + kColP + static_cast<uint32_t>(b) * 64u;
+    uint64_t acc2[2] = {0ull, 0ull};  // packed partial row sums (full halves)
+    const uint64_t nm2 = f32x2(-m_used, -m_used);
+    const uint32_t pcol = tmem + lane_base + kColP + static_cast<uint32_t>(b) * 64u + 32u * half;
 #pragma unroll
-    for (int c4 = 0; c4 < 4; ++c4) {
+    for (int c4 = 0; c4 < 2; ++c4) {
       uint32_t w16[16];
       if (full) {
         // 3 of every 8 pairs on the FMA pipe, the rest on the MUFU
@@ -372,13 +385,18 @@ __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t t
     if (!__all_sync(0xFFFFFFFFu, w)) return;
     tc_fence_after();
   }
+  // the row sum over both halves (added in half order)
+  float* xl = sm.xchg + (n & 1) * 256;  // the buffer the last tile did not use
+  xl[half * 128 + row] = l;
+  named_barrier(bar_id, 64);
+  const float lt = xl[row] + xl[128 + row];
   const int q = q0 + row;
-  const float inv = 1.0f / l;
-  uint16_t* dst = p.o + static_cast<size_t>(q) * p.ldo + static_cast<size_t>(head) * 128;
+  const float inv = 1.0f / lt;
+  uint16_t* dst = p.o + static_cast<size_t>(q) * p.ldo + static_cast<size_t>(head) * 128 + 64 * half;
 #pragma unroll
-  for (int c4 = 0; c4 < 4; ++c4) {
+  for (int c4 = 0; c4 < 2; ++c4) {
     uint32_t ov[32];
-    MP_TMEM_LD_32X32B_X32(tmem + lane_base + kColO + static_cast<uint32_t>(32 * c4), ov);
+    MP_TMEM_LD_32X32B_X32(tmem + lane_base + kColO + 64u * half + static_cast<uint32_t>(32 * c4), ov);
     MP_TMEM_WAIT_LD_REGS32(ov);
     if (q < p.S) {
 #pragma unroll
@@ -404,16 +422,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
   const int n = (p.S + kAttnTile - 1) / kAttnTile;
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(sm.q_full), 1);
-    for (int st = 0; st < kKvStages; ++st) {
+    for (int st = 0; st < kKStages; ++st) {
       mbar_init(smem_u32(&sm.k_full[st]), 1);
       mbar_init(smem_u32(&sm.k_empty[st]), 1);
+    }
+    for (int st = 0; st < kVStages; ++st) {
       mbar_init(smem_u32(&sm.v_full[st]), 1);
       mbar_init(smem_u32(&sm.v_empty[st]), 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&sm.s_full[b]), 1);
-      mbar_init(smem_u32(&sm.s_free[b]), 4);  // one arrive per softmax warp
-      mbar_init(smem_u32(&sm.p_full[b]), 4);
+      mbar_init(smem_u32(&sm.s_free[b]), kSoftWarps);  // one arrive per softmax warp
+      mbar_init(smem_u32(&sm.p_full[b]), kSoftWarps);
       mbar_init(smem_u32(&sm.o_done[b]), 1);
     }
     mbar_init(smem_u32(sm.drain), 1);
@@ -437,7 +457,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
     if (lane == 0) attn_producer_k(p, sm, q0, head, n);
   } else if (warp == 1) {
     if (lane == 0) attn_mma(p, sm, tmem, n);
-  } else if (warp == 6) {
+  } else if (warp == 10) {
     if (lane == 0) attn_producer_v(p, sm, head, n);
   } else {
     attn_softmax(p, sm, tmem, q0, head, n);
