@@ -1255,13 +1255,15 @@ int mp_attention(mp_ctx* c, const void* q, const void* k, const void* v, int s, 
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(mp::kHeadDim), static_cast<cuuint64_t>(s),
                               static_cast<cuuint64_t>(nh)};
   const cuuint64_t strides[2] = {mp::kHeadDim * 2, static_cast<cuuint64_t>(s) * mp::kHeadDim * 2};
-  const cuuint32_t box[3] = {64, 128, 1};
+  // q and v: boxes of 64 dims x 128 rows; k: 64 dims x 64 keys (each CTA of a
+  // pair loads half of a 128-key step)
+  const cuuint32_t boxes[3][3] = {{64, 128, 1}, {64, 64, 1}, {64, 128, 1}};
   const cuuint32_t estr[3] = {1, 1, 1};
   CUtensorMap* maps[3] = {&p.tm_q, &p.tm_k, &p.tm_v};
   const void* srcs[3] = {q, k, v};
   for (int i = 0; i < 3; ++i)
     if (fn(maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(srcs[i]), dims, strides,
-           box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           boxes[i], estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return fail(c, MP_ECUDA, "tensor map encode failed (attention operand %d)", i);
   p.o = static_cast<uint16_t*>(o);

@@ -4,31 +4,35 @@
 //   o[i, 128h .. 128h + 127] = softmax(scale · q_i · K^T) · V
 //
 // the reference's run_attn over the joint rows of a block (src/ming-dit.cc:
-// 1905-2039; q, k and v as its tr_rope / transpose leave them). One CTA per
-// (128-query tile, head), single-CTA MMAs (cta_group::1, M = 128):
-//   * warp 0 loads Q once and K_j (128 keys) per step into a three-stage ring
-//     (released as soon as S_j is done), warp 10 loads V_j into a two-stage
-//     ring (released once P_j · V_j is), with TMA;
-//   * warp 1 issues S_j = Q · K_j^T into one of two TMEM S buffers, then
-//     O += P_{j-1} · V_{j-1} into the TMEM accumulator O, with P read from
-//     TMEM and V as an MN-major operand straight from its [keys][head dim]
-//     tile;
-//   * warps 2-9 (thread = query row, TMEM lane; two warps per row, one per
-//     64-key half of each tile) read S_j into registers once
-//     (freeing its buffer for S_{j+2}), and write P_j = 2^(s·c − m) in bf16
-//     (c = scale·log2 e) into one of two TMEM P buffers with the
-//     row sum, in packed f32x2 arithmetic, three of every eight exponential
-//     pairs on the FMA pipe and the rest on the MUFU. The exponent base m is the row maximum seen when it was last
-//     raised: only when a tile's maximum exceeds it by more than 8 (a factor
-//     256) does the warp rescale its rows of O in TMEM (after the previous
-//     P·V has landed) and move m up; otherwise p <= 256 and O, the row sum
-//     and the final quotient stay exact relative to the older m;
+// 1905-2039; q, k and v as its tr_rope / transpose leave them). A CTA PAIR
+// (cluster of 2, cta_group::2 MMAs with M = 256) takes 256 query rows of one
+// head, 128 per CTA; each step covers 128 keys:
+//   * per step each CTA loads only its half of the operands the pair MMA
+//     splits along N: 64 keys of K_j (for S = Q · K^T, N = keys) and 64 head
+//     dims of V_j (for O += P · V, N = head dims); K / V traffic per FLOP is
+//     half that of single-CTA tiles. Warp 0 loads Q once and the K ring
+//     (4 stages), warp 10 the V ring (4 stages); every pair load completes on
+//     the leader CTA's barrier;
+//   * warp 1 of the leader issues S_j into one of two TMEM S buffers of both
+//     CTAs, then O += P_{j-1} · V_{j-1} with P read from each CTA's TMEM and
+//     V as an MN-major operand straight from its [keys][dims] tile;
+//   * warps 2-9 of each CTA (thread = query row, TMEM lane; two warps per row,
+//     one per 64-key half of each tile) read S_j into registers once
+//     (freeing its buffer for S_{j+2}) and write P_j = 2^(s·c − m) in bf16
+//     (c = scale·log2 e) into one of two TMEM P buffers with the row sum, in
+//     packed f32x2 arithmetic, three of every eight exponential pairs on the
+//     FMA pipe and the rest on the MUFU. The exponent base m is the row
+//     maximum seen when it was last raised: only when a tile's maximum
+//     exceeds it by more than 8 (a factor 256) does the warp rescale its rows
+//     of O in TMEM (after the previous P·V has landed) and move m up;
+//     otherwise p <= 256 and O, the row sum and the final quotient stay exact
+//     relative to the older m;
 //   * after the last step the rows of O are divided by their sums and stored
 //     bf16 token-major.
 // S and P are double-buffered, so the softmax of tile j overlaps the MMAs
 // of tiles j + 1 (S) and j - 1 (PV). Keys past S are masked (their tiles read
-// zeros); rows past S are computed and not stored. Every wait is bounded;
-// on a timeout the CTA unwinds and reports MP_ETIMEOUT.
+// zeros); rows past S are computed and not stored. No TMA multicast. Every
+// wait is bounded; on a timeout the CTA unwinds and reports MP_ETIMEOUT.
 #include <cuda_runtime.h>
 
 #include "mp_device.cuh"
@@ -39,19 +43,24 @@ namespace mp {
 namespace {
 
 constexpr int kAttnTile = 128;                          // query rows per CTA, keys per step
-constexpr uint32_t kAttnBlk = 128 * 64 * 2;             // [128 rows][64 bf16], one TMA box
-constexpr uint32_t kAttnOp = 2 * kAttnBlk;              // 128 rows x 128 bf16
-constexpr int kKStages = 3;
-constexpr int kVStages = 2;
+constexpr uint32_t kQBlk = 128 * 64 * 2;                // Q: [128 rows][64 dims] bf16, one TMA box
+constexpr uint32_t kQBytes = 2 * kQBlk;                 // Q: 128 rows x 128 dims
+constexpr uint32_t kKBlk = 64 * 64 * 2;                 // K half: [64 keys][64 dims], one TMA box
+constexpr uint32_t kKHalf = 2 * kKBlk;                  // this CTA's 64 keys x 128 dims
+constexpr uint32_t kVHalf = 128 * 64 * 2;               // this CTA's 64 dims of 128 keys, one box
+constexpr int kKStages = 4;
+constexpr int kVStages = 4;
 constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffK = kOffQ + kAttnOp;             // K ring
-constexpr uint32_t kOffV = kOffK + kKStages * kAttnOp;  // V ring
-constexpr uint32_t kAttnTiles = kOffV + kVStages * kAttnOp;  // 192 KB
+constexpr uint32_t kOffK = kOffQ + kQBytes;             // K ring
+constexpr uint32_t kOffV = kOffK + kKStages * kKHalf;   // V ring
+constexpr uint32_t kAttnTiles = kOffV + kVStages * kVHalf;  // 160 KB
 constexpr uint32_t kXchgBytes = 2 * 2 * 128 * 4;        // row maxima [tile parity][half][row]
+static_assert((1 + 2 * kKStages + 2 * kVStages + 9) * 8 + 8 <= 256, "barrier region");
 constexpr uint32_t kAttnSmem = kAttnTiles + 1024 + 256 + kXchgBytes;
 static_assert(kAttnSmem <= 232448, "shared memory per CTA");
 constexpr int kAttnThreads = 352;  // warp 0 Q+K, 1 MMA, 2-9 softmax, 10 V
 constexpr int kSoftWarps = 8;      // two per TMEM lane quarter: keys 0-63 / 64-127 of each row
+static_assert(kAttnTiles % 1024 == 0, "barrier region after the tiles");
 constexpr uint32_t kAttnCols = 512;  // S[0] S[1] (128 each), O (128), P[0] P[1] (64 each)
 constexpr uint32_t kColO = 256;      // TMEM column of the O accumulator
 constexpr uint32_t kColP = 384;      // TMEM columns of P[0] (P[1] 64 further): bf16 pairs
@@ -82,38 +91,39 @@ __device__ __forceinline__ AttnSmem carve_attn(uint8_t* raw) {
   s.tiles = reinterpret_cast<uint8_t*>(base);
   uint64_t* b = reinterpret_cast<uint64_t*>(s.tiles + kAttnTiles);
   s.q_full = b;
-  s.k_full = b + 1;
-  s.k_empty = b + 4;
-  s.v_full = b + 7;
-  s.v_empty = b + 9;
-  s.s_full = b + 11;
-  s.s_free = b + 13;
-  s.p_full = b + 15;
-  s.o_done = b + 17;
-  s.drain = b + 19;
-  s.tmem_slot = reinterpret_cast<uint32_t*>(b + 20);
+  s.k_full = s.q_full + 1;
+  s.k_empty = s.k_full + kKStages;
+  s.v_full = s.k_empty + kKStages;
+  s.v_empty = s.v_full + kVStages;
+  s.s_full = s.v_empty + kVStages;
+  s.s_free = s.s_full + 2;
+  s.p_full = s.s_free + 2;
+  s.o_done = s.p_full + 2;
+  s.drain = s.o_done + 2;
+  s.tmem_slot = reinterpret_cast<uint32_t*>(s.drain + 1);
   s.abort = s.tmem_slot + 1;
   s.xchg = reinterpret_cast<float*>(s.tiles + kAttnTiles + 256);
   return s;
 }
 
-// K-major operand (128 rows x 128 bf16 as two [128][64] 128-byte-swizzled
-// blocks): the 16-wide K step kk sits in block kk / 4 at byte 32 (kk % 4).
-__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile, int kk) {
-  return make_sdesc_sw128(tile + static_cast<uint32_t>(kk >> 2) * kAttnBlk +
+// K-major operand of `rows` rows x 128 dims as two [rows][64] 128-byte-
+// swizzled blocks of `blk` bytes: the 16-wide K step kk sits in block kk / 4
+// at byte 32 (kk % 4).
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile, uint32_t blk, int kk) {
+  return make_sdesc_sw128(tile + static_cast<uint32_t>(kk >> 2) * blk +
                           static_cast<uint32_t>(kk & 3) * 32u);
 }
 
-// V as the MN-major B operand of P · V: its tile is [128 keys][128 head dims]
-// as two [128 keys][64 dims] 128-byte-swizzled blocks, i.e. 8-key x 64-dim
-// swizzle atoms of 1024 bytes. A 16-key step starts 2048 bytes further; the
-// second 64-dim half lies one block (LBO) away; 8-key groups are 1024 bytes
-// apart (SBO).
+// This CTA's half of V as the MN-major B operand of P · V: [128 keys][64
+// dims], one 128-byte-swizzled block (8-key x 64-dim swizzle atoms of 1024
+// bytes, one atom wide along N). A 16-key step starts 2048 bytes further;
+// 8-key groups are 1024 bytes apart (SBO); the leading byte offset (the next
+// 64-dim block) is not reached by a 64-wide half.
 __device__ __forceinline__ uint64_t vmn_desc(uint32_t tile, int kk) {
   uint64_t d = 0;
   const uint32_t a = tile + static_cast<uint32_t>(kk) * 2048u;
   d |= static_cast<uint64_t>((a & 0x3FFFFu) >> 4);
-  d |= static_cast<uint64_t>(kAttnBlk >> 4) << 16;  // leading byte offset: the next 64 dims
+  d |= static_cast<uint64_t>(kVHalf >> 4) << 16;    // leading byte offset (unused: one block)
   d |= static_cast<uint64_t>(1024u >> 4) << 32;     // stride byte offset: the next 8 keys
   d |= static_cast<uint64_t>(1u) << 46;             // descriptor version (sm_100)
   d |= static_cast<uint64_t>(2u) << 61;             // SWIZZLE_128B
@@ -151,27 +161,34 @@ __device__ __forceinline__ bool attn_wait(const AttnSmem& sm, uint64_t* bar, uin
   return mbar_wait(smem_u32(bar), parity, sm.abort, kAttnSiteWait, limit);
 }
 
-// Warp 0, one thread: Q, then the K ring.
-__device__ void attn_producer_k(const AttnParams& p, const AttnSmem& sm, int q0, int head, int n) {
+// Warp 0 of each CTA, one thread: its Q rows, then its halves of the K ring.
+// Pair loads complete on the leader's barriers; the leader expects both CTAs'
+// bytes.
+__device__ void attn_producer_k(const AttnParams& p, const AttnSmem& sm, bool leader, int rank,
+                                int q0, int head, int n) {
   const uint32_t base = smem_u32(sm.tiles);
-  mbar_arrive_expect_tx(smem_u32(sm.q_full), kAttnOp);
-  tma_load_3d(base + kOffQ, &p.tm_q, smem_u32(sm.q_full), 0, q0, head);
-  tma_load_3d(base + kOffQ + kAttnBlk, &p.tm_q, smem_u32(sm.q_full), 64, q0, head);
+  const uint32_t qbar = mapa_shared(smem_u32(sm.q_full), 0);
+  if (leader) mbar_arrive_expect_tx(smem_u32(sm.q_full), 2 * kQBytes);
+  tma_load_3d_pair(base + kOffQ, &p.tm_q, qbar, 0, q0, head);
+  tma_load_3d_pair(base + kOffQ + kQBlk, &p.tm_q, qbar, 64, q0, head);
   for (int j = 0; j < n; ++j) {
     const int st = j % kKStages;
     if (j >= kKStages &&
         !attn_wait(sm, &sm.k_empty[st], static_cast<uint32_t>(j / kKStages - 1) & 1u,
                    p.wait_limit_ns))
       return;
-    const uint32_t kb = base + kOffK + static_cast<uint32_t>(st) * kAttnOp;
-    mbar_arrive_expect_tx(smem_u32(&sm.k_full[st]), kAttnOp);
-    tma_load_3d(kb, &p.tm_k, smem_u32(&sm.k_full[st]), 0, j * kAttnTile, head);
-    tma_load_3d(kb + kAttnBlk, &p.tm_k, smem_u32(&sm.k_full[st]), 64, j * kAttnTile, head);
+    const uint32_t kb = base + kOffK + static_cast<uint32_t>(st) * kKHalf;
+    const uint32_t bar = mapa_shared(smem_u32(&sm.k_full[st]), 0);
+    if (leader) mbar_arrive_expect_tx(smem_u32(&sm.k_full[st]), 2 * kKHalf);
+    const int key0 = j * kAttnTile + rank * 64;
+    tma_load_3d_pair(kb, &p.tm_k, bar, 0, key0, head);
+    tma_load_3d_pair(kb + kKBlk, &p.tm_k, bar, 64, key0, head);
   }
 }
 
-// Warp 10, one thread: the V ring.
-__device__ void attn_producer_v(const AttnParams& p, const AttnSmem& sm, int head, int n) {
+// Warp 10 of each CTA, one thread: its 64 dims of the V ring.
+__device__ void attn_producer_v(const AttnParams& p, const AttnSmem& sm, bool leader, int rank,
+                                int head, int n) {
   const uint32_t base = smem_u32(sm.tiles);
   for (int j = 0; j < n; ++j) {
     const int st = j % kVStages;
@@ -179,17 +196,17 @@ __device__ void attn_producer_v(const AttnParams& p, const AttnSmem& sm, int hea
         !attn_wait(sm, &sm.v_empty[st], static_cast<uint32_t>(j / kVStages - 1) & 1u,
                    p.wait_limit_ns))
       return;
-    const uint32_t vb = base + kOffV + static_cast<uint32_t>(st) * kAttnOp;
-    mbar_arrive_expect_tx(smem_u32(&sm.v_full[st]), kAttnOp);
-    tma_load_3d(vb, &p.tm_v, smem_u32(&sm.v_full[st]), 0, j * kAttnTile, head);
-    tma_load_3d(vb + kAttnBlk, &p.tm_v, smem_u32(&sm.v_full[st]), 64, j * kAttnTile, head);
+    const uint32_t vb = base + kOffV + static_cast<uint32_t>(st) * kVHalf;
+    const uint32_t bar = mapa_shared(smem_u32(&sm.v_full[st]), 0);
+    if (leader) mbar_arrive_expect_tx(smem_u32(&sm.v_full[st]), 2 * kVHalf);
+    tma_load_3d_pair(vb, &p.tm_v, bar, rank * 64, j * kAttnTile, head);
   }
 }
 
-// Warp 1, one thread.
+// Warp 1 of the leader, one thread: pair MMAs for both CTAs.
 __device__ void attn_mma(const AttnParams& p, const AttnSmem& sm, uint32_t tmem, int n) {
   const uint32_t base = smem_u32(sm.tiles);
-  const uint32_t idesc_qk = make_idesc_bf16(kAttnTile, kAttnTile);
+  const uint32_t idesc_qk = make_idesc_bf16(2 * kAttnTile, kAttnTile);  // M 256, N 128
   const uint32_t idesc_pv = idesc_qk | (1u << 16);  // B (V) MN-major
   bool ok = attn_wait(sm, sm.q_full, 0, p.wait_limit_ns);
   auto issue_s = [&](int j) -> bool {
@@ -201,13 +218,13 @@ __device__ void attn_mma(const AttnParams& p, const AttnSmem& sm, uint32_t tmem,
         !attn_wait(sm, &sm.s_free[b], static_cast<uint32_t>((j - 2) >> 1) & 1u, p.wait_limit_ns))
       return false;
     tc_fence_after();
-    const uint32_t kt = base + kOffK + static_cast<uint32_t>(st) * kAttnOp;
+    const uint32_t kt = base + kOffK + static_cast<uint32_t>(st) * kKHalf;
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk)
-      umma_ss(tmem + static_cast<uint32_t>(b) * 128u, kmajor_desc(base + kOffQ, kk),
-              kmajor_desc(kt, kk), idesc_qk, kk > 0 ? 1u : 0u);
-    umma_commit(smem_u32(&sm.s_full[b]));
-    umma_commit(smem_u32(&sm.k_empty[st]));
+      umma_ss_pair(tmem + static_cast<uint32_t>(b) * 128u, kmajor_desc(base + kOffQ, kQBlk, kk),
+                   kmajor_desc(kt, kKBlk, kk), idesc_qk, kk > 0 ? 1u : 0u);
+    umma_commit_pair(smem_u32(&sm.s_full[b]), 0x3);
+    umma_commit_pair(smem_u32(&sm.k_empty[st]), 0x3);
     return true;
   };
   auto issue_pv = [&](int t) -> bool {
@@ -218,21 +235,22 @@ __device__ void attn_mma(const AttnParams& p, const AttnSmem& sm, uint32_t tmem,
     if (!attn_wait(sm, &sm.p_full[b], static_cast<uint32_t>(t >> 1) & 1u, p.wait_limit_ns))
       return false;
     tc_fence_after();
-    const uint32_t vt = base + kOffV + static_cast<uint32_t>(st) * kAttnOp;
-    // A = P_t from TMEM: 16 keys (8 columns of bf16 pairs) per step
+    const uint32_t vt = base + kOffV + static_cast<uint32_t>(st) * kVHalf;
+    // A = P_t from each CTA's TMEM: 16 keys (8 columns of bf16 pairs) per step
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk)
-      umma_ts(tmem + kColO, tmem + kColP + static_cast<uint32_t>(b) * 64u + static_cast<uint32_t>(kk) * 8u,
-              vmn_desc(vt, kk), idesc_pv, (t > 0 || kk > 0) ? 1u : 0u);
-    umma_commit(smem_u32(&sm.o_done[b]));
-    umma_commit(smem_u32(&sm.v_empty[st]));
+      umma_ts_pair(tmem + kColO,
+                   tmem + kColP + static_cast<uint32_t>(b) * 64u + static_cast<uint32_t>(kk) * 8u,
+                   vmn_desc(vt, kk), idesc_pv, (t > 0 || kk > 0) ? 1u : 0u);
+    umma_commit_pair(smem_u32(&sm.o_done[b]), 0x3);
+    umma_commit_pair(smem_u32(&sm.v_empty[st]), 0x3);
     return true;
   };
   if (ok) ok = issue_s(0);
   for (int j = 1; ok && j < n; ++j) ok = issue_s(j) && issue_pv(j - 1);
   if (ok) ok = issue_pv(n - 1);
   // every MMA issued has completed before TMEM is freed
-  umma_commit(smem_u32(sm.drain));
+  umma_commit_pair(smem_u32(sm.drain), 0x1);
   const uint64_t t0 = global_timer_ns();
   while (!mbar_try_wait(smem_u32(sm.drain), 0)) {
     if (global_timer_ns() - t0 > p.wait_limit_ns) {
@@ -274,7 +292,7 @@ __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t t
     MP_TMEM_WAIT_LD_REGS32(s1);
     tc_fence_before();  // S_j is in registers: its buffer may take S_{j+2}
     __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(&sm.s_free[b]));
+    if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&sm.s_free[b]), 0));
     const int valid = p.S - j * kAttnTile - 64 * half;  // keys of this half below S (may be <= 0)
     const bool full = valid >= 64;  // the same in every thread of the warp
     float mx;
@@ -375,7 +393,7 @@ __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t t
     tmem_wait_st();     // P_j (and an O rescale) written to TMEM
     tc_fence_before();  // ... before P_j · V is issued
     __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(&sm.p_full[b]));
+    if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&sm.p_full[b]), 0));
   }
   // all of O: P_{n-1} · V landed
   {
@@ -412,12 +430,15 @@ __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t t
   }
 }
 
-__global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kAttnThreads, 1)
+    attn_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   const AttnSmem sm = carve_attn(smem_raw);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int q0 = static_cast<int>(blockIdx.x) * kAttnTile;
+  const int rank = static_cast<int>(cluster_ctarank());
+  const bool leader = rank == 0;
+  const int q0 = static_cast<int>(blockIdx.x >> 1) * 2 * kAttnTile + rank * kAttnTile;
   const int head = static_cast<int>(blockIdx.y);
   const int n = (p.S + kAttnTile - 1) / kAttnTile;
   if (threadIdx.x == 0) {
@@ -432,8 +453,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&sm.s_full[b]), 1);
-      mbar_init(smem_u32(&sm.s_free[b]), kSoftWarps);  // one arrive per softmax warp
-      mbar_init(smem_u32(&sm.p_full[b]), kSoftWarps);
+      mbar_init(smem_u32(&sm.s_free[b]), 2 * kSoftWarps);  // leader: every softmax warp of the pair
+      mbar_init(smem_u32(&sm.p_full[b]), 2 * kSoftWarps);
       mbar_init(smem_u32(&sm.o_done[b]), 1);
     }
     mbar_init(smem_u32(sm.drain), 1);
@@ -446,19 +467,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
     tma_prefetch_map(&p.tm_v);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(sm.tmem_slot), kAttnCols);
-    tmem_relinquish();
+    tmem_alloc_pair(smem_u32(sm.tmem_slot), kAttnCols);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();
   tc_fence_after();
   const uint32_t tmem = *sm.tmem_slot;
   if (warp == 0) {
-    if (lane == 0) attn_producer_k(p, sm, q0, head, n);
+    if (lane == 0) attn_producer_k(p, sm, leader, rank, q0, head, n);
   } else if (warp == 1) {
-    if (lane == 0) attn_mma(p, sm, tmem, n);
+    if (lane == 0 && leader) attn_mma(p, sm, tmem, n);
   } else if (warp == 10) {
-    if (lane == 0) attn_producer_v(p, sm, head, n);
+    if (lane == 0) attn_producer_v(p, sm, leader, rank, head, n);
   } else {
     attn_softmax(p, sm, tmem, q0, head, n);
   }
@@ -468,9 +489,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
     while (global_timer_ns() - t_settle < 100000ull) __nanosleep(1000);
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, kAttnCols);
+  if (warp == 1) tmem_dealloc_pair(tmem, kAttnCols);
   if (threadIdx.x == 0 && *sm.abort != 0u) atomicOr(p.err, kErrTimeout);
 }
 
@@ -489,7 +510,8 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     g_attn_configured[dev] = true;
   }
-  const dim3 grid(static_cast<unsigned>((p.S + kAttnTile - 1) / kAttnTile),
+  // one CTA pair per 256 query rows
+  const dim3 grid(static_cast<unsigned>(2 * ((p.S + 2 * kAttnTile - 1) / (2 * kAttnTile))),
                   static_cast<unsigned>(p.NH), 1);
   attn_kernel<<<grid, kAttnThreads, kAttnSmem, stream>>>(p);
   return cudaGetLastError();

@@ -171,8 +171,9 @@ constexpr int kNormMaxH = 8192;
 
 // Non-causal attention over head-major q, k, v (mp_attn.cu): for head h and
 // query row i < S,  o[i, 128h .. 128h + 127] = softmax(scale · q_i · K^T) · V.
-// tm_q / tm_k / tm_v: bf16 [NH][S][128] as 3-D maps {128, S, NH}, box
-// {64, 128, 1}, 128-byte swizzle (rows past S read zeros). o: bf16 [S][ldo].
+// tm_q / tm_k / tm_v: bf16 [NH][S][128] as 3-D maps {128, S, NH}, boxes
+// {64, 128, 1} (q, v) and {64, 64, 1} (k), 128-byte swizzle (rows past S read
+// zeros). o: bf16 [S][ldo].
 struct AttnParams {
   CUtensorMap tm_q;
   CUtensorMap tm_k;
