@@ -13,12 +13,15 @@
 //     half that of single-CTA tiles. Warp 0 loads Q once and the K ring
 //     (4 stages), warp 10 the V ring (4 stages); every pair load completes on
 //     the leader CTA's barrier;
-//   * warp 1 of the leader issues S_j into one of two TMEM S buffers of both
-//     CTAs, then O += P_{j-1} · V_{j-1} with P read from each CTA's TMEM and
-//     V as an MN-major operand straight from its [keys][dims] tile;
+//   * each CTA's softmax warps copy its Q rows into TMEM once; warp 1 of the
+//     leader then issues S_j = Q · K_j^T with Q read from TMEM (so the only
+//     shared-memory operand is the K half) into the TMEM S buffer of both
+//     CTAs as soon as the softmax has read S_{j-1} out, then O += P_{j-1} ·
+//     V_{j-1} with P read from TMEM and V as an MN-major operand straight from
+//     its [keys][dims] tile;
 //   * warps 2-9 of each CTA (thread = query row, TMEM lane; two warps per row,
 //     one per 64-key half of each tile) read S_j into registers once
-//     (freeing its buffer for S_{j+2}) and write P_j = 2^(s·c − m) in bf16
+//     (freeing S for S_{j+1}) and write P_j = 2^(s·c − m) in bf16
 //     (c = scale·log2 e) into one of two TMEM P buffers with the row sum, in
 //     packed f32x2 arithmetic, three of every eight exponential pairs on the
 //     FMA pipe and the rest on the MUFU. The exponent base m is the row
@@ -29,8 +32,8 @@
 //     relative to the older m;
 //   * after the last step the rows of O are divided by their sums and stored
 //     bf16 token-major.
-// S and P are double-buffered, so the softmax of tile j overlaps the MMAs
-// of tiles j + 1 (S) and j - 1 (PV). Keys past S are masked (their tiles read
+// S_{j+1} and P_{j-1} · V_{j-1} run while the softmax of tile j works (P is
+// double-buffered). Keys past S are masked (their tiles read
 // zeros); rows past S are computed and not stored. No TMA multicast. Every
 // wait is bounded; on a timeout the CTA unwinds and reports MP_ETIMEOUT.
 #include <cuda_runtime.h>
@@ -55,15 +58,17 @@ constexpr uint32_t kOffK = kOffQ + kQBytes;             // K ring
 constexpr uint32_t kOffV = kOffK + kKStages * kKHalf;   // V ring
 constexpr uint32_t kAttnTiles = kOffV + kVStages * kVHalf;  // 160 KB
 constexpr uint32_t kXchgBytes = 2 * 2 * 128 * 4;        // row maxima [tile parity][half][row]
-static_assert((1 + 2 * kKStages + 2 * kVStages + 9) * 8 + 8 <= 256, "barrier region");
+static_assert((1 + 2 * kKStages + 2 * kVStages + 8) * 8 + 8 <= 256, "barrier region");
 constexpr uint32_t kAttnSmem = kAttnTiles + 1024 + 256 + kXchgBytes;
 static_assert(kAttnSmem <= 232448, "shared memory per CTA");
 constexpr int kAttnThreads = 352;  // warp 0 Q+K, 1 MMA, 2-9 softmax, 10 V
 constexpr int kSoftWarps = 8;      // two per TMEM lane quarter: keys 0-63 / 64-127 of each row
 static_assert(kAttnTiles % 1024 == 0, "barrier region after the tiles");
-constexpr uint32_t kAttnCols = 512;  // S[0] S[1] (128 each), O (128), P[0] P[1] (64 each)
-constexpr uint32_t kColO = 256;      // TMEM column of the O accumulator
-constexpr uint32_t kColP = 384;      // TMEM columns of P[0] (P[1] 64 further): bf16 pairs
+constexpr uint32_t kAttnCols = 512;  // Q (64), S (128), O (128), P[0] P[1] (64 each)
+constexpr uint32_t kColQ = 0;        // Q rows as bf16 pairs (the A operand of S = Q · K^T)
+constexpr uint32_t kColS = 64;       // S (f32)
+constexpr uint32_t kColO = 192;      // the O accumulator (f32)
+constexpr uint32_t kColP = 320;      // P[0] (P[1] 64 further): bf16 pairs
 constexpr float kRescaleLog2 = 8.0f;                    // move m only when a max exceeds it by this
 
 enum : uint32_t { kAttnSiteWait = 0x2100u, kAttnSiteDrain = 0x2200u };
@@ -75,8 +80,9 @@ struct AttnSmem {
   uint64_t* k_empty;  // [kKStages]
   uint64_t* v_full;   // [kVStages]
   uint64_t* v_empty;  // [kVStages]
-  uint64_t* s_full;   // [2]
-  uint64_t* s_free;   // [2]
+  uint64_t* q_ready;  // leader: every softmax warp of the pair has put its Q part in TMEM
+  uint64_t* s_full;   // S_j complete (both CTAs)
+  uint64_t* s_free;   // leader: S_j read out by every softmax warp of the pair
   uint64_t* p_full;   // [2]
   uint64_t* o_done;   // [2] P_t · V_t (t % 2) accumulated: P buffer free, O includes it
   uint64_t* drain;
@@ -95,9 +101,10 @@ __device__ __forceinline__ AttnSmem carve_attn(uint8_t* raw) {
   s.k_empty = s.k_full + kKStages;
   s.v_full = s.k_empty + kKStages;
   s.v_empty = s.v_full + kVStages;
-  s.s_full = s.v_empty + kVStages;
-  s.s_free = s.s_full + 2;
-  s.p_full = s.s_free + 2;
+  s.q_ready = s.v_empty + kVStages;
+  s.s_full = s.q_ready + 1;
+  s.s_free = s.s_full + 1;
+  s.p_full = s.s_free + 1;
   s.o_done = s.p_full + 2;
   s.drain = s.o_done + 2;
   s.tmem_slot = reinterpret_cast<uint32_t*>(s.drain + 1);
@@ -161,16 +168,16 @@ __device__ __forceinline__ bool attn_wait(const AttnSmem& sm, uint64_t* bar, uin
   return mbar_wait(smem_u32(bar), parity, sm.abort, kAttnSiteWait, limit);
 }
 
-// Warp 0 of each CTA, one thread: its Q rows, then its halves of the K ring.
-// Pair loads complete on the leader's barriers; the leader expects both CTAs'
-// bytes.
+// Warp 0 of each CTA, one thread: its Q rows, then its halves of the K ring
+// (pair loads completing on the leader's barriers; the leader expects both
+// CTAs' bytes).
 __device__ void attn_producer_k(const AttnParams& p, const AttnSmem& sm, bool leader, int rank,
                                 int q0, int head, int n) {
   const uint32_t base = smem_u32(sm.tiles);
-  const uint32_t qbar = mapa_shared(smem_u32(sm.q_full), 0);
-  if (leader) mbar_arrive_expect_tx(smem_u32(sm.q_full), 2 * kQBytes);
-  tma_load_3d_pair(base + kOffQ, &p.tm_q, qbar, 0, q0, head);
-  tma_load_3d_pair(base + kOffQ + kQBlk, &p.tm_q, qbar, 64, q0, head);
+  // this CTA's Q rows, on its own barrier (its softmax warps copy them to TMEM)
+  mbar_arrive_expect_tx(smem_u32(sm.q_full), kQBytes);
+  tma_load_3d(base + kOffQ, &p.tm_q, smem_u32(sm.q_full), 0, q0, head);
+  tma_load_3d(base + kOffQ + kQBlk, &p.tm_q, smem_u32(sm.q_full), 64, q0, head);
   for (int j = 0; j < n; ++j) {
     const int st = j % kKStages;
     if (j >= kKStages &&
@@ -208,22 +215,22 @@ __device__ void attn_mma(const AttnParams& p, const AttnSmem& sm, uint32_t tmem,
   const uint32_t base = smem_u32(sm.tiles);
   const uint32_t idesc_qk = make_idesc_bf16(2 * kAttnTile, kAttnTile);  // M 256, N 128
   const uint32_t idesc_pv = idesc_qk | (1u << 16);  // B (V) MN-major
-  bool ok = attn_wait(sm, sm.q_full, 0, p.wait_limit_ns);
+  bool ok = attn_wait(sm, sm.q_ready, 0, p.wait_limit_ns);
   auto issue_s = [&](int j) -> bool {
-    const int b = j & 1;
     const int st = j % kKStages;
     if (!attn_wait(sm, &sm.k_full[st], static_cast<uint32_t>(j / kKStages) & 1u, p.wait_limit_ns))
       return false;
-    if (j >= 2 &&
-        !attn_wait(sm, &sm.s_free[b], static_cast<uint32_t>((j - 2) >> 1) & 1u, p.wait_limit_ns))
+    if (j >= 1 &&
+        !attn_wait(sm, sm.s_free, static_cast<uint32_t>(j - 1) & 1u, p.wait_limit_ns))
       return false;
     tc_fence_after();
     const uint32_t kt = base + kOffK + static_cast<uint32_t>(st) * kKHalf;
+    // A = Q from each CTA's TMEM: 16 dims (8 columns of bf16 pairs) per step
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk)
-      umma_ss_pair(tmem + static_cast<uint32_t>(b) * 128u, kmajor_desc(base + kOffQ, kQBlk, kk),
+      umma_ts_pair(tmem + kColS, tmem + kColQ + static_cast<uint32_t>(kk) * 8u,
                    kmajor_desc(kt, kKBlk, kk), idesc_qk, kk > 0 ? 1u : 0u);
-    umma_commit_pair(smem_u32(&sm.s_full[b]), 0x3);
+    umma_commit_pair(smem_u32(sm.s_full), 0x3);
     umma_commit_pair(smem_u32(&sm.k_empty[st]), 0x3);
     return true;
   };
@@ -277,22 +284,43 @@ __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t t
   const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
   const float c = p.scale_log2;
   const uint64_t c2 = f32x2(c, c);
+  {
+    // this thread's Q row, dims [64 half, 64 half + 64), from the 128-byte-
+    // swizzled smem tile into TMEM as bf16 pairs (column = dim / 2)
+    bool w = attn_wait(sm, sm.q_full, 0, p.wait_limit_ns);
+    if (!__all_sync(0xFFFFFFFFu, w)) return;
+    const uint32_t qrow = smem_u32(sm.tiles) + kOffQ + static_cast<uint32_t>(half) * kQBlk +
+                          static_cast<uint32_t>(row) * 128u;
+    uint32_t qv[32];
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+      const uint32_t a = qrow + ((static_cast<uint32_t>(ch) ^ static_cast<uint32_t>(row & 7)) << 4);
+      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(qv[4 * ch]), "=r"(qv[4 * ch + 1]), "=r"(qv[4 * ch + 2]), "=r"(qv[4 * ch + 3])
+                   : "r"(a));
+    }
+    MP_TMEM_ST_32X32B_X32(tmem + lane_base + kColQ + 32u * half, qv);
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(sm.q_ready), 0));
+  }
   float m_used = -INFINITY, l = 0.0f;
   for (int j = 0; j < n; ++j) {
     const int b = j & 1;
-    bool w = attn_wait(sm, &sm.s_full[b], static_cast<uint32_t>(j >> 1) & 1u, p.wait_limit_ns);
+    bool w = attn_wait(sm, sm.s_full, static_cast<uint32_t>(j) & 1u, p.wait_limit_ns);
     if (!__all_sync(0xFFFFFFFFu, w)) return;
     tc_fence_after();
-    const uint32_t sb = tmem + lane_base + static_cast<uint32_t>(b) * 128u + 64u * half;
+    const uint32_t sb = tmem + lane_base + kColS + 64u * half;
     uint32_t sv[64];
     uint32_t* const s1 = sv + 32;
     MP_TMEM_LD_32X32B_X32(sb, sv);
     MP_TMEM_LD_32X32B_X32(sb + 32u, s1);
     MP_TMEM_WAIT_LD_REGS32(sv);
     MP_TMEM_WAIT_LD_REGS32(s1);
-    tc_fence_before();  // S_j is in registers: its buffer may take S_{j+2}
+    tc_fence_before();  // S_j is in registers: S may take S_{j+1}
     __syncwarp();
-    if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&sm.s_free[b]), 0));
+    if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(sm.s_free), 0));
     const int valid = p.S - j * kAttnTile - 64 * half;  // keys of this half below S (may be <= 0)
     const bool full = valid >= 64;  // the same in every thread of the warp
     float mx;
@@ -451,9 +479,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kAttnThreads, 1)
       mbar_init(smem_u32(&sm.v_full[st]), 1);
       mbar_init(smem_u32(&sm.v_empty[st]), 1);
     }
+    mbar_init(smem_u32(sm.q_ready), 2 * kSoftWarps);  // leader: every softmax warp of the pair
+    mbar_init(smem_u32(sm.s_full), 1);
+    mbar_init(smem_u32(sm.s_free), 2 * kSoftWarps);
     for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_u32(&sm.s_full[b]), 1);
-      mbar_init(smem_u32(&sm.s_free[b]), 2 * kSoftWarps);  // leader: every softmax warp of the pair
       mbar_init(smem_u32(&sm.p_full[b]), 2 * kSoftWarps);
       mbar_init(smem_u32(&sm.o_done[b]), 1);
     }
