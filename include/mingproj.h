@@ -240,6 +240,50 @@ int mp_modulation_free(mp_ctx* ctx, mp_modset* set);
 int mp_modulation_all(mp_ctx* ctx, const mp_modset* set, const void* temb, int m, void* mods,
                       void* nw1, void* nw3, void* stream);
 
+/* ---- pack I/O ------------------------------------------------------------ */
+
+/* A safetensors checkpoint or pack opened for reading: one file, or every
+ * *.safetensors file of a directory (shards), memory-mapped; host only (no
+ * device needed). Replaces: the WeightSet reads of the DiT's tensors
+ * (load_qw_ / load_block_, src/ming-dit.cc:802-864). */
+typedef struct mp_pack mp_pack;
+typedef struct {
+  const char* name;   /* valid while the pack is open */
+  const char* dtype;  /* "BF16", "F16", "F32", "U32", ... */
+  int32_t ndim;
+  int64_t shape[8];
+  const void* data;   /* host pointer into the mapped file */
+  size_t bytes;
+} mp_tensor_info;
+int mp_pack_open(const char* path, mp_pack** out);
+/* Why the last mp_pack_open / mp_pack_quantize of this thread failed. */
+const char* mp_pack_last_error(void);
+int mp_pack_close(mp_pack* pack);
+int mp_pack_count(const mp_pack* pack);
+int mp_pack_tensor_at(const mp_pack* pack, int i, mp_tensor_info* info);
+/* MP_EINVAL when the tensor is absent. */
+int mp_pack_find(const mp_pack* pack, const char* name, mp_tensor_info* info);
+/* A "__metadata__" value, or NULL. */
+const char* mp_pack_metadata(const mp_pack* pack, const char* key);
+const char* mp_pack_error(const mp_pack* pack);
+/* Uploads projection `base` ("layers.3.attention.to_q") as load_qw_ does
+ * (src/ming-dit.cc:802-831, detection :1115-1135): packed when
+ * `<base>.scales` sits beside `<base>.weight` (U32 codes [N, K*bits/32],
+ * scales / biases [N, K/64] narrowed to bf16; no biases = symmetric 8-bit),
+ * bits from the shapes (4 or 8); otherwise the dense `<base>.weight`
+ * (narrowed to bf16). */
+int mp_pack_upload(mp_ctx* ctx, const mp_pack* pack, const char* base, mp_weight** out);
+/* Writes a w8 / w4 pack of the dense checkpoint `src` (a .safetensors file,
+ * or a directory of shards plus config.json) to `dst` (a file, or a
+ * directory created if needed): the reference's selection
+ * (src/ming-quant-family.cc:31-59) quantized with per-64-group affine
+ * min/max scales and biases (bf16) and codes packed LSB first; every other
+ * tensor copied unchanged; config.json gains "quantization": {"bits",
+ * "group_size"}. Host only. Counts of quantized / copied tensors in
+ * *n_quantized / *n_kept (nullable). Replaces: the host's model-quantize run
+ * for this family (tests/ming-quant-test.cc:507-549 pins its selection). */
+int mp_pack_quantize(const char* src, const char* dst, int bits, int* n_quantized, int* n_kept);
+
 /* ---- allocation-free projection ---------------------------------------- */
 
 /* No counterpart in the reference. For callers that cannot call cudaMalloc —

@@ -94,6 +94,42 @@ def test_pack_forward(ctx):
     assert err <= BAR, f"pack rel-L2 {err:.4f}"
 
 
+def test_pack_file_forward(ctx, tmp_path):
+    """The same w8 pack written by the library's C++ pack writer to a
+    .safetensors file and read back by its reader (projections uploaded by
+    mp_pack_upload's load_qw_-style detection): the forward is bit-identical to
+    the one built from the Python-quantized arrays, and within the bar of the
+    fp32 oracle on the dequantized weights."""
+    from mingproj.lora import write_safetensors
+    from mingproj.packio import Pack, quantize_pack
+    w = fx.make_weights(0)
+    src, dst = tmp_path / "dense.safetensors", tmp_path / "w8.safetensors"
+    write_safetensors(src, w)
+    nq, _ = quantize_pack(src, dst, 8)
+    assert nq == 6 * (2 * fx.NREF + fx.NLAY) + (fx.NREF + fx.NLAY)  # w2 (K 2730) stays dense
+    packed, deq = dict(w), fx.as_f32(w)
+    for k, v in w.items():
+        base = k[:-len(".weight")] if k.endswith(".weight") else None
+        if base is None or not any(base.endswith(n) for n in P.PROJ_NAMES + ("adaLN_modulation.0",)):
+            continue
+        if v.shape[1] % 64:
+            continue
+        pw = P.quantize_affine(P.bf16_bits_to_f32(v), 8)
+        packed[k] = pw
+        deq[k] = O.dequant(pw.data, pw.scales, pw.biases, pw.n, pw.k, 8).astype(np.float32)
+    with Pack(dst) as pk:
+        fwd = DitForward(ctx, CFG, pk, torch.device("cuda", 0))
+    y_file = _gpu(fwd, "case_b")
+    fwd.free()
+    fwd = DitForward(ctx, CFG, packed, torch.device("cuda", 0))
+    y_dict = _gpu(fwd, "case_b")
+    fwd.free()
+    ctx.sync_check()
+    assert torch.equal(y_file.view(torch.int16), y_dict.view(torch.int16))
+    err = O.rel_l2(y_file.float().cpu().numpy(), _ref(deq, "case_b"))
+    assert err <= BAR, f"pack-file rel-L2 {err:.4f}"
+
+
 def _adapter(seed=5, rank=8, alpha=16.0):
     rng = np.random.default_rng(seed)
     bound, fused_delta = {}, {}

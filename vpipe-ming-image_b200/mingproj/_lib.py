@@ -39,6 +39,11 @@ class Engagement(C.Structure):
         return {name: getattr(self, name) for name, _ in self._fields_}
 
 
+class TensorInfo(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("dtype", C.c_char_p), ("ndim", _i32),
+                ("shape", _i64 * 8), ("data", C.c_void_p), ("bytes", C.c_size_t)]
+
+
 SIGNATURES = {
     "mp_create": (C.c_int, [C.c_int, C.POINTER(_vp)]),
     "mp_destroy": (C.c_int, [_vp]),
@@ -70,6 +75,17 @@ SIGNATURES = {
     "mp_modulation_all": (C.c_int, [_vp, _vp, _vp, C.c_int, _vp, _vp, _vp, _vp]),
     "mp_linear_lora_static": (C.c_int, [_vp, _vp, _vp, _i64, _vp, _vp, C.c_int, C.c_float, _vp,
                                         _i64, C.c_int, _vp]),
+    "mp_pack_open": (C.c_int, [C.c_char_p, C.POINTER(_vp)]),
+    "mp_pack_last_error": (C.c_char_p, []),
+    "mp_pack_close": (C.c_int, [_vp]),
+    "mp_pack_count": (C.c_int, [_vp]),
+    "mp_pack_tensor_at": (C.c_int, [_vp, C.c_int, C.POINTER(TensorInfo)]),
+    "mp_pack_find": (C.c_int, [_vp, C.c_char_p, C.POINTER(TensorInfo)]),
+    "mp_pack_metadata": (C.c_char_p, [_vp, C.c_char_p]),
+    "mp_pack_error": (C.c_char_p, [_vp]),
+    "mp_pack_upload": (C.c_int, [_vp, _vp, C.c_char_p, C.POINTER(_vp)]),
+    "mp_pack_quantize": (C.c_int, [C.c_char_p, C.c_char_p, C.c_int, C.POINTER(C.c_int),
+                                   C.POINTER(C.c_int)]),
     "mp_engagement_get": (C.c_int, [_vp, C.POINTER(Engagement)]),
     "mp_engagement_reset": (C.c_int, [_vp]),
 }

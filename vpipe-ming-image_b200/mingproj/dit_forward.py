@@ -23,6 +23,7 @@ import torch.nn.functional as F
 
 from .dit import DitDims, DitProjectionSet
 from .pack import PROJ_NAMES, PackedWeight, bf16_bits_to_f32
+from .packio import Pack
 from .proj import Context
 
 X_EMBEDDER = "all_x_embedder.2-1"
@@ -61,7 +62,7 @@ class DitModelConfig:
 
 
 def _bf16(a) -> torch.Tensor:
-    """uint16 bf16 bits (numpy) or float array -> torch bf16 (CPU)."""
+    """uint16 bf16 bits (numpy) or float array (f16 / f32) -> torch bf16 (CPU)."""
     if isinstance(a, torch.Tensor):
         return a.to(torch.bfloat16)
     a = np.asarray(a)
@@ -99,51 +100,56 @@ def layout_positions(grid_h: int, grid_w: int, cap_len: int) -> np.ndarray:
 
 
 class DitForward:
-    """One DiT on one device. `weights` maps checkpoint names to bf16 bit
-    arrays (uint16) for dense tensors, and block projections may instead be
-    PackedWeight (a w8/w4 pack)."""
+    """One DiT on one device. `weights` is either a dict mapping checkpoint
+    names to bf16 bit arrays (uint16) for dense tensors, where block
+    projections may instead be PackedWeight (a w8/w4 pack), or an open
+    mingproj.packio.Pack (a checkpoint or pack read by the library's own
+    safetensors reader; projections uploaded as load_qw_ detects them)."""
 
-    def __init__(self, ctx: Context, cfg: DitModelConfig, weights: dict, device):
+    def __init__(self, ctx: Context, cfg: DitModelConfig, weights, device):
         self.ctx, self.cfg, self.dev = ctx, cfg, device
         dims = cfg.proj_dims()
         self.dims = dims
         self.proj = DitProjectionSet(ctx, dims)
+        is_pack = isinstance(weights, Pack)
+
+        def matrix(base: str):
+            if is_pack:
+                return weights.upload(ctx, base)
+            v = weights[base + ".weight"] if (base + ".weight") in weights else weights[base]
+            if isinstance(v, PackedWeight):
+                return ctx.upload(v.n, v.k, v.bits, v.data, v.scales, v.biases, mode=v.mode)
+            t = _bf16(v)
+            return ctx.upload(t.shape[0], t.shape[1], 0, t.contiguous())
+
+        def tensor(name: str):
+            return _bf16(weights.array(name) if is_pack else weights[name])
+
         for b in range(dims.n_blocks):
             pre = dims.block_prefix(b)
             for name in PROJ_NAMES:
-                v = weights[pre + name + ".weight"] if (pre + name + ".weight") in weights else \
-                    weights[pre + name]
-                if isinstance(v, PackedWeight):
-                    w = ctx.upload(v.n, v.k, v.bits, v.data, v.scales, v.biases, mode=v.mode)
-                else:
-                    t = _bf16(v)
-                    w = ctx.upload(t.shape[0], t.shape[1], 0, t.contiguous())
-                self.proj.blocks[b].proj[name] = w
+                self.proj.blocks[b].proj[name] = matrix(pre + name)
         # adaLN of the modulated blocks, in the order noise_refiner..., layers...
         ada, biases, an1, fn1 = [], [], [], []
         for b in range(cfg.n_refiner, dims.n_blocks):
             pre = dims.block_prefix(b)
-            v = weights[pre + "adaLN_modulation.0.weight"]
-            if isinstance(v, PackedWeight):
-                ada.append(ctx.upload(v.n, v.k, v.bits, v.data, v.scales, v.biases, mode=v.mode))
-            else:
-                t = _bf16(v)
-                ada.append(ctx.upload(t.shape[0], t.shape[1], 0, t.contiguous()))
-            biases.append(_bf16(weights[pre + "adaLN_modulation.0.bias"]).to(device))
-            an1.append(_bf16(weights[pre + "attention_norm1.weight"]).to(device))
-            fn1.append(_bf16(weights[pre + "ffn_norm1.weight"]).to(device))
+            ada.append(matrix(pre + "adaLN_modulation.0"))
+            biases.append(tensor(pre + "adaLN_modulation.0.bias").to(device))
+            an1.append(tensor(pre + "attention_norm1.weight").to(device))
+            fn1.append(tensor(pre + "ffn_norm1.weight").to(device))
         self.ada = ada
         self.modset = ctx.modulation_set(ada, biases, an1, fn1)
         self._keep = (biases, an1, fn1)
         # every other tensor as a device bf16 tensor
         self.t = {}
-        for k, v in weights.items():
-            if isinstance(v, PackedWeight):
+        names = weights.names() if is_pack else list(weights)
+        for k in names:
+            if not is_pack and isinstance(weights[k], PackedWeight):
                 continue
             if any(k.startswith(dims.block_prefix(b) + n) for b in range(dims.n_blocks)
                    for n in PROJ_NAMES + ("adaLN_modulation.0",)):
                 continue
-            self.t[k] = _bf16(v).to(device)
+            self.t[k] = tensor(k).to(device)
 
     # ---- pieces ------------------------------------------------------------
     def _rms(self, x: torch.Tensor, w: torch.Tensor | None, eps: float | None = None):

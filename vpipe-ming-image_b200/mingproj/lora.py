@@ -40,7 +40,8 @@ _PREFIXES = ("base_model.model.", "transformer.", "diffusion_model.", "model.")
 _META_ALPHA_KEYS = ("lora_alpha", "alpha", "ss_network_alpha")
 
 _DTYPES = {"BF16": (np.uint16, 2), "F16": (np.float16, 2), "F32": (np.float32, 4),
-           "F64": (np.float64, 8)}
+           "F64": (np.float64, 8), "U32": (np.uint32, 4), "I32": (np.int32, 4),
+           "U8": (np.uint8, 1), "I64": (np.int64, 8)}
 
 
 def read_safetensors(path) -> tuple[dict[str, np.ndarray], dict[str, str], dict[str, str]]:
@@ -74,7 +75,9 @@ def write_safetensors(path, tensors: dict[str, np.ndarray], dtypes: dict[str, st
         dt = (dtypes or {}).get(name)
         if dt is None:
             dt = {np.dtype(np.uint16): "BF16", np.dtype(np.float16): "F16",
-                  np.dtype(np.float32): "F32", np.dtype(np.float64): "F64"}[arr.dtype]
+                  np.dtype(np.float32): "F32", np.dtype(np.float64): "F64",
+                  np.dtype(np.uint32): "U32", np.dtype(np.int32): "I32",
+                  np.dtype(np.uint8): "U8", np.dtype(np.int64): "I64"}[arr.dtype]
         b = arr.tobytes()
         header[name] = {"dtype": dt, "shape": list(arr.shape), "data_offsets": [off, off + len(b)]}
         blobs.append(b)
