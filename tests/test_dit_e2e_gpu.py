@@ -130,6 +130,55 @@ def test_pack_file_forward(ctx, tmp_path):
     assert err <= BAR, f"pack-file rel-L2 {err:.4f}"
 
 
+def test_caption_cache(ctx, dense):
+    """The caption cache (src/ming-dit.cc:1543-1577): the same caption bytes
+    hit (also for another image size) and give the bits a cold forward gives;
+    another caption, a strength change or a new adapter binding misses."""
+    fwd, w = dense
+    fwd._cap_cache.clear()
+    lat, cap, q, gh, gw = fx.make_inputs("case_a")
+    y0 = fwd.forward(_dev(lat), _dev(cap), q, gh, gw, fx.SIGMA)
+    assert not fwd.last_cap_cache_hit
+    y1 = fwd.forward(_dev(lat), _dev(cap), q, gh, gw, fx.SIGMA)
+    assert fwd.last_cap_cache_hit and torch.equal(y0.view(torch.int16), y1.view(torch.int16))
+    # another image size (case_c: 16 x 15) with the same caption: a hit, and
+    # the bits of a forward with the cache off
+    lat_c, _, _, gh_c, gw_c = fx.make_inputs("case_c")
+    y2 = fwd.forward(_dev(lat_c), _dev(cap), q, gh_c, gw_c, 0.3)
+    assert fwd.last_cap_cache_hit
+    fwd.cap_cache_entries = 0
+    fwd._cap_cache.clear()
+    y2_cold = fwd.forward(_dev(lat_c), _dev(cap), q, gh_c, gw_c, 0.3)
+    assert torch.equal(y2.view(torch.int16), y2_cold.view(torch.int16))
+    fwd.cap_cache_entries = 4
+    fwd.forward(_dev(lat), _dev(cap), q, gh, gw, fx.SIGMA)  # refills the entry
+    assert not fwd.last_cap_cache_hit
+    # a different caption misses; both entries then serve
+    _, cap_b, q_b, _, _ = fx.make_inputs("case_b")
+    fwd.forward(_dev(lat), _dev(cap_b), q_b, gh, gw, fx.SIGMA)
+    assert not fwd.last_cap_cache_hit
+    fwd.forward(_dev(lat), _dev(cap), q, gh, gw, fx.SIGMA)
+    assert fwd.last_cap_cache_hit
+    fwd.forward(_dev(lat), _dev(cap_b), q_b, gh, gw, fx.SIGMA)
+    assert fwd.last_cap_cache_hit
+    # a strength change drops every entry
+    ctx.set_strength(3, 0.5)
+    fwd.forward(_dev(lat), _dev(cap), q, gh, gw, fx.SIGMA)
+    assert not fwd.last_cap_cache_hit
+    ctx.set_strength(3, 1.0)
+    fwd.forward(_dev(lat), _dev(cap), q, gh, gw, fx.SIGMA)
+    assert not fwd.last_cap_cache_hit
+    # a new binding drops them too (its strength was already 1.0)
+    binding, _ = _adapter(seed=9)
+    fwd.proj.bind_slot(1, binding)
+    ya = fwd.forward(_dev(lat), _dev(cap), q, gh, gw, fx.SIGMA)
+    assert not fwd.last_cap_cache_hit
+    fwd.proj.unbind_slot(1)
+    yb = fwd.forward(_dev(lat), _dev(cap), q, gh, gw, fx.SIGMA)
+    assert not fwd.last_cap_cache_hit and torch.equal(yb.view(torch.int16), y1.view(torch.int16))
+    assert not torch.equal(ya.view(torch.int16), y1.view(torch.int16))
+
+
 def _adapter(seed=5, rank=8, alpha=16.0):
     rng = np.random.default_rng(seed)
     bound, fused_delta = {}, {}

@@ -132,6 +132,7 @@ class DitProjectionSet:
         self.modset: ModSet | None = None
         self.ada: list[Weight] = []
         self.slot_ranks: list[dict[str, int]] = [dict() for _ in range(8)]
+        self.binding_version = 0  # counts bind / unbind calls (caches keyed on the adapters)
 
     # ---- construction ------------------------------------------------------
     @classmethod
@@ -192,6 +193,7 @@ class DitProjectionSet:
         """Binds what `binding` holds into slot `slot` of every module; returns
         the number of modules bound (0 when the slot was refused)."""
         self.unbind_slot(slot)
+        self.binding_version += 1
         for b in range(self.dims.n_blocks):
             pre = self.dims.block_prefix(b)
             for name in PROJ_NAMES:
@@ -204,6 +206,7 @@ class DitProjectionSet:
     def bind_synthetic(self, slot: int, rank: int, seed: int, device, b_std: float = 0.01) -> int:
         """A ~N(0, 1/r), B ~N(0, b_std) on every module."""
         self.unbind_slot(slot)
+        self.binding_version += 1
         gen = torch.Generator(device=device)
         gen.manual_seed(seed)
         for b in range(self.dims.n_blocks):
@@ -221,6 +224,7 @@ class DitProjectionSet:
     def unbind_slot(self, slot: int) -> None:
         if not self.slot_ranks[slot]:
             return
+        self.binding_version += 1
         for b in range(self.dims.n_blocks):
             for name in PROJ_NAMES:
                 w = self.blocks[b].proj[name]

@@ -150,6 +150,11 @@ class DitForward:
                    for n in PROJ_NAMES + ("adaLN_modulation.0",)):
                 continue
             self.t[k] = tensor(k).to(device)
+        self.cap_cache_entries = 4
+        self._cap_cache: list[dict] = []
+        self._cap_strengths: tuple | None = None
+        self._tick = 0
+        self.last_cap_cache_hit = False
 
     # ---- pieces ------------------------------------------------------------
     def _rms(self, x: torch.Tensor, w: torch.Tensor | None, eps: float | None = None):
@@ -244,11 +249,7 @@ class DitForward:
         nref = cfg.n_refiner
         for i in range(nref):
             x = self._block(nref + i, x, cos[:img], sin[:img], i, mods, nw1, nw3)
-        ca = self._rms(cap[:query_rows, : cfg.cap_feat_dim].to(dev), self.t["cap_embedder.0.weight"])
-        ca = self._linear(ca, "cap_embedder.1")
-        cj = torch.cat([ca, cap[query_rows:, : cfg.dim].to(dev)], dim=0)
-        for i in range(nref):
-            cj = self._block(i, cj, cos[img:], sin[img:], None, mods, nw1, nw3)
+        cj = self._context(cap, query_rows, cos[img:], sin[img:], mods, nw1, nw3)
         j = torch.cat([x, cj], dim=0).contiguous()
         for i in range(cfg.n_layers):
             j = self._block(2 * nref + i, j, cos, sin, nref + i, mods, nw1, nw3)
@@ -256,6 +257,43 @@ class DitForward:
         xi = F.layer_norm(j[:img].float(), (cfg.dim,), eps=1e-6)
         xi = (xi * (1.0 + scale.float())).to(torch.bfloat16)
         return self._linear(xi, FINAL + ".linear")
+
+    def _context(self, cap: torch.Tensor, query_rows: int, cos, sin, mods, nw1, nw3) -> torch.Tensor:
+        """The caption rows after the context refiner, through the caption
+        cache (the reference's, src/ming-dit.cc:1543-1577): keyed on the
+        caption's exact bytes, its shape and the query-row split; the context
+        rows' rotary positions depend on the caption alone, so one entry serves
+        every image size; a few entries, least recently used replaced; an
+        entry is stored only once its rows are complete. The context refiner's
+        projections carry the adapters, so any change of a live strength drops
+        every entry (set_lora_scale does, :3031-3038; here the strengths and
+        the adapter bindings are compared with those the entries were made
+        under)."""
+        cfg, dev = self.cfg, self.dev
+        strengths = (tuple(self.ctx.strength(i) for i in range(8)), self.proj.binding_version)
+        if strengths != self._cap_strengths:
+            self._cap_cache.clear()
+            self._cap_strengths = strengths
+        key = cap.to(dev)
+        self._tick += 1
+        for e in self._cap_cache:
+            if (e["q"] == query_rows and e["key"].shape == key.shape and
+                    torch.equal(e["key"].view(torch.int16), key.view(torch.int16))):
+                e["tick"] = self._tick
+                self.last_cap_cache_hit = True
+                return e["out"]
+        self.last_cap_cache_hit = False
+        ca = self._rms(key[:query_rows, : cfg.cap_feat_dim], self.t["cap_embedder.0.weight"])
+        ca = self._linear(ca, "cap_embedder.1")
+        cj = torch.cat([ca, key[query_rows:, : cfg.dim]], dim=0)
+        for i in range(cfg.n_refiner):
+            cj = self._block(i, cj, cos, sin, None, mods, nw1, nw3)
+        if self.cap_cache_entries > 0:
+            if len(self._cap_cache) >= self.cap_cache_entries:
+                self._cap_cache.remove(min(self._cap_cache, key=lambda e: e["tick"]))
+            self._cap_cache.append({"key": key.clone(), "q": query_rows, "out": cj,
+                                    "tick": self._tick})
+        return cj
 
     def free(self) -> None:
         self.proj.free()
