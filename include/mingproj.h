@@ -196,13 +196,16 @@ int mp_linear_heads(mp_ctx* ctx, const mp_weight* const* ws, void* const* ys, in
 /* Non-causal attention, head dim 128, over the head-major q, k, v that
  * mp_linear_heads writes: for head h and query row i < s,
  *   o[i][128h .. 128h + 127] = softmax(scale * q_i . K_h^T) . V_h   (bf16 out)
- * q, k, v: device bf16 [nh][s][128], 16-byte aligned; o: device bf16 [s][ldo],
- * ldo >= 128 * nh and a multiple of 8 (token-major: the to_out projection's
- * input as it is). P is rounded to bf16 for the P.V product; row statistics
- * in f32. Replaces: run_attn over a block's rows and the transpose back to
+ * q, k, v: device bf16, head h's s rows of 128 at element offset
+ * h * head_stride (0: s * 128, i.e. [nh][s][128]; a batch of images sharing
+ * one head-major tensor passes its own first row and the whole tensor's
+ * head stride), 16-byte aligned; o: device bf16 [s][ldo], ldo >= 128 * nh
+ * and a multiple of 8 (token-major: the to_out projection's input as it
+ * is). P is rounded to bf16 for the P.V product; row statistics in f32.
+ * Replaces: run_attn over a block's rows and the transpose back to
  * token-major (src/ming-dit.cc:1905-2039, :2090-2092). */
 int mp_attention(mp_ctx* ctx, const void* q, const void* k, const void* v, int s, int nh,
-                 float scale, void* o, int64_t ldo, void* stream);
+                 int64_t head_stride, float scale, void* o, int64_t ldo, void* stream);
 
 /* The sandwich-norm residual step after to_out and after w2, one pass over
  * the rows:

@@ -222,3 +222,26 @@ def test_runtime_lora_matches_fused_and_strength_zero_is_base(ctx, dense):
     assert moved > 0.1 and moved > 10 * vs_fused, f"moved {moved:.4f}, err {vs_fused:.4f}"
     assert torch.equal(off.view(torch.int16), base.view(torch.int16)), "strength 0 != base"
     assert torch.equal(again.view(torch.int16), adapted.view(torch.int16)), "not repeatable"
+
+
+def test_cfg_batch_matches_separate_forwards(ctx, dense):
+    """Classifier-free guidance as one batched pass (the conditional and the
+    negative caption over the same latents): every
+    projection runs once over both images' rows, and each image's output has
+    the bits of its own forward, with per-image timesteps too."""
+    fwd, w = dense
+    lat, cap, q, gh, gw = fx.make_inputs("case_a")
+    neg = np.zeros_like(cap)
+    lat2 = fx.make_inputs("case_b")[0]
+    lat_d = torch.stack([_dev(lat), _dev(lat2)])
+    fwd._cap_cache.clear()
+    yb = fwd.forward_batch(lat_d, [_dev(cap), _dev(neg)], q, gh, gw, [fx.SIGMA, 0.3])
+    fwd._cap_cache.clear()
+    y0 = fwd.forward(_dev(lat), _dev(cap), q, gh, gw, fx.SIGMA)
+    y1 = fwd.forward(_dev(lat2), _dev(neg), q, gh, gw, 0.3)
+    assert yb.shape == (2,) + tuple(y0.shape)
+    assert torch.equal(yb[0].view(torch.int16), y0.view(torch.int16)), "image 0 differs"
+    assert torch.equal(yb[1].view(torch.int16), y1.view(torch.int16)), "image 1 differs"
+    # and against the fp32 restatement, image by image
+    ref0 = _ref(fx.as_f32(w), "case_a")
+    assert O.rel_l2(yb[0].float().cpu().numpy(), ref0) <= BAR

@@ -1236,7 +1236,7 @@ int mp_linear_heads(mp_ctx* c, const mp_weight* const* ws, void* const* ys, int 
 }
 
 int mp_attention(mp_ctx* c, const void* q, const void* k, const void* v, int s, int nh,
-                 float scale, void* o, int64_t ldo, void* stream) {
+                 int64_t head_stride, float scale, void* o, int64_t ldo, void* stream) {
   if (c == nullptr) return MP_EINVAL;
   if (s <= 0 || nh <= 0) return fail(c, MP_EINVAL, "s and nh must be positive (%d, %d)", s, nh);
   if (!(scale > 0.0f)) return fail(c, MP_EINVAL, "scale must be positive");
@@ -1246,6 +1246,10 @@ int mp_attention(mp_ctx* c, const void* q, const void* k, const void* v, int s, 
   if (ldo < static_cast<int64_t>(nh) * mp::kHeadDim || ldo % 8 != 0)
     return fail(c, MP_EINVAL, "ldo must be >= 128 * nh and a multiple of 8 (got %lld)",
                 static_cast<long long>(ldo));
+  if (head_stride == 0) head_stride = static_cast<int64_t>(s) * mp::kHeadDim;
+  if (head_stride < static_cast<int64_t>(s) * mp::kHeadDim || head_stride % 8 != 0)
+    return fail(c, MP_EINVAL, "head_stride must be >= 128 * s and a multiple of 8 (got %lld)",
+                static_cast<long long>(head_stride));
   int rc = use_device(c);
   if (rc != MP_OK) return rc;
   EncodeTiledFn fn = encode_fn();
@@ -1254,7 +1258,7 @@ int mp_attention(mp_ctx* c, const void* q, const void* k, const void* v, int s, 
   std::memset(&p, 0, sizeof(p));
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(mp::kHeadDim), static_cast<cuuint64_t>(s),
                               static_cast<cuuint64_t>(nh)};
-  const cuuint64_t strides[2] = {mp::kHeadDim * 2, static_cast<cuuint64_t>(s) * mp::kHeadDim * 2};
+  const cuuint64_t strides[2] = {mp::kHeadDim * 2, static_cast<cuuint64_t>(head_stride) * 2};
   // q and v: boxes of 64 dims x 128 rows; k: 64 dims x 64 keys (each CTA of a
   // pair loads half of a 128-key step)
   const cuuint32_t boxes[3][3] = {{64, 128, 1}, {64, 64, 1}, {64, 128, 1}};

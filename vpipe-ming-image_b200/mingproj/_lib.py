@@ -57,7 +57,8 @@ SIGNATURES = {
                                   C.POINTER(_vp), C.c_float, _vp, _vp, _vp]),
     "mp_rms_residual": (C.c_int, [_vp, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _vp, C.c_int,
                                   C.c_int, C.c_float, _vp]),
-    "mp_attention": (C.c_int, [_vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_float, _vp, _i64, _vp]),
+    "mp_attention": (C.c_int, [_vp, _vp, _vp, _vp, C.c_int, C.c_int, _i64, C.c_float, _vp, _i64,
+                               _vp]),
     "mp_weight_upload": (C.c_int, [_vp, C.POINTER(WeightDesc), _vp, _vp, _vp, C.POINTER(_vp)]),
     "mp_weight_free": (C.c_int, [_vp, _vp]),
     "mp_weight_read_codes": (C.c_int, [_vp, _vp, _vp, C.c_size_t]),

@@ -177,51 +177,66 @@ class DitForward:
     def _linear(self, x: torch.Tensor, name: str) -> torch.Tensor:
         return F.linear(x, self.t[name + ".weight"], self.t.get(name + ".bias"))
 
-    def _block(self, b: int, x: torch.Tensor, cos, sin, mod_idx: int | None, mods, nw1, nw3):
+    def _block(self, b: int, x: torch.Tensor, cos, sin, mod_idx: int | None, mods, nw1, nw3,
+               nb: int = 1):
+        """Block b over `nb` sequences of equal length stacked in x (updated in
+        place): the projections run once over all rows, norms, gates and the
+        attention per sequence (sequence i takes modulation row i)."""
         cfg, pre = self.cfg, self.dims.block_prefix(b)
         t = self.t
-        R = x.shape[0]
+        R = x.shape[0] // nb
         H, nh, hd, FF = cfg.dim, cfg.n_heads, cfg.head_dim, cfg.ffn
         p = self.proj.blocks[b].proj
         modulated = mod_idx is not None
-        gain1 = nw1[mod_idx, 0] if modulated else t[pre + "attention_norm1.weight"]
-        nrm = self.ctx.rms_residual(x, None, nrm_gain=gain1, eps=cfg.norm_eps)
+        segs = [slice(i * R, (i + 1) * R) for i in range(nb)]
+        nrm = torch.empty_like(x)
+        for i, sl in enumerate(segs):
+            gain1 = nw1[mod_idx, i] if modulated else t[pre + "attention_norm1.weight"]
+            self.ctx.rms_residual(x[sl], None, nrm_gain=gain1, eps=cfg.norm_eps, nrm=nrm[sl])
         qkv = [p["attention.to_q"], p["attention.to_k"], p["attention.to_v"]]
         if hd == 128:
             # one launch: q/k/v head-major, q and k through the head RMSNorm and
-            # the rotary embedding in the projection epilogue
+            # the rotary embedding in the projection epilogue; then the tcgen05
+            # attention per sequence, writing its rows of the token-major to_out input
+            cs, sn = (cos, sin) if nb == 1 else (cos.repeat(nb, 1), sin.repeat(nb, 1))
             q, k, v = self.ctx.linear_heads(
                 qkv, nrm, norm_w=[t[pre + "attention.norm_q.weight"],
                                   t[pre + "attention.norm_k.weight"], None],
-                eps=cfg.norm_eps, rope_cos=cos, rope_sin=sin)
+                eps=cfg.norm_eps, rope_cos=cs, rope_sin=sn)
+            a = torch.empty((nb * R, H), dtype=torch.bfloat16, device=x.device)
+            for sl in segs:
+                self.ctx.attention(q[:, sl], k[:, sl], v[:, sl], out=a[sl])
         else:
-            q, k, v = self.ctx.linear_shared(qkv, nrm)
-            q = self._rope(self._rms(q.view(R, nh, hd), t[pre + "attention.norm_q.weight"]),
-                           cos, sin).transpose(0, 1)
-            k = self._rope(self._rms(k.view(R, nh, hd), t[pre + "attention.norm_k.weight"]),
-                           cos, sin).transpose(0, 1)
-            v = v.view(R, nh, hd).transpose(0, 1)
-        if hd == 128:
-            # the tcgen05 attention kernel, writing the token-major to_out input
-            a = self.ctx.attention(q, k, v)
-        else:
-            att = F.scaled_dot_product_attention(q[None], k[None], v[None])
-            a = att[0].transpose(0, 1).reshape(R, H).contiguous()
+            qa, ka, va = self.ctx.linear_shared(qkv, nrm)
+            a = torch.empty((nb * R, H), dtype=torch.bfloat16, device=x.device)
+            for sl in segs:
+                q = self._rope(self._rms(qa[sl].reshape(R, nh, hd),
+                                         t[pre + "attention.norm_q.weight"]), cos, sin)
+                k = self._rope(self._rms(ka[sl].reshape(R, nh, hd),
+                                         t[pre + "attention.norm_k.weight"]), cos, sin)
+                v = va[sl].reshape(R, nh, hd)
+                att = F.scaled_dot_product_attention(q.transpose(0, 1)[None],
+                                                     k.transpose(0, 1)[None],
+                                                     v.transpose(0, 1)[None])
+                a[sl] = att[0].transpose(0, 1).reshape(R, H)
         o = self.ctx.linear(p["attention.to_out.0"], a)
-        # one pass: x += [tanh(gate_msa) *] rms(o, norm2); nrm = rms(x, ffn norm)
-        # (x is this block's own copy of the stream: updated in place)
-        gain3 = nw3[mod_idx, 0] if modulated else t[pre + "ffn_norm1.weight"]
-        nrm = self.ctx.rms_residual(x, o, t[pre + "attention_norm2.weight"],
-                                    mods[mod_idx, 0, H:2 * H] if modulated else None,
-                                    gain3, eps=cfg.norm_eps)
+        # one pass per sequence: x += [tanh(gate_msa) *] rms(o, norm2);
+        # nrm = rms(x, ffn norm) (x is this block's own copy of the stream)
+        for i, sl in enumerate(segs):
+            gain3 = nw3[mod_idx, i] if modulated else t[pre + "ffn_norm1.weight"]
+            self.ctx.rms_residual(x[sl], o[sl], t[pre + "attention_norm2.weight"],
+                                  mods[mod_idx, i, H:2 * H] if modulated else None,
+                                  gain3, eps=cfg.norm_eps, nrm=nrm[sl])
         # gate and up projections with the SwiGLU in their epilogue (one launch):
         # h = bf16(silu(g) * u) of the bf16 gate and up values, as gpu_ff computes it
         ld = (FF + 7) // 8 * 8
-        h = torch.empty((R, ld), dtype=torch.bfloat16, device=x.device)
+        h = torch.empty((nb * R, ld), dtype=torch.bfloat16, device=x.device)
         self.ctx.linear_swiglu(p["feed_forward.w1"], p["feed_forward.w3"], nrm, out=h[:, :FF])
         f = self.ctx.linear(p["feed_forward.w2"], h[:, :FF])
-        self.ctx.rms_residual(x, f, t[pre + "ffn_norm2.weight"],
-                              mods[mod_idx, 0, 3 * H:] if modulated else None, eps=cfg.norm_eps)
+        for i, sl in enumerate(segs):
+            self.ctx.rms_residual(x[sl], f[sl], t[pre + "ffn_norm2.weight"],
+                                  mods[mod_idx, i, 3 * H:] if modulated else None,
+                                  eps=cfg.norm_eps)
         return x
 
     # ---- the forward -------------------------------------------------------
@@ -231,32 +246,61 @@ class DitForward:
         """latents bf16 [img, patch_dim]; cap bf16 [cap_len, >= dim] (stream A in
         rows [0, query_rows) x columns [0, cap_feat_dim)). Returns bf16
         [img, patch_dim], the model output before the pipeline's negation."""
+        return self.forward_batch(latents[None], [cap], query_rows, grid_h, grid_w, sigma)[0]
+
+    @torch.no_grad()
+    def forward_batch(self, latents: torch.Tensor, caps, query_rows: int, grid_h: int,
+                      grid_w: int, sigmas) -> torch.Tensor:
+        """A batch of B images of one layout in ONE pass (CFG: the conditional
+        and the negative caption with the same latents):
+        latents bf16 [B, img, patch_dim]; caps: B captions of the same shape;
+        sigmas: one value or B values. Every projection runs over the B images'
+        rows at once; the modulation takes B timestep rows in its one launch;
+        norms, gates and attention stay per image, so image i's output is what
+        forward() gives for it alone. Returns bf16 [B, img, patch_dim]."""
         cfg, dev = self.cfg, self.dev
+        B = latents.shape[0]
+        if len(caps) != B or any(c.shape != caps[0].shape for c in caps):
+            raise ValueError("one caption per image, all of the same shape")
+        sig = [float(sigmas)] * B if np.isscalar(sigmas) else [float(x) for x in sigmas]
+        if len(sig) != B or B > 4:
+            raise ValueError("one sigma per image; at most 4 images (the modulation's rows)")
         img = grid_h * grid_w
-        cap_len = cap.shape[0]
+        cap_len = caps[0].shape[0]
         c, s = rope_tables(layout_positions(grid_h, grid_w, cap_len), cfg.head_dim, cfg.axes,
                            cfg.rope_theta)
         cos = torch.from_numpy(c).to(dev)
         sin = torch.from_numpy(s).to(dev)
         half = cfg.time_freq // 2
-        tt = cfg.t_scale * (1.0 - sigma)
         f = np.exp(-math.log(10000.0) * np.arange(half, dtype=np.float64) / half)
-        emb = np.concatenate([np.cos(tt * f), np.sin(tt * f)]).astype(np.float32)
-        emb = torch.from_numpy(emb).to(dev).to(torch.bfloat16)[None]
-        temb = self._linear(F.silu(self._linear(emb, "t_embedder.mlp.0")), "t_embedder.mlp.2")
+        emb = np.stack([np.concatenate([np.cos(cfg.t_scale * (1.0 - sg) * f),
+                                        np.sin(cfg.t_scale * (1.0 - sg) * f)]) for sg in sig])
+        emb = torch.from_numpy(emb.astype(np.float32)).to(dev).to(torch.bfloat16)
+        # the model-level dense layers (library GEMMs) run per image: a library
+        # GEMM over B rows may pick another algorithm than over one, and image
+        # i's bits must not depend on the batch; the modulation, projections
+        # and norms are this library's kernels, row-independent by design
+        temb = torch.cat([self._linear(F.silu(self._linear(emb[bi:bi + 1], "t_embedder.mlp.0")),
+                                       "t_embedder.mlp.2") for bi in range(B)])
         mods, nw1, nw3 = self.ctx.modulation(self.modset, temb.contiguous())
-        x = self._linear(latents.to(dev), X_EMBEDDER)
+        lat = latents.to(dev)
+        x = torch.cat([self._linear(lat[bi], X_EMBEDDER) for bi in range(B)])
         nref = cfg.n_refiner
         for i in range(nref):
-            x = self._block(nref + i, x, cos[:img], sin[:img], i, mods, nw1, nw3)
-        cj = self._context(cap, query_rows, cos[img:], sin[img:], mods, nw1, nw3)
-        j = torch.cat([x, cj], dim=0).contiguous()
+            x = self._block(nref + i, x, cos[:img], sin[:img], i, mods, nw1, nw3, nb=B)
+        cjs = [self._context(cp, query_rows, cos[img:], sin[img:], mods, nw1, nw3) for cp in caps]
+        j = torch.cat([t for bi in range(B) for t in (x[bi * img:(bi + 1) * img], cjs[bi])],
+                      dim=0).contiguous()
         for i in range(cfg.n_layers):
-            j = self._block(2 * nref + i, j, cos, sin, nref + i, mods, nw1, nw3)
-        scale = self._linear(F.silu(temb), FINAL + ".adaLN_modulation.1")[0]
-        xi = F.layer_norm(j[:img].float(), (cfg.dim,), eps=1e-6)
-        xi = (xi * (1.0 + scale.float())).to(torch.bfloat16)
-        return self._linear(xi, FINAL + ".linear")
+            j = self._block(2 * nref + i, j, cos, sin, nref + i, mods, nw1, nw3, nb=B)
+        L = img + cap_len
+        out = []
+        for bi in range(B):
+            scale = self._linear(F.silu(temb[bi:bi + 1]), FINAL + ".adaLN_modulation.1")
+            xi = F.layer_norm(j[bi * L:bi * L + img].float(), (cfg.dim,), eps=1e-6)
+            xi = (xi * (1.0 + scale.float())).to(torch.bfloat16)
+            out.append(self._linear(xi, FINAL + ".linear"))
+        return torch.stack(out)
 
     def _context(self, cap: torch.Tensor, query_rows: int, cos, sin, mods, nw1, nw3) -> torch.Tensor:
         """The caption rows after the context refiner, through the caption

@@ -306,17 +306,21 @@ class Context:
                   scale: float | None = None, out: torch.Tensor | None = None,
                   stream=None) -> torch.Tensor:
         """Non-causal attention over head-major q, k, v (bf16 [nh, s, 128], as
-        linear_heads returns them); returns token-major bf16 [s, nh * 128]."""
+        linear_heads returns them, or one image's rows of a batch's head-major
+        tensor: a [:, r0:r1, :] view); returns token-major bf16 [s, nh * 128]
+        (into `out` when given, e.g. that image's rows of the batch)."""
         nh, s, hd = q.shape
         if hd != 128 or k.shape != q.shape or v.shape != q.shape:
             raise ValueError(f"q, k, v must be [nh, s, 128] alike (got {tuple(q.shape)}, "
                              f"{tuple(k.shape)}, {tuple(v.shape)})")
-        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        if not all(t.stride(1) == 128 and t.stride(2) == 1 and t.stride(0) == q.stride(0)
+                   for t in (q, k, v)):
+            q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
         if out is None:
             out = torch.empty((s, nh * 128), dtype=torch.bfloat16, device=q.device)
         sc = float(scale) if scale is not None else 1.0 / math.sqrt(hd)
-        self._check(self.lib.mp_attention(self.h, _ptr(q), _ptr(k), _ptr(v), s, nh, sc, _ptr(out),
-                                          out.stride(0), _stream_handle(stream)))
+        self._check(self.lib.mp_attention(self.h, _ptr(q), _ptr(k), _ptr(v), s, nh, q.stride(0),
+                                          sc, _ptr(out), out.stride(0), _stream_handle(stream)))
         return out
 
     def rms_residual(self, x: torch.Tensor, o: torch.Tensor | None, o_gain=None, gate=None,
