@@ -259,6 +259,91 @@ def run_rows(args) -> None:
         dist.destroy_process_group()
 
 
+def run_forward(args) -> None:
+    """`--forward`: the whole DiT forward of one 1024x1024 image (64 x 64
+    patches + 256 caption rows, the real model's shapes, seeded synthetic w8
+    weights and eight LoRA slots as in the default workload) per sampler step,
+    eager and as one CUDA-graph replay, for one image and for the CFG batch of
+    two (conditional + zero negative caption). The context refiner runs once
+    per caption (the caption cache) and is outside the timed steps, as in a
+    denoising loop. One GPU; prints one JSON line (not the projection metric)."""
+    import numpy as np
+    import torch
+
+    from mingproj.dit import Layout, projection_flops
+    from mingproj.dit_forward import DitForward, DitModelConfig
+    from mingproj.proj import Context
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = DitModelConfig()
+    ctx = Context(0)
+    fwd = DitForward.synthetic(ctx, cfg, bits=8, seed=1, device=dev)
+    for i, r in enumerate(RANKS):
+        fwd.proj.bind_synthetic(i, r, seed=100 + i, device=dev)
+    for i, sg in enumerate(np.random.default_rng(2).uniform(-1.0, 1.5, size=8)):
+        ctx.set_strength(i, float(sg))
+    gh = gw = 64
+    cap_len = q = 256
+    img = gh * gw
+    gen = torch.Generator(device=dev).manual_seed(3)
+    lat = torch.randn((2, img, cfg.patch_dim), device=dev, generator=gen).to(torch.bfloat16)
+    cap = torch.zeros((cap_len, cfg.dim), device=dev, dtype=torch.bfloat16)
+    cap[:, :cfg.cap_feat_dim] = torch.randn((cap_len, cfg.cap_feat_dim), device=dev,
+                                            generator=gen).to(torch.bfloat16)
+    caps = [cap, torch.zeros_like(cap)]
+    sigmas = np.linspace(0.95, 0.05, args.warmup + args.steps)
+    S = img + cap_len
+    layout = Layout(img=img, cap=cap_len)
+    base_f, lora_f = projection_flops(fwd.dims, layout, RANKS)
+    hd, nh = cfg.head_dim, cfg.n_heads
+    # attention: Q K^T and P V, 4 S^2 hd per head; noise refiner over the image
+    # rows, main layers over the joint rows (the context refiner is cached)
+    attn_f = 4.0 * hd * nh * (cfg.n_refiner * img * img + cfg.n_layers * S * S)
+    # projection_flops counts the context refiner's blocks too; they run once
+    # per caption, outside the step
+    H, FF, rsum = cfg.dim, cfg.ffn, float(sum(RANKS))
+    n_ctx = sum(fwd.dims.block_kind(b) == "cap" for b in range(fwd.dims.n_blocks))
+    ctx_f = n_ctx * 2.0 * cap_len * ((4 * H * H + 3 * FF * H) +
+                                     rsum * (4 * (H + H) + 3 * (H + FF)))
+    step_f = base_f + lora_f - ctx_f + attn_f
+
+    res = {}
+    with ClockSampler(0) as clk:
+        for B in (1, 2):
+            lb, cb = lat[:B], caps[:B]
+            runner = fwd.graph(B, q, gh, gw, cap_len)
+            for mode in ("eager", "graph"):
+                call = ((lambda sg: fwd.forward_batch(lb, cb, q, gh, gw, [sg] * B))
+                        if mode == "eager" else (lambda sg: runner(lb, cb, [sg] * B)))
+                for i in range(args.warmup):
+                    call(float(sigmas[i]))
+                torch.cuda.synchronize(dev)
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+                t0 = time.perf_counter()
+                ev[0].record()
+                for i in range(args.steps):
+                    call(float(sigmas[args.warmup + i]))
+                ev[1].record()
+                torch.cuda.synchronize(dev)
+                wall = (time.perf_counter() - t0) * 1e3 / args.steps
+                ms = ev[0].elapsed_time(ev[1]) / args.steps
+                res[f"{mode}_b{B}"] = {"ms_per_step": ms, "host_ms_per_step": wall,
+                                       "tflops": B * step_f / (ms / 1e3) / 1e12}
+            runner.release()
+    ctx.sync_check()
+    print(json.dumps({
+        "workload": "forward", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "config": {"model": "Ming-Image DiT (H 3840, 30 heads, 2+2 refiner, 30 layers), "
+                            "synthetic w8 g64, 8 LoRA slots r={4,..,64}",
+                   "image": "1024x1024 (64x64 patches)", "caption_rows": cap_len,
+                   "cfg_batch": [1, 2]},
+        "flops_per_image_step": step_f, "results": res, "clocks": clk.summary(),
+        "data": "synthetic"}))
+    fwd.free()
+    ctx.close()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -268,7 +353,12 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--shard", choices=["images", "rows"], default="images")
+    ap.add_argument("--forward", action="store_true",
+                    help="time the whole DiT forward (eager and CUDA graph) instead")
     args = ap.parse_args()
+    if args.forward:
+        run_forward(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return

@@ -149,6 +149,19 @@ int mp_get_strength(const mp_ctx* ctx, int slot, float* s);
  * own strength vectors uses it. */
 int mp_set_strengths_rows(mp_ctx* ctx, const float* s, const int32_t* row_starts, int batch);
 
+/* A counter that every change of a strength (to another value), of the row
+ * segments or of a LoRA binding advances. Launches captured into a CUDA graph
+ * keep the strengths, segments and stacked factors of their capture: a graph
+ * captured at version v is replayed only while the version is still v, and
+ * captured again otherwise. A launch made while its stream is capturing adds
+ * to the graph what keeps it correct on every replay (the fused LoRA
+ * prologue's ready flags are cleared before it), and the context never frees
+ * a buffer that grows after a capture (it is kept until mp_destroy). Warm up
+ * (one uncaptured call of the same shapes) before capturing, so that no
+ * buffer grows and no stacked factor is rebuilt inside the capture. No
+ * counterpart in the reference, which runs each block's encoder live. */
+int mp_state_version(const mp_ctx* ctx, uint64_t* version);
+
 /* ---- projections ------------------------------------------------------ */
 
 /* y[m, n] = x[m, k] · deq(W)^T + sum over live slots s_i · (x A_i^T) B_i^T,

@@ -245,3 +245,43 @@ def test_cfg_batch_matches_separate_forwards(ctx, dense):
     # and against the fp32 restatement, image by image
     ref0 = _ref(fx.as_f32(w), "case_a")
     assert O.rel_l2(yb[0].float().cpu().numpy(), ref0) <= BAR
+
+
+def test_graph_replay_matches_eager(ctx, dense):
+    """The per-step forward as one CUDA-graph replay: the bits of the eager
+    batched forward on the same inputs, step after step with new latents and
+    timesteps (one capture); a LoRA strength or binding change captures again
+    and the replay follows the new state."""
+    fwd, w = dense
+    lat, cap, q, gh, gw = fx.make_inputs("case_a")
+    lat2 = fx.make_inputs("case_b")[0]
+    caps = [_dev(cap), _dev(np.zeros_like(cap))]
+    runner = fwd.graph(2, q, gh, gw, cap.shape[0])
+    steps = [(torch.stack([_dev(lat), _dev(lat2)]), [0.9, 0.9]),
+             (torch.stack([_dev(lat2), _dev(lat)]), [0.5, 0.3]),
+             (torch.stack([_dev(lat), _dev(lat)]), [0.1, 0.7])]
+    outs = [runner(l, caps, s) for l, s in steps]
+    assert runner.captures == 1 and runner.replays == 3
+    for (l, s), y in zip(steps, outs):
+        ye = fwd.forward_batch(l, caps, q, gh, gw, s)
+        assert torch.equal(y.view(torch.int16), ye.view(torch.int16)), s
+    # an adapter bound and engaged: captured again, close to the eager path
+    # (which may take the fused LoRA prologue, with its own summation order)
+    binding, _ = _adapter(seed=11)
+    fwd.proj.bind_slot(2, binding)
+    ctx.set_strength(2, 0.8)
+    ya = runner(*steps[1][:1], caps, steps[1][1])
+    assert runner.captures == 2
+    ye = fwd.forward_batch(steps[1][0], caps, q, gh, gw, steps[1][1])
+    moved = O.rel_l2(outs[1].float().cpu().numpy(), ya.float().cpu().numpy())
+    err = O.rel_l2(ye.float().cpu().numpy(), ya.float().cpu().numpy())
+    assert moved > 0.05 and err < 5e-3, (moved, err)
+    # strength 0: captured again, and the base bits come back
+    ctx.set_strength(2, 0.0)
+    y0 = runner(*steps[1][:1], caps, steps[1][1])
+    assert runner.captures == 3
+    assert torch.equal(y0.view(torch.int16), outs[1].view(torch.int16))
+    fwd.proj.unbind_slot(2)
+    ctx.set_strength(2, 1.0)
+    runner.release()
+    ctx.sync_check()

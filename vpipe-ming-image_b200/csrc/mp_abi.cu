@@ -127,6 +127,15 @@ struct mp_ctx {
   size_t flags_cap = 0;         // entries
   uint32_t epoch = 0;           // value of a flag that is set, per fused launch
   bool fuse_off = false;        // cooperative launches refused on this device
+  // Set once a call was made while its stream was being captured into a CUDA
+  // graph: from then on the graph may hold this context's buffers, so a
+  // buffer that has to grow is retired (freed at destroy), never freed.
+  bool captured = false;
+  std::vector<void*> retired;
+  // Bumped by every change that alters what a launch computes (a strength,
+  // the row segments, a LoRA binding): a captured graph holds the values of
+  // its capture and is stale once this moves.
+  uint64_t state_version = 0;
   uint64_t wait_limit_ns = 2000000000ull;
   mp_engagement eng{};
   std::map<std::vector<uintptr_t>, SharedStack> shared;
@@ -228,17 +237,44 @@ uint32_t live_mask(const mp_ctx* c, const mp_weight* w) {
   return mask;
 }
 
+// True while `stream` is being captured into a CUDA graph (also marks the
+// context as captured). Kernels launched then are replayed later with the
+// parameters they had at capture, so a launch whose correctness rests on a
+// per-launch host value (the fused prologue's epoch) puts what makes it safe
+// on replay into the graph too.
+bool capturing(mp_ctx* c, cudaStream_t stream) {
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &st) != cudaSuccess) {
+    (void)cudaGetLastError();
+    st = cudaStreamCaptureStatusActive;  // the legacy stream while another captures
+  }
+  if (st == cudaStreamCaptureStatusNone) return false;
+  c->captured = true;
+  return true;
+}
+
 template <class T>
 int ensure_buf(mp_ctx* c, T** p, size_t* cap, size_t elems, cudaStream_t stream) {
   if (*cap >= elems && *p != nullptr) return MP_OK;
   if (*p != nullptr) {
-    cudaStreamSynchronize(stream);
-    cudaFree(*p);
+    if (capturing(c, stream) || c->captured) {
+      // a graph may read the old buffer on replay: keep it until destroy
+      // (no synchronisation and no free are allowed during a capture)
+      c->retired.push_back(*p);
+    } else {
+      cudaStreamSynchronize(stream);
+      cudaFree(*p);
+    }
     *p = nullptr;
     *cap = 0;
   }
   void* q = nullptr;
+  // an allocation is not a stream operation; a capture in global mode would
+  // still refuse it from this thread unless the thread's mode is relaxed
+  cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+  cudaThreadExchangeStreamCaptureMode(&mode);
   cudaError_t e = cudaMalloc(&q, std::max<size_t>(elems, 1) * sizeof(T));
+  cudaThreadExchangeStreamCaptureMode(&mode);
   if (e != cudaSuccess) return cuda_fail(c, e, "cudaMalloc");
   *p = static_cast<T*>(q);
   *cap = elems;
@@ -672,6 +708,12 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
     c->epoch = c->epoch + 1 == 0 ? 1 : c->epoch + 1;
     p.flags = c->flags;
     p.epoch = c->epoch;
+    if (capturing(c, stream)) {
+      // a replay reuses this epoch: the flags are cleared in the graph before
+      // every replay of the launch, so no flag holds it when the launch starts
+      MP_CUDA(c, cudaMemsetAsync(c->flags, 0, static_cast<size_t>(p.n_pre) * 2 * sizeof(uint32_t),
+                                 stream));
+    }
     p.scale = *pro->es;
     mp::ProjMember& pre = p.pre;
     pre.tm_w = *pro->tm_a;
@@ -850,6 +892,7 @@ int mp_destroy(mp_ctx* c) {
   cudaFree(c->scratch);
   cudaFree(c->part);
   cudaFree(c->flags);
+  for (void* p : c->retired) cudaFree(p);
   for (auto& kv : c->shared) {
     cudaFree(kv.second.a);
     cudaFree(kv.second.bc);
@@ -1031,6 +1074,7 @@ int mp_lora_bind(mp_ctx* c, mp_weight* w, int slot, const uint16_t* a, const uin
   MP_CUDA(c, cudaMemcpy(w->lb[slot], b, nb * 2, cudaMemcpyDefault));
   w->rank[slot] = rank;
   w->bind_version += 1;
+  c->state_version += 1;
   return MP_OK;
 }
 
@@ -1046,6 +1090,7 @@ int mp_lora_unbind(mp_ctx* c, mp_weight* w, int slot) {
   w->la[slot] = w->lb[slot] = nullptr;
   w->rank[slot] = 0;
   w->bind_version += 1;
+  c->state_version += 1;
   return MP_OK;
 }
 
@@ -1053,7 +1098,14 @@ int mp_set_strength(mp_ctx* c, int slot, float s) {
   if (c == nullptr) return MP_EINVAL;
   if (slot < 0 || slot >= mp::kMaxSlots)
     return fail(c, MP_EINVAL, "slot %d outside [0, %d)", slot, mp::kMaxSlots);
+  if (c->strength[slot] != s) c->state_version += 1;
   c->strength[slot] = s;
+  return MP_OK;
+}
+
+int mp_state_version(const mp_ctx* c, uint64_t* v) {
+  if (c == nullptr || v == nullptr) return MP_EINVAL;
+  *v = c->state_version;
   return MP_OK;
 }
 
@@ -1066,6 +1118,7 @@ int mp_get_strength(const mp_ctx* c, int slot, float* s) {
 int mp_set_strengths_rows(mp_ctx* c, const float* s, const int32_t* row_starts, int batch) {
   if (c == nullptr) return MP_EINVAL;
   if (batch == 0) {
+    if (c->n_seg != 0) c->state_version += 1;
     c->n_seg = 0;
     return MP_OK;
   }
@@ -1075,6 +1128,7 @@ int mp_set_strengths_rows(mp_ctx* c, const float* s, const int32_t* row_starts, 
   for (int g = 0; g < batch; ++g)
     if (row_starts[g + 1] < row_starts[g])
       return fail(c, MP_EINVAL, "row_starts must be non-decreasing");
+  c->state_version += 1;
   c->n_seg = batch;
   for (int g = 0; g <= batch; ++g) c->seg_start[g] = row_starts[g];
   for (int g = 0; g < batch; ++g)

@@ -150,11 +150,60 @@ class DitForward:
                    for n in PROJ_NAMES + ("adaLN_modulation.0",)):
                 continue
             self.t[k] = tensor(k).to(device)
+        self._init_caches()
+
+    def _init_caches(self) -> None:
         self.cap_cache_entries = 4
         self._cap_cache: list[dict] = []
         self._cap_strengths: tuple | None = None
         self._tick = 0
+        self._rope_cache: dict = {}
         self.last_cap_cache_hit = False
+
+    @classmethod
+    def synthetic(cls, ctx: Context, cfg: DitModelConfig, bits: int, seed: int,
+                  device) -> "DitForward":
+        """Seeded random weights of the model's shapes, made on the device (no
+        checkpoint; for timing whole forwards): the block projections and the
+        adaLN Linears as DitProjectionSet.synthetic makes them (w8 / w4 packs
+        or dense bf16), every other matrix bf16 ~N(0, 1/k), biases
+        ~N(0, 0.02^2) and norm gains ~1 + N(0, 0.1^2)."""
+        self = cls.__new__(cls)
+        self.ctx, self.cfg, self.dev = ctx, cfg, device
+        self.dims = cfg.proj_dims()
+        self.proj = DitProjectionSet.synthetic(ctx, self.dims, bits, seed, device)
+        self.ada, self.modset = self.proj.ada, self.proj.modset
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed + 1)
+        H, hd = cfg.dim, cfg.head_dim
+
+        def lin(n, k):
+            return (torch.randn((n, k), device=device, generator=gen) / math.sqrt(k)).to(
+                torch.bfloat16)
+
+        def vec(n, mean=0.0, std=0.02):
+            return (mean + std * torch.randn(n, device=device, generator=gen)).to(torch.bfloat16)
+
+        t = {X_EMBEDDER + ".weight": lin(H, cfg.patch_dim), X_EMBEDDER + ".bias": vec(H),
+             "cap_embedder.0.weight": vec(cfg.cap_feat_dim, 1.0, 0.1),
+             "cap_embedder.1.weight": lin(H, cfg.cap_feat_dim), "cap_embedder.1.bias": vec(H),
+             "t_embedder.mlp.0.weight": lin(cfg.time_mid, cfg.time_freq),
+             "t_embedder.mlp.0.bias": vec(cfg.time_mid),
+             "t_embedder.mlp.2.weight": lin(cfg.adaln, cfg.time_mid),
+             "t_embedder.mlp.2.bias": vec(cfg.adaln),
+             FINAL + ".adaLN_modulation.1.weight": lin(H, cfg.adaln),
+             FINAL + ".adaLN_modulation.1.bias": vec(H),
+             FINAL + ".linear.weight": lin(cfg.patch_dim, H), FINAL + ".linear.bias": vec(cfg.patch_dim)}
+        for b in range(self.dims.n_blocks):
+            pre = self.dims.block_prefix(b)
+            t[pre + "attention.norm_q.weight"] = vec(hd, 1.0, 0.1)
+            t[pre + "attention.norm_k.weight"] = vec(hd, 1.0, 0.1)
+            for nm in ("attention_norm1", "attention_norm2", "ffn_norm1", "ffn_norm2"):
+                t[pre + nm + ".weight"] = vec(H, 1.0, 0.1)
+        self.t = t
+        self._keep = ()
+        self._init_caches()
+        return self
 
     # ---- pieces ------------------------------------------------------------
     def _rms(self, x: torch.Tensor, w: torch.Tensor | None, eps: float | None = None):
@@ -258,24 +307,60 @@ class DitForward:
         rows at once; the modulation takes B timestep rows in its one launch;
         norms, gates and attention stay per image, so image i's output is what
         forward() gives for it alone. Returns bf16 [B, img, patch_dim]."""
-        cfg, dev = self.cfg, self.dev
+        B, sig = self._check_batch(latents, caps, sigmas)
+        img = grid_h * grid_w
+        cos, sin = self._rope_dev(grid_h, grid_w, caps[0].shape[0])
+        cj = [self._context(cp, query_rows, cos[img:], sin[img:]) for cp in caps]
+        return self._core(latents.to(self.dev), self._timestep_emb(sig).to(self.dev), cj,
+                          cos, sin, img)
+
+    def graph(self, batch: int, query_rows: int, grid_h: int, grid_w: int,
+              cap_len: int) -> "ForwardGraph":
+        """A CUDA-graph runner of forward_batch for one layout (see ForwardGraph)."""
+        return ForwardGraph(self, batch, query_rows, grid_h, grid_w, cap_len)
+
+    # ---- pieces of the forward ----------------------------------------------
+    def _check_batch(self, latents, caps, sigmas):
         B = latents.shape[0]
         if len(caps) != B or any(c.shape != caps[0].shape for c in caps):
             raise ValueError("one caption per image, all of the same shape")
         sig = [float(sigmas)] * B if np.isscalar(sigmas) else [float(x) for x in sigmas]
         if len(sig) != B or B > 4:
             raise ValueError("one sigma per image; at most 4 images (the modulation's rows)")
-        img = grid_h * grid_w
-        cap_len = caps[0].shape[0]
-        c, s = rope_tables(layout_positions(grid_h, grid_w, cap_len), cfg.head_dim, cfg.axes,
-                           cfg.rope_theta)
-        cos = torch.from_numpy(c).to(dev)
-        sin = torch.from_numpy(s).to(dev)
+        return B, sig
+
+    def _rope_dev(self, grid_h: int, grid_w: int, cap_len: int):
+        """f32 cos / sin [img + cap_len, head_dim / 2] of the layout, on the
+        device (kept per layout: a denoising loop asks for the same one)."""
+        key = (grid_h, grid_w, cap_len)
+        hit = self._rope_cache.get(key)
+        if hit is None:
+            c, s = rope_tables(layout_positions(grid_h, grid_w, cap_len), self.cfg.head_dim,
+                               self.cfg.axes, self.cfg.rope_theta)
+            if len(self._rope_cache) >= 8:
+                self._rope_cache.clear()
+            hit = (torch.from_numpy(c).to(self.dev), torch.from_numpy(s).to(self.dev))
+            self._rope_cache[key] = hit
+        return hit
+
+    def _timestep_emb(self, sig) -> torch.Tensor:
+        """f32 [B, time_freq] sinusoids of t = t_scale * (1 - sigma), on the host
+        (the reference's timestep embedding, f32 then bf16 on the device)."""
+        cfg = self.cfg
         half = cfg.time_freq // 2
         f = np.exp(-math.log(10000.0) * np.arange(half, dtype=np.float64) / half)
         emb = np.stack([np.concatenate([np.cos(cfg.t_scale * (1.0 - sg) * f),
                                         np.sin(cfg.t_scale * (1.0 - sg) * f)]) for sg in sig])
-        emb = torch.from_numpy(emb.astype(np.float32)).to(dev).to(torch.bfloat16)
+        return torch.from_numpy(emb.astype(np.float32))
+
+    def _core(self, lat: torch.Tensor, emb: torch.Tensor, cj, cos, sin, img: int) -> torch.Tensor:
+        """The device part of one step: lat bf16 [B, img, patch_dim], emb f32
+        [B, time_freq], cj: the B images' context rows [cap_len, dim]. Launches
+        kernels only (no host synchronisation, no host-to-device copy), so a
+        CUDA graph can hold it."""
+        cfg = self.cfg
+        B = lat.shape[0]
+        emb = emb.to(torch.bfloat16)
         # the model-level dense layers (library GEMMs) run per image: a library
         # GEMM over B rows may pick another algorithm than over one, and image
         # i's bits must not depend on the batch; the modulation, projections
@@ -283,17 +368,15 @@ class DitForward:
         temb = torch.cat([self._linear(F.silu(self._linear(emb[bi:bi + 1], "t_embedder.mlp.0")),
                                        "t_embedder.mlp.2") for bi in range(B)])
         mods, nw1, nw3 = self.ctx.modulation(self.modset, temb.contiguous())
-        lat = latents.to(dev)
         x = torch.cat([self._linear(lat[bi], X_EMBEDDER) for bi in range(B)])
         nref = cfg.n_refiner
         for i in range(nref):
             x = self._block(nref + i, x, cos[:img], sin[:img], i, mods, nw1, nw3, nb=B)
-        cjs = [self._context(cp, query_rows, cos[img:], sin[img:], mods, nw1, nw3) for cp in caps]
-        j = torch.cat([t for bi in range(B) for t in (x[bi * img:(bi + 1) * img], cjs[bi])],
-                      dim=0).contiguous()
+        j = torch.cat([t for bi in range(B) for t in (x[bi * img:(bi + 1) * img], cj[bi])],
+                      dim=0)
         for i in range(cfg.n_layers):
             j = self._block(2 * nref + i, j, cos, sin, nref + i, mods, nw1, nw3, nb=B)
-        L = img + cap_len
+        L = j.shape[0] // B
         out = []
         for bi in range(B):
             scale = self._linear(F.silu(temb[bi:bi + 1]), FINAL + ".adaLN_modulation.1")
@@ -302,7 +385,7 @@ class DitForward:
             out.append(self._linear(xi, FINAL + ".linear"))
         return torch.stack(out)
 
-    def _context(self, cap: torch.Tensor, query_rows: int, cos, sin, mods, nw1, nw3) -> torch.Tensor:
+    def _context(self, cap: torch.Tensor, query_rows: int, cos, sin) -> torch.Tensor:
         """The caption rows after the context refiner, through the caption
         cache (the reference's, src/ming-dit.cc:1543-1577): keyed on the
         caption's exact bytes, its shape and the query-row split; the context
@@ -331,7 +414,7 @@ class DitForward:
         ca = self._linear(ca, "cap_embedder.1")
         cj = torch.cat([ca, key[query_rows:, : cfg.dim]], dim=0)
         for i in range(cfg.n_refiner):
-            cj = self._block(i, cj, cos, sin, None, mods, nw1, nw3)
+            cj = self._block(i, cj, cos, sin, None, None, None, None)
         if self.cap_cache_entries > 0:
             if len(self._cap_cache) >= self.cap_cache_entries:
                 self._cap_cache.remove(min(self._cap_cache, key=lambda e: e["tick"]))
@@ -346,4 +429,86 @@ class DitForward:
         self.modset.free()
 
 
-__all__ = ["DitForward", "DitModelConfig", "layout_positions", "rope_tables"]
+class ForwardGraph:
+    """forward_batch for one layout (B images of grid_h x grid_w patches,
+    captions of cap_len rows, query_rows of them query rows) as ONE CUDA-graph
+    replay per denoising step.
+
+    The graph holds the per-step work: the timestep embedder, the batched
+    modulation, the x embedder, every noise-refiner and main block
+    (projections, norms, attention) and the final layer — the work the
+    reference's forward launches one by one on every sampler step
+    (src/ming-dit.cc:1490-2642). Outside it: the context refiner, whose rows
+    depend on the caption alone and come through the caption cache (copied
+    into the graph's input rows), and the timestep sinusoid, made on the host
+    and copied in as f32.
+
+    A graph keeps the LoRA strengths, row segments and bindings of its capture
+    (Context.state_version): a call after any change of them captures again,
+    after a warm-up on the new state. Inputs are copied into the graph's
+    static buffers; the result is a copy of its static output, so image i's
+    bits are those of forward_batch on the same inputs.
+    """
+
+    def __init__(self, fwd: DitForward, batch: int, query_rows: int, grid_h: int, grid_w: int,
+                 cap_len: int, warmup: int = 2):
+        if not 1 <= batch <= 4:
+            raise ValueError("1 to 4 images (the modulation's rows)")
+        cfg, dev = fwd.cfg, fwd.dev
+        self.fwd, self.batch, self.query_rows = fwd, batch, query_rows
+        self.img, self.cap_len, self.warmup = grid_h * grid_w, cap_len, warmup
+        self.lat = torch.zeros((batch, self.img, cfg.patch_dim), dtype=torch.bfloat16, device=dev)
+        self.emb = torch.zeros((batch, cfg.time_freq), dtype=torch.float32, device=dev)
+        self.cj = torch.zeros((batch, cap_len, cfg.dim), dtype=torch.bfloat16, device=dev)
+        self.cos, self.sin = fwd._rope_dev(grid_h, grid_w, cap_len)
+        self.g: torch.cuda.CUDAGraph | None = None
+        self.out: torch.Tensor | None = None
+        self.version: int | None = None
+        self.captures = 0
+        self.replays = 0
+
+    def _run(self) -> torch.Tensor:
+        return self.fwd._core(self.lat, self.emb, self.cj, self.cos, self.sin, self.img)
+
+    def _capture(self) -> None:
+        self.g, self.out = None, None  # the old graph's memory pool goes first
+        dev = self.fwd.dev
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            # warm-up: the library's buffers reach their sizes and the LoRA
+            # stacks are built here, so the capture holds kernels only
+            for _ in range(self.warmup):
+                self._run()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.out = self._run()
+        self.g = g
+        self.version = self.fwd.ctx.state_version()
+        self.captures += 1
+
+    @torch.no_grad()
+    def __call__(self, latents: torch.Tensor, caps, sigmas) -> torch.Tensor:
+        fwd = self.fwd
+        B, sig = fwd._check_batch(latents, caps, sigmas)
+        if (B != self.batch or tuple(latents.shape[1:]) != tuple(self.lat.shape[1:])
+                or caps[0].shape[0] != self.cap_len):
+            raise ValueError(f"this graph takes {self.batch} x {tuple(self.lat.shape[1:])} "
+                             f"latents and captions of {self.cap_len} rows")
+        for bi, cp in enumerate(caps):
+            self.cj[bi].copy_(fwd._context(cp, self.query_rows, self.cos[self.img:],
+                                           self.sin[self.img:]))
+        self.lat.copy_(latents)
+        self.emb.copy_(fwd._timestep_emb(sig))
+        if self.g is None or fwd.ctx.state_version() != self.version:
+            self._capture()
+        self.g.replay()
+        self.replays += 1
+        return self.out.clone()
+
+    def release(self) -> None:
+        self.g, self.out = None, None
+
+
+__all__ = ["DitForward", "DitModelConfig", "ForwardGraph", "layout_positions", "rope_tables"]

@@ -204,6 +204,13 @@ class Context:
         self._check(self.lib.mp_get_strength(self.h, slot, C.byref(v)))
         return float(v.value)
 
+    def state_version(self) -> int:
+        """Advanced by every change of a strength, the row segments or a LoRA
+        binding: a CUDA graph captured at one version is stale at another."""
+        v = C.c_uint64()
+        self._check(self.lib.mp_state_version(self.h, C.byref(v)))
+        return int(v.value)
+
     def set_strengths_rows(self, strengths, row_starts) -> None:
         """strengths: [batch, 8] floats; row_starts: [batch + 1] token rows.
         Pass batch 0 (empty) to return to per-slot strengths."""
