@@ -214,8 +214,11 @@ __device__ __forceinline__ Tile decode_tile(const ProjParams& p, int tile, int r
   const int per_split = p.n_pairs * p.n_ttiles;
   t.z = tile / per_split;
   const int rem = tile - t.z * per_split;
-  const int tt = rem / p.n_pairs;
-  const int pair = rem - tt * p.n_pairs;
+  // token tile fastest: the pairs running at one time share a few feature
+  // pairs' weight tiles (each read from memory once, then from L2 by the
+  // other token tiles) and sweep the whole of x, which stays in L2
+  const int pair = rem / p.n_ttiles;
+  const int tt = rem - pair * p.n_ttiles;
   int mi = 0;
   while (mi + 1 < p.n_members && pair >= p.mem[mi + 1].pair_begin) ++mi;
   t.mi = mi;
