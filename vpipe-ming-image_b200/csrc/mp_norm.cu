@@ -12,11 +12,13 @@
 // the projection (every CTA pair of its launch), so it runs here, after the
 // projection, rather than in the projection's epilogue.
 //
-// HBM-bound: per row it reads o and x and writes x and nrm once (16-byte
-// accesses). A CTA of 256 threads takes kRowsPerCta rows; tanh(gate) is
-// tabulated once per CTA in shared memory. Each row's two sums of squares are
-// reduced in a fixed order (per-thread sequential, warp xor tree, warps in
-// order), so results do not depend on timing.
+// Memory-bound: per row it reads o and x and writes x and nrm once (16-byte
+// accesses). A CTA of 256 threads walks rows blockIdx.x, + gridDim.x, ...
+// (a few CTAs per SM), with the next row's x and o loads in flight while
+// the current row is reduced and stored; tanh(gate) is tabulated once per
+// CTA in shared memory. Each row's two sums of squares are reduced in a
+// fixed order (two FMA chains per thread, warp xor tree, warps in order), so
+// results do not depend on timing.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -28,8 +30,7 @@ namespace {
 
 constexpr int kNormThreads = 256;
 constexpr int kNormWarps = kNormThreads / 32;
-constexpr int kRowsPerCta = 4;
-constexpr int kMaxChunks = kNormMaxH / 8 / kNormThreads;  // 16-byte chunks per thread
+constexpr int kNormCtasPerSm = 4;
 
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
@@ -38,23 +39,120 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Sum over the CTA, in a fixed order; `red` holds kNormWarps floats and is
-// free again when this returns (the trailing barrier).
-__device__ __forceinline__ float cta_sum(float v, float* red) {
+// Sum over the CTA, in a fixed order. `red` alternates between two buffers
+// call by call: the barrier of the next call orders this call's reads
+// before the buffer is written again, so one barrier per call suffices.
+__device__ __forceinline__ float cta_sum(float v, float (*red)[kNormWarps], int& parity) {
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, off);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  float* buf = red[parity];
+  parity ^= 1;
+  if ((threadIdx.x & 31) == 0) buf[threadIdx.x >> 5] = v;
   __syncthreads();
-  float t = red[0];
+  float t = buf[0];
 #pragma unroll
-  for (int w = 1; w < kNormWarps; ++w) t += red[w];
-  __syncthreads();
+  for (int w = 1; w < kNormWarps; ++w) t += buf[w];
   return t;
 }
 
+// Sum of squares of this thread's chunks (two chains: even and odd elements).
+template <int CH>
+__device__ __forceinline__ float sum_squares(const uint4 (&v)[CH], int chunks) {
+  float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+  for (int i = 0; i < CH; ++i) {
+    const int c = static_cast<int>(threadIdx.x) + i * kNormThreads;
+    if (c < chunks) {
+      const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        s0 = fmaf(bf16lo(w[e]), bf16lo(w[e]), s0);
+        s1 = fmaf(bf16hi(w[e]), bf16hi(w[e]), s1);
+      }
+    }
+  }
+  return s0 + s1;
+}
+
+template <int CH>
+__device__ __forceinline__ void load_row(const RmsResidualParams& p, int r, int chunks,
+                                         uint4 (&xv)[CH], uint4 (&ov)[CH]) {
+  const uint16_t* xrow = p.x + static_cast<size_t>(r) * p.ldx;
+#pragma unroll
+  for (int i = 0; i < CH; ++i) {
+    const int c = static_cast<int>(threadIdx.x) + i * kNormThreads;
+    if (c < chunks) xv[i] = *reinterpret_cast<const uint4*>(xrow + 8 * c);
+  }
+  if (p.o != nullptr) {
+    const uint16_t* orow = p.o + static_cast<size_t>(r) * p.ldo;
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+      const int c = static_cast<int>(threadIdx.x) + i * kNormThreads;
+      if (c < chunks) ov[i] = *reinterpret_cast<const uint4*>(orow + 8 * c);
+    }
+  }
+}
+
+template <int CH>
+__device__ __forceinline__ void process_row(const RmsResidualParams& p, int r, int chunks,
+                                            float inv_h, const float* tgate,
+                                            float (*red)[kNormWarps], int& parity,
+                                            uint4 (&xv)[CH], const uint4 (&ov)[CH]) {
+  if (p.o != nullptr) {
+    const float ro =
+        rsqrtf(__fadd_rn(__fmul_rn(cta_sum(sum_squares<CH>(ov, chunks), red, parity), inv_h), p.eps));
+    uint16_t* xrow = p.x + static_cast<size_t>(r) * p.ldx;
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+      const int c = static_cast<int>(threadIdx.x) + i * kNormThreads;
+      if (c >= chunks) continue;
+      const uint4 gv = __ldg(reinterpret_cast<const uint4*>(p.o_gain) + c);
+      const uint32_t ow[4] = {ov[i].x, ov[i].y, ov[i].z, ov[i].w};
+      const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+      uint32_t xw[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        // s = bf16((o * ro) * gain): the sub-layer output's RMSNorm
+        const uint32_t sw = pack2(__fmul_rn(__fmul_rn(bf16lo(ow[e]), ro), bf16lo(gw[e])),
+                                  __fmul_rn(__fmul_rn(bf16hi(ow[e]), ro), bf16hi(gw[e])));
+        float s0 = bf16lo(sw), s1 = bf16hi(sw);
+        if (p.gate != nullptr) {
+          const float2 tg = *reinterpret_cast<const float2*>(tgate + 8 * c + 2 * e);
+          s0 = __fmul_rn(tg.x, s0);
+          s1 = __fmul_rn(tg.y, s1);
+        }
+        xw[e] = pack2(__fadd_rn(bf16lo(xw[e]), s0), __fadd_rn(bf16hi(xw[e]), s1));
+      }
+      xv[i] = make_uint4(xw[0], xw[1], xw[2], xw[3]);
+      *reinterpret_cast<uint4*>(xrow + 8 * c) = xv[i];
+    }
+  }
+  if (p.nrm != nullptr) {
+    const float rx =
+        rsqrtf(__fadd_rn(__fmul_rn(cta_sum(sum_squares<CH>(xv, chunks), red, parity), inv_h), p.eps));
+    uint16_t* nrow = p.nrm + static_cast<size_t>(r) * p.ldn;
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+      const int c = static_cast<int>(threadIdx.x) + i * kNormThreads;
+      if (c >= chunks) continue;
+      const uint4 gv = __ldg(reinterpret_cast<const uint4*>(p.nrm_gain) + c);
+      const uint32_t xw[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
+      const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+      uint32_t nw[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        nw[e] = pack2(__fmul_rn(__fmul_rn(bf16lo(xw[e]), rx), bf16lo(gw[e])),
+                      __fmul_rn(__fmul_rn(bf16hi(xw[e]), rx), bf16hi(gw[e])));
+      *reinterpret_cast<uint4*>(nrow + 8 * c) = make_uint4(nw[0], nw[1], nw[2], nw[3]);
+    }
+  }
+}
+
+// CH = 16-byte chunks per thread and row (H / 8 / 256, rounded up).
+template <int CH>
 __global__ void __launch_bounds__(kNormThreads) rms_residual_kernel(const RmsResidualParams p) {
   extern __shared__ float tgate[];  // [H] tanh(gate) (gated calls)
-  __shared__ float red[kNormWarps];
+  __shared__ float red[2][kNormWarps];
   const int chunks = p.H / 8;
   const float inv_h = 1.0f / static_cast<float>(p.H);  // mean = sum * (1 / H)
   if (p.gate != nullptr) {
@@ -62,99 +160,45 @@ __global__ void __launch_bounds__(kNormThreads) rms_residual_kernel(const RmsRes
       tgate[i] = tanhf(__uint_as_float(static_cast<uint32_t>(p.gate[i]) << 16));
     __syncthreads();
   }
-  const int row_end = min(p.M, (static_cast<int>(blockIdx.x) + 1) * kRowsPerCta);
-  for (int r = static_cast<int>(blockIdx.x) * kRowsPerCta; r < row_end; ++r) {
-    uint16_t* xrow = p.x + static_cast<size_t>(r) * p.ldx;
-    uint4 xv[kMaxChunks];
-#pragma unroll
-    for (int i = 0; i < kMaxChunks; ++i) {
-      const int c = static_cast<int>(threadIdx.x) + i * kNormThreads;
-      if (c < chunks) xv[i] = *reinterpret_cast<const uint4*>(xrow + 8 * c);
-    }
-    if (p.o != nullptr) {
-      const uint16_t* orow = p.o + static_cast<size_t>(r) * p.ldo;
-      uint4 ov[kMaxChunks];
-      float ss = 0.0f;
-#pragma unroll
-      for (int i = 0; i < kMaxChunks; ++i) {
-        const int c = static_cast<int>(threadIdx.x) + i * kNormThreads;
-        if (c < chunks) {
-          ov[i] = *reinterpret_cast<const uint4*>(orow + 8 * c);
-          const uint32_t w[4] = {ov[i].x, ov[i].y, ov[i].z, ov[i].w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            ss = __fadd_rn(ss, __fmul_rn(bf16lo(w[e]), bf16lo(w[e])));
-            ss = __fadd_rn(ss, __fmul_rn(bf16hi(w[e]), bf16hi(w[e])));
-          }
-        }
-      }
-      const float ro = rsqrtf(__fadd_rn(__fmul_rn(cta_sum(ss, red), inv_h), p.eps));
-#pragma unroll
-      for (int i = 0; i < kMaxChunks; ++i) {
-        const int c = static_cast<int>(threadIdx.x) + i * kNormThreads;
-        if (c >= chunks) continue;
-        const uint4 gv = __ldg(reinterpret_cast<const uint4*>(p.o_gain) + c);
-        const uint32_t ow[4] = {ov[i].x, ov[i].y, ov[i].z, ov[i].w};
-        const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-        uint32_t xw[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int f = 8 * c + 2 * e;
-          // s = bf16((o * ro) * gain): the sub-layer output's RMSNorm
-          const uint32_t sw = pack2(__fmul_rn(__fmul_rn(bf16lo(ow[e]), ro), bf16lo(gw[e])),
-                                    __fmul_rn(__fmul_rn(bf16hi(ow[e]), ro), bf16hi(gw[e])));
-          float s0 = bf16lo(sw), s1 = bf16hi(sw);
-          if (p.gate != nullptr) {
-            s0 = __fmul_rn(tgate[f], s0);
-            s1 = __fmul_rn(tgate[f + 1], s1);
-          }
-          xw[e] = pack2(__fadd_rn(bf16lo(xw[e]), s0), __fadd_rn(bf16hi(xw[e]), s1));
-        }
-        xv[i] = make_uint4(xw[0], xw[1], xw[2], xw[3]);
-        *reinterpret_cast<uint4*>(xrow + 8 * c) = xv[i];
-      }
-    }
-    if (p.nrm != nullptr) {
-      float ss = 0.0f;
-#pragma unroll
-      for (int i = 0; i < kMaxChunks; ++i) {
-        const int c = static_cast<int>(threadIdx.x) + i * kNormThreads;
-        if (c < chunks) {
-          const uint32_t w[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            ss = __fadd_rn(ss, __fmul_rn(bf16lo(w[e]), bf16lo(w[e])));
-            ss = __fadd_rn(ss, __fmul_rn(bf16hi(w[e]), bf16hi(w[e])));
-          }
-        }
-      }
-      const float rx = rsqrtf(__fadd_rn(__fmul_rn(cta_sum(ss, red), inv_h), p.eps));
-      uint16_t* nrow = p.nrm + static_cast<size_t>(r) * p.ldn;
-#pragma unroll
-      for (int i = 0; i < kMaxChunks; ++i) {
-        const int c = static_cast<int>(threadIdx.x) + i * kNormThreads;
-        if (c >= chunks) continue;
-        const uint4 gv = __ldg(reinterpret_cast<const uint4*>(p.nrm_gain) + c);
-        const uint32_t xw[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
-        const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-        uint32_t nw[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          nw[e] = pack2(__fmul_rn(__fmul_rn(bf16lo(xw[e]), rx), bf16lo(gw[e])),
-                        __fmul_rn(__fmul_rn(bf16hi(xw[e]), rx), bf16hi(gw[e])));
-        *reinterpret_cast<uint4*>(nrow + 8 * c) = make_uint4(nw[0], nw[1], nw[2], nw[3]);
-      }
-    }
+  int parity = 0;
+  const int step = static_cast<int>(gridDim.x);
+  int r = static_cast<int>(blockIdx.x);
+  if (r >= p.M) return;
+  uint4 xa[CH], oa[CH], xb[CH], ob[CH];
+  load_row<CH>(p, r, chunks, xa, oa);
+  // two rows per iteration, so the register buffers keep fixed names
+#pragma unroll 1
+  for (; r < p.M; r += 2 * step) {
+    if (r + step < p.M) load_row<CH>(p, r + step, chunks, xb, ob);
+    process_row<CH>(p, r, chunks, inv_h, tgate, red, parity, xa, oa);
+    if (r + step >= p.M) break;
+    if (r + 2 * step < p.M) load_row<CH>(p, r + 2 * step, chunks, xa, oa);
+    process_row<CH>(p, r + step, chunks, inv_h, tgate, red, parity, xb, ob);
   }
+}
+
+template <int CH>
+cudaError_t launch_ch(const RmsResidualParams& p, cudaStream_t stream) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int blocks = p.M < sms * kNormCtasPerSm ? p.M : sms * kNormCtasPerSm;
+  const size_t smem = p.gate != nullptr ? static_cast<size_t>(p.H) * sizeof(float) : 0;
+  rms_residual_kernel<CH><<<blocks, kNormThreads, smem, stream>>>(p);
+  return cudaGetLastError();
 }
 
 }  // namespace
 
 cudaError_t launch_rms_residual(const RmsResidualParams& p, cudaStream_t stream) {
-  const unsigned blocks = static_cast<unsigned>((p.M + kRowsPerCta - 1) / kRowsPerCta);
-  const size_t smem = p.gate != nullptr ? static_cast<size_t>(p.H) * sizeof(float) : 0;
-  rms_residual_kernel<<<blocks, kNormThreads, smem, stream>>>(p);
-  return cudaGetLastError();
+  const int ch = (p.H / 8 + kNormThreads - 1) / kNormThreads;
+  static_assert(kNormMaxH / 8 / kNormThreads == 4, "chunk counts dispatched below");
+  switch (ch) {
+    case 1: return launch_ch<1>(p, stream);
+    case 2: return launch_ch<2>(p, stream);
+    case 3: return launch_ch<3>(p, stream);
+    default: return launch_ch<4>(p, stream);
+  }
 }
 
 }  // namespace mp
