@@ -15,14 +15,14 @@
 //     the leader CTA's barrier;
 //   * each CTA's softmax warps copy its Q rows into TMEM once; warp 1 of the
 //     leader then issues S_j = Q · K_j^T with Q read from TMEM (so the only
-//     shared-memory operand is the K half) into the TMEM S buffer of both
-//     CTAs as soon as the softmax has read S_{j-1} out, then O += P_{j-1} ·
-//     V_{j-1} with P read from TMEM and V as an MN-major operand straight from
-//     its [keys][dims] tile;
+//     shared-memory operand is the K half) into S[j % 2] of both CTAs, two
+//     tiles ahead of O += P_j · V_j, which reads P from TMEM (written over
+//     S[j % 2] by the softmax) and V as an MN-major operand straight from its
+//     [keys][dims] tile;
 //   * warps 2-9 of each CTA (thread = query row, TMEM lane; two warps per row,
 //     one per 64-key half of each tile) read S_j into registers once
-//     (freeing S for S_{j+1}) and write P_j = 2^(s·c − m) in bf16
-//     (c = scale·log2 e) into one of two TMEM P buffers with the row sum, in
+//     and write P_j = 2^(s·c − m) in bf16
+//     (c = scale·log2 e) over its half of S_j's columns with the row sum, in
 //     packed f32x2 arithmetic, three of every eight exponential pairs on the
 //     FMA pipe and the rest on the MUFU. The exponent base m is the row
 //     maximum seen when it was last raised: only when a tile's maximum
@@ -32,8 +32,8 @@
 //     relative to the older m;
 //   * after the last step the rows of O are divided by their sums and stored
 //     bf16 token-major.
-// S_{j+1} and P_{j-1} · V_{j-1} run while the softmax of tile j works (P is
-// double-buffered). Keys past S are masked (their tiles read
+// S_{j+1}, S_{j+2} and P_{j-1} · V_{j-1} run while the softmax of tile j
+// works (S is double-buffered). Keys past S are masked (their tiles read
 // zeros); rows past S are computed and not stored. No TMA multicast. Every
 // wait is bounded; on a timeout the CTA unwinds and reports MP_ETIMEOUT.
 #include <cuda_runtime.h>
@@ -64,11 +64,10 @@ static_assert(kAttnSmem <= 232448, "shared memory per CTA");
 constexpr int kAttnThreads = 352;  // warp 0 Q+K, 1 MMA, 2-9 softmax, 10 V
 constexpr int kSoftWarps = 8;      // two per TMEM lane quarter: keys 0-63 / 64-127 of each row
 static_assert(kAttnTiles % 1024 == 0, "barrier region after the tiles");
-constexpr uint32_t kAttnCols = 512;  // Q (64), S (128), O (128), P[0] P[1] (64 each)
+constexpr uint32_t kAttnCols = 512;  // Q (64), S[0] S[1] (128 each), O (128)
 constexpr uint32_t kColQ = 0;        // Q rows as bf16 pairs (the A operand of S = Q · K^T)
-constexpr uint32_t kColS = 64;       // S (f32)
-constexpr uint32_t kColO = 192;      // the O accumulator (f32)
-constexpr uint32_t kColP = 320;      // P[0] (P[1] 64 further): bf16 pairs
+constexpr uint32_t kColS = 64;       // S[b] (f32) at 64 + 128 b; P_j (bf16 pairs) overwrites S[j % 2]
+constexpr uint32_t kColO = 320;      // the O accumulator (f32)
 constexpr float kRescaleLog2 = 8.0f;                    // move m only when a max exceeds it by this
 
 enum : uint32_t { kAttnSiteWait = 0x2100u, kAttnSiteDrain = 0x2200u };
@@ -81,10 +80,9 @@ struct AttnSmem {
   uint64_t* v_full;   // [kVStages]
   uint64_t* v_empty;  // [kVStages]
   uint64_t* q_ready;  // leader: every softmax warp of the pair has put its Q part in TMEM
-  uint64_t* s_full;   // S_j complete (both CTAs)
-  uint64_t* s_free;   // leader: S_j read out by every softmax warp of the pair
-  uint64_t* p_full;   // [2]
-  uint64_t* o_done;   // [2] P_t · V_t (t % 2) accumulated: P buffer free, O includes it
+  uint64_t* s_full;   // [2] S_j (j % 2) complete (both CTAs)
+  uint64_t* p_full;   // [2] leader: P_j written over S_j by every softmax warp of the pair
+  uint64_t* o_done;   // [2] P_t · V_t (t % 2) accumulated: O includes it
   uint64_t* drain;
   uint32_t* tmem_slot;
   volatile uint32_t* abort;
@@ -103,8 +101,7 @@ __device__ __forceinline__ AttnSmem carve_attn(uint8_t* raw) {
   s.v_empty = s.v_full + kVStages;
   s.q_ready = s.v_empty + kVStages;
   s.s_full = s.q_ready + 1;
-  s.s_free = s.s_full + 1;
-  s.p_full = s.s_free + 1;
+  s.p_full = s.s_full + 2;
   s.o_done = s.p_full + 2;
   s.drain = s.o_done + 2;
   s.tmem_slot = reinterpret_cast<uint32_t*>(s.drain + 1);
@@ -220,17 +217,17 @@ __device__ void attn_mma(const AttnParams& p, const AttnSmem& sm, uint32_t tmem,
     const int st = j % kKStages;
     if (!attn_wait(sm, &sm.k_full[st], static_cast<uint32_t>(j / kKStages) & 1u, p.wait_limit_ns))
       return false;
-    if (j >= 1 &&
-        !attn_wait(sm, sm.s_free, static_cast<uint32_t>(j - 1) & 1u, p.wait_limit_ns))
-      return false;
     tc_fence_after();
     const uint32_t kt = base + kOffK + static_cast<uint32_t>(st) * kKHalf;
+    // S[j % 2] held P_{j-2}, which P_{j-2} · V (issued before this) reads
+    // first: the tensor core runs a thread's MMAs in order
+    const uint32_t sc = tmem + kColS + 128u * static_cast<uint32_t>(j & 1);
     // A = Q from each CTA's TMEM: 16 dims (8 columns of bf16 pairs) per step
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk)
-      umma_ts_pair(tmem + kColS, tmem + kColQ + static_cast<uint32_t>(kk) * 8u,
-                   kmajor_desc(kt, kKBlk, kk), idesc_qk, kk > 0 ? 1u : 0u);
-    umma_commit_pair(smem_u32(sm.s_full), 0x3);
+      umma_ts_pair(sc, tmem + kColQ + static_cast<uint32_t>(kk) * 8u, kmajor_desc(kt, kKBlk, kk),
+                   idesc_qk, kk > 0 ? 1u : 0u);
+    umma_commit_pair(smem_u32(&sm.s_full[j & 1]), 0x3);
     umma_commit_pair(smem_u32(&sm.k_empty[st]), 0x3);
     return true;
   };
@@ -243,19 +240,27 @@ __device__ void attn_mma(const AttnParams& p, const AttnSmem& sm, uint32_t tmem,
       return false;
     tc_fence_after();
     const uint32_t vt = base + kOffV + static_cast<uint32_t>(st) * kVHalf;
-    // A = P_t from each CTA's TMEM: 16 keys (8 columns of bf16 pairs) per step
+    // A = P_t from each CTA's TMEM, over S[b]: keys 64h .. 64h + 63 as bf16
+    // pairs in columns 64h .. 64h + 31 of the buffer; 16 keys per step
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk)
       umma_ts_pair(tmem + kColO,
-                   tmem + kColP + static_cast<uint32_t>(b) * 64u + static_cast<uint32_t>(kk) * 8u,
+                   tmem + kColS + 128u * static_cast<uint32_t>(b) +
+                       64u * static_cast<uint32_t>(kk >> 2) + 8u * static_cast<uint32_t>(kk & 3),
                    vmn_desc(vt, kk), idesc_pv, (t > 0 || kk > 0) ? 1u : 0u);
     umma_commit_pair(smem_u32(&sm.o_done[b]), 0x3);
     umma_commit_pair(smem_u32(&sm.v_empty[st]), 0x3);
     return true;
   };
+  // S runs two tiles ahead of P · V: S_{j+2} is computed while the softmax
+  // works on S_{j+1}, so the tensor core never waits for the softmax to have
+  // read a tile before the next one can start
   if (ok) ok = issue_s(0);
-  for (int j = 1; ok && j < n; ++j) ok = issue_s(j) && issue_pv(j - 1);
-  if (ok) ok = issue_pv(n - 1);
+  if (ok && n > 1) ok = issue_s(1);
+  for (int j = 0; ok && j < n; ++j) {
+    ok = issue_pv(j);
+    if (ok && j + 2 < n) ok = issue_s(j + 2);
+  }
   // every MMA issued has completed before TMEM is freed
   umma_commit_pair(smem_u32(sm.drain), 0x1);
   const uint64_t t0 = global_timer_ns();
@@ -308,19 +313,16 @@ __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t t
   float m_used = -INFINITY, l = 0.0f;
   for (int j = 0; j < n; ++j) {
     const int b = j & 1;
-    bool w = attn_wait(sm, sm.s_full, static_cast<uint32_t>(j) & 1u, p.wait_limit_ns);
+    bool w = attn_wait(sm, &sm.s_full[b], static_cast<uint32_t>(j >> 1) & 1u, p.wait_limit_ns);
     if (!__all_sync(0xFFFFFFFFu, w)) return;
     tc_fence_after();
-    const uint32_t sb = tmem + lane_base + kColS + 64u * half;
+    const uint32_t sb = tmem + lane_base + kColS + 128u * static_cast<uint32_t>(b) + 64u * half;
     uint32_t sv[64];
     uint32_t* const s1 = sv + 32;
     MP_TMEM_LD_32X32B_X32(sb, sv);
     MP_TMEM_LD_32X32B_X32(sb + 32u, s1);
     MP_TMEM_WAIT_LD_REGS32(sv);
     MP_TMEM_WAIT_LD_REGS32(s1);
-    tc_fence_before();  // S_j is in registers: S may take S_{j+1}
-    __syncwarp();
-    if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(sm.s_free), 0));
     const int valid = p.S - j * kAttnTile - 64 * half;  // keys of this half below S (may be <= 0)
     const bool full = valid >= 64;  // the same in every thread of the warp
     float mx;
@@ -372,16 +374,11 @@ __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t t
         if (need) m_used = mc;
       }
     }
-    // P buffer b is free once P_{j-2} · V has been accumulated
-    if (j >= 2) {
-      const int t = j - 2;
-      w = attn_wait(sm, &sm.o_done[b], static_cast<uint32_t>(t >> 1) & 1u, p.wait_limit_ns);
-      if (!__all_sync(0xFFFFFFFFu, w)) return;
-    }
     float sum = 0.0f;
     uint64_t acc2[2] = {0ull, 0ull};  // packed partial row sums (full halves)
     const uint64_t nm2 = f32x2(-m_used, -m_used);
-    const uint32_t pcol = tmem + lane_base + kColP + static_cast<uint32_t>(b) * 64u + 32u * half;
+    // P_j over this warp's own (already read) half of S[b]
+    const uint32_t pcol = sb;
 #pragma unroll
     for (int c4 = 0; c4 < 2; ++c4) {
       uint32_t w16[16];
@@ -480,9 +477,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kAttnThreads, 1)
       mbar_init(smem_u32(&sm.v_empty[st]), 1);
     }
     mbar_init(smem_u32(sm.q_ready), 2 * kSoftWarps);  // leader: every softmax warp of the pair
-    mbar_init(smem_u32(sm.s_full), 1);
-    mbar_init(smem_u32(sm.s_free), 2 * kSoftWarps);
     for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&sm.s_full[b]), 1);
       mbar_init(smem_u32(&sm.p_full[b]), 2 * kSoftWarps);
       mbar_init(smem_u32(&sm.o_done[b]), 1);
     }
