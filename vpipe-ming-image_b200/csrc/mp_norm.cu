@@ -16,12 +16,15 @@
 // accesses). A CTA of 256 threads walks rows blockIdx.x, + gridDim.x, ...
 // (a few CTAs per SM), with the next row's x and o loads in flight while
 // the current row is reduced and stored; tanh(gate) is tabulated once per
-// CTA in shared memory. Each row's two sums of squares are reduced in a
-// fixed order (two FMA chains per thread, warp xor tree, warps in order), so
-// results do not depend on timing.
+// CTA in shared memory. The arithmetic runs on packed fp32 pairs (each
+// product and sum rounded once, as the scalar sequence). Each row's two sums
+// of squares are reduced in a fixed order (even and odd elements as one
+// packed FMA chain per thread, warp xor tree, warps in order), so results do
+// not depend on timing.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include "mp_device.cuh"
 #include "mp_kernels.h"
 
 namespace mp {
@@ -32,11 +35,9 @@ constexpr int kNormThreads = 256;
 constexpr int kNormWarps = kNormThreads / 32;
 constexpr int kNormCtasPerSm = 4;
 
-__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
+// bf16x2 word -> packed fp32 pair (low half from the low bf16)
+__device__ __forceinline__ uint64_t unpack2(uint32_t w) {
+  return (static_cast<uint64_t>(w & 0xFFFF0000u) << 32) | static_cast<uint64_t>(w << 16);
 }
 
 // Sum over the CTA, in a fixed order. `red` alternates between two buffers
@@ -55,10 +56,11 @@ __device__ __forceinline__ float cta_sum(float v, float (*red)[kNormWarps], int&
   return t;
 }
 
-// Sum of squares of this thread's chunks (two chains: even and odd elements).
+// Sum of squares of this thread's chunks (two chains, even and odd elements,
+// as one packed fp32 pair).
 template <int CH>
 __device__ __forceinline__ float sum_squares(const uint4 (&v)[CH], int chunks) {
-  float s0 = 0.0f, s1 = 0.0f;
+  uint64_t s2 = 0ull;
 #pragma unroll
   for (int i = 0; i < CH; ++i) {
     const int c = static_cast<int>(threadIdx.x) + i * kNormThreads;
@@ -66,12 +68,12 @@ __device__ __forceinline__ float sum_squares(const uint4 (&v)[CH], int chunks) {
       const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        s0 = fmaf(bf16lo(w[e]), bf16lo(w[e]), s0);
-        s1 = fmaf(bf16hi(w[e]), bf16hi(w[e]), s1);
+        const uint64_t a = unpack2(w[e]);
+        s2 = fma_f32x2(a, a, s2);
       }
     }
   }
-  return s0 + s1;
+  return f32x2_lo(s2) + f32x2_hi(s2);
 }
 
 template <int CH>
@@ -101,6 +103,7 @@ __device__ __forceinline__ void process_row(const RmsResidualParams& p, int r, i
   if (p.o != nullptr) {
     const float ro =
         rsqrtf(__fadd_rn(__fmul_rn(cta_sum(sum_squares<CH>(ov, chunks), red, parity), inv_h), p.eps));
+    const uint64_t ro2 = f32x2(ro, ro);
     uint16_t* xrow = p.x + static_cast<size_t>(r) * p.ldx;
 #pragma unroll
     for (int i = 0; i < CH; ++i) {
@@ -113,15 +116,13 @@ __device__ __forceinline__ void process_row(const RmsResidualParams& p, int r, i
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         // s = bf16((o * ro) * gain): the sub-layer output's RMSNorm
-        const uint32_t sw = pack2(__fmul_rn(__fmul_rn(bf16lo(ow[e]), ro), bf16lo(gw[e])),
-                                  __fmul_rn(__fmul_rn(bf16hi(ow[e]), ro), bf16hi(gw[e])));
-        float s0 = bf16lo(sw), s1 = bf16hi(sw);
+        const uint32_t sw = f32x2_to_bf16x2(mul_f32x2(mul_f32x2(unpack2(ow[e]), ro2), unpack2(gw[e])));
+        uint64_t s2 = unpack2(sw);
         if (p.gate != nullptr) {
           const float2 tg = *reinterpret_cast<const float2*>(tgate + 8 * c + 2 * e);
-          s0 = __fmul_rn(tg.x, s0);
-          s1 = __fmul_rn(tg.y, s1);
+          s2 = mul_f32x2(f32x2(tg.x, tg.y), s2);
         }
-        xw[e] = pack2(__fadd_rn(bf16lo(xw[e]), s0), __fadd_rn(bf16hi(xw[e]), s1));
+        xw[e] = f32x2_to_bf16x2(add_f32x2(unpack2(xw[e]), s2));
       }
       xv[i] = make_uint4(xw[0], xw[1], xw[2], xw[3]);
       *reinterpret_cast<uint4*>(xrow + 8 * c) = xv[i];
@@ -130,6 +131,7 @@ __device__ __forceinline__ void process_row(const RmsResidualParams& p, int r, i
   if (p.nrm != nullptr) {
     const float rx =
         rsqrtf(__fadd_rn(__fmul_rn(cta_sum(sum_squares<CH>(xv, chunks), red, parity), inv_h), p.eps));
+    const uint64_t rx2 = f32x2(rx, rx);
     uint16_t* nrow = p.nrm + static_cast<size_t>(r) * p.ldn;
 #pragma unroll
     for (int i = 0; i < CH; ++i) {
@@ -141,8 +143,7 @@ __device__ __forceinline__ void process_row(const RmsResidualParams& p, int r, i
       uint32_t nw[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e)
-        nw[e] = pack2(__fmul_rn(__fmul_rn(bf16lo(xw[e]), rx), bf16lo(gw[e])),
-                      __fmul_rn(__fmul_rn(bf16hi(xw[e]), rx), bf16hi(gw[e])));
+        nw[e] = f32x2_to_bf16x2(mul_f32x2(mul_f32x2(unpack2(xw[e]), rx2), unpack2(gw[e])));
       *reinterpret_cast<uint4*>(nrow + 8 * c) = make_uint4(nw[0], nw[1], nw[2], nw[3]);
     }
   }
