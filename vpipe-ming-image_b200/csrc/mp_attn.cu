@@ -12,7 +12,11 @@
 //     dims of V_j (for O += P · V, N = head dims); K / V traffic per FLOP is
 //     half that of single-CTA tiles. Warp 0 loads Q once and the K ring
 //     (4 stages), warp 10 the V ring (4 stages); every pair load completes on
-//     the leader CTA's barrier;
+//     the leader CTA's barrier. The MMA thread commits once per step, after
+//     P_j · V_j and S_{j+2} (which the tensor core completes in issue order),
+//     to barrier (j + 2) % 4 of one ring: its phase says S_{j+2} is ready for
+//     the softmax, K stage (j + 2) % 4 and V stage j % 4 are free for the
+//     producers, and O includes P_j · V_j;
 //   * each CTA's softmax warps copy its Q rows into TMEM once; warp 1 of the
 //     leader then issues S_j = Q · K_j^T with Q read from TMEM (so the only
 //     shared-memory operand is the K half) into S[j % 2] of both CTAs, two
@@ -58,7 +62,8 @@ constexpr uint32_t kOffK = kOffQ + kQBytes;             // K ring
 constexpr uint32_t kOffV = kOffK + kKStages * kKHalf;   // V ring
 constexpr uint32_t kAttnTiles = kOffV + kVStages * kVHalf;  // 160 KB
 constexpr uint32_t kXchgBytes = 2 * 2 * 128 * 4;        // row maxima [tile parity][half][row]
-static_assert((1 + 2 * kKStages + 2 * kVStages + 8) * 8 + 8 <= 256, "barrier region");
+static_assert(kKStages == kVStages, "one completion ring for the K and V stages");
+static_assert((1 + 3 * kKStages + 5) * 8 + 8 <= 256, "barrier region");
 constexpr uint32_t kAttnSmem = kAttnTiles + 1024 + 256 + kXchgBytes;
 static_assert(kAttnSmem <= 232448, "shared memory per CTA");
 constexpr int kAttnThreads = 352;  // warp 0 Q+K, 1 MMA, 2-9 softmax, 10 V
@@ -76,13 +81,11 @@ struct AttnSmem {
   uint8_t* tiles;
   uint64_t* q_full;
   uint64_t* k_full;   // [kKStages]
-  uint64_t* k_empty;  // [kKStages]
   uint64_t* v_full;   // [kVStages]
-  uint64_t* v_empty;  // [kVStages]
   uint64_t* q_ready;  // leader: every softmax warp of the pair has put its Q part in TMEM
-  uint64_t* s_full;   // [2] S_j (j % 2) complete (both CTAs)
+  uint64_t* done;     // [kKStages] phase i / 4 of barrier i % 4: S_i and P_{i-2} · V_{i-2}
+                      // complete in both CTAs (for i >= n only the latter)
   uint64_t* p_full;   // [2] leader: P_j written over S_j by every softmax warp of the pair
-  uint64_t* o_done;   // [2] P_t · V_t (t % 2) accumulated: O includes it
   uint64_t* drain;
   uint32_t* tmem_slot;
   volatile uint32_t* abort;
@@ -96,14 +99,11 @@ __device__ __forceinline__ AttnSmem carve_attn(uint8_t* raw) {
   uint64_t* b = reinterpret_cast<uint64_t*>(s.tiles + kAttnTiles);
   s.q_full = b;
   s.k_full = s.q_full + 1;
-  s.k_empty = s.k_full + kKStages;
-  s.v_full = s.k_empty + kKStages;
-  s.v_empty = s.v_full + kVStages;
-  s.q_ready = s.v_empty + kVStages;
-  s.s_full = s.q_ready + 1;
-  s.p_full = s.s_full + 2;
-  s.o_done = s.p_full + 2;
-  s.drain = s.o_done + 2;
+  s.v_full = s.k_full + kKStages;
+  s.q_ready = s.v_full + kVStages;
+  s.done = s.q_ready + 1;
+  s.p_full = s.done + kKStages;
+  s.drain = s.p_full + 2;
   s.tmem_slot = reinterpret_cast<uint32_t*>(s.drain + 1);
   s.abort = s.tmem_slot + 1;
   s.xchg = reinterpret_cast<float*>(s.tiles + kAttnTiles + 256);
@@ -177,8 +177,9 @@ __device__ void attn_producer_k(const AttnParams& p, const AttnSmem& sm, bool le
   tma_load_3d(base + kOffQ + kQBlk, &p.tm_q, smem_u32(sm.q_full), 64, q0, head);
   for (int j = 0; j < n; ++j) {
     const int st = j % kKStages;
+    // K_{j - 4} is free once S_{j - 4} has completed
     if (j >= kKStages &&
-        !attn_wait(sm, &sm.k_empty[st], static_cast<uint32_t>(j / kKStages - 1) & 1u,
+        !attn_wait(sm, &sm.done[st], static_cast<uint32_t>(j / kKStages - 1) & 1u,
                    p.wait_limit_ns))
       return;
     const uint32_t kb = base + kOffK + static_cast<uint32_t>(st) * kKHalf;
@@ -196,8 +197,9 @@ __device__ void attn_producer_v(const AttnParams& p, const AttnSmem& sm, bool le
   const uint32_t base = smem_u32(sm.tiles);
   for (int j = 0; j < n; ++j) {
     const int st = j % kVStages;
+    // V_{j - 4} is free once P_{j - 4} · V has completed: barrier i = j - 2
     if (j >= kVStages &&
-        !attn_wait(sm, &sm.v_empty[st], static_cast<uint32_t>(j / kVStages - 1) & 1u,
+        !attn_wait(sm, &sm.done[(j - 2) % kKStages], static_cast<uint32_t>((j - 2) / kKStages) & 1u,
                    p.wait_limit_ns))
       return;
     const uint32_t vb = base + kOffV + static_cast<uint32_t>(st) * kVHalf;
@@ -227,8 +229,7 @@ __device__ void attn_mma(const AttnParams& p, const AttnSmem& sm, uint32_t tmem,
     for (int kk = 0; kk < 8; ++kk)
       umma_ts_pair(sc, tmem + kColQ + static_cast<uint32_t>(kk) * 8u, kmajor_desc(kt, kKBlk, kk),
                    idesc_qk, kk > 0 ? 1u : 0u);
-    umma_commit_pair(smem_u32(&sm.s_full[j & 1]), 0x3);
-    umma_commit_pair(smem_u32(&sm.k_empty[st]), 0x3);
+    umma_commit_pair(smem_u32(&sm.done[st]), 0x3);  // with P_{j-2} · V before it
     return true;
   };
   auto issue_pv = [&](int t) -> bool {
@@ -248,9 +249,7 @@ __device__ void attn_mma(const AttnParams& p, const AttnSmem& sm, uint32_t tmem,
                    tmem + kColS + 128u * static_cast<uint32_t>(b) +
                        64u * static_cast<uint32_t>(kk >> 2) + 8u * static_cast<uint32_t>(kk & 3),
                    vmn_desc(vt, kk), idesc_pv, (t > 0 || kk > 0) ? 1u : 0u);
-    umma_commit_pair(smem_u32(&sm.o_done[b]), 0x3);
-    umma_commit_pair(smem_u32(&sm.v_empty[st]), 0x3);
-    return true;
+    return true;  // committed with S_{t+2} (or alone past the last S)
   };
   // S runs two tiles ahead of P · V: S_{j+2} is computed while the softmax
   // works on S_{j+1}, so the tensor core never waits for the softmax to have
@@ -259,7 +258,10 @@ __device__ void attn_mma(const AttnParams& p, const AttnSmem& sm, uint32_t tmem,
   if (ok && n > 1) ok = issue_s(1);
   for (int j = 0; ok && j < n; ++j) {
     ok = issue_pv(j);
-    if (ok && j + 2 < n) ok = issue_s(j + 2);
+    if (ok && j + 2 < n)
+      ok = issue_s(j + 2);
+    else if (ok)
+      umma_commit_pair(smem_u32(&sm.done[(j + 2) % kKStages]), 0x3);
   }
   // every MMA issued has completed before TMEM is freed
   umma_commit_pair(smem_u32(sm.drain), 0x1);
@@ -313,7 +315,8 @@ __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t t
   float m_used = -INFINITY, l = 0.0f;
   for (int j = 0; j < n; ++j) {
     const int b = j & 1;
-    bool w = attn_wait(sm, &sm.s_full[b], static_cast<uint32_t>(j >> 1) & 1u, p.wait_limit_ns);
+    bool w = attn_wait(sm, &sm.done[j % kKStages], static_cast<uint32_t>(j / kKStages) & 1u,
+                       p.wait_limit_ns);
     if (!__all_sync(0xFFFFFFFFu, w)) return;
     tc_fence_after();
     const uint32_t sb = tmem + lane_base + kColS + 128u * static_cast<uint32_t>(b) + 64u * half;
@@ -355,7 +358,8 @@ __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t t
         // O holds P_0..P_{j-1} · V relative to m_used: once P_{j-1} · V has
         // landed, scale this warp's half of its rows to the new base
         const int t = j - 1;
-        w = attn_wait(sm, &sm.o_done[t & 1], static_cast<uint32_t>(t >> 1) & 1u, p.wait_limit_ns);
+        w = attn_wait(sm, &sm.done[(t + 2) % kKStages],
+                      static_cast<uint32_t>((t + 2) / kKStages) & 1u, p.wait_limit_ns);
         if (!__all_sync(0xFFFFFFFFu, w)) return;
         tc_fence_after();
         const float alpha = need ? ex2(m_used - mc) : 1.0f;
@@ -423,8 +427,8 @@ __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t t
   // all of O: P_{n-1} · V landed
   {
     const int t = n - 1;
-    const bool w = attn_wait(sm, &sm.o_done[t & 1], static_cast<uint32_t>(t >> 1) & 1u,
-                             p.wait_limit_ns);
+    const bool w = attn_wait(sm, &sm.done[(t + 2) % kKStages],
+                             static_cast<uint32_t>((t + 2) / kKStages) & 1u, p.wait_limit_ns);
     if (!__all_sync(0xFFFFFFFFu, w)) return;
     tc_fence_after();
   }
@@ -470,18 +474,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kAttnThreads, 1)
     mbar_init(smem_u32(sm.q_full), 1);
     for (int st = 0; st < kKStages; ++st) {
       mbar_init(smem_u32(&sm.k_full[st]), 1);
-      mbar_init(smem_u32(&sm.k_empty[st]), 1);
-    }
-    for (int st = 0; st < kVStages; ++st) {
       mbar_init(smem_u32(&sm.v_full[st]), 1);
-      mbar_init(smem_u32(&sm.v_empty[st]), 1);
+      mbar_init(smem_u32(&sm.done[st]), 1);
     }
     mbar_init(smem_u32(sm.q_ready), 2 * kSoftWarps);  // leader: every softmax warp of the pair
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_u32(&sm.s_full[b]), 1);
-      mbar_init(smem_u32(&sm.p_full[b]), 2 * kSoftWarps);
-      mbar_init(smem_u32(&sm.o_done[b]), 1);
-    }
+    for (int b = 0; b < 2; ++b) mbar_init(smem_u32(&sm.p_full[b]), 2 * kSoftWarps);
     mbar_init(smem_u32(sm.drain), 1);
     *sm.abort = 0u;
     fence_mbar_init();
