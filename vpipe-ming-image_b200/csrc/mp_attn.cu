@@ -37,10 +37,19 @@
 //   * after the last step the rows of O are divided by their sums and stored
 //     bf16 token-major.
 // S_{j+1}, S_{j+2} and P_{j-1} · V_{j-1} run while the softmax of tile j
-// works (S is double-buffered). Keys past S are masked (their tiles read
+// works (S is double-buffered). The kernel is persistent: each CTA pair
+// walks the (head, 256-row block) tiles cid, cid + pairs, ... and its rings,
+// barrier phases and S buffers run on as one stream of steps across tiles,
+// so the next tile's Q and first K / V tiles load, and its first two S tiles
+// are computed, while the softmax warps finish the previous tile (its Q is
+// copied into TMEM as soon as the previous tile's last S has completed; the
+// output is read out of TMEM before the next tile's first P · V overwrites
+// it). Keys past S are masked (their tiles read
 // zeros); rows past S are computed and not stored. No TMA multicast. Every
 // wait is bounded; on a timeout the CTA unwinds and reports MP_ETIMEOUT.
 #include <cuda_runtime.h>
+
+#include <algorithm>
 
 #include "mp_device.cuh"
 #include "mp_kernels.h"
@@ -61,9 +70,10 @@ constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffK = kOffQ + kQBytes;             // K ring
 constexpr uint32_t kOffV = kOffK + kKStages * kKHalf;   // V ring
 constexpr uint32_t kAttnTiles = kOffV + kVStages * kVHalf;  // 160 KB
-constexpr uint32_t kXchgBytes = 2 * 2 * 128 * 4;        // row maxima [tile parity][half][row]
+// row maxima [step parity][half][row], then the row sums of a tile's end [half][row]
+constexpr uint32_t kXchgBytes = 3 * 2 * 128 * 4;
 static_assert(kKStages == kVStages, "one completion ring for the K and V stages");
-static_assert((1 + 3 * kKStages + 5) * 8 + 8 <= 256, "barrier region");
+static_assert((2 + 3 * kKStages + 4) * 8 + 8 <= 256, "barrier region");
 constexpr uint32_t kAttnSmem = kAttnTiles + 1024 + 256 + kXchgBytes;
 static_assert(kAttnSmem <= 232448, "shared memory per CTA");
 constexpr int kAttnThreads = 352;  // warp 0 Q+K, 1 MMA, 2-9 softmax, 10 V
@@ -80,6 +90,7 @@ enum : uint32_t { kAttnSiteWait = 0x2100u, kAttnSiteDrain = 0x2200u };
 struct AttnSmem {
   uint8_t* tiles;
   uint64_t* q_full;
+  uint64_t* q_empty;  // every softmax warp of this CTA has copied the tile's Q rows to TMEM
   uint64_t* k_full;   // [kKStages]
   uint64_t* v_full;   // [kVStages]
   uint64_t* q_ready;  // leader: every softmax warp of the pair has put its Q part in TMEM
@@ -98,7 +109,8 @@ __device__ __forceinline__ AttnSmem carve_attn(uint8_t* raw) {
   s.tiles = reinterpret_cast<uint8_t*>(base);
   uint64_t* b = reinterpret_cast<uint64_t*>(s.tiles + kAttnTiles);
   s.q_full = b;
-  s.k_full = s.q_full + 1;
+  s.q_empty = s.q_full + 1;
+  s.k_full = s.q_empty + 1;
   s.v_full = s.k_full + kKStages;
   s.q_ready = s.v_full + kVStages;
   s.done = s.q_ready + 1;
@@ -165,103 +177,159 @@ __device__ __forceinline__ bool attn_wait(const AttnSmem& sm, uint64_t* bar, uin
   return mbar_wait(smem_u32(bar), parity, sm.abort, kAttnSiteWait, limit);
 }
 
-// Warp 0 of each CTA, one thread: its Q rows, then its halves of the K ring
-// (pair loads completing on the leader's barriers; the leader expects both
-// CTAs' bytes).
-__device__ void attn_producer_k(const AttnParams& p, const AttnSmem& sm, bool leader, int rank,
-                                int q0, int head, int n) {
+// The tiles of this CTA pair: (head, 256-row block) tile cid + t * ncl for
+// t < tiles (cid = the pair's index, ncl = pairs in the grid), n steps each.
+struct AttnSched {
+  int cid, ncl, nq, n, tiles;
+};
+
+__device__ __forceinline__ AttnSched attn_sched(const AttnParams& p) {
+  AttnSched s;
+  s.n = (p.S + kAttnTile - 1) / kAttnTile;
+  s.nq = (p.S + 2 * kAttnTile - 1) / (2 * kAttnTile);
+  const int total = s.nq * p.NH;
+  s.cid = static_cast<int>(blockIdx.x >> 1);
+  s.ncl = static_cast<int>(gridDim.x >> 1);
+  s.tiles = s.cid < total ? (total - s.cid + s.ncl - 1) / s.ncl : 0;
+  return s;
+}
+
+// Head and this CTA's first query row of the pair's tile t.
+__device__ __forceinline__ void attn_tile(const AttnSched& s, int t, int rank, int& q0, int& head) {
+  const int tile = s.cid + t * s.ncl;
+  head = tile / s.nq;
+  q0 = (tile - head * s.nq) * 2 * kAttnTile + rank * kAttnTile;
+}
+
+// Warp 0 of each CTA, one thread: per tile its Q rows, then its halves of
+// the K ring (pair loads completing on the leader's barriers; the leader
+// expects both CTAs' bytes). g counts steps over all of the pair's tiles.
+__device__ void attn_producer_k(const AttnParams& p, const AttnSmem& sm, const AttnSched& sc,
+                                bool leader, int rank) {
   const uint32_t base = smem_u32(sm.tiles);
-  // this CTA's Q rows, on its own barrier (its softmax warps copy them to TMEM)
-  mbar_arrive_expect_tx(smem_u32(sm.q_full), kQBytes);
-  tma_load_3d(base + kOffQ, &p.tm_q, smem_u32(sm.q_full), 0, q0, head);
-  tma_load_3d(base + kOffQ + kQBlk, &p.tm_q, smem_u32(sm.q_full), 64, q0, head);
-  for (int j = 0; j < n; ++j) {
-    const int st = j % kKStages;
-    // K_{j - 4} is free once S_{j - 4} has completed
-    if (j >= kKStages &&
-        !attn_wait(sm, &sm.done[st], static_cast<uint32_t>(j / kKStages - 1) & 1u,
-                   p.wait_limit_ns))
+  int g = 0;
+  for (int t = 0; t < sc.tiles; ++t) {
+    int q0, head;
+    attn_tile(sc, t, rank, q0, head);
+    // this CTA's Q rows, on its own barrier (its softmax warps copy them to
+    // TMEM), once the previous tile's Q has left shared memory
+    if (t > 0 && !attn_wait(sm, sm.q_empty, static_cast<uint32_t>(t - 1) & 1u, p.wait_limit_ns))
       return;
-    const uint32_t kb = base + kOffK + static_cast<uint32_t>(st) * kKHalf;
-    const uint32_t bar = mapa_shared(smem_u32(&sm.k_full[st]), 0);
-    if (leader) mbar_arrive_expect_tx(smem_u32(&sm.k_full[st]), 2 * kKHalf);
-    const int key0 = j * kAttnTile + rank * 64;
-    tma_load_3d_pair(kb, &p.tm_k, bar, 0, key0, head);
-    tma_load_3d_pair(kb + kKBlk, &p.tm_k, bar, 64, key0, head);
+    mbar_arrive_expect_tx(smem_u32(sm.q_full), kQBytes);
+    tma_load_3d(base + kOffQ, &p.tm_q, smem_u32(sm.q_full), 0, q0, head);
+    tma_load_3d(base + kOffQ + kQBlk, &p.tm_q, smem_u32(sm.q_full), 64, q0, head);
+    for (int j = 0; j < sc.n; ++j, ++g) {
+      const int st = g % kKStages;
+      // K_{g - 4} is free once S_{g - 4} has completed
+      if (g >= kKStages &&
+          !attn_wait(sm, &sm.done[st], static_cast<uint32_t>(g / kKStages - 1) & 1u,
+                     p.wait_limit_ns))
+        return;
+      const uint32_t kb = base + kOffK + static_cast<uint32_t>(st) * kKHalf;
+      const uint32_t bar = mapa_shared(smem_u32(&sm.k_full[st]), 0);
+      if (leader) mbar_arrive_expect_tx(smem_u32(&sm.k_full[st]), 2 * kKHalf);
+      const int key0 = j * kAttnTile + rank * 64;
+      tma_load_3d_pair(kb, &p.tm_k, bar, 0, key0, head);
+      tma_load_3d_pair(kb + kKBlk, &p.tm_k, bar, 64, key0, head);
+    }
   }
 }
 
 // Warp 10 of each CTA, one thread: its 64 dims of the V ring.
-__device__ void attn_producer_v(const AttnParams& p, const AttnSmem& sm, bool leader, int rank,
-                                int head, int n) {
+__device__ void attn_producer_v(const AttnParams& p, const AttnSmem& sm, const AttnSched& sc,
+                                bool leader, int rank) {
   const uint32_t base = smem_u32(sm.tiles);
-  for (int j = 0; j < n; ++j) {
-    const int st = j % kVStages;
-    // V_{j - 4} is free once P_{j - 4} · V has completed: barrier i = j - 2
-    if (j >= kVStages &&
-        !attn_wait(sm, &sm.done[(j - 2) % kKStages], static_cast<uint32_t>((j - 2) / kKStages) & 1u,
-                   p.wait_limit_ns))
-      return;
-    const uint32_t vb = base + kOffV + static_cast<uint32_t>(st) * kVHalf;
-    const uint32_t bar = mapa_shared(smem_u32(&sm.v_full[st]), 0);
-    if (leader) mbar_arrive_expect_tx(smem_u32(&sm.v_full[st]), 2 * kVHalf);
-    tma_load_3d_pair(vb, &p.tm_v, bar, rank * 64, j * kAttnTile, head);
+  int g = 0;
+  for (int t = 0; t < sc.tiles; ++t) {
+    int q0, head;
+    attn_tile(sc, t, rank, q0, head);
+    for (int j = 0; j < sc.n; ++j, ++g) {
+      const int st = g % kVStages;
+      // V_{g - 4} is free once P_{g - 4} · V has completed: barrier i = g - 2
+      if (g >= kVStages &&
+          !attn_wait(sm, &sm.done[(g - 2) % kKStages],
+                     static_cast<uint32_t>((g - 2) / kKStages) & 1u, p.wait_limit_ns))
+        return;
+      const uint32_t vb = base + kOffV + static_cast<uint32_t>(st) * kVHalf;
+      const uint32_t bar = mapa_shared(smem_u32(&sm.v_full[st]), 0);
+      if (leader) mbar_arrive_expect_tx(smem_u32(&sm.v_full[st]), 2 * kVHalf);
+      tma_load_3d_pair(vb, &p.tm_v, bar, rank * 64, j * kAttnTile, head);
+    }
   }
 }
 
-// Warp 1 of the leader, one thread: pair MMAs for both CTAs.
-__device__ void attn_mma(const AttnParams& p, const AttnSmem& sm, uint32_t tmem, int n) {
+// Warp 1 of the leader, one thread: pair MMAs for both CTAs, over the steps
+// g of all the pair's tiles (tile g / n, key tile g % n).
+__device__ void attn_mma(const AttnParams& p, const AttnSmem& sm, const AttnSched& sc,
+                         uint32_t tmem) {
   const uint32_t base = smem_u32(sm.tiles);
   const uint32_t idesc_qk = make_idesc_bf16(2 * kAttnTile, kAttnTile);  // M 256, N 128
   const uint32_t idesc_pv = idesc_qk | (1u << 16);  // B (V) MN-major
-  bool ok = attn_wait(sm, sm.q_ready, 0, p.wait_limit_ns);
-  auto issue_s = [&](int j) -> bool {
-    const int st = j % kKStages;
-    if (!attn_wait(sm, &sm.k_full[st], static_cast<uint32_t>(j / kKStages) & 1u, p.wait_limit_ns))
+  const int n = sc.n;
+  const int steps = sc.tiles * n;
+  // tile and step within it of the next S and the next P · V, kept as
+  // counters (no division on the issue path)
+  int s_tile = 0, s_j = 0, pv_j = 0;
+  auto issue_s = [&](int g) -> bool {
+    // a tile's first S waits for its Q rows in both CTAs' TMEM
+    if (s_j == 0 &&
+        !attn_wait(sm, sm.q_ready, static_cast<uint32_t>(s_tile) & 1u, p.wait_limit_ns))
+      return false;
+    if (++s_j == n) {
+      s_j = 0;
+      ++s_tile;
+    }
+    const int st = g % kKStages;
+    if (!attn_wait(sm, &sm.k_full[st], static_cast<uint32_t>(g / kKStages) & 1u, p.wait_limit_ns))
       return false;
     tc_fence_after();
     const uint32_t kt = base + kOffK + static_cast<uint32_t>(st) * kKHalf;
-    // S[j % 2] held P_{j-2}, which P_{j-2} · V (issued before this) reads
+    // S[g % 2] held P_{g-2}, which P_{g-2} · V (issued before this) reads
     // first: the tensor core runs a thread's MMAs in order
-    const uint32_t sc = tmem + kColS + 128u * static_cast<uint32_t>(j & 1);
+    const uint32_t sc_col = tmem + kColS + 128u * static_cast<uint32_t>(g & 1);
     // A = Q from each CTA's TMEM: 16 dims (8 columns of bf16 pairs) per step
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk)
-      umma_ts_pair(sc, tmem + kColQ + static_cast<uint32_t>(kk) * 8u, kmajor_desc(kt, kKBlk, kk),
-                   idesc_qk, kk > 0 ? 1u : 0u);
-    umma_commit_pair(smem_u32(&sm.done[st]), 0x3);  // with P_{j-2} · V before it
+      umma_ts_pair(sc_col, tmem + kColQ + static_cast<uint32_t>(kk) * 8u,
+                   kmajor_desc(kt, kKBlk, kk), idesc_qk, kk > 0 ? 1u : 0u);
+    umma_commit_pair(smem_u32(&sm.done[st]), 0x3);  // with P_{g-2} · V before it
     return true;
   };
-  auto issue_pv = [&](int t) -> bool {
-    const int b = t & 1;
-    const int st = t % kVStages;
-    if (!attn_wait(sm, &sm.v_full[st], static_cast<uint32_t>(t / kVStages) & 1u, p.wait_limit_ns))
+  auto issue_pv = [&](int g) -> bool {
+    const int b = g & 1;
+    const int st = g % kVStages;
+    if (!attn_wait(sm, &sm.v_full[st], static_cast<uint32_t>(g / kVStages) & 1u, p.wait_limit_ns))
       return false;
-    if (!attn_wait(sm, &sm.p_full[b], static_cast<uint32_t>(t >> 1) & 1u, p.wait_limit_ns))
+    if (!attn_wait(sm, &sm.p_full[b], static_cast<uint32_t>(g >> 1) & 1u, p.wait_limit_ns))
       return false;
     tc_fence_after();
     const uint32_t vt = base + kOffV + static_cast<uint32_t>(st) * kVHalf;
-    // A = P_t from each CTA's TMEM, over S[b]: keys 64h .. 64h + 63 as bf16
-    // pairs in columns 64h .. 64h + 31 of the buffer; 16 keys per step
+    // A = P_g from each CTA's TMEM, over S[b]: keys 64h .. 64h + 63 as bf16
+    // pairs in columns 64h .. 64h + 31 of the buffer; 16 keys per step. A
+    // tile's first P · V overwrites O (read out by then: the softmax warps
+    // store the previous tile's output before they write this P).
+    const bool first = pv_j == 0;
+    if (++pv_j == n) pv_j = 0;
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk)
       umma_ts_pair(tmem + kColO,
                    tmem + kColS + 128u * static_cast<uint32_t>(b) +
                        64u * static_cast<uint32_t>(kk >> 2) + 8u * static_cast<uint32_t>(kk & 3),
-                   vmn_desc(vt, kk), idesc_pv, (t > 0 || kk > 0) ? 1u : 0u);
-    return true;  // committed with S_{t+2} (or alone past the last S)
+                   vmn_desc(vt, kk), idesc_pv, (!first || kk > 0) ? 1u : 0u);
+    return true;  // committed with S_{g+2} (or alone past the last S)
   };
-  // S runs two tiles ahead of P · V: S_{j+2} is computed while the softmax
-  // works on S_{j+1}, so the tensor core never waits for the softmax to have
+  // S runs two steps ahead of P · V: S_{g+2} is computed while the softmax
+  // works on S_{g+1}, so the tensor core never waits for the softmax to have
   // read a tile before the next one can start
-  if (ok) ok = issue_s(0);
-  if (ok && n > 1) ok = issue_s(1);
-  for (int j = 0; ok && j < n; ++j) {
-    ok = issue_pv(j);
-    if (ok && j + 2 < n)
-      ok = issue_s(j + 2);
+  bool ok = true;
+  if (steps > 0) ok = issue_s(0);
+  if (ok && steps > 1) ok = issue_s(1);
+  for (int g = 0; ok && g < steps; ++g) {
+    ok = issue_pv(g);
+    if (ok && g + 2 < steps)
+      ok = issue_s(g + 2);
     else if (ok)
-      umma_commit_pair(smem_u32(&sm.done[(j + 2) % kKStages]), 0x3);
+      umma_commit_pair(smem_u32(&sm.done[(g + 2) % kKStages]), 0x3);
   }
   // every MMA issued has completed before TMEM is freed
   umma_commit_pair(smem_u32(sm.drain), 0x1);
@@ -274,14 +342,43 @@ __device__ void attn_mma(const AttnParams& p, const AttnSmem& sm, uint32_t tmem,
   }
 }
 
+// A softmax thread's Q row of tile t, dims [64 half, 64 half + 64), from the
+// 128-byte-swizzled smem tile into TMEM as bf16 pairs (column = dim / 2);
+// then shared memory is free for the next tile's Q and the leader's MMA
+// thread may issue the tile's S.
+__device__ __forceinline__ bool attn_copy_q(const AttnParams& p, const AttnSmem& sm, uint32_t tmem,
+                                            int t, int half, int row, uint32_t lane_base) {
+  const bool w = attn_wait(sm, sm.q_full, static_cast<uint32_t>(t) & 1u, p.wait_limit_ns);
+  if (!__all_sync(0xFFFFFFFFu, w)) return false;
+  const uint32_t qrow = smem_u32(sm.tiles) + kOffQ + static_cast<uint32_t>(half) * kQBlk +
+                        static_cast<uint32_t>(row) * 128u;
+  uint32_t qv[32];
+#pragma unroll
+  for (int ch = 0; ch < 8; ++ch) {
+    const uint32_t a = qrow + ((static_cast<uint32_t>(ch) ^ static_cast<uint32_t>(row & 7)) << 4);
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(qv[4 * ch]), "=r"(qv[4 * ch + 1]), "=r"(qv[4 * ch + 2]), "=r"(qv[4 * ch + 3])
+                 : "r"(a));
+  }
+  MP_TMEM_ST_32X32B_X32(tmem + lane_base + kColQ + 32u * half, qv);
+  tmem_wait_st();
+  tc_fence_before();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) {
+    mbar_arrive(smem_u32(sm.q_empty));
+    mbar_arrive_remote(mapa_shared(smem_u32(sm.q_ready), 0));
+  }
+  return true;
+}
+
 // Warps 2-9: two warps per TMEM lane quarter; thread = query row (lane),
 // half = which 64 keys of each 128-key tile (and which 64 columns of O) this
 // warp takes. The two halves of a row exchange their partial maxima through
-// shared memory (one named barrier per quarter pair and tile) and so move
+// shared memory (one named barrier per quarter pair and step) and so move
 // the row's exponent base identically; each keeps its own partial row sum,
-// added to the other once at the end.
-__device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t tmem, int q0,
-                             int head, int n) {
+// added to the other once at the tile's end.
+__device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, const AttnSched& sc,
+                             uint32_t tmem, int rank) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int quarter = warp & 3;
@@ -291,31 +388,16 @@ __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t t
   const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
   const float c = p.scale_log2;
   const uint64_t c2 = f32x2(c, c);
-  {
-    // this thread's Q row, dims [64 half, 64 half + 64), from the 128-byte-
-    // swizzled smem tile into TMEM as bf16 pairs (column = dim / 2)
-    bool w = attn_wait(sm, sm.q_full, 0, p.wait_limit_ns);
-    if (!__all_sync(0xFFFFFFFFu, w)) return;
-    const uint32_t qrow = smem_u32(sm.tiles) + kOffQ + static_cast<uint32_t>(half) * kQBlk +
-                          static_cast<uint32_t>(row) * 128u;
-    uint32_t qv[32];
-#pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
-      const uint32_t a = qrow + ((static_cast<uint32_t>(ch) ^ static_cast<uint32_t>(row & 7)) << 4);
-      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                   : "=r"(qv[4 * ch]), "=r"(qv[4 * ch + 1]), "=r"(qv[4 * ch + 2]), "=r"(qv[4 * ch + 3])
-                   : "r"(a));
-    }
-    MP_TMEM_ST_32X32B_X32(tmem + lane_base + kColQ + 32u * half, qv);
-    tmem_wait_st();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(sm.q_ready), 0));
-  }
+  // schedule values recomputed from the parameters where used (fewer live
+  // registers through the steps)
+  const int n = (p.S + kAttnTile - 1) / kAttnTile;
+  if (sc.tiles == 0 || !attn_copy_q(p, sm, tmem, 0, half, row, lane_base)) return;
+  int g = 0;  // steps over all of the pair's tiles
+  for (int t = 0; t < attn_sched(p).tiles; ++t) {
   float m_used = -INFINITY, l = 0.0f;
-  for (int j = 0; j < n; ++j) {
-    const int b = j & 1;
-    bool w = attn_wait(sm, &sm.done[j % kKStages], static_cast<uint32_t>(j / kKStages) & 1u,
+  for (int j = 0; j < n; ++j, ++g) {
+    const int b = g & 1;
+    bool w = attn_wait(sm, &sm.done[g % kKStages], static_cast<uint32_t>(g / kKStages) & 1u,
                        p.wait_limit_ns);
     if (!__all_sync(0xFFFFFFFFu, w)) return;
     tc_fence_after();
@@ -356,10 +438,10 @@ __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t t
       const bool need = mc > m_used + kRescaleLog2;
       if (__any_sync(0xFFFFFFFFu, need)) {
         // O holds P_0..P_{j-1} · V relative to m_used: once P_{j-1} · V has
-        // landed, scale this warp's half of its rows to the new base
-        const int t = j - 1;
-        w = attn_wait(sm, &sm.done[(t + 2) % kKStages],
-                      static_cast<uint32_t>((t + 2) / kKStages) & 1u, p.wait_limit_ns);
+        // landed (with S_{g+1}: barrier g + 1), scale this warp's half of its
+        // rows to the new base
+        w = attn_wait(sm, &sm.done[(g + 1) % kKStages],
+                      static_cast<uint32_t>((g + 1) / kKStages) & 1u, p.wait_limit_ns);
         if (!__all_sync(0xFFFFFFFFu, w)) return;
         tc_fence_after();
         const float alpha = need ? ex2(m_used - mc) : 1.0f;
@@ -424,19 +506,27 @@ __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t t
     __syncwarp();
     if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&sm.p_full[b]), 0));
   }
-  // all of O: P_{n-1} · V landed
+  // the tile's last S has completed (waited above): the next tile's Q may
+  // replace this one in TMEM
+  if (t + 1 < attn_sched(p).tiles && !attn_copy_q(p, sm, tmem, t + 1, half, row, lane_base))
+    return;
+  // all of O: the tile's last P · V (step g - 1) landed, with S_{g+1}:
+  // barrier g + 1
   {
-    const int t = n - 1;
-    const bool w = attn_wait(sm, &sm.done[(t + 2) % kKStages],
-                             static_cast<uint32_t>((t + 2) / kKStages) & 1u, p.wait_limit_ns);
+    const bool w = attn_wait(sm, &sm.done[(g + 1) % kKStages],
+                             static_cast<uint32_t>((g + 1) / kKStages) & 1u, p.wait_limit_ns);
     if (!__all_sync(0xFFFFFFFFu, w)) return;
     tc_fence_after();
   }
-  // the row sum over both halves (added in half order)
-  float* xl = sm.xchg + (n & 1) * 256;  // the buffer the last tile did not use
+  // the row sum over both halves (added in half order), in a buffer of its
+  // own: the next tile's first maxima go to buffer g % 2 while the partner
+  // warp may still read this
+  float* xl = sm.xchg + 2 * 256;
   xl[half * 128 + row] = l;
   named_barrier(bar_id, 64);
   const float lt = xl[row] + xl[128 + row];
+  int q0, head;
+  attn_tile(attn_sched(p), t, rank, q0, head);
   const int q = q0 + row;
   const float inv = 1.0f / lt;
   uint16_t* dst = p.o + static_cast<size_t>(q) * p.ldo + static_cast<size_t>(head) * 128 + 64 * half;
@@ -457,6 +547,7 @@ __device__ void attn_softmax(const AttnParams& p, const AttnSmem& sm, uint32_t t
       }
     }
   }
+  }
 }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kAttnThreads, 1)
@@ -467,11 +558,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kAttnThreads, 1)
   const int lane = threadIdx.x & 31;
   const int rank = static_cast<int>(cluster_ctarank());
   const bool leader = rank == 0;
-  const int q0 = static_cast<int>(blockIdx.x >> 1) * 2 * kAttnTile + rank * kAttnTile;
-  const int head = static_cast<int>(blockIdx.y);
-  const int n = (p.S + kAttnTile - 1) / kAttnTile;
+  const AttnSched sc = attn_sched(p);
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(sm.q_full), 1);
+    mbar_init(smem_u32(sm.q_empty), kSoftWarps);  // this CTA's softmax warps
     for (int st = 0; st < kKStages; ++st) {
       mbar_init(smem_u32(&sm.k_full[st]), 1);
       mbar_init(smem_u32(&sm.v_full[st]), 1);
@@ -497,13 +587,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kAttnThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *sm.tmem_slot;
   if (warp == 0) {
-    if (lane == 0) attn_producer_k(p, sm, leader, rank, q0, head, n);
+    if (lane == 0) attn_producer_k(p, sm, sc, leader, rank);
   } else if (warp == 1) {
-    if (lane == 0 && leader) attn_mma(p, sm, tmem, n);
+    if (lane == 0 && leader) attn_mma(p, sm, sc, tmem);
   } else if (warp == 10) {
-    if (lane == 0) attn_producer_v(p, sm, leader, rank, head, n);
+    if (lane == 0) attn_producer_v(p, sm, sc, leader, rank);
   } else {
-    attn_softmax(p, sm, tmem, q0, head, n);
+    attn_softmax(p, sm, sc, tmem, rank);
   }
   if (*sm.abort != 0u) {
     // error path only: let copies issued before the abort land before leaving
@@ -518,6 +608,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kAttnThreads, 1)
 }
 
 bool g_attn_configured[64] = {};
+int g_attn_pairs[64] = {};  // CTA pairs of this kernel resident at once
 
 }  // namespace
 
@@ -530,12 +621,29 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream) {
     e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kAttnSmem));
     if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(kAttnThreads, 1, 1);
+    cfg.dynamicSmemBytes = kAttnSmem;
+    int pairs = 0;
+    if (cudaOccupancyMaxActiveClusters(&pairs, attn_kernel, &cfg) != cudaSuccess || pairs <= 0) {
+      (void)cudaGetLastError();
+      int sms = 0;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      pairs = sms > 1 ? sms / 2 : 1;
+    }
+    g_attn_pairs[dev] = pairs;
     g_attn_configured[dev] = true;
   }
-  // one CTA pair per 256 query rows
-  const dim3 grid(static_cast<unsigned>(2 * ((p.S + 2 * kAttnTile - 1) / (2 * kAttnTile))),
-                  static_cast<unsigned>(p.NH), 1);
-  attn_kernel<<<grid, kAttnThreads, kAttnSmem, stream>>>(p);
+  // persistent CTA pairs, at most one per (head, 256-row block) tile. With a
+  // single 128-key step per tile (S <= 128) every tile gets a pair of its
+  // own: a pair's step stream commits a tile's last P · V together with the
+  // S two steps later, which would then belong to a tile whose Q can only
+  // arrive after this tile's output is stored.
+  const long long tiles = static_cast<long long>((p.S + 2 * kAttnTile - 1) / (2 * kAttnTile)) * p.NH;
+  const long long pairs = p.S > kAttnTile ? std::min<long long>(tiles, g_attn_pairs[dev]) : tiles;
+  if (pairs <= 0 || pairs > (1ll << 30)) return cudaErrorInvalidValue;
+  attn_kernel<<<dim3(static_cast<unsigned>(2 * pairs), 1, 1), kAttnThreads, kAttnSmem, stream>>>(p);
   return cudaGetLastError();
 }
 
