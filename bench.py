@@ -1,24 +1,31 @@
 """Benchmark of the fused quant + 8-slot-LoRA DiT projection path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config 3|2|5]
 
-One STEP is one pass of the hot path over one image's batch: the full 34-block
-projection set of a 1024x1024 Ming-Image DiT forward (
-4096 image rows + 256 caption rows, joint 4352; hidden 3840, FFN 10240; w8
-affine group-64 packs; eight LoRA slots of ranks {4,8,8,16,16,32,32,64} with
-strengths ~U(-1, 1.5)) plus the batched adaLN modulation of the 32 modulated
-blocks. Inputs are seeded synthetic tensors of those shapes (the reference's
-checkpoint and prompts are not available); every block streams its own
-weights (6.2 GB of codes per step, far larger than L2).
+One STEP is one forward's worth of the hot path: the full 34-block projection
+set of a Ming-Image DiT forward plus the batched adaLN modulation of the 32
+modulated blocks. The headline (default) workload is BASELINE config 3, the
+north-star target: a 2048x2048 image (16384 image rows + 512 caption rows,
+joint 16896), w4 affine group-64 packs, eight LoRA slots all of rank 32, the
+strengths re-drawn before every forward as the denoise schedule re-sets them
+(11 steps = one 11-forward generation). Inputs are seeded synthetic tensors
+of the stated shapes (the reference's checkpoint and prompts are not
+available); every forward streams every block's packed weights (3.4 GB at w4),
+far more than L2, so no flush is needed between steps.
 
-Under torchrun (N > 1) every rank runs one image of its own (image sharding,
-no collective on the data path: weak scaling); the JSON line reports the
-whole-job TFLOP/s over the max-over-ranks device time.
+Under torchrun (N > 1) every rank runs a config-3 forward of its own image
+(image sharding, no collective on the data path: weak scaling); the JSON line
+reports the whole-job TFLOP/s over the max-over-ranks device time. The same
+run also measures BASELINE config 5 (`config5_batch`): a batch of 8 images,
+split by image over the N ranks (8 / N per rank, all in one launch per
+projection, per-image strength vectors), its device time per step as the max
+over ranks (strong scaling; --no-config5 skips it).
 
 `--shard rows` instead splits ONE image's token rows across the N ranks
-(128-row-aligned slices, configs 2-4): every rank projects its slice of every
-block, and each block's K and V are all-gathered over NCCL on a side stream
-while the block's remaining projections run (strong scaling).
+(equal 32-row-aligned slices, configs 2-4): every rank projects its slice of
+every block, and each block's K and V are all-gathered over NCCL on a side
+stream while the block's remaining projections run (strong scaling).
 """
 from __future__ import annotations
 
@@ -36,11 +43,7 @@ sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(ROOT / "vpipe-ming-image_b200"))
 
 METRIC = "fused quant+8-LoRA DiT-projection TFLOP/s & % TC peak at 1/2/4/8 B200"
-RANKS = (4, 8, 8, 16, 16, 32, 32, 64)
-WORKLOAD = ("config2: full 34-block projection set of one 1024x1024 DiT forward "
-            "(IMG 4096 + CAP 256 rows, joint 4352; H 3840, FFN 10240; w8 affine g64; "
-            "8 LoRA slots r={4,8,8,16,16,32,32,64}, s~U(-1,1.5)) + batched adaLN modulation "
-            "of 32 blocks")
+RANKS = (4, 8, 8, 16, 16, 32, 32, 64)  # --forward and --shard rows: config 2's slots
 
 
 def load_peaks() -> dict:
@@ -107,41 +110,77 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def cpu_baseline(sample_rows: int = 4352) -> dict:
+# The benchmark workloads (seeded synthetic tensors of the
+# stated shapes and distributions: the reference's checkpoint is not here).
+CONFIGS = {
+    3: {"img": 16384, "cap": 512, "bits": 4, "ranks": (32,) * 8, "images": 1,
+        "workload": ("config3: full 34-block projection set of one 2048x2048 DiT forward "
+                     "(IMG 16384 + CAP 512 rows, joint 16896; H 3840, FFN 10240; w4 affine g64; "
+                     "8 LoRA slots all r=32; strengths re-drawn ~U(-1,1.5) before every forward "
+                     "of the 11-forward denoise schedule) + batched adaLN modulation of 32 "
+                     "blocks; one step = one forward")},
+    2: {"img": 4096, "cap": 256, "bits": 8, "ranks": (4, 8, 8, 16, 16, 32, 32, 64), "images": 1,
+        "workload": ("config2: full 34-block projection set of one 1024x1024 DiT forward "
+                     "(IMG 4096 + CAP 256 rows, joint 4352; w8 affine g64; 8 LoRA slots "
+                     "r={4,8,8,16,16,32,32,64}, s~U(-1,1.5)) + batched adaLN modulation of 32 "
+                     "blocks; one step = one forward")},
+    5: {"img": 4096, "cap": 256, "bits": 8, "ranks": (8, 8, 16, 16, 32, 32, 64, 64), "images": 8,
+        "workload": ("config5: 34-block projection set of a batch of 8 independent 1024x1024 "
+                     "images (each 4096 + 256 rows; w8 affine g64; shared slots "
+                     "r={8,8,16,16,32,32,64,64}; per-image strength vectors ~U(-1,1.5) re-drawn "
+                     "every step) + batched modulation (one temb row per image); the 8 images "
+                     "are split by image over the ranks (8/N each, all of a rank's images in "
+                     "one launch per projection); one step = one forward of the whole batch")},
+}
+
+
+def cpu_sample_rows(cfg: dict) -> int:
+    """Rows of the bounded CPU sample: one main-layer block at the joint row
+    count of one image (the block kind 30 of the 34 blocks run)."""
+    return cfg["img"] + cfg["cap"]
+
+
+def cpu_baseline(cfg: dict) -> dict:
     from oracle import cpu_ref
-    r = cpu_ref.time_block(sample_rows, reps=1)
+    rows = cpu_sample_rows(cfg)
+    r = cpu_ref.time_block(rows, bits=cfg["bits"], ranks=cfg["ranks"], reps=1)
     return {"value": r["tflops"], "unit": "TFLOP/s", "cores": r["threads"], "kind": "port",
-            "sample": (f"one main-layer block's 7 projections (w8 dequantized once, 8 LoRA "
-                       f"slots) at {r['rows']} rows, torch fp32 CPU, {r['seconds']:.1f} s; "
-                       "TFLOP/s of that sample")}
+            "sample": (f"one main-layer block's 7 projections (w{cfg['bits']} dequantized once, "
+                       f"{len(cfg['ranks'])} LoRA slots) at {r['rows']} rows, torch fp32 CPU "
+                       f"restatement, {r['seconds']:.1f} s; TFLOP/s of that sample (a forward "
+                       "extrapolates by FLOPs: every block runs the same arithmetic per row)")}
 
 
 def run_reference(args) -> None:
     """The reference arm: the CPU port of the path (the reference itself is
-    Metal-only), one bounded sample per step, all host threads, rank 0 only."""
+    Metal-only), one bounded sample per step (the same sample as the main
+    arm's cpu_baseline), all host threads, rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     from oracle import cpu_ref
-    rows = 1088  # a quarter of the joint sequence per step keeps K + W steps within minutes
+    cfg = CONFIGS[args.config]
+    rows = cpu_sample_rows(cfg)
+    blk = cpu_ref.CpuBlock(3840, 10240, cfg["bits"], cfg["ranks"], seed=0)
     vals = []
     for i in range(args.warmup + args.steps):
-        r = cpu_ref.time_block(rows, reps=1, seed=i)
+        r = cpu_ref.time_block(rows, bits=cfg["bits"], ranks=cfg["ranks"], reps=1, seed=i,
+                               block=blk)
         if i >= args.warmup:
             vals.append(r)
     flops = sum(v["flops"] for v in vals)
     secs = sum(v["seconds"] for v in vals)
     value = flops / secs / 1e12
+    sample = (f"one main-layer block's 7 projections at {rows} rows per step (torch fp32 CPU "
+              "restatement with the path's dequant and LoRA rule; the reference is Metal-only)")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": secs / len(vals) * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample": f"one main-layer block at {rows} rows per step"},
+        "config": {"workload": cfg["workload"], "sample": sample},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": vals[0]["threads"],
-                         "kind": "port",
-                         "sample": f"one main-layer block's 7 projections at {rows} rows per step "
-                                   "(torch fp32 CPU restatement; the reference is Metal-only)"},
+                         "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -245,7 +284,7 @@ def run_rows(args) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": WORKLOAD, "l2": "inputs larger than L2",
+            "config": {"workload": CONFIGS[2]["workload"], "l2": "inputs larger than L2",
                        "flops_per_step": step_flops,
                        "parallelism": f"token-rows x{world} (128-row-aligned slices), NCCL "
                                       "all-gather of each block's K and V overlapping the "
@@ -344,14 +383,106 @@ def run_forward(args) -> None:
     ctx.close()
 
 
+def _workload_state(cfg: dict, world: int, rank: int, dev, ctx, seed_base: int):
+    """Projection set, slots, inputs and outputs of one rank of a workload.
+    Configs 2 and 3: the rank's own image (weak scaling: every rank draws its
+    own weights, inputs and strengths). Config 5: the rank's 8 / world images
+    of the shared batch (strong scaling: the same model on every rank)."""
+    import numpy as np
+    import torch
+
+    from mingproj.dit import DitDims, DitProjectionSet, Layout, alloc_outputs
+
+    dims = DitDims()
+    layout = Layout(img=cfg["img"], cap=cfg["cap"])
+    strong = cfg["images"] > 1
+    if strong and cfg["images"] % world != 0:
+        raise SystemExit(f"{cfg['images']} images do not split evenly over {world} ranks")
+    n_img = cfg["images"] // world if strong else 1
+    wseed = seed_base if strong else seed_base + rank
+    pset = DitProjectionSet.synthetic(ctx, dims, bits=cfg["bits"], seed=wseed, device=dev)
+    for i, r in enumerate(cfg["ranks"]):
+        pset.bind_synthetic(i, r, seed=100 * wseed + i, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(wseed + 7 + (rank if strong else 0))
+    rows = n_img * layout.joint
+    st = {
+        "dims": dims, "layout": layout, "n_img": n_img, "pset": pset,
+        "nrm": torch.randn((rows, dims.dim), device=dev, generator=gen).to(torch.bfloat16),
+        "ao": torch.randn((rows, dims.dim), device=dev, generator=gen).to(torch.bfloat16),
+        "ffi": torch.randn((rows, dims.ffn), device=dev, generator=gen).to(torch.bfloat16),
+        "temb": torch.randn((n_img, dims.adaln), device=dev, generator=gen).to(torch.bfloat16),
+        "outs": alloc_outputs(dims, rows, dev),
+        "rng": np.random.default_rng(wseed + 11 + (rank if strong else 0)),
+    }
+    return st
+
+
+def _step_flops(cfg: dict, st: dict) -> tuple[float, float, float]:
+    from mingproj.dit import modulation_flops, projection_flops
+    base_f, lora_f = projection_flops(st["dims"], st["layout"], cfg["ranks"])
+    n = st["n_img"]
+    return n * base_f, n * lora_f, modulation_flops(st["dims"], n)
+
+
+def _draw(st: dict):
+    """This step's strength vectors (one per image), ~U(-1, 1.5)."""
+    return st["rng"].uniform(-1.0, 1.5, size=(st["n_img"], 8))
+
+
+def run_strong_batch(args, world: int, rank: int, dev, ctx) -> dict:
+    """Config 5 as a second measurement of the same run: the 8-image batch
+    split by image over the ranks, device time per step (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    cfg = CONFIGS[5]
+    st = _workload_state(cfg, world, rank, dev, ctx, seed_base=51)
+    base_f, lora_f, mod_f = _step_flops(cfg, st)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        st["pset"].forward_projections_batch(st["layout"], st["n_img"], _draw(st), st["nrm"],
+                                             st["ao"], st["ffi"], st["outs"], temb=st["temb"])
+    for _ in range(args.warmup):
+        step()
+    ctx.sync_check()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    ev[0].record(stream)
+    for _ in range(args.steps):
+        step()
+    ev[1].record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ctx.sync_check()
+    t = torch.tensor([ev[0].elapsed_time(ev[1])], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item()) / args.steps
+    ctx.clear_strengths_rows()
+    st["pset"].free()
+    total_f = world * (base_f + lora_f + mod_f)  # the whole batch's FLOPs per step
+    return {"workload": cfg["workload"], "scaling": "strong", "images_per_rank": st["n_img"],
+            "ms_per_step": ms, "value": total_f / (ms / 1e3) / 1e12, "unit": "TFLOP/s",
+            "flops_per_step": total_f, "steps": args.steps, "warmup": args.warmup}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=11,
+                    help="timed steps (forwards); 11 = one denoise schedule")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=3,
+                    help="headline workload (BASELINE config; default 3, the north-star target)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-config5", action="store_true",
+                    help="skip the embedded config-5 strong-scaling measurement")
     ap.add_argument("--shard", choices=["images", "rows"], default="images")
     ap.add_argument("--forward", action="store_true",
                     help="time the whole DiT forward (eager and CUDA graph) instead")
@@ -366,53 +497,43 @@ def main() -> None:
         run_rows(args)
         return
 
-    import numpy as np
     import torch
     import torch.distributed as dist
 
-    from mingproj.dit import (DitDims, DitProjectionSet, Layout, alloc_outputs,
-                              modulation_flops, projection_flops)
     from mingproj.proj import Context
 
+    cfg = CONFIGS[args.config]
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     peaks = load_peaks()
-
-    dims = DitDims()
-    layout = Layout(img=4096, cap=256)
     ctx = Context(local)
-    pset = DitProjectionSet.synthetic(ctx, dims, bits=8, seed=1 + rank, device=dev)
-    for i, r in enumerate(RANKS):
-        pset.bind_synthetic(i, r, seed=100 + 10 * rank + i, device=dev)
-    rng = np.random.default_rng(2 + rank)
-    for i, s in enumerate(rng.uniform(-1.0, 1.5, size=8)):
-        ctx.set_strength(i, float(s))
-
-    gen = torch.Generator(device=dev).manual_seed(3 + rank)
-    JT = layout.joint
-    nrm = torch.randn((JT, dims.dim), device=dev, generator=gen).to(torch.bfloat16)
-    ao = torch.randn((JT, dims.dim), device=dev, generator=gen).to(torch.bfloat16)
-    ffi = torch.randn((JT, dims.ffn), device=dev, generator=gen).to(torch.bfloat16)
-    temb = torch.randn((1, dims.adaln), device=dev, generator=gen).to(torch.bfloat16)
-    outs = alloc_outputs(dims, JT, dev)
+    st = _workload_state(cfg, world, rank, dev, ctx, seed_base=1)
+    dims, layout, pset = st["dims"], st["layout"], st["pset"]
+    n_img = st["n_img"]
+    base_f, lora_f, mod_f = _step_flops(cfg, st)
+    step_flops = base_f + lora_f + mod_f
     stream = torch.cuda.current_stream(dev)
 
-    base_f, lora_f = projection_flops(dims, layout, RANKS)
-    mod_f = modulation_flops(dims, 1)
-    step_flops = base_f + lora_f + mod_f
-
-    def step():
-        pset.forward_projections(layout, nrm, ao, ffi, outs, temb=temb)
+    def step(nrm, ao, ffi, outs, around=None, mod_ev=None):
+        s = _draw(st)  # strengths re-set before every forward
+        if mod_ev is not None:
+            mod_ev[0].record(stream)
+            pset.ctx.modulation(pset.modset, st["temb"])
+            mod_ev[1].record(stream)
+            pset.forward_projections_batch(layout, n_img, s, nrm, ao, ffi, outs, around=around)
+        else:
+            pset.forward_projections_batch(layout, n_img, s, nrm, ao, ffi, outs,
+                                           temb=st["temb"], around=around)
 
     for _ in range(args.warmup):
-        step()
+        step(st["nrm"], st["ao"], st["ffi"], st["outs"])
     ctx.sync_check()
 
     # ---- timed region: inputs resident in HBM --------------------------------
@@ -439,21 +560,14 @@ def main() -> None:
         torch.cuda.synchronize(dev)
         ev[0].record(stream)
         for i in range(args.steps):
-            mod_ev[i][0].record(stream)
-            ctx.modulation(pset.modset, temb)
-            mod_ev[i][1].record(stream)
-            for b in range(dims.n_blocks):
-                m = layout.rows(dims.block_kind(b))
-                pset.block_projections(b, nrm[:m], ao[:m], ffi[:m], outs, around=timed)
+            step(st["nrm"], st["ao"], st["ffi"], st["outs"], around=timed, mod_ev=mod_ev[i])
         ev[1].record(stream)
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
     ctx.sync_check()
     eng = ctx.engagement()
-    elapsed_ms = ev[0].elapsed_time(ev[1])
-    mod_ms = sum(a.elapsed_time(b) for a, b in mod_ev)
-    t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
+    t = torch.tensor([ev[0].elapsed_time(ev[1])], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     max_ms = float(t.item())
@@ -463,8 +577,9 @@ def main() -> None:
     # Roofline of the dominant kernel (proj_pair_kernel): the algorithmic FLOPs of
     # one projection call (base 2*M*N*K of its members + the live slots' LoRA
     # FLOPs) over that call's device time between its two events, averaged.
-    proj_launches = eng["kernels"] - eng["modulation"]
+    proj_launches = eng["kernels"] - args.steps * ((n_img + 3) // 4)  # minus modulation launches
     proj_ms = sum(a.elapsed_time(b) for a, b in call_ev)
+    mod_ms = sum(a.elapsed_time(b) for a, b in mod_ev)
     proj_flops = (base_f + lora_f) * args.steps
     achieved = proj_flops / (proj_ms / 1e3) / 1e12
     roofline = {
@@ -476,25 +591,31 @@ def main() -> None:
         "unit_of_work": "one projection call: q+k+v, to_out, w1+w3 or w2 of one block",
         "calls_per_step": n_calls / args.steps,
         "launches_per_step": proj_launches / args.steps,
-        "launches_of": "proj_pair_kernel (pre-GEMMs and fused projections) + lora_reduce_kernel",
+        "launches_of": "proj_pair_kernel (fused projections and any separate pre-GEMMs) + "
+                       "lora_reduce_kernel",
         "avg_call_us": proj_ms * 1e3 / n_calls,
         "flops_per_call": proj_flops / n_calls,
         "traffic": None,
-        "modulation": {"kernel": "mod_kernel", "bound": "hbm",
-                       "achieved_gbs": None,
-                       "us_per_launch": mod_ms * 1e3 / args.steps},
     }
-    # modulation: minimal bytes per launch = 32 packed adaLN weights + params
-    mod_bytes = dims.n_modulated * (4 * dims.dim * dims.adaln * 1.0 +
-                                    4 * dims.dim * (dims.adaln // 64) * 4.0 + 4 * dims.dim * 4.0)
-    roofline["modulation"]["achieved_gbs"] = mod_bytes / (mod_ms / args.steps / 1e3) / 1e9
-    roofline["modulation"]["peak_gbs"] = peaks["hbm_gbs"]
-    roofline["modulation"]["frac"] = roofline["modulation"]["achieved_gbs"] / peaks["hbm_gbs"]
+    # modulation: minimal bytes per step = 32 packed adaLN weights + group params
+    # + bias, and the gains read and written
+    H, K = dims.dim, dims.adaln
+    wb = K * cfg["bits"] / 8 + 4 * (K // 64) if cfg["bits"] else 2 * K
+    mod_bytes = dims.n_modulated * (4 * H * (wb + 2) + 2 * H * 2 * (1 + n_img) +
+                                    4 * H * 2 * n_img)
+    mod_us = mod_ms * 1e3 / args.steps
+    roofline["modulation"] = {
+        "kernel": "mod_rows_kernel", "bound": "hbm", "us_per_step": mod_us,
+        "bytes_per_step": mod_bytes, "achieved_gbs": mod_bytes / (mod_us * 1e-6) / 1e9,
+        "peak_gbs": peaks["hbm_gbs"],
+        "frac": mod_bytes / (mod_us * 1e-6) / 1e9 / peaks["hbm_gbs"]}
     traffic_file = ROOT / "profiles" / "traffic.json"
     if traffic_file.exists():
         try:
-            roofline["traffic"] = json.loads(traffic_file.read_text()).get("proj_kernel_bytes_per_launch")
-        except (ValueError, OSError):
+            tr = json.loads(traffic_file.read_text())
+            roofline["traffic"] = tr.get(f"config{args.config}", {}).get("bytes_per_launch")
+            roofline["traffic_of"] = tr.get(f"config{args.config}", {}).get("launch")
+        except (ValueError, OSError, AttributeError):
             pass
 
     # ---- e2e: through the public API with host buffers ------------------------
@@ -505,13 +626,14 @@ def main() -> None:
     # first input copy to the last result copy.
     e2e = None
     if not args.no_e2e:
+        nrm, ao, ffi, outs = st["nrm"], st["ao"], st["ffi"], st["outs"]
         h_in = [(nrm.cpu().pin_memory(), ao.cpu().pin_memory(), ffi.cpu().pin_memory())
                 for _ in range(2)]
         d_in = [(nrm, ao, ffi), (torch.empty_like(nrm), torch.empty_like(ao), torch.empty_like(ffi))]
         d_out = [outs, {k: torch.empty_like(v) for k, v in outs.items()}]
         h_out = [{k: torch.empty_like(v, device="cpu").pin_memory() for k, v in outs.items()}
                  for _ in range(2)]
-        h2d = sum(t.numel() for t in h_in[0]) * 2
+        h2d = sum(t_.numel() for t_ in h_in[0]) * 2
         d2h = sum(v.numel() for v in outs.values()) * 2
         h2d_s = torch.cuda.Stream(dev)
         d2h_s = torch.cuda.Stream(dev)
@@ -537,7 +659,7 @@ def main() -> None:
                 if i >= 2:
                     stream.wait_event(ev_read[i % 2])  # step i - 2's results are read out
                 x_n, x_a, x_f = d_in[i % 2]
-                pset.forward_projections(layout, x_n, x_a, x_f, d_out[i % 2], temb=temb)
+                step(x_n, x_a, x_f, d_out[i % 2])
                 ev_done[i % 2].record(stream)
                 with torch.cuda.stream(d2h_s):
                     d2h_s.wait_event(ev_done[i % 2])
@@ -558,6 +680,7 @@ def main() -> None:
         run_e2e(args.steps)
         ev[1].record(stream)
         torch.cuda.synchronize(dev)
+        ctx.sync_check()
         e_ms = torch.tensor([ev[0].elapsed_time(ev[1])], device=dev, dtype=torch.float64)
         if world > 1:
             dist.barrier()
@@ -568,33 +691,49 @@ def main() -> None:
                "what": "C-ABI calls with pinned-host inputs copied in and every projection "
                        "output of the last block copied out each step; copies on their own "
                        "streams, double-buffered, overlapping the neighbouring steps' compute"}
+        del h_in, d_in, d_out, h_out
+    ctx.clear_strengths_rows()
+    pset.free()
+    del st
+    torch.cuda.empty_cache()
+
+    strong = None
+    if args.config != 5 and not args.no_config5:
+        strong = run_strong_batch(args, world, rank, dev, ctx)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline()
+        cpu = cpu_baseline(cfg)
 
     if world > 1:
         dist.barrier()
     if rank == 0:
+        par = (f"image-sharded x{world}: {n_img} of the batch's {cfg['images']} images per rank, "
+               "all in one launch per projection (no data-path collective)"
+               if cfg["images"] > 1 else
+               f"image-sharded x{world}: one image per rank (no data-path collective)")
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": max_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": max_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if cfg["images"] > 1 else "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD,
-                       "l2": "inputs larger than L2: each step streams 6.2 GB of packed weights",
-                       "flops_per_step": step_flops, "lora_flops_per_step": lora_f,
-                       "parallelism": f"image-sharded x{world} (no data-path collective)"},
+            "config": {"workload": cfg["workload"],
+                       "l2": "inputs larger than L2: each step streams every block's packed "
+                             "weights (w4 3.4 GB / w8 6.4 GB per forward)",
+                       "flops_per_step": world * step_flops,
+                       "lora_flops_per_step": world * lora_f,
+                       "parallelism": par},
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": int(eng["kernels"]),
             "clocks": clocks,
-            "engagement": {k: eng[k] for k in ("linear_calls", "lora_proj", "gemm_w8",
+            "engagement": {k: eng[k] for k in ("linear_calls", "lora_proj", "gemm_w8", "gemm_w4",
                                                "lora_down", "modulation", "kernels")},
+            "config5_batch": strong,
         }
         print(json.dumps(line), flush=True)
-    pset.free()
     ctx.close()
     if world > 1:
         dist.destroy_process_group()

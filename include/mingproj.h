@@ -251,7 +251,8 @@ int mp_modulation_free(mp_ctx* ctx, mp_modset* set);
 /* mods[b, i, :] = W_b · temb[i] + bias_b (bf16 [n_blocks, m, 4H]);
  * nw1[b, i, :] = an1_b · (1 + mods[b, i, 0:H]), nw3[b, i, :] = fn1_b ·
  * (1 + mods[b, i, 2H:3H]) (bf16 [n_blocks, m, H]; either may be NULL).
- * temb: device bf16 [m, K_ada], m <= 4. Replaces: fill_mod
+ * temb: device bf16 [m, K_ada], m <= 16 (one token per image of a batch;
+ * a token's rows are the same bits whatever m is). Replaces: fill_mod
  * (src/ming-dit.cc:2266-2273) for every modulated block at once. */
 int mp_modulation_all(mp_ctx* ctx, const mp_modset* set, const void* temb, int m, void* mods,
                       void* nw1, void* nw3, void* stream);

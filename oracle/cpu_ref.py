@@ -76,12 +76,13 @@ def block_flops(m: int, H: int, FF: int, ranks) -> float:
 
 def time_block(rows: int, H: int = 3840, FF: int = 10240, bits: int = 8,
                ranks=(4, 8, 8, 16, 16, 32, 32, 64), reps: int = 1, seed: int = 0,
-               threads: int | None = None) -> dict:
+               threads: int | None = None, block: CpuBlock | None = None) -> dict:
     """Times `reps` runs of one block's projections at `rows` rows on all host
-    threads; returns TFLOP/s and what the sample was."""
+    threads (weights made once per call unless `block` is given); returns
+    TFLOP/s and what the sample was."""
     threads = threads or os.cpu_count() or 1
     torch.set_num_threads(threads)
-    blk = CpuBlock(H, FF, bits, ranks, seed)
+    blk = block if block is not None else CpuBlock(H, FF, bits, ranks, seed)
     g = torch.Generator().manual_seed(seed + 1)
     x_h = torch.randn((rows, H), generator=g)
     x_ff = torch.randn((rows, FF), generator=g)

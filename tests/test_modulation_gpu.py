@@ -51,3 +51,37 @@ def test_modulation_matches_oracle(ctx, bits, m, H, K):
         want1 = O.bf16_to_f64(an1[b])[None, :] * (1.0 + mb[:, :H])
         want3 = O.bf16_to_f64(fn1[b])[None, :] * (1.0 + mb[:, 2 * H:3 * H])
         assert O.rel_l2(nw1[b], want1) <= 4e-3 and O.rel_l2(nw3[b], want3) <= 4e-3
+
+
+@pytest.mark.parametrize("bits", [8, 4, 0])
+@pytest.mark.parametrize("H,K", [(256, 256), (256, 3840)])
+def test_modulation_rows_independent_of_batch(ctx, bits, H, K):
+    """A token's modulation row has the same bits whether it is computed alone
+    (M = 1, one image) or inside a batch (M = 2 or 4 in one launch, M = 8 in
+    two): the batched DiT forward relies on it for image i to equal its own
+    forward."""
+    rng = np.random.default_rng(7 + bits + K)
+    nb = 2
+    ws, biases, an1, fn1 = [], [], [], []
+    for _ in range(nb):
+        pw = (P.synthetic_affine(rng, 4 * H, K, bits) if bits else
+              P.synthetic_dense(rng, 4 * H, K, std=0.05))
+        ws.append(ctx.upload(pw.n, pw.k, pw.bits, pw.data, pw.scales, pw.biases))
+        biases.append(P.f32_to_bf16_bits(rng.normal(0, 0.02, 4 * H).astype(np.float32)))
+        an1.append(P.f32_to_bf16_bits((1 + 0.1 * rng.normal(size=H)).astype(np.float32)))
+        fn1.append(P.f32_to_bf16_bits((1 + 0.1 * rng.normal(size=H)).astype(np.float32)))
+    mset = ctx.modulation_set(ws, biases, an1, fn1)
+    temb = _dev(P.f32_to_bf16_bits(rng.normal(size=(8, K)).astype(np.float32)))
+    try:
+        batched = {mm: ctx.modulation(mset, temb[:mm]) for mm in (2, 4, 8)}
+        single = [ctx.modulation(mset, temb[i:i + 1]) for i in range(8)]
+        ctx.sync_check()
+        for mm, outs in batched.items():
+            for i in range(mm):
+                for got, want in zip(outs, single[i]):
+                    assert torch.equal(got[:, i].view(torch.int16), want[:, 0].view(torch.int16)), \
+                        f"M={mm} row {i} differs from its M=1 launch"
+    finally:
+        mset.free()
+        for w in ws:
+            w.free()

@@ -450,6 +450,10 @@ int begin_launch(mp_ctx* c, ProjParams* p, const void* x, int64_t ldx, int k, in
   p->M = m;
   p->K = k;
   p->n_tok = n_tok > 0 ? n_tok : mp::pick_ntok_pair(m, pairs);
+  // x larger than about a third of L2 is swept once per group of 16 feature
+  // pairs instead of once per round of resident pairs
+  const double x_bytes = 2.0 * m * static_cast<double>(k);
+  p->tile_group = x_bytes > 48.0 * 1024 * 1024 ? std::min(16, pairs) : 1;
   if (!encode_2d(&p->tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, k, m,
                  static_cast<uint64_t>(ldx) * 2, 64, static_cast<uint32_t>(sub_tok(p->n_tok) / 2),
                  CU_TENSOR_MAP_SWIZZLE_128B))
@@ -1503,8 +1507,8 @@ int mp_modulation_free(mp_ctx* c, mp_modset* set) {
 int mp_modulation_all(mp_ctx* c, const mp_modset* set, const void* temb, int m, void* mods,
                       void* nw1, void* nw3, void* stream) {
   if (c == nullptr || set == nullptr || temb == nullptr || mods == nullptr) return MP_EINVAL;
-  if (m <= 0 || m > mp::kModMaxTok)
-    return fail(c, MP_EINVAL, "modulation m %d outside [1, %d]", m, mp::kModMaxTok);
+  if (m <= 0 || m > mp::kModMaxBatch)
+    return fail(c, MP_EINVAL, "modulation m %d outside [1, %d]", m, mp::kModMaxBatch);
   int rc = use_device(c);
   if (rc != MP_OK) return rc;
   mp::ModParams p;
@@ -1519,15 +1523,20 @@ int mp_modulation_all(mp_ctx* c, const mp_modset* set, const void* temb, int m, 
   p.code_xor = sym ? 0x80808080u : 0u;
   p.code_magic = sym ? 8388736.0f : 8388608.0f;
   p.sb_stride = set->sb_stride;
-  p.M = m;
-  p.temb = static_cast<const uint16_t*>(temb);
-  p.mods = static_cast<uint16_t*>(mods);
-  p.nw1 = static_cast<uint16_t*>(nw1);
-  p.nw3 = static_cast<uint16_t*>(nw3);
-  cudaError_t e = mp::launch_mod(p, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return cuda_fail(c, e, "mod_kernel");
+  p.m_stride = m;
+  // launches of at most kModMaxTok tokens; every token's row is computed the
+  // same way whichever launch holds it
+  for (int m0 = 0; m0 < m; m0 += mp::kModMaxTok) {
+    p.M = std::min(mp::kModMaxTok, m - m0);
+    p.temb = static_cast<const uint16_t*>(temb) + static_cast<size_t>(m0) * set->k;
+    p.mods = static_cast<uint16_t*>(mods) + static_cast<size_t>(m0) * set->n;
+    p.nw1 = nw1 != nullptr ? static_cast<uint16_t*>(nw1) + static_cast<size_t>(m0) * p.H : nullptr;
+    p.nw3 = nw3 != nullptr ? static_cast<uint16_t*>(nw3) + static_cast<size_t>(m0) * p.H : nullptr;
+    cudaError_t e = mp::launch_mod(p, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(c, e, "mod_kernel");
+    c->eng.kernels += 1;
+  }
   c->eng.modulation += 1;
-  c->eng.kernels += 1;
   const double wbytes = set->bits == 0 ? 2.0 * set->n * set->k : set->n * set->k * set->bits / 8.0;
   c->eng.flops += 2.0 * m * set->n * static_cast<double>(set->k) * set->n_blocks;
   c->eng.bytes += set->n_blocks * (wbytes + (set->bits ? set->n * (set->k / 64) * 4.0 : 0.0) +

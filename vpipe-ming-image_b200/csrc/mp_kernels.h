@@ -90,6 +90,12 @@ struct ProjParams {
   int32_t n_pairs;    // feature pairs of the launch (all members)
   int32_t n_ttiles;   // token tiles: ceil(M / n_tok)
   int32_t n_tiles;    // n_pairs * n_ttiles * max(ksplit, 1): the persistent grid's work list
+  // Order of the work list within a K split: tile_group <= 1 walks token
+  // tiles fastest (feature pair after feature pair); tile_group = G > 1 takes
+  // the feature pairs in groups of G, and within a group the pair fastest,
+  // then the token tile, so the tiles running at one time share a few x
+  // tiles (each read from memory once per group) and G pairs' weights.
+  int32_t tile_group;
   uint64_t wait_limit_ns;
   uint32_t* err;      // device error word
   EpilogueScale scale;  // rank-space pre-GEMM / prologue only
@@ -153,14 +159,16 @@ struct ModParams {
   uint32_t code_xor;
   float code_magic;
   int32_t sb_stride;
-  int32_t M;               // tokens (<= 4)
+  int32_t M;               // tokens of this launch (<= kModMaxTok)
+  int32_t m_stride;        // tokens per block in the output arrays (>= M)
   const uint16_t* temb;    // bf16 [M, K]
-  uint16_t* mods;          // bf16 [n_blocks, M, N]
-  uint16_t* nw1;           // bf16 [n_blocks, M, H] or null
-  uint16_t* nw3;           // bf16 [n_blocks, M, H] or null
+  uint16_t* mods;          // bf16 [n_blocks, m_stride, N] (token 0 of this launch)
+  uint16_t* nw1;           // bf16 [n_blocks, m_stride, H] or null
+  uint16_t* nw3;           // bf16 [n_blocks, m_stride, H] or null
 };
 
-constexpr int kModMaxTok = 4;
+constexpr int kModMaxTok = 4;      // tokens of one launch (registers scale with it)
+constexpr int kModMaxBatch = 16;   // tokens of one mp_modulation_all call (launches of <= 4)
 
 // The sandwich-norm residual step (mp_norm.cu), per token row r < M:
 //   s   = bf16(o * rsqrt(mean(o^2) + eps) * o_gain)          (o != null)

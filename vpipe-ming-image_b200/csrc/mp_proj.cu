@@ -214,11 +214,25 @@ __device__ __forceinline__ Tile decode_tile(const ProjParams& p, int tile, int r
   const int per_split = p.n_pairs * p.n_ttiles;
   t.z = tile / per_split;
   const int rem = tile - t.z * per_split;
-  // token tile fastest: the pairs running at one time share a few feature
-  // pairs' weight tiles (each read from memory once, then from L2 by the
-  // other token tiles) and sweep the whole of x, which stays in L2
-  const int pair = rem / p.n_ttiles;
-  const int tt = rem - pair * p.n_ttiles;
+  int pair, tt;
+  if (p.tile_group <= 1) {
+    // token tile fastest: the pairs running at one time share a few feature
+    // pairs' weight tiles (each read from memory once, then from L2 by the
+    // other token tiles) and sweep the whole of x, which stays in L2 when it
+    // fits there
+    pair = rem / p.n_ttiles;
+    tt = rem - pair * p.n_ttiles;
+  } else {
+    // groups of tile_group feature pairs, pair fastest within a group: an x
+    // tile is read by every pair of the group at about the same time (once
+    // from memory when x does not fit in L2), the group's weights stay in L2
+    const int per_group = p.tile_group * p.n_ttiles;
+    const int g = rem / per_group;
+    const int within = rem - g * per_group;
+    const int gp = min(p.tile_group, p.n_pairs - g * p.tile_group);
+    tt = within / gp;
+    pair = g * p.tile_group + (within - tt * gp);
+  }
   int mi = 0;
   while (mi + 1 < p.n_members && pair >= p.mem[mi + 1].pair_begin) ++mi;
   t.mi = mi;

@@ -276,6 +276,36 @@ class DitProjectionSet:
             self.block_projections(b, nrm[:m], attn_out[:m], ffn_in[:m], outs, stream)
         return mod
 
+    def forward_projections_batch(self, layout: Layout, n_images: int, strengths,
+                                  nrm: torch.Tensor, attn_out: torch.Tensor,
+                                  ffn_in: torch.Tensor, outs: dict[str, torch.Tensor],
+                                  temb: torch.Tensor | None = None, stream=None, around=None):
+        """Every block's projections for `n_images` images of the same layout,
+        each with its own strength vector over the shared slots (`strengths`
+        [n_images, 8]). A block's inputs hold the images one after another
+        (image i's rows of a block kind are rows [i R, (i + 1) R), R =
+        layout.rows(kind)); every projection runs ONCE over all images' rows
+        with per-image row segments, and the modulation takes one temb row per
+        image. A single image uses the per-slot strengths."""
+        s = np.asarray(strengths, dtype=np.float32).reshape(n_images, -1)
+        if n_images == 1:
+            self.ctx.clear_strengths_rows()
+            for i, v in enumerate(s[0]):
+                self.ctx.set_strength(i, float(v))
+        mod = None
+        if temb is not None and self.modset is not None:
+            mod = self.ctx.modulation(self.modset, temb, stream=stream)
+        kind_prev = None
+        for b in range(self.dims.n_blocks):
+            kind = self.dims.block_kind(b)
+            R = layout.rows(kind)
+            if n_images > 1 and kind != kind_prev:
+                self.ctx.set_strengths_rows(s, np.arange(n_images + 1, dtype=np.int32) * R)
+            kind_prev = kind
+            m = n_images * R
+            self.block_projections(b, nrm[:m], attn_out[:m], ffn_in[:m], outs, stream, around)
+        return mod
+
     def free(self) -> None:
         for blk in self.blocks:
             for w in blk.proj.values():
