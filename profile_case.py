@@ -1,27 +1,34 @@
 """One kernel of the path on synthetic inputs, for profiling and timing.
 
-    python -m mingproj.profile_case --m 4352 --n 10240 --k 3840 --bits 8 \
-        --ranks 4,8,8,16,16,32,32,64 --reps 20
-    python -m mingproj.profile_case --op attention --m 4352 --heads 30 --reps 20
-    python -m mingproj.profile_case --op rms_residual --m 4352 --k 3840 --reps 20
+    python profile_case.py --m 16896 --n 10240 --k 3840 --bits 4 \
+        --ranks 32,32,32,32,32,32,32,32 --reps 20
+    python profile_case.py --op attention --m 4352 --heads 30 --reps 20
+    python profile_case.py --op rms_residual --m 4352 --k 3840 --reps 20
+    python profile_case.py --op modulation --m 1 --bits 8 --reps 20
 
 Prints the CUDA-event time per call and the algorithmic rate: TFLOP/s for a
 projection (mp_linear: rank-space pre-GEMM + fused projection) or the
 attention (mp_attention over head-major q / k / v of m rows), GB/s for the
-gated sandwich-norm residual step (mp_rms_residual over m rows of width k).
-Holds only that call's tensors on the device, so it is a small case for
-`ncu`.
+gated sandwich-norm residual step (mp_rms_residual over m rows of width k)
+and for the batched modulation (mp_modulation_all over 32 blocks' adaLN
+weights [4 * 3840, k] for m tokens; every call is preceded by a write of a
+256 MB buffer, so the weights come from HBM, not L2). Holds only that call's
+tensors on the device, so it is a small case for `ncu`.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import sys
+from pathlib import Path
 
 import numpy as np
 import torch
 
-from .dit import _device_affine, _device_dense
-from .proj import Context
+sys.path.insert(0, str(Path(__file__).resolve().parent / "vpipe-ming-image_b200"))
+
+from mingproj.dit import _device_affine, _device_dense  # noqa: E402
+from mingproj.proj import Context  # noqa: E402
 
 
 def _timed(fn, reps: int, warmup: int, ctx) -> float:
@@ -59,9 +66,46 @@ def _rms_residual(a, ctx, dev, gen) -> None:
                       "gbs": nbytes / (us * 1e-6) / 1e9}))
 
 
+def _modulation(a, ctx, dev, gen) -> None:
+    H, K, nb = 3840, a.k if a.k != 3840 or a.op_k_set else 256, 32
+    ws, bias, an1, fn1 = [], [], [], []
+    for _ in range(nb):
+        if a.bits:
+            ws.append(ctx.upload(4 * H, K, a.bits, *_device_affine(gen, 4 * H, K, a.bits, dev)))
+        else:
+            ws.append(ctx.upload(4 * H, K, 0, _device_dense(gen, 4 * H, K, dev)))
+        bias.append((torch.randn(4 * H, device=dev, generator=gen) * 0.02).to(torch.bfloat16))
+        an1.append(torch.ones(H, device=dev, dtype=torch.bfloat16))
+        fn1.append(torch.ones(H, device=dev, dtype=torch.bfloat16))
+    mset = ctx.modulation_set(ws, bias, an1, fn1)
+    temb = torch.randn((a.m, K), device=dev, generator=gen).to(torch.bfloat16)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(a.warmup):
+        ctx.modulation(mset, temb)
+    ctx.sync_check()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(a.reps)]
+    for e0, e1 in ev:
+        flush.fill_(1)  # evicts the weights from L2
+        e0.record()
+        ctx.modulation(mset, temb)
+        e1.record()
+    torch.cuda.synchronize()
+    ctx.sync_check()
+    us = float(np.median([e0.elapsed_time(e1) * 1e3 for e0, e1 in ev]))
+    wb = (K * a.bits / 8 + 4 * (K // 64)) if a.bits else 2 * K
+    nbytes = nb * (4 * H * (wb + 2) + 2 * H * 2 * (1 + a.m) + 4 * H * 2 * a.m)
+    print(json.dumps({"op": "modulation", "blocks": nb, "k": K, "bits": a.bits, "m": a.m,
+                      "us_per_call": us, "bytes": nbytes, "gbs": nbytes / (us * 1e-6) / 1e9}))
+    mset.free()
+    for w in ws:
+        w.free()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", choices=["linear", "attention", "rms_residual"], default="linear")
+    ap.add_argument("--op", choices=["linear", "attention", "rms_residual", "modulation"],
+                    default="linear")
     ap.add_argument("--heads", type=int, default=30)
     ap.add_argument("--m", type=int, default=4352)
     ap.add_argument("--n", type=int, default=10240)
@@ -71,11 +115,13 @@ def main() -> None:
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args()
+    a.op_k_set = "--k" in sys.argv
     dev = torch.device("cuda", 0)
     ctx = Context(0)
     gen = torch.Generator(device=dev).manual_seed(0)
     if a.op != "linear":
-        (_attention if a.op == "attention" else _rms_residual)(a, ctx, dev, gen)
+        {"attention": _attention, "rms_residual": _rms_residual,
+         "modulation": _modulation}[a.op](a, ctx, dev, gen)
         ctx.close()
         return
     if a.bits == 0:

@@ -435,10 +435,30 @@ int fill_member(mp_ctx* c, ProjParams* p, int i, const CUtensorMap& tm_w, const 
   return MP_OK;
 }
 
+// Order of a launch's work list (ProjParams::tile_group) from the bytes it
+// streams: token tile fastest while x fits comfortably in L2 (each weight tile
+// is read once, x stays resident); otherwise feature pair fastest, over the
+// whole launch when its weights fit in L2 (x streams exactly once) or in
+// groups of 16 pairs (x streams once per group, each group's weights stay
+// resident).
+int tile_group_for(double x_bytes, double w_bytes, int pairs) {
+#ifdef MP_FORCE_TILE_GROUP
+  (void)x_bytes;
+  (void)w_bytes;
+  return MP_FORCE_TILE_GROUP > 0 ? std::min(MP_FORCE_TILE_GROUP, pairs) : pairs;
+#else
+  constexpr double kResident = 48.0 * 1024 * 1024;
+  if (x_bytes <= kResident) return 1;
+  if (w_bytes <= kResident) return pairs;
+  return std::min(16, pairs);
+#endif
+}
+
 // Sets the launch-wide fields for `count` members whose output widths are
-// `ns`, choosing the token tile from the total pair count.
+// `ns`, choosing the token tile from the total pair count; `w_bytes` are the
+// bytes of the members' weights (codes or bf16) the launch streams.
 int begin_launch(mp_ctx* c, ProjParams* p, const void* x, int64_t ldx, int k, int m,
-                 const int* ns, int count, int n_tok = 0) {
+                 const int* ns, int count, double w_bytes, int n_tok = 0) {
   base_params(c, p);
   int pairs = 0;
   for (int i = 0; i < count; ++i) {
@@ -450,10 +470,7 @@ int begin_launch(mp_ctx* c, ProjParams* p, const void* x, int64_t ldx, int k, in
   p->M = m;
   p->K = k;
   p->n_tok = n_tok > 0 ? n_tok : mp::pick_ntok_pair(m, pairs);
-  // x larger than about a third of L2 is swept once per group of 16 feature
-  // pairs instead of once per round of resident pairs
-  const double x_bytes = 2.0 * m * static_cast<double>(k);
-  p->tile_group = x_bytes > 48.0 * 1024 * 1024 ? std::min(16, pairs) : 1;
+  p->tile_group = tile_group_for(2.0 * m * static_cast<double>(k), w_bytes, pairs);
   if (!encode_2d(&p->tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, k, m,
                  static_cast<uint64_t>(ldx) * 2, 64, static_cast<uint32_t>(sub_tok(p->n_tok) / 2),
                  CU_TENSOR_MAP_SWIZZLE_128B))
@@ -542,7 +559,7 @@ int launch_lora_down(mp_ctx* c, const CUtensorMap& tm_a, int rtot, const mp::Epi
   const mp::SplitChoice sc = mp::choose_ksplit(m, pairs_of(rtot), base_kt, rtot);
   const int ks = sc.ksplit;
   ProjParams p;
-  int rc = begin_launch(c, &p, x, ldx, k, m, &rtot, 1, sc.n_tok);
+  int rc = begin_launch(c, &p, x, ldx, k, m, &rtot, 1, 2.0 * rtot * k, sc.n_tok);
   if (rc != MP_OK) return rc;
   p.scale = es;
   rc = fill_member(c, &p, 0, tm_a, nullptr, 0, rtot, 0, 0, c->scratch, rtot, LoraTiles{});
@@ -627,7 +644,9 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
     for (int i = 0; i < count; ++i) pairs += pairs_of(ns[i]);
     n_tok = std::max(mp::kMaxTok, mp::pick_ntok_pair(m, pairs));
   }
-  int rc = begin_launch(c, &p, x, ldx, ws[0]->d.k, m, ns, members, n_tok);
+  double w_bytes = 0.0;
+  for (int i = 0; i < count; ++i) w_bytes += static_cast<double>(ws[i]->w_bytes);
+  int rc = begin_launch(c, &p, x, ldx, ws[0]->d.k, m, ns, members, w_bytes, n_tok);
   if (rc != MP_OK) return rc;
   // prologue units are 512-token tiles: they share the member tiles' stage
   // layout and x map, so the member tiles must be 512-token tiles too
@@ -1637,7 +1656,7 @@ extern "C" int mp_linear_lora_static(mp_ctx* c, const mp_weight* w, const void* 
                  static_cast<uint64_t>(k) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(c, MP_ECUDA, "tensor map encode failed (static LoRA A)");
   ProjParams p;
-  rc = begin_launch(c, &p, x, ldx, k, m, &rpad, 1);
+  rc = begin_launch(c, &p, x, ldx, k, m, &rpad, 1, 2.0 * rpad * k);
   if (rc != MP_OK) return rc;
   p.scale.enabled = 1;
   p.scale.n_seg = 1;
@@ -1661,7 +1680,7 @@ extern "C" int mp_linear_lora_static(mp_ctx* c, const mp_weight* w, const void* 
                  static_cast<uint64_t>(rank) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(c, MP_ECUDA, "tensor map encode failed (static LoRA B)");
   ProjParams q;
-  rc = begin_launch(c, &q, x, ldx, k, m, &n, 1);
+  rc = begin_launch(c, &q, x, ldx, k, m, &n, 1, static_cast<double>(w->w_bytes));
   if (rc != MP_OK) return rc;
   LoraTiles lt;
   lt.rpad = rpad;
