@@ -316,7 +316,12 @@ int mp_pack_quantize(const char* src, const char* dst, int bits, int* n_quantize
  *   the slots bound to `w` with mp_lora_bind are NOT applied here;
  *   strength 0 runs the base projection alone.
  * The first call on a device looks up the array's device address (once per
- * device); make that first call before any stream capture. Every call shares
+ * device, kept for the process); make that first call before any stream
+ * capture. The kept address does not survive cudaDeviceReset: do not call
+ * this entry point again in a process that reset the device. The rank-space
+ * pre-GEMM runs unsplit (a K split needs fp32 partial sums in memory this
+ * entry point does not allocate), so at few rows and a long K (to_out or w2
+ * over caption rows) it is slower than mp_linear's. Every call shares
  * the one array and it keeps the last call's contents: calls whose kernels
  * overlap on the GPU (other streams, other contexts on the same device) race
  * on it — order them on one stream. */

@@ -170,6 +170,29 @@ def projection(x_bf16, data, scales, biases, n, k, bits, symmetric=False, slots=
     return y
 
 
+def projection_two_rounding(x_bf16, data, scales, biases, n, k, bits, symmetric=False,
+                            slots=(), round_t: bool = False) -> np.ndarray:
+    """The reference's ORDER of the LoRA addition (src/ming-dit.cc:1763-1771):
+    `lin_base` writes the base output y, rounded to bf16, then
+    `lora::Applier::apply` adds every live slot's s * B (A x) onto it and the
+    sum is rounded to bf16 again (the fused kernel rounds once). With
+    `round_t` the rank-space intermediate s * (A x) is rounded to bf16 too
+    (the applier's intermediate dtype is not pinned by the reference tree).
+    fp64 arithmetic between the roundings; returns the bf16 values as fp64."""
+    x = bf16_to_f64(np.asarray(x_bf16, dtype=np.uint16))
+    w = dequant_np(data, scales, biases, n, k, bits, symmetric)
+    y = bf16_to_f64(f32_to_bf16((x @ w.T).astype(np.float32)))
+    delta = np.zeros_like(y)
+    for a, b, s in slots:
+        if s == 0.0:
+            continue
+        t = (x @ bf16_to_f64(a).T) * s
+        if round_t:
+            t = bf16_to_f64(f32_to_bf16(t.astype(np.float32)))
+        delta = delta + t @ bf16_to_f64(b).T
+    return bf16_to_f64(f32_to_bf16((y + delta).astype(np.float32)))
+
+
 def modulation(temb_bf16, data, scales, biases, bias, n, k, bits, symmetric=False) -> np.ndarray:
     t = np.ascontiguousarray(temb_bf16, dtype=np.uint16)
     m = t.shape[0]

@@ -28,7 +28,9 @@ def find(root: Path, rel: str, pattern: str) -> tuple[int, re.Match]:
 
 
 def main() -> None:
-    root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: make_reference_pins.py <reference root>")
+    root = Path(sys.argv[1])
     pins = {}
 
     # quantized block matrices of a pack: CHECK(quant == 32 * 8 + 2 * 7)

@@ -47,6 +47,34 @@ def test_attention_matches_fp32(ctx, nh, s, std):
     assert torch.equal(o.view(torch.int16), o2.view(torch.int16)), "not bit-identical run to run"
 
 
+def _ref_rows(q, k, v, scale, rows):
+    """fp32 reference for the query rows `rows` only (every key), head by head."""
+    outs = []
+    for h in range(q.shape[0]):
+        lg = (q[h, rows].float() @ k[h].float().T) * scale
+        outs.append(torch.softmax(lg, dim=-1) @ v[h].float())
+    return torch.stack(outs, 0).transpose(0, 1).reshape(len(rows), -1)
+
+
+@pytest.mark.parametrize("nh,s", [(30, 16896), (30, 8448), (8, 16384), (4, 357), (4, 390)])
+def test_attention_long_and_caption_lengths(ctx, nh, s):
+    """The config-3 joint length (16384 image + 512 caption rows), the
+    noise-refiner length at 2048^2, half the joint length, and caption-like
+    256 + N lengths whose last key tile is ragged; the fp32 reference is
+    taken on a sample of query rows (first, last, the ragged tail and random
+    rows) against all keys."""
+    q, k, v = _inputs(nh, s, 1.0, 7 * nh + s)
+    scale = 1.0 / math.sqrt(128)
+    o = ctx.attention(q, k, v)
+    ctx.sync_check()
+    g = torch.Generator().manual_seed(s)
+    rows = sorted(set([0, 1, s - 1] + list(range(max(0, s - 130), s, 7)) +
+                      torch.randint(0, s, (min(s, 384),), generator=g).tolist()))
+    ref = _ref_rows(q, k, v, scale, torch.tensor(rows, device="cuda"))
+    err = O.rel_l2(o[rows].float().cpu().numpy(), ref.cpu().numpy())
+    assert err <= TOL, f"rel-L2 {err:.2e}"
+
+
 def test_attention_rising_maximum(ctx):
     """Keys ordered so each 128-key tile holds larger logits than the last:
     every tile raises the running maximum and rescales the partial output."""

@@ -55,25 +55,31 @@ def dense(ctx):
     fwd.free()
 
 
+N_PROJ = 7 * (2 * fx.NREF + fx.NLAY)  # projection modules of the small DiT (28)
+
+
 @pytest.mark.parametrize("case", sorted(fx.CASES))
 def test_forward_matches_fp32(ctx, dense, case):
     fwd, w = dense
+    fwd._cap_cache.clear()
     ctx.reset_engagement()
     y = _gpu(fwd, case).float().cpu().numpy()
     ctx.sync_check()
     e = ctx.engagement()
+    # engagement first (tests/ming-dit-test.cc:638-676): every projection of
+    # every block ran through the kernels once, dense, no adapter engaged, and
+    # all modulated blocks in one modulation call -- only then accuracy
+    assert e["linear_calls"] == N_PROJ and e["gemm_dense"] == N_PROJ
+    assert e["lora_proj"] == 0 and e["lora_down"] == 0 and e["modulation"] == 1
     ref = _ref(fx.as_f32(w), case)
     err = O.rel_l2(y, ref)
-    # every projection of every block ran through the kernels, once
-    assert e["linear_calls"] == 7 * (2 * fx.NREF + fx.NLAY) and e["modulation"] == 1
     assert err <= BAR, f"{case}: rel-L2 {err:.4f} > {BAR}"
 
 
-def test_pack_forward(ctx):
-    """w8 pack: every block matrix whose width the group divides is packed
-    (w2's K = 2730 stays dense, as the reference's selection rule does); the
-    oracle runs the same dequantized weights in fp32."""
-    w = fx.make_weights(0)
+def _packed(w: dict, bits: int = 8):
+    """Every block matrix whose width the group divides, quantized (w2's K =
+    2730 stays dense, as the reference's selection rule does), and the same
+    weights dequantized for the fp32 oracle."""
     packed, deq = dict(w), fx.as_f32(w)
     for k, v in w.items():
         base = k[:-len(".weight")] if k.endswith(".weight") else None
@@ -81,9 +87,17 @@ def test_pack_forward(ctx):
             continue
         if v.shape[1] % 64:
             continue
-        pw = P.quantize_affine(P.bf16_bits_to_f32(v), 8)
+        pw = P.quantize_affine(P.bf16_bits_to_f32(v), bits)
         packed[k] = pw
-        deq[k] = O.dequant(pw.data, pw.scales, pw.biases, pw.n, pw.k, 8).astype(np.float32)
+        deq[k] = O.dequant(pw.data, pw.scales, pw.biases, pw.n, pw.k, bits).astype(np.float32)
+    return packed, deq
+
+
+def test_pack_forward(ctx):
+    """w8 pack (see _packed); the oracle runs the same dequantized weights in
+    fp32."""
+    w = fx.make_weights(0)
+    packed, deq = _packed(w)
     fwd = DitForward(ctx, CFG, packed, torch.device("cuda", 0))
     ctx.reset_engagement()
     y = _gpu(fwd, "case_a").float().cpu().numpy()
@@ -285,3 +299,105 @@ def test_graph_replay_matches_eager(ctx, dense):
     ctx.set_strength(2, 1.0)
     runner.release()
     ctx.sync_check()
+
+
+def test_lora_pack_moves_like_bf16(ctx, dense):
+    """The same adapter on a w8 pack of the same model moves the pack's
+    output as it moves the bf16 model's: the reference's test_lora_pack
+    (tests/ming-dit-test.cc:2056-2102), restated on the synthetic small DiT.
+    Engagement is checked first: packed GEMMs ran and every projection took
+    the adapter; strength 0 gives the pack's base bits."""
+    fwd_bf, w = dense
+    binding, _ = _adapter(seed=21)
+    fwd_bf._cap_cache.clear()
+    bf_base = _gpu(fwd_bf, "case_b").float().cpu().numpy()
+    assert fwd_bf.proj.bind_slot(0, binding) == N_PROJ
+    ctx.set_strength(0, 1.0)
+    bf_lora = _gpu(fwd_bf, "case_b").float().cpu().numpy()
+    fwd_bf.proj.unbind_slot(0)
+
+    packed, _ = _packed(w)
+    fwd = DitForward(ctx, CFG, packed, torch.device("cuda", 0))
+    try:
+        base = _gpu(fwd, "case_b")
+        assert fwd.proj.bind_slot(0, binding) == N_PROJ
+        ctx.reset_engagement()
+        r = _gpu(fwd, "case_b")
+        ctx.sync_check()
+        e = ctx.engagement()
+        assert e["gemm_w8"] > 0 and e["lora_proj"] == N_PROJ
+        ctx.set_strength(0, 0.0)
+        z = _gpu(fwd, "case_b")
+        ctx.set_strength(0, 1.0)
+    finally:
+        fwd.free()
+    rn, bn = r.float().cpu().numpy(), base.float().cpu().numpy()
+    moved = O.rel_l2(rn, bn)
+    bf_moved = O.rel_l2(bf_lora, bf_base)
+    d_base = O.rel_l2(bn, bf_base)
+    d_lora = O.rel_l2(rn, bf_lora)
+    assert 0.5 * bf_moved < moved < 2.0 * bf_moved, (moved, bf_moved)
+    assert d_lora < 1.5 * d_base + 0.01, (d_lora, d_base)
+    assert torch.equal(z.view(torch.int16), base.view(torch.int16)), "strength 0 != pack base"
+
+
+def test_config_keys_drive_the_slots(ctx, tmp_path):
+    """The caller-side keys (mingproj.lora_config) on a real forward, as the
+    reference's generator test drives them (tests/ming-lora-test.cc:268-337):
+    `lora2` alone binds slot 1 at `lora2_scale`; its strength is live per
+    request (0 gives the base bits, back to 0.5 gives the adapted bits
+    again); a later beat naming another `lora2` path is ignored and said."""
+    from mingproj import lora as L
+    from mingproj import lora_config as LC
+
+    rng = np.random.default_rng(3)
+    t = {}
+    for pre in fx.block_prefixes():
+        for name in P.PROJ_NAMES:
+            out, inp = ((fx.FFN, fx.DIM) if name in ("feed_forward.w1", "feed_forward.w3") else
+                        (fx.DIM, fx.FFN) if name == "feed_forward.w2" else (fx.DIM, fx.DIM))
+            t[f"transformer.{pre}{name}.lora_A.weight"] = P.f32_to_bf16_bits(
+                rng.normal(0, 1 / np.sqrt(inp), size=(8, inp)).astype(np.float32))
+            t[f"transformer.{pre}{name}.lora_B.weight"] = P.f32_to_bf16_bits(
+                rng.normal(0, 0.2, size=(out, 8)).astype(np.float32))
+    adir = tmp_path / "style"
+    adir.mkdir()
+    L.write_safetensors(adir / "style.safetensors", t)
+
+    def resolve(ref):  # a directory holding one .safetensors, or a file
+        pth = Path(ref)
+        if pth.is_dir():
+            files = sorted(pth.glob("*.safetensors"))
+            return str(files[0]) if len(files) == 1 else None
+        return str(pth) if pth.is_file() else None
+
+    fwd = DitForward(ctx, CFG, fx.make_weights(0), torch.device("cuda", 0))
+    try:
+        base = _gpu(fwd, "case_a")
+        cfg = {"lora2": str(adir), "lora2_scale": 0.5}
+        st = LC.bind_from_config(fwd.proj, LC.forwarded_config(cfg), resolve, fx.DIM, fx.FFN)
+        assert fwd.proj.lora_modules(1) == N_PROJ and fwd.proj.lora_modules(0) == 0
+        assert f"runtime LoRA modules bound: lora2 {N_PROJ}" in st.infos
+        assert ctx.strength(1) == 0.5 and ctx.strength(0) == 1.0
+        ctx.reset_engagement()
+        h = _gpu(fwd, "case_a")
+        assert ctx.engagement()["lora_proj"] == N_PROJ
+        v0 = ctx.state_version()
+        assert LC.apply_keys({"lora2_scale": 0.0}, st, ctx.set_strength) == 1
+        assert ctx.state_version() != v0
+        z = _gpu(fwd, "case_a")
+        assert LC.apply_keys({"lora2_scale": 0.5, "shift": 3.0}, st, ctx.set_strength) == 1
+        h2 = _gpu(fwd, "case_a")
+        assert LC.apply_keys({"lora2": "/nonexistent/x.safetensors", "lora2_scale": 0.5}, st,
+                             ctx.set_strength, fwd.proj.lora_modules) == 0
+        h3 = _gpu(fwd, "case_a")
+        ctx.sync_check()
+    finally:
+        for i in range(8):
+            ctx.set_strength(i, 1.0)
+        fwd.free()
+    assert any("is IGNORED" in m for m in st.warnings)
+    assert O.rel_l2(h.float().cpu().numpy(), base.float().cpu().numpy()) > 0.005
+    assert torch.equal(z.view(torch.int16), base.view(torch.int16)), "lora2_scale 0 != base"
+    assert torch.equal(h2.view(torch.int16), h.view(torch.int16)), "back to 0.5 != first"
+    assert torch.equal(h3.view(torch.int16), h.view(torch.int16)), "ignored path changed it"

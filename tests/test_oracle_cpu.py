@@ -160,3 +160,33 @@ def test_bf16_rounding_matches_torch():
     ref = torch.from_numpy(f).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
     assert np.array_equal(mine, ref)
     assert np.array_equal(O.f32_to_bf16(f), ref)
+
+
+@pytest.mark.parametrize("round_t", [False, True])
+def test_two_rounding_order_within_the_bar(round_t):
+    """The reference adds the adapters onto a base output already rounded to
+    bf16 and rounds again (src/ming-dit.cc:1763-1771); this build rounds the
+    fused sum once. At config-2 magnitudes (w8 affine, codes U{0..255},
+    scales U(0.002, 0.02), bias -128 s; x ~N(0,1); eight slots of ranks
+    {4..64} with A ~N(0, 1/r), B ~N(0, 0.01), strengths ~U(-1, 1.5)) the two
+    orders agree well inside the per-projection bar of 5e-3, and both sit
+    within it of the exact fp64 value."""
+    rng = np.random.default_rng(17)
+    m, n, k = 48, 512, 3840
+    pw = P.synthetic_affine(rng, n, k, 8)
+    x = P.f32_to_bf16_bits(rng.normal(size=(m, k)).astype(np.float32))
+    slots = []
+    for r in (4, 8, 8, 16, 16, 32, 32, 64):
+        a, b = P.synthetic_lora(rng, n, k, r, b_std=0.01)
+        slots.append((a, b, float(rng.uniform(-1.0, 1.5))))
+    exact = O.projection_np(x, pw.data, pw.scales, pw.biases, n, k, 8, False, slots)
+    fused = O.bf16_to_f64(O.f32_to_bf16(exact.astype(np.float32)))
+    two = O.projection_two_rounding(x, pw.data, pw.scales, pw.biases, n, k, 8, False, slots,
+                                    round_t=round_t)
+    assert O.rel_l2(two, fused) <= 5e-3
+    assert O.rel_l2(two, exact) <= 5e-3 and O.rel_l2(fused, exact) <= 5e-3
+    # the adapters are not lost in the second rounding: they move the output
+    # past the reference's 0.01 floor and well beyond the rounding-order gap
+    base = O.projection_np(x, pw.data, pw.scales, pw.biases, n, k, 8, False, ())
+    moved = O.rel_l2(two, base)
+    assert moved > 0.01 and moved > 5 * O.rel_l2(two, fused)

@@ -381,3 +381,37 @@ def test_shared_stack_cache_follows_reuploaded_weights(ctx):
             assert err <= TOL, f"re-upload {rep}, weight {j}: rel-L2 {err:.3e}"
         for w in ws:
             w.free()
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_reference_rounding_order_within_the_bar(ctx, bits):
+    """The fused kernel rounds base + adapters once; the reference rounds the
+    base output to bf16 and the sum again (src/ming-dit.cc:1763-1771). At
+    config-2/3 magnitudes (4352-row text-plus-image shape cut to 640 rows,
+    K 3840, eight slots of ranks {4..64}, B ~N(0, 0.01), strengths
+    ~U(-1, 1.5)) the kernel's output sits within the per-projection bar of
+    the reference-order result, as it does of the exact fp64 value."""
+    rng = np.random.default_rng(31 + bits)
+    m, n, k = 640, 768, 3840
+    pw = P.synthetic_affine(rng, n, k, bits)
+    w = _upload(ctx, pw)
+    slots = []
+    for i, r in enumerate((4, 8, 8, 16, 16, 32, 32, 64)):
+        a, b = P.synthetic_lora(rng, n, k, r, b_std=0.01)
+        s = float(rng.uniform(-1.0, 1.5))
+        w.bind(i, a, b)
+        ctx.set_strength(i, s)
+        slots.append((a, b, s))
+    x = _x(rng, m, k)
+    try:
+        y = _host(ctx.linear(w, _to_dev(x)))
+        ctx.sync_check()
+    finally:
+        for i in range(8):
+            ctx.set_strength(i, 1.0)
+        w.free()
+    two = O.projection_two_rounding(x, pw.data, pw.scales, pw.biases, n, k, bits, False, slots,
+                                    round_t=True)
+    exact = O.projection(x, pw.data, pw.scales, pw.biases, n, k, bits, False, slots)
+    assert O.rel_l2(y, two) <= TOL, f"vs reference order {O.rel_l2(y, two):.3e}"
+    assert O.rel_l2(y, exact) <= TOL, f"vs exact {O.rel_l2(y, exact):.3e}"

@@ -66,3 +66,42 @@ def test_static_scratch_rejects_oversize():
         ctx.linear_lora_static(w, x, a, b, 1.0)
     w.free()
     ctx.close()
+
+
+def test_static_scratch_allocates_nothing_and_ignores_bound_slots():
+    """Device memory is unchanged across static calls (after a first call
+    that loads the kernels), strength 0 gives the bits of the plain base
+    projection, and a slot bound to the weight with mp_lora_bind is not
+    applied: the result still matches the single-adapter oracle."""
+    ctx = Context(0)
+    rng = np.random.default_rng(99)
+    m, n, k, rank = 260, 256, 384, 24
+    pw = P.synthetic_affine(rng, n, k, 4)
+    w = ctx.upload(n, k, 4, pw.data, pw.scales, pw.biases)
+    x = P.f32_to_bf16_bits(rng.normal(size=(m, k)).astype(np.float32))
+    a, b = P.synthetic_lora(rng, n, k, rank, b_std=0.05)
+    xd, ad, bd = _dev(x), _dev(a), _dev(b)
+    outs = [torch.empty((m, n), dtype=torch.bfloat16, device="cuda") for _ in range(3)]
+    base = ctx.linear(w, xd)  # no slot bound: the plain base projection
+    ctx.linear_lora_static(w, xd, ad, bd, 0.5, out=outs[0])  # loads the kernels
+    other_a, other_b = P.synthetic_lora(rng, n, k, 16, b_std=0.5)
+    w.bind(0, other_a, other_b)  # bound and live, but not this entry point's business
+    ctx.set_strength(0, 1.0)
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    ctx.linear_lora_static(w, xd, ad, bd, 0.0, out=outs[1])
+    ctx.linear_lora_static(w, xd, ad, bd, 0.5, out=outs[2])
+    ctx.sync_check()
+    free1 = torch.cuda.mem_get_info()[0]
+    ref = O.projection(x, pw.data, pw.scales, pw.biases, n, k, 4, False, [(a, b, 0.5)])
+    try:
+        assert free1 == free0, f"device memory moved by {free0 - free1} bytes"
+        assert torch.equal(outs[1].view(torch.int16), base.view(torch.int16)), \
+            "strength 0 != the base projection"
+        assert torch.equal(outs[2].view(torch.int16), outs[0].view(torch.int16)), \
+            "a bound slot changed the static result"
+        assert O.rel_l2(outs[2].float().cpu().numpy(), ref) <= TOL
+    finally:
+        w.unbind(0)
+        w.free()
+        ctx.close()

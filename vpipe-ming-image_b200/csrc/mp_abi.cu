@@ -524,14 +524,15 @@ struct SplitChoice {
 // the least modelled time. A 64-wide K stage takes ~890 cycles on a
 // 256-token tile and ~1250 on a 512-token tile, a CTA adds ~6000 cycles of
 // set-up and epilogue, 74 pairs run at once (one CTA per SM), and the second
-// pass of a split launch costs ~2 us plus its traffic at ~4 TB/s.
-SplitChoice choose_ksplit(int m, int pairs, int base_kt, int r) {
+// pass of a split launch costs ~2 us plus its traffic at ~4 TB/s. At most
+// `max_split` splits.
+SplitChoice choose_ksplit(int m, int pairs, int base_kt, int r, int max_split = kMaxSplits) {
   SplitChoice best{kMaxTok, 1, 0.0};
   double best_us = 1e300;
   for (int nt : {kMaxTileTok, kMaxTok}) {
     const double stage_cycles = nt > kMaxTok ? 1250.0 : 890.0;
     const long long tiles = (m + nt - 1) / nt;
-    for (int s = 1; s <= kMaxSplits && s <= base_kt; ++s) {
+    for (int s = 1; s <= max_split && s <= base_kt; ++s) {
       const int kps = (base_kt + s - 1) / s;
       if ((base_kt + kps - 1) / kps != s) continue;  // every split gets at least one tile
       const long long waves = (pairs * tiles * s + 73) / 74;
@@ -1597,17 +1598,21 @@ namespace {
 
 // Device address of g_static_rank_scratch, looked up once per device with that
 // device current (host code only has a host-side stand-in for the symbol).
-uint16_t* g_static_rank_scratch_dev[64] = {};
+// Atomic, so two host threads making their first call on the same device at
+// once both store the same value without a data race.
+std::atomic<uint16_t*> g_static_rank_scratch_dev[64] = {};
 
 int static_rank_scratch(mp_ctx* c, uint16_t** out) {
   if (c->device < 0 || c->device >= 64) return fail(c, MP_EINVAL, "device index out of range");
-  if (g_static_rank_scratch_dev[c->device] == nullptr) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_static_rank_scratch);
+  uint16_t* p = g_static_rank_scratch_dev[c->device].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    void* sym = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&sym, g_static_rank_scratch);
     if (e != cudaSuccess) return cuda_fail(c, e, "cudaGetSymbolAddress(g_static_rank_scratch)");
-    g_static_rank_scratch_dev[c->device] = static_cast<uint16_t*>(p);
+    p = static_cast<uint16_t*>(sym);
+    g_static_rank_scratch_dev[c->device].store(p, std::memory_order_release);
   }
-  *out = g_static_rank_scratch_dev[c->device];
+  *out = p;
   return MP_OK;
 }
 
@@ -1655,8 +1660,12 @@ extern "C" int mp_linear_lora_static(mp_ctx* c, const mp_weight* w, const void* 
   if (!encode_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a, k, rank,
                  static_cast<uint64_t>(k) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(c, MP_ECUDA, "tensor map encode failed (static LoRA A)");
+  // the token tile the separate pre-GEMM would take, without a K split (its
+  // fp32 partial sums would need memory this entry point does not allocate)
+  const mp::SplitChoice sc =
+      mp::choose_ksplit(m, pairs_of(rpad), (k + mp::kBlockK - 1) / mp::kBlockK, rpad, 1);
   ProjParams p;
-  rc = begin_launch(c, &p, x, ldx, k, m, &rpad, 1, 2.0 * rpad * k);
+  rc = begin_launch(c, &p, x, ldx, k, m, &rpad, 1, 2.0 * rpad * k, sc.n_tok);
   if (rc != MP_OK) return rc;
   p.scale.enabled = 1;
   p.scale.n_seg = 1;

@@ -366,6 +366,14 @@ class Context:
         device array (see mp_linear_lora_static). a: bf16 [rank, k], b: bf16
         [n, rank], both on the device; the slots bound to `w` are not applied."""
         m = x.shape[0]
+        rank = a.shape[0] if a.dim() == 2 else -1
+        for name, t, shape in (("a", a, (rank, w.k)), ("b", b, (w.n, rank))):
+            if t.dim() != 2 or tuple(t.shape) != shape:
+                raise ValueError(f"{name} must be [{shape[0]}, {shape[1]}], got {tuple(t.shape)}")
+            if t.dtype != torch.bfloat16:
+                raise ValueError(f"{name} must be bfloat16, got {t.dtype}")
+            if t.device != x.device:
+                raise ValueError(f"{name} is on {t.device}, x on {x.device}")
         if out is None:
             out = _alloc_out(m, w.n, x.device)
         a = a.contiguous()
