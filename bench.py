@@ -188,10 +188,11 @@ def run_reference(args) -> None:
 
 
 def run_rows(args) -> None:
-    """One image's rows sharded over the ranks (strong scaling): projections of
-    the local 128-row-aligned slice, K and V all-gathered per block on side
-    streams that overlap to_out, w1/w3 and w2; the timed region ends when every
-    gather has landed."""
+    """One image's rows sharded over the ranks (strong scaling; configs 2 and
+    3): every rank projects its equal, 32-row-aligned slice of every block,
+    and each block's K and V are all-gathered over NCCL on side streams that
+    overlap the block's to_out, w1/w3 and w2; the timed region ends when every
+    gather has landed. Reports the gathers' own device time per block."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -201,25 +202,27 @@ def run_rows(args) -> None:
     from mingproj.parallel import RowGather, row_shards
     from mingproj.proj import Context
 
+    if args.config == 5:
+        raise SystemExit("--shard rows splits one image's rows: use --config 2 or 3")
+    cfg = CONFIGS[args.config]
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     peaks = load_peaks()
     dims = DitDims()
-    layout = Layout(img=4096, cap=256)
+    layout = Layout(img=cfg["img"], cap=cfg["cap"])
     ctx = Context(local)
     # one model and one image shared by all ranks: same seeds everywhere
-    pset = DitProjectionSet.synthetic(ctx, dims, bits=8, seed=1, device=dev)
-    for i, r in enumerate(RANKS):
+    pset = DitProjectionSet.synthetic(ctx, dims, bits=cfg["bits"], seed=1, device=dev)
+    for i, r in enumerate(cfg["ranks"]):
         pset.bind_synthetic(i, r, seed=100 + i, device=dev)
-    for i, s_ in enumerate(np.random.default_rng(2).uniform(-1.0, 1.5, size=8)):
-        ctx.set_strength(i, float(s_))
+    rng = np.random.default_rng(2)
     gen = torch.Generator(device=dev).manual_seed(3)
     JT = layout.joint
     nrm = torch.randn((JT, dims.dim), device=dev, generator=gen).to(torch.bfloat16)
@@ -228,18 +231,27 @@ def run_rows(args) -> None:
     temb = torch.randn((1, dims.adaln), device=dev, generator=gen).to(torch.bfloat16)
     outs = alloc_outputs(dims, JT, dev)
     stream = torch.cuda.current_stream(dev)
-    base_f, lora_f = projection_flops(dims, layout, RANKS)
+    base_f, lora_f = projection_flops(dims, layout, cfg["ranks"])
     step_flops = base_f + lora_f + modulation_flops(dims, 1)
-    sizes = sorted({layout.rows(dims.block_kind(b)) for b in range(dims.n_blocks)})
-    gathers = {m: [[RowGather(m, dims.dim, world, rank, dev) for _ in range(2)] for _ in range(2)]
-               for m in sizes} if world > 1 else {}
+    # a K and a V gather per block, so every block's collective time is kept
+    gathers = ([(RowGather(layout.rows(dims.block_kind(b)), dims.dim, world, rank, dev),
+                 RowGather(layout.rows(dims.block_kind(b)), dims.dim, world, rank, dev))
+                for b in range(dims.n_blocks)] if world > 1 else None)
 
     def step():
+        for i, s_ in enumerate(rng.uniform(-1.0, 1.5, size=8)):  # re-set every forward
+            ctx.set_strength(i, float(s_))
         ctx.modulation(pset.modset, temb)
         for b in range(dims.n_blocks):
             m = layout.rows(dims.block_kind(b))
             sh = row_shards(m, world)[rank]
-            gk, gv = gathers[m][b % 2] if world > 1 else (None, None)
+            gk, gv = gathers[b] if gathers is not None else (None, None)
+            if gk is not None and b > 0:
+                # the previous block's gathers send its K and V rows as they
+                # lie: joined before this block's q/k/v overwrite them (they
+                # overlapped the previous block's to_out, w1/w3 and w2)
+                for g in gathers[b - 1]:
+                    g.wait()
 
             def around(i, call, rows=sh.rows, gk=gk, gv=gv):
                 if rows > 0:
@@ -249,11 +261,9 @@ def run_rows(args) -> None:
                     gv.start(outs["attention.to_v"][:rows])
             pset.block_projections(b, nrm[sh.start:sh.stop], ao[sh.start:sh.stop],
                                    ffi[sh.start:sh.stop], outs, around=around)
-        for pair in gathers.values():
-            for g2 in pair:
-                for g in g2:
-                    if g.pending:
-                        g.wait()
+        if gathers is not None:
+            for g in gathers[-1]:
+                g.wait()
 
     for _ in range(args.warmup):
         step()
@@ -274,8 +284,17 @@ def run_rows(args) -> None:
             dist.barrier()
     ctx.sync_check()
     t = torch.tensor([ev[0].elapsed_time(ev[1])], device=dev, dtype=torch.float64)
+    nccl = None
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        per_block = [sum(g.last_ms() or 0.0 for g in pair) for pair in gathers]
+        nt = torch.tensor([sum(per_block)], device=dev, dtype=torch.float64)
+        dist.all_reduce(nt, op=dist.ReduceOp.MAX)
+        nccl = {"ms_per_step": float(nt.item()), "ms_per_block_avg": float(nt.item()) / len(per_block),
+                "what": "device time of each block's K and V all-gathers on their own streams "
+                        "(last step, max over ranks); they overlap the block's remaining "
+                        "projections",
+                "bytes_received_per_block": 2 * layout.joint * dims.dim * 2 * (world - 1) / world}
     max_ms = float(t.item())
     value = step_flops * args.steps / (max_ms / 1e3) / 1e12
     if rank == 0:
@@ -284,16 +303,19 @@ def run_rows(args) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": CONFIGS[2]["workload"], "l2": "inputs larger than L2",
+            "config": {"workload": cfg["workload"], "l2": "inputs larger than L2",
                        "flops_per_step": step_flops,
-                       "parallelism": f"token-rows x{world} (128-row-aligned slices), NCCL "
+                       "parallelism": f"token-rows x{world} (equal 32-row-aligned slices), NCCL "
                                       "all-gather of each block's K and V overlapping the "
                                       "block's remaining projections"},
+            "nccl_gather": nccl,
             "roofline": None, "cpu_baseline": None, "e2e": None,
             "gpu_launches": ctx.engagement()["kernels"], "clocks": clk.summary(),
             "peaks": peaks.get("source"),
         }
         print(json.dumps(line), flush=True)
+    pset.free()
+    ctx.close()
     if world > 1:
         dist.destroy_process_group()
 

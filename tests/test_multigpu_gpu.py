@@ -1,5 +1,5 @@
 """Token-row sharding across GPUs (one process per GPU, NCCL): each rank
-projects its 128-row-aligned slice of the rows, the row all-gather on its own
+projects its slice of the rows (equal, 32-row aligned), the row all-gather on its own
 stream reassembles the full output on every rank, and that equals the
 single-GPU projection of all rows — bit for bit without adapters (rows are
 independent and every row's K loop runs in the same order), within the
