@@ -25,6 +25,7 @@ int resident_pairs();
 int pick_ntok_pair(int m, int pairs);
 cudaError_t launch_wait_selftest(uint64_t limit_ns, uint32_t* err, cudaStream_t stream);
 cudaError_t launch_mod(const ModParams& p, cudaStream_t stream);
+int mod_tokens_per_launch(int n, int k);
 cudaError_t launch_rms_residual(const RmsResidualParams& p, cudaStream_t stream);
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream);
 }  // namespace mp
@@ -1544,10 +1545,11 @@ int mp_modulation_all(mp_ctx* c, const mp_modset* set, const void* temb, int m, 
   p.code_magic = sym ? 8388736.0f : 8388608.0f;
   p.sb_stride = set->sb_stride;
   p.m_stride = m;
-  // launches of at most kModMaxTok tokens; every token's row is computed the
-  // same way whichever launch holds it
-  for (int m0 = 0; m0 < m; m0 += mp::kModMaxTok) {
-    p.M = std::min(mp::kModMaxTok, m - m0);
+  // launches of at most a few tokens (8 on the tensor-core path); every
+  // token's row is computed the same way whichever launch holds it
+  const int per_launch = mp::mod_tokens_per_launch(set->n, set->k);
+  for (int m0 = 0; m0 < m; m0 += per_launch) {
+    p.M = std::min(per_launch, m - m0);
     p.temb = static_cast<const uint16_t*>(temb) + static_cast<size_t>(m0) * set->k;
     p.mods = static_cast<uint16_t*>(mods) + static_cast<size_t>(m0) * set->n;
     p.nw1 = nw1 != nullptr ? static_cast<uint16_t*>(nw1) + static_cast<size_t>(m0) * p.H : nullptr;

@@ -1,4 +1,5 @@
-// Batched adaLN modulation for all modulated blocks in ONE launch.
+// Batched adaLN modulation for all modulated blocks in ONE launch (per <= 8
+// tokens).
 //
 // The reference runs `fill_mod` once per modulated block
 // (src/ming-dit.cc:2266-2273): a bare Linear `mods = W_ada · temb + b`
@@ -6,34 +7,33 @@
 // norm gains (nw1 = an1 · (1 + scale_msa), nw3 = fn1 · (1 + scale_mlp)).
 // Every block reads the SAME temb, so all of them are one weight-streaming
 // pass here: the work is reading the packed adaLN weights once (HBM-bound),
-// with M <= 4 tokens riding along in registers.
+// with the few tokens riding along.
 //
-// Persistent warps. The n_blocks * N weight rows form one list; warp w of the
-// grid owns a contiguous, balanced slice of it and streams it with eight
-// 16-byte loads per lane in flight (rows are contiguous in memory, so a warp
-// reads whole rows with fully coalesced loads).
+// Persistent warps over balanced, contiguous slices of the n_blocks * N
+// weight rows (rows are contiguous in memory, so a warp reads whole rows with
+// coalesced loads), the next step's loads issued before the current step's
+// math:
 //
-//  * Row-packed path (a row is 8, 16 or 32 chunks of 16 bytes: K = 256 at
-//    w4 / w8 / bf16): one load instruction covers 32 / C whole rows and lane
-//    l always reads chunk l % C of its row (its temb values come from shared
-//    memory, one 8-byte word per code pair and token, shared by the eight
-//    rows in flight). The eight per-instruction partial sums are reduced
-//    across the row's C lanes with a transposing butterfly (7 shuffles per
-//    token instead of 28).
-//  * Generic path (any other K, e.g. the [4H, 3840] shape): a warp per row,
-//    lanes striding over the row's chunks, temb from shared memory, a full
-//    warp reduction per row.
+//  * Tensor-core path (K a multiple of 256 -- the reference's 256 and the
+//    [4H, 3840] shape -- and N a multiple of 16): tiles of 16 rows; per
+//    64-wide group the dot products with up to 8 tokens are mma.sync
+//    m16n8k16 with the weights as the A fragment (packed codes become exact
+//    fp16 integers) and the tokens' temb as the B fragment (see
+//    mod_mma_kernel).
+//  * Generic path (any other K): a warp per row, lanes striding over the
+//    row's 16-byte chunks in fp32 FMAs, temb from shared memory, a full warp
+//    reduction per row.
 //
-// Quantized weights: a chunk lies inside one 64-wide group, so
-//   sum_k (s q_k + b) t_k = s * sum_k q_k t_k + b * sum_k t_k,
-// and each code enters as an exact small integer (byte-permute into the float
-// 2^23 + q, minus 2^23) in packed fp32-pair FMAs. Every token's sums are
+// Packed weights: a group's dequantized dot is s * sum_k q_k t_k + b * sum_k
+// t_k with the codes entering as exact integers. Every token's sums are
 // formed in a fixed order that does not depend on M, the grid or the row's
 // position, so a row's result is the same bits whatever launch computes it
 // (a CFG batch equals its per-image launches).
 #include <cuda_runtime.h>
 
 #include <atomic>
+
+#include <cuda_fp16.h>
 
 #include "mp_device.cuh"
 #include "mp_kernels.h"
@@ -92,25 +92,45 @@ __device__ __forceinline__ float chunk_dot(const uint4& c, const uint64_t* t2, u
   return f32x2_lo(acc) + f32x2_hi(acc);
 }
 
-// The row's epilogue: bias, the bf16 mods row values of every token, and the
-// (1 + scale) folds into the norm gains (chunks 0 and 2 of the 4H outputs).
+// A row's bias and, for the rows whose (1 + scale) folds into a norm gain
+// (chunk 0 into an1, chunk 2 into fn1), that gain (0 otherwise), as bf16 bits.
+struct RowEpi {
+  uint32_t bias, gain;
+};
+
+__device__ __forceinline__ RowEpi row_epi(const ModParams& p, const ModBlock& blk, int n) {
+  RowEpi e;
+  e.bias = __ldg(blk.bias + n);
+  e.gain = 0u;
+  if (n < p.H && blk.an1 != nullptr) e.gain = __ldg(blk.an1 + n);
+  if (n >= 2 * p.H && n < 3 * p.H && blk.fn1 != nullptr) e.gain = __ldg(blk.fn1 + (n - 2 * p.H));
+  return e;
+}
+
+// One output of a row: bias, the bf16 mods value of token m, and the
+// (1 + scale) fold into the norm gain of chunks 0 and 2 of the 4H outputs.
+__device__ __forceinline__ void write_token(const ModParams& p, const ModBlock& blk, int b, int n,
+                                            int m, float v, RowEpi e) {
+  const size_t bm = static_cast<size_t>(b) * p.m_stride + m;
+  const __nv_bfloat16 mv = __float2bfloat16_rn(v + bf16_bits_to_f32(e.bias));
+  reinterpret_cast<__nv_bfloat16*>(p.mods)[bm * p.N + n] = mv;
+  const float scale1 = 1.0f + __bfloat162float(mv);
+  if (p.nw1 != nullptr && blk.an1 != nullptr && n < p.H)
+    reinterpret_cast<__nv_bfloat16*>(p.nw1)[bm * p.H + n] =
+        __float2bfloat16_rn(bf16_bits_to_f32(e.gain) * scale1);
+  if (p.nw3 != nullptr && blk.fn1 != nullptr && n >= 2 * p.H && n < 3 * p.H)
+    reinterpret_cast<__nv_bfloat16*>(p.nw3)[bm * p.H + (n - 2 * p.H)] =
+        __float2bfloat16_rn(bf16_bits_to_f32(e.gain) * scale1);
+}
+
 template <int MT>
 __device__ __forceinline__ void write_row(const ModParams& p, const ModBlock& blk, int b, int n,
                                           const float* v) {
-  const float bias = bf16_bits_to_f32(blk.bias[n]);
+  const RowEpi e = row_epi(p, blk, n);
 #pragma unroll
   for (int m = 0; m < MT; ++m) {
     if (m >= p.M) break;
-    const size_t bm = static_cast<size_t>(b) * p.m_stride + m;
-    const __nv_bfloat16 mv = __float2bfloat16_rn(v[m] + bias);
-    reinterpret_cast<__nv_bfloat16*>(p.mods)[bm * p.N + n] = mv;
-    const float scale1 = 1.0f + __bfloat162float(mv);
-    if (p.nw1 != nullptr && blk.an1 != nullptr && n < p.H)
-      reinterpret_cast<__nv_bfloat16*>(p.nw1)[bm * p.H + n] =
-          __float2bfloat16_rn(bf16_bits_to_f32(blk.an1[n]) * scale1);
-    if (p.nw3 != nullptr && blk.fn1 != nullptr && n >= 2 * p.H && n < 3 * p.H)
-      reinterpret_cast<__nv_bfloat16*>(p.nw3)[bm * p.H + (n - 2 * p.H)] =
-          __float2bfloat16_rn(bf16_bits_to_f32(blk.fn1[n - 2 * p.H]) * scale1);
+    write_token(p, blk, b, n, m, v[m], e);
   }
 }
 
@@ -121,148 +141,267 @@ __device__ __forceinline__ void warp_slice(long long total, long long w, long lo
   end = total * (w + 1) / nw;
 }
 
-// ---- row-packed path: C = 8, 16 or 32 chunks per row ------------------------
-// Shared memory: the block table, then this launch's temb as fp32 pairs in
-// the order [token][pair of the chunk][chunk] (the lanes of an instruction
-// read consecutive 8-byte words), then the per-chunk temb sums [token][chunk].
-template <int BITS, int MT, int C>
-__global__ void __launch_bounds__(kModThreads) mod_rows_kernel(const __grid_constant__ ModParams p) {
-  using F = ModFmt<BITS>;
-  constexpr int RI = 32 / C;  // rows per load instruction
+// ---- tensor-core path: K a multiple of 256, N a multiple of 16 --------------
+// A warp takes tiles of 16 weight rows; per 64-wide K group each lane reads
+// the 16 consecutive weights [16q, 16q + 16) of the group (q = lane % 4) of
+// rows g and g + 8 (g = lane / 4): w8 16 bytes, w4 8 bytes, bf16 32 bytes.
+// The group's dot products with up to 8 tokens are four mma.sync m16n8k16:
+// the lane's weights are the A fragment (packed codes become exact fp16
+// integers: one byte-permute makes two 1024 + q halves, one half subtraction
+// removes the 1024; bf16 weights are used as they are), the tokens' temb
+// values the B fragment (the same permutation of K, built once per CTA in
+// shared memory; fp16 for packed weights, so temb must lie within fp16's
+// range, |t| < 65504), fp32 accumulation. A packed group is summed on its own
+// and folded in as s * sum(q t) + b * sum(t) (the temb sums per group and
+// token also in shared memory); bf16 weights accumulate over all of K. Each
+// token is one MMA column, computed the same way whatever the other columns
+// hold.
+constexpr int kMmaTok = 8;     // tokens of one launch (the MMA's N)
+constexpr int kGroupsPerStep = 4;
+
+template <int BITS>
+struct MmaFmt {
+  // bytes of one lane's slice of one row's group
+  static constexpr int kLaneBytes = BITS == 0 ? 32 : (BITS == 8 ? 16 : 8);
+  static constexpr int kWords = kLaneBytes / 4;
+  static constexpr int kGroupBytes = 4 * kLaneBytes;
+};
+
+// K offsets (within a group) of the A slots (a0 low, a0 high, a2 low, a2
+// high) of k-step s for quad q: the lane's weights in the order its packed
+// words give them.
+template <int BITS>
+__device__ __forceinline__ void mma_kslots(int s, int q, int (&k)[4]) {
+  if constexpr (BITS == 4) {
+    const int base = 16 * q + 8 * (s >> 1) + 4 * (s & 1);
+    k[0] = base; k[1] = base + 2; k[2] = base + 1; k[3] = base + 3;
+  } else {
+    const int base = 16 * q + 4 * s;
+    k[0] = base; k[1] = base + 1; k[2] = base + 2; k[3] = base + 3;
+  }
+}
+
+__device__ __forceinline__ uint32_t half2_bits_of(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// A-fragment words (the a0 / a2 halves) of k-step s from a lane's words w[]:
+// two weights each, as f16x2 exact integers (packed) or bf16x2 (dense).
+template <int BITS>
+__device__ __forceinline__ void mma_afrag(const uint32_t* w, int s, uint32_t code_xor,
+                                          uint32_t magic2, uint32_t& lo, uint32_t& hi) {
+  if constexpr (BITS == 0) {
+    lo = w[2 * s];
+    hi = w[2 * s + 1];
+  } else {
+    uint32_t x0, x1;
+    if constexpr (BITS == 8) {
+      const uint32_t v = w[s] ^ code_xor;
+      x0 = __byte_perm(v, 0x64u, 0x4140u);  // codes 0, 1 of the word
+      x1 = __byte_perm(v, 0x64u, 0x4342u);  // codes 2, 3
+    } else {
+      const uint32_t v = w[s >> 1];
+      const uint32_t ev = v & 0x0F0F0F0Fu, od = (v >> 4) & 0x0F0F0F0Fu;
+      const uint32_t sel = (s & 1) ? 0x4342u : 0x4140u;
+      x0 = __byte_perm(ev, 0x64u, sel);  // codes 4h, 4h + 2 (h = s & 1)
+      x1 = __byte_perm(od, 0x64u, sel);  // codes 4h + 1, 4h + 3
+    }
+    __half2 h0 = __hsub2(*reinterpret_cast<__half2*>(&x0), *reinterpret_cast<const __half2*>(&magic2));
+    __half2 h1 = __hsub2(*reinterpret_cast<__half2*>(&x1), *reinterpret_cast<const __half2*>(&magic2));
+    lo = *reinterpret_cast<uint32_t*>(&h0);
+    hi = *reinterpret_cast<uint32_t*>(&h1);
+  }
+}
+
+template <int BITS>
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+  if constexpr (BITS == 0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+
+// One step's loads: kGroupsPerStep groups of the two rows of this lane.
+template <int BITS>
+struct MmaStep {
+  uint32_t w0[kGroupsPerStep][MmaFmt<BITS>::kWords];  // row g
+  uint32_t w1[kGroupsPerStep][MmaFmt<BITS>::kWords];  // row g + 8
+  uint32_t sb0[kGroupsPerStep], sb1[kGroupsPerStep];
+  RowEpi e0, e1;  // loaded with the last step of a tile
+};
+
+template <int BITS>
+__device__ __forceinline__ void mma_load(const ModParams& p, const ModBlock* blocks, long long tile,
+                                         int gb, int lane, MmaStep<BITS>& st) {
+  using F = MmaFmt<BITS>;
+  const long long r0 = tile * 16 + (lane >> 2);
+  const int b = static_cast<int>(r0 / p.N);
+  const int n0 = static_cast<int>(r0 - static_cast<long long>(b) * p.N);
+  const ModBlock& blk = blocks[b];
+  const size_t row_bytes = static_cast<size_t>(p.K) * (BITS == 0 ? 16 : BITS) / 8;
+  const uint8_t* base0 = blk.w + static_cast<size_t>(n0) * row_bytes +
+                         (lane & 3) * F::kLaneBytes;
+  const uint8_t* base1 = base0 + 8 * row_bytes;
+#pragma unroll
+  for (int gi = 0; gi < kGroupsPerStep; ++gi) {
+    const size_t off = static_cast<size_t>(gb * kGroupsPerStep + gi) * F::kGroupBytes;
+    if constexpr (F::kLaneBytes == 8) {
+      const uint2 v0 = __ldg(reinterpret_cast<const uint2*>(base0 + off));
+      const uint2 v1 = __ldg(reinterpret_cast<const uint2*>(base1 + off));
+      st.w0[gi][0] = v0.x; st.w0[gi][1] = v0.y;
+      st.w1[gi][0] = v1.x; st.w1[gi][1] = v1.y;
+    } else {
+#pragma unroll
+      for (int c = 0; c < F::kLaneBytes / 16; ++c) {
+        const uint4 v0 = ld_global_nc_v4(base0 + off + 16 * c);
+        const uint4 v1 = ld_global_nc_v4(base1 + off + 16 * c);
+        st.w0[gi][4 * c] = v0.x; st.w0[gi][4 * c + 1] = v0.y;
+        st.w0[gi][4 * c + 2] = v0.z; st.w0[gi][4 * c + 3] = v0.w;
+        st.w1[gi][4 * c] = v1.x; st.w1[gi][4 * c + 1] = v1.y;
+        st.w1[gi][4 * c + 2] = v1.z; st.w1[gi][4 * c + 3] = v1.w;
+      }
+    }
+    if constexpr (BITS != 0) {
+      const uint32_t* sbr = blk.sb + static_cast<size_t>(n0) * p.sb_stride + gb * kGroupsPerStep + gi;
+      st.sb0[gi] = __ldg(sbr);
+      st.sb1[gi] = __ldg(sbr + 8 * static_cast<size_t>(p.sb_stride));
+    }
+  }
+  if ((gb + 1) * kGroupsPerStep * 64 == p.K) {  // the tile's last step: its rows' epilogue inputs
+    st.e0 = row_epi(p, blk, n0);
+    st.e1 = row_epi(p, blk, n0 + 8);
+  }
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(kModThreads) mod_mma_kernel(const __grid_constant__ ModParams p) {
   extern __shared__ uint8_t mod_smem[];
   ModBlock* blocks = reinterpret_cast<ModBlock*>(mod_smem);
   const size_t blk_bytes = (static_cast<size_t>(p.n_blocks) * sizeof(ModBlock) + 15) & ~size_t(15);
-  uint64_t* t2s = reinterpret_cast<uint64_t*>(mod_smem + blk_bytes);
-  float* ts = reinterpret_cast<float*>(t2s + MT * F::kPairs * C);
+  const int G = p.K / 64;
+  uint2* bfrag = reinterpret_cast<uint2*>(mod_smem + blk_bytes);       // [G][4][32]
+  float* tsum = reinterpret_cast<float*>(bfrag + static_cast<size_t>(G) * 4 * 32);  // [G][8]
   for (int i = threadIdx.x; i < p.n_blocks; i += blockDim.x) blocks[i] = p.blocks[i];
-  for (int i = threadIdx.x; i < MT * F::kPairs * C; i += blockDim.x) {
-    const int m = i / (F::kPairs * C), rem = i % (F::kPairs * C);
-    const int q = rem / C, ch = rem % C;
-    float a = 0.0f, b = 0.0f;
-    if (m < p.M) {
-      const uint16_t* t = p.temb + static_cast<size_t>(m) * p.K + ch * F::kPer + 2 * q;
-      a = bf16_bits_to_f32(t[0]);
-      b = bf16_bits_to_f32(t[1]);
+  for (int i = threadIdx.x; i < G * 4 * 32; i += blockDim.x) {
+    const int gi = i >> 7, s = (i >> 5) & 3, ln = i & 31;
+    const int n = ln >> 2, q = ln & 3;
+    int k[4];
+    mma_kslots<BITS>(s, q, k);
+    uint16_t tb[4] = {0, 0, 0, 0};
+    if (n < p.M)
+      for (int j = 0; j < 4; ++j) tb[j] = p.temb[static_cast<size_t>(n) * p.K + gi * 64 + k[j]];
+    uint2 v;
+    if constexpr (BITS == 0) {
+      v.x = static_cast<uint32_t>(tb[0]) | (static_cast<uint32_t>(tb[1]) << 16);
+      v.y = static_cast<uint32_t>(tb[2]) | (static_cast<uint32_t>(tb[3]) << 16);
+    } else {
+      v.x = half2_bits_of(bf16_bits_to_f32(tb[0]), bf16_bits_to_f32(tb[1]));
+      v.y = half2_bits_of(bf16_bits_to_f32(tb[2]), bf16_bits_to_f32(tb[3]));
     }
-    t2s[i] = f32x2(a, b);
+    bfrag[i] = v;
   }
-  __syncthreads();
-  for (int i = threadIdx.x; i < MT * C; i += blockDim.x) {
-    const int m = i / C, ch = i % C;
-    float s = 0.0f;
-    for (int q = 0; q < F::kPairs; ++q) {
-      const uint64_t v = t2s[(m * F::kPairs + q) * C + ch];
-      s += f32x2_lo(v);
-      s += f32x2_hi(v);
+  if constexpr (BITS != 0) {
+    // per (group, token) the sum of its 64 temb values: a warp each, lanes
+    // adding two values, then a fixed xor tree (the same bits for a token
+    // whatever else the launch holds)
+    const int wl = threadIdx.x & 31;
+    for (int i = threadIdx.x >> 5; i < G * kMmaTok; i += kModWarps) {
+      const int gi = i / kMmaTok, n = i % kMmaTok;
+      float v = 0.0f;
+      if (n < p.M) {
+        const uint16_t* t = p.temb + static_cast<size_t>(n) * p.K + gi * 64;
+        v = bf16_bits_to_f32(t[wl]) + bf16_bits_to_f32(t[32 + wl]);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+      if (wl == 0) tsum[i] = v;
     }
-    ts[i] = s;
   }
   __syncthreads();
 
   const int lane = threadIdx.x & 31;
-  const int kc = lane % C;      // this lane's chunk of every row it reads
-  const int rsub = lane / C;    // its row within an instruction's RI rows
-  const int row_bytes = C * 16;
-  const uint64_t neg_magic2 = f32x2(-p.code_magic, -p.code_magic);
-  float tsum[MT];
-#pragma unroll
-  for (int m = 0; m < MT; ++m) tsum[m] = ts[m * C + kc];
-  const int group_of_chunk = BITS == 0 ? 0 : (kc * F::kPer) / 64;
-
-  const long long total_units = static_cast<long long>(p.n_blocks) * p.N / RI;
+  const int q = lane & 3;
+  const uint32_t code_xor = p.code_xor;
+  // 1024 (affine) or 1152 (signed 8-bit codes, offset by 128), as f16x2
+  const uint32_t magic2 = code_xor != 0u ? 0x64806480u : 0x64006400u;
+  const int steps_per_tile = G / kGroupsPerStep;
+  const long long total_tiles = static_cast<long long>(p.n_blocks) * p.N / 16;
   const long long nwarps = static_cast<long long>(gridDim.x) * kModWarps;
   const long long gw = static_cast<long long>(blockIdx.x) * kModWarps + (threadIdx.x >> 5);
-  long long u_begin, u_end;
-  warp_slice(total_units, gw, nwarps, u_begin, u_end);
+  long long t_begin, t_end;
+  warp_slice(total_tiles, gw, nwarps, t_begin, t_end);
+  if (t_begin >= t_end) return;
+  const long long st_end = (t_end - t_begin) * steps_per_tile;
 
-  for (long long u0 = u_begin; u0 < u_end; u0 += kUnroll) {
-    const int nvalid = static_cast<int>(min(static_cast<long long>(kUnroll), u_end - u0));
-    const long long row0 = u0 * RI;
-    const int b0 = static_cast<int>(row0 / p.N);
-    const long long next_block_row = static_cast<long long>(b0 + 1) * p.N;
-    uint4 c[kUnroll];
-    uint32_t sbw[kUnroll];
+  MmaStep<BITS> cur, nxt;
+  mma_load<BITS>(p, blocks, t_begin, 0, lane, cur);
+  float y[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // rows g, g + 8 x tokens 2q, 2q + 1
+  for (long long st = 0; st < st_end; ++st) {
+    const long long tile = t_begin + st / steps_per_tile;
+    const int gb = static_cast<int>(st % steps_per_tile);
+    if (st + 1 < st_end) {
+      const long long st1 = st + 1;
+      mma_load<BITS>(p, blocks, t_begin + st1 / steps_per_tile,
+                     static_cast<int>(st1 % steps_per_tile), lane, nxt);
+    }
 #pragma unroll
-    for (int j = 0; j < kUnroll; ++j) {
-      c[j] = make_uint4(0u, 0u, 0u, 0u);
-      sbw[j] = 0u;
-      if (j < nvalid) {
-        const long long r = row0 + j * RI + rsub;
-        const int b = r >= next_block_row ? b0 + 1 : b0;
-        const int n = static_cast<int>(r - static_cast<long long>(b) * p.N);
-        const ModBlock& blk = blocks[b];
-        c[j] = ld_global_nc_v4(blk.w + static_cast<size_t>(n) * row_bytes + kc * 16);
-        if (BITS != 0) sbw[j] = __ldg(blk.sb + static_cast<size_t>(n) * p.sb_stride + group_of_chunk);
+    for (int gi = 0; gi < kGroupsPerStep; ++gi) {
+      const int g_abs = gb * kGroupsPerStep + gi;
+      float c[4];
+      if constexpr (BITS == 0) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) c[j] = y[j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) c[j] = 0.0f;
+      }
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        uint32_t a0, a2, a1, a3;
+        mma_afrag<BITS>(cur.w0[gi], s, code_xor, magic2, a0, a2);
+        mma_afrag<BITS>(cur.w1[gi], s, code_xor, magic2, a1, a3);
+        const uint2 b = bfrag[(g_abs * 4 + s) * 32 + lane];
+        mma_16816<BITS>(c, a0, a1, a2, a3, b.x, b.y);
+      }
+      if constexpr (BITS == 0) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) y[j] = c[j];
+      } else {
+        const float2 ts = *reinterpret_cast<const float2*>(&tsum[g_abs * kMmaTok + 2 * q]);
+        const float s0 = bf16_bits_to_f32(cur.sb0[gi] & 0xFFFFu), b0 = bf16_bits_to_f32(cur.sb0[gi] >> 16);
+        const float s1 = bf16_bits_to_f32(cur.sb1[gi] & 0xFFFFu), b1 = bf16_bits_to_f32(cur.sb1[gi] >> 16);
+        y[0] += fmaf(s0, c[0], b0 * ts.x);
+        y[1] += fmaf(s0, c[1], b0 * ts.y);
+        y[2] += fmaf(s1, c[2], b1 * ts.x);
+        y[3] += fmaf(s1, c[3], b1 * ts.y);
       }
     }
-    // per instruction and token: this lane's chunk dot (pairs in order, even
-    // and odd weights in two chains), then the group scale and bias
-    uint64_t acc[MT][kUnroll];
-#pragma unroll
-    for (int m = 0; m < MT; ++m)
-#pragma unroll
-      for (int j = 0; j < kUnroll; ++j) acc[m][j] = f32x2(0.0f, 0.0f);
-#pragma unroll
-    for (int q = 0; q < F::kPairs; ++q) {
-      uint64_t tv[MT];
-#pragma unroll
-      for (int m = 0; m < MT; ++m) tv[m] = t2s[(m * F::kPairs + q) * C + kc];
-#pragma unroll
-      for (int j = 0; j < kUnroll; ++j) {
-        const uint64_t w2 = chunk_pair<BITS>(c[j], q, p.code_xor, neg_magic2);
-#pragma unroll
-        for (int m = 0; m < MT; ++m) acc[m][j] = fma_f32x2(w2, tv[m], acc[m][j]);
-      }
-    }
-    float v[MT][kUnroll];
-#pragma unroll
-    for (int j = 0; j < kUnroll; ++j) {
-#pragma unroll
-      for (int m = 0; m < MT; ++m) {
-        const float d = f32x2_lo(acc[m][j]) + f32x2_hi(acc[m][j]);
-        if constexpr (BITS == 0) {
-          v[m][j] = d;
-        } else {
-          const float sc = bf16_bits_to_f32(sbw[j] & 0xFFFFu);
-          const float bi = bf16_bits_to_f32(sbw[j] >> 16);
-          v[m][j] = fmaf(sc, d, bi * tsum[m]);
-        }
-      }
-    }
-    // Transposing butterfly over the row's C lanes: at offset o the lane
-    // with bit o clear keeps the lower half of its values, the other the
-    // upper half, each adding its partner's copy; after three halvings a
-    // lane holds one instruction's row (index from its bits C/2, C/4, C/8),
-    // summed over 8 lanes; plain xor steps finish the sum.
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-#pragma unroll
-      for (int step = 0; step < 3; ++step) {
-        const int o = C >> (step + 1);
-        const int half = kUnroll >> (step + 1);
-        const bool upper = (lane & o) != 0;
-#pragma unroll
-        for (int i = 0; i < half; ++i) {
-          const float send = upper ? v[m][i] : v[m][i + half];
-          const float keep = upper ? v[m][i + half] : v[m][i];
-          v[m][i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, o);
+    if (gb + 1 == steps_per_tile) {
+      // the tile's rows are complete: rows g and g + 8, tokens 2q and 2q + 1
+      const long long r0 = tile * 16 + (lane >> 2);
+      const int b = static_cast<int>(r0 / p.N);
+      const int n0 = static_cast<int>(r0 - static_cast<long long>(b) * p.N);
+      for (int h = 0; h < 2; ++h) {
+        for (int e = 0; e < 2; ++e) {
+          const int m = 2 * q + e;
+          if (m < p.M) write_token(p, blocks[b], b, n0 + 8 * h, m, y[2 * h + e], h ? cur.e1 : cur.e0);
         }
       }
 #pragma unroll
-      for (int o = C >> 4; o > 0; o >>= 1) v[m][0] += __shfl_xor_sync(0xFFFFFFFFu, v[m][0], o);
+      for (int j = 0; j < 4; ++j) y[j] = 0.0f;
     }
-    const int jrow = ((lane & (C >> 1)) ? 4 : 0) + ((lane & (C >> 2)) ? 2 : 0) +
-                     ((lane & (C >> 3)) ? 1 : 0);
-    const bool writer = (kc & ((C >> 3) - 1)) == 0;
-    if (writer && jrow < nvalid) {
-      const long long r = row0 + jrow * RI + rsub;
-      const int b = r >= next_block_row ? b0 + 1 : b0;
-      const int n = static_cast<int>(r - static_cast<long long>(b) * p.N);
-      float out[MT];
-#pragma unroll
-      for (int m = 0; m < MT; ++m) out[m] = v[m][0];
-      write_row<MT>(p, blocks[b], b, n, out);
-    }
+    cur = nxt;
   }
 }
 
@@ -405,44 +544,50 @@ cudaError_t launch_persistent(K kernel, const ModParams& p, size_t smem, long lo
 }
 
 template <int BITS, int MT>
-cudaError_t launch_mod_t(const ModParams& p, cudaStream_t stream) {
+cudaError_t launch_mod_warp(const ModParams& p, cudaStream_t stream) {
   const int row_bytes = BITS == 0 ? p.K * 2 : p.K * BITS / 8;
   const int C = row_bytes / 16;
   const size_t blk_bytes = (static_cast<size_t>(p.n_blocks) * sizeof(ModBlock) + 15) & ~size_t(15);
   const long long rows = static_cast<long long>(p.n_blocks) * p.N;
-  if (C == 8 || C == 16 || C == 32) {
-    const int ri = 32 / C;
-    // a group of eight instructions then spans at most one block boundary
-    if (p.N % ri == 0 && p.N >= kUnroll * ri) {
-      const long long work = (rows / ri + kUnroll - 1) / kUnroll;  // warps with a full group
-      const size_t smem = blk_bytes + static_cast<size_t>(MT) * ModFmt<BITS>::kPairs * C * 8 +
-                          static_cast<size_t>(MT) * C * 4;
-      static std::atomic<int> cache8[64], cache16[64], cache32[64];
-      if (C == 8) return launch_persistent(mod_rows_kernel<BITS, MT, 8>, p, smem, work, cache8, stream);
-      if (C == 16) return launch_persistent(mod_rows_kernel<BITS, MT, 16>, p, smem, work, cache16, stream);
-      return launch_persistent(mod_rows_kernel<BITS, MT, 32>, p, smem, work, cache32, stream);
-    }
-  }
   constexpr int Q = ModFmt<BITS>::kPer / 4;
   const size_t smem = blk_bytes + static_cast<size_t>(MT) * Q * C * 16 + static_cast<size_t>(MT) * C * 4;
-  static std::atomic<int> cachew[64];
-  return launch_persistent(mod_warp_kernel<BITS, MT>, p, smem, rows, cachew, stream);
+  static std::atomic<int> cache[64];
+  return launch_persistent(mod_warp_kernel<BITS, MT>, p, smem, rows, cache, stream);
 }
 
-// Token count rounded up to 1, 2 or 4: registers scale with it.
+template <int BITS>
+cudaError_t launch_mod_mma(const ModParams& p, cudaStream_t stream) {
+  const size_t blk_bytes = (static_cast<size_t>(p.n_blocks) * sizeof(ModBlock) + 15) & ~size_t(15);
+  const int G = p.K / 64;
+  const size_t smem = blk_bytes + static_cast<size_t>(G) * 4 * 32 * 8 +
+                      static_cast<size_t>(G) * kMmaTok * 4;
+  const long long tiles = static_cast<long long>(p.n_blocks) * p.N / 16;
+  static std::atomic<int> cache[64];
+  return launch_persistent(mod_mma_kernel<BITS>, p, smem, tiles, cache, stream);
+}
+
+bool mma_shape(int n, int k) { return k % (64 * kGroupsPerStep) == 0 && n % 16 == 0; }
+
+// The generic path's token count rounded up to 1, 2 or 4: registers scale with it.
 template <int BITS>
 cudaError_t launch_mod_bits(const ModParams& p, cudaStream_t stream) {
-  if (p.M == 1) return launch_mod_t<BITS, 1>(p, stream);
-  if (p.M == 2) return launch_mod_t<BITS, 2>(p, stream);
-  return launch_mod_t<BITS, 4>(p, stream);
+  if (mma_shape(p.N, p.K)) {
+    if (p.M > kMmaTok) return cudaErrorInvalidValue;
+    return launch_mod_mma<BITS>(p, stream);
+  }
+  if (p.M > kModMaxTok) return cudaErrorInvalidValue;
+  if (p.M == 1) return launch_mod_warp<BITS, 1>(p, stream);
+  if (p.M == 2) return launch_mod_warp<BITS, 2>(p, stream);
+  return launch_mod_warp<BITS, 4>(p, stream);
 }
 
 }  // namespace
 
+int mod_tokens_per_launch(int n, int k) { return mma_shape(n, k) ? kMmaTok : kModMaxTok; }
+
 cudaError_t launch_mod(const ModParams& p, cudaStream_t stream) {
   const int row_bytes = p.bits == 0 ? p.K * 2 : p.K * p.bits / 8;
-  if (row_bytes % 16 != 0 || p.M < 1 || p.M > kModMaxTok || p.m_stride < p.M)
-    return cudaErrorInvalidValue;
+  if (row_bytes % 16 != 0 || p.M < 1 || p.m_stride < p.M) return cudaErrorInvalidValue;
   if (p.bits != 0 && p.K % 64 != 0) return cudaErrorInvalidValue;
   if (p.bits == 8) return launch_mod_bits<8>(p, stream);
   if (p.bits == 4) return launch_mod_bits<4>(p, stream);
