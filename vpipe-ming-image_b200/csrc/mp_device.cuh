@@ -42,6 +42,15 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
       : "memory");
 }
 
+// `count` arrivals at once.
+__device__ __forceinline__ void mbar_arrive_count(uint32_t bar, uint32_t count) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(bar),
+      "r"(count)
+      : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile(
       "{\n\t.reg .b64 st;\n\t"

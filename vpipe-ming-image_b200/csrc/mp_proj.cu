@@ -99,7 +99,6 @@ static_assert(kMaxStages <= 8, "per-slot parity bit masks");
 enum : uint32_t {
   kSiteEmpty = 0x1100u,
   kSiteFull = 0x1200u,
-  kSiteDeq = 0x1300u,
   kSiteCodes = 0x1400u,
   kSiteEpi = 0x1500u,
   kSiteDrain = 0x1600u,
@@ -112,7 +111,7 @@ enum : uint32_t {
 #ifdef MP_TRACE
 constexpr int kTraceStages = 96;
 enum { kTrProducer = 0, kTrDeqStart, kTrDeqEnd, kTrMma, kTrEpiStart, kTrEpiEnd, kTrDeqMath,
-       kTrDeqStored, kTrEvents };
+       kTrDeqStored, kTrMmaPre, kTrMmaIssued, kTrEvents };
 __device__ long long g_trace[2][kTrEvents][kTraceStages];
 __device__ __forceinline__ void trace_mark(int ev, int kt) {
   if (blockIdx.x < 2 && blockIdx.y == 0 && kt < kTraceStages) g_trace[blockIdx.x][ev][kt] = clock64();
@@ -124,10 +123,9 @@ __device__ __forceinline__ void trace_mark(int ev, int kt) {
 
 struct PairSmem {
   uint8_t* tiles;
-  uint64_t* full;    // [stages] leader: both CTAs' TMA tiles of the MMA
+  uint64_t* full;    // [stages] leader: both CTAs' TMA tiles and dequantized A tiles of the MMA
   uint64_t* empty;   // [stages] each CTA: stage released by the MMA
   uint64_t* cfull;   // [stages] each CTA: its own codes tile landed
-  uint64_t* afull;   // [stages] leader: both CTAs' dequantized A tile written
   uint64_t* tfull;   // each CTA: the tile's accumulators complete
   uint64_t* tempty;  // [2] leader: accumulator j read out by both CTAs' epilogues
   uint64_t* drain;   // leader: every MMA issued has completed
@@ -146,8 +144,7 @@ __device__ __forceinline__ PairSmem carve_pair(uint8_t* raw) {
   s.full = bars;
   s.empty = bars + kMaxStages;
   s.cfull = bars + 2 * kMaxStages;
-  s.afull = bars + 3 * kMaxStages;
-  s.tfull = bars + 4 * kMaxStages;
+  s.tfull = bars + 3 * kMaxStages;
   s.tempty = s.tfull + 1;
   s.drain = s.tempty + 2;
   s.tmem_slot = reinterpret_cast<uint32_t*>(s.drain + 1);
@@ -407,7 +404,10 @@ __device__ void pair_producer(const ProjParams& p, const PairSmem& sm, bool lead
         pend_codes_par = (pend_codes_par & ~bit) | (cpar & bit);
         cpar ^= bit;
       } else {
-        if (leader) mbar_arrive_expect_tx(full_local, xbytes_pair + 2u * kWStageBytes);
+        if (leader) {
+          mbar_arrive_expect_tx(full_local, xbytes_pair + 2u * kWStageBytes);
+          mbar_arrive_count(full_local, 2 * kDeqThreads / 32);  // no dequant: the dequantizers' share
+        }
         if (lora) {
           // SwiGLU: the interleaved B stack holds 128 rows per 64 features
           tma_load_2d_pair(wb, &mb.tm_b, full_leader, xk, mb.swiglu ? 2 * t.f0 : t.f0);
@@ -451,15 +451,12 @@ __device__ void pair_mma(const ProjParams& p, const PairSmem& sm, uint32_t tmem,
   using G = Geo<NT>;
   constexpr uint32_t stages = G::kStages;
   uint32_t it = 0;
-  uint32_t apar = 0;  // per slot: parity of the slot's next dequant phase
   uint32_t tcount = 0;
   bool aborted = false;
   UnitIter units = units_begin(p);
   for (int unit = units_next(p, units); unit != kNoUnit && !aborted;
        unit = units_next(p, units), ++tcount) {
     const Tile t = decode_unit(p, unit, 0, base_kt);
-    const ProjMember& mb = unit_member(p, t);
-    const bool quant = mb.bits != 0;
     // token-row tiles: D[token][feature] (A = the x sub-tile, M = its tokens
     // across the pair; B = the weight tile, N = the pair's 256 features);
     // narrower tiles: D[feature][token] (A = weights, B = x)
@@ -472,17 +469,10 @@ __device__ void pair_mma(const ProjParams& p, const PairSmem& sm, uint32_t tmem,
     for (int kt = t.kt_begin; kt < t.kt_end; ++kt, ++it) {
       const int s = static_cast<int>(it % stages);
       const uint32_t ph = (it / stages) & 1u;
+      MP_TRACE_MARK(kTrMmaPre, static_cast<int>(it));
       if (!mbar_wait(smem_u32(&sm.full[s]), ph, sm.abort, kSiteFull | s, p.wait_limit_ns)) {
         aborted = true;
         break;
-      }
-      if (quant && kt < base_kt) {
-        if (!mbar_wait(smem_u32(&sm.afull[s]), (apar >> s) & 1u, sm.abort, kSiteDeq | s,
-                       p.wait_limit_ns)) {
-          aborted = true;
-          break;
-        }
-        apar ^= 1u << s;
       }
       tc_fence_after();
       MP_TRACE_MARK(kTrMma, static_cast<int>(it));
@@ -514,6 +504,7 @@ __device__ void pair_mma(const ProjParams& p, const PairSmem& sm, uint32_t tmem,
         acc = 1;
       }
       if (aborted) break;
+      MP_TRACE_MARK(kTrMmaIssued, static_cast<int>(it));
       umma_commit_pair(smem_u32(&sm.empty[s]), 0x3);
     }
     if (!aborted) umma_commit_pair(smem_u32(sm.tfull), 0x3);
@@ -557,13 +548,20 @@ __device__ void pair_dequant(const ProjParams& p, const PairSmem& sm, int rank, 
     const bool row_ok = n < mb.N;
     const uint32_t* sbase = (mb.swiglu && r >= 64) ? mb.sb3 : mb.sb;
     const uint32_t* sbrow = sbase + static_cast<size_t>(row_ok ? n : 0) * mb.sb_stride;
-    uint4 sbv = make_uint4(0, 0, 0, 0);
+    // the row's scale/bias words of 4 groups at a time, the next 4 loaded
+    // when the current 4 come into use (a load on the stage that needs it
+    // would put a memory round trip on every fourth stage)
+    const uint4 zero4 = make_uint4(0, 0, 0, 0);
+    uint4 sbv = zero4, sbn = zero4;
     int sb_group = -1;  // which 4 groups sbv holds
     for (int kt = t.kt_begin; kt < base_end; ++kt, ++it) {
       const int s = static_cast<int>(it % stages);
-      if ((kt >> 2) != sb_group) {
-        sbv = row_ok ? ld_global_nc_v4(sbrow + (kt & ~3)) : make_uint4(0, 0, 0, 0);
-        sb_group = kt >> 2;
+      const int g4 = kt >> 2;
+      if (g4 != sb_group) {
+        sbv = (sb_group >= 0 && g4 == sb_group + 1) ? sbn
+                                                     : (row_ok ? ld_global_nc_v4(sbrow + 4 * g4) : zero4);
+        sb_group = g4;
+        if (row_ok && 4 * (g4 + 1) < base_end) sbn = ld_global_nc_v4(sbrow + 4 * (g4 + 1));
       }
       const uint32_t sbw = pick4p(sbv, kt & 3);
       const float sc = bf16_bits_to_f32(sbw & 0xFFFFu);
@@ -613,7 +611,7 @@ __device__ void pair_dequant(const ProjParams& p, const PairSmem& sm, int rank, 
       fence_proxy_async_shared();
       if (threadIdx.x == 64) MP_TRACE_MARK(kTrDeqStored, static_cast<int>(it));
       __syncwarp();
-      if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&sm.afull[s]), 0));
+      if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&sm.full[s]), 0));
       if (threadIdx.x == 64) MP_TRACE_MARK(kTrDeqEnd, static_cast<int>(it));
     }
     it += static_cast<uint32_t>(t.kt_end - base_end);  // appended LoRA stages: nothing to do
@@ -1207,10 +1205,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kMaxStages; ++s) {
-      mbar_init(smem_u32(&sm.full[s]), 1);
+      // the leader producer's arrive (with the expected TMA bytes) + one
+      // arrive per dequant warp of both CTAs (the producer arrives those
+      // itself for stages without dequant work)
+      mbar_init(smem_u32(&sm.full[s]), 1 + 2 * kDeqThreads / 32);
       mbar_init(smem_u32(&sm.empty[s]), 1);
       mbar_init(smem_u32(&sm.cfull[s]), 1);
-      mbar_init(smem_u32(&sm.afull[s]), 2 * kDeqThreads / 32);  // one arrive per dequant warp
     }
     mbar_init(smem_u32(sm.tfull), 1);
     mbar_init(smem_u32(&sm.tempty[0]), 2 * kEpiThreads / 32);  // one arrive per epilogue warp
