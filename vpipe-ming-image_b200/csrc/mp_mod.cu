@@ -15,7 +15,7 @@
 // math:
 //
 //  * Tensor-core path (K a multiple of 256 -- the reference's 256 and the
-//    [4H, 3840] shape -- and N a multiple of 16): tiles of 16 rows; per
+//    [4H, 3840] shape -- and N a multiple of 64): tiles of 16 rows; per
 //    64-wide group the dot products with up to 8 tokens are mma.sync
 //    m16n8k16 with the weights as the A fragment (packed codes become exact
 //    fp16 integers) and the tokens' temb as the B fragment (see
@@ -141,7 +141,7 @@ __device__ __forceinline__ void warp_slice(long long total, long long w, long lo
   end = total * (w + 1) / nw;
 }
 
-// ---- tensor-core path: K a multiple of 256, N a multiple of 16 --------------
+// ---- tensor-core path: K a multiple of 256, N a multiple of 64 --------------
 // A warp takes tiles of 16 weight rows; per 64-wide K group each lane reads
 // the 16 consecutive weights [16q, 16q + 16) of the group (q = lane % 4) of
 // rows g and g + 8 (g = lane / 4): w8 16 bytes, w4 8 bytes, bf16 32 bytes.
@@ -218,13 +218,13 @@ template <int BITS>
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                           uint32_t a3, uint32_t b0, uint32_t b1) {
   if constexpr (BITS == 0) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
         "{%8,%9}, {%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   } else {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
         "{%8,%9}, {%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -232,66 +232,114 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
   }
 }
 
-// One step's loads: kGroupsPerStep groups of the two rows of this lane.
+// Each warp streams its steps (16 rows x kGroupsPerStep groups) through a
+// private ring of RING slots in shared memory with 16-byte cp.async copies,
+// RING - 1 steps in flight: a slot holds the step's weights (16 rows, the
+// 16-byte chunks of a row XOR-swizzled so the lanes' fragment reads are
+// conflict-free), the rows' scale/bias words of the step's groups, and with
+// the tile's last step the rows' bias and norm gain.
 template <int BITS>
-struct MmaStep {
-  uint32_t w0[kGroupsPerStep][MmaFmt<BITS>::kWords];  // row g
-  uint32_t w1[kGroupsPerStep][MmaFmt<BITS>::kWords];  // row g + 8
-  uint32_t sb0[kGroupsPerStep], sb1[kGroupsPerStep];
-  RowEpi e0, e1;  // loaded with the last step of a tile
+struct RingFmt {
+  static constexpr int kRowBytes = kGroupsPerStep * MmaFmt<BITS>::kGroupBytes;  // one row, one step
+  static constexpr int kCpr = kRowBytes / 16;                                   // 16-byte chunks per row
+  static constexpr int kData = 16 * kRowBytes;
+  static constexpr int kSb = BITS == 0 ? 0 : 16 * 16;
+  static constexpr int kSlot = ((kData + kSb + 64) + 127) / 128 * 128;
+  __device__ static __forceinline__ int swz(int row) {
+    return BITS == 8 ? 4 * (row & 1) : (BITS == 4 ? 2 * (row & 3) : (row & 1));
+  }
 };
 
-template <int BITS>
-__device__ __forceinline__ void mma_load(const ModParams& p, const ModBlock* blocks, long long tile,
-                                         int gb, int lane, MmaStep<BITS>& st) {
-  using F = MmaFmt<BITS>;
-  const long long r0 = tile * 16 + (lane >> 2);
-  const int b = static_cast<int>(r0 / p.N);
-  const int n0 = static_cast<int>(r0 - static_cast<long long>(b) * p.N);
-  const ModBlock& blk = blocks[b];
-  const size_t row_bytes = static_cast<size_t>(p.K) * (BITS == 0 ? 16 : BITS) / 8;
-  const uint8_t* base0 = blk.w + static_cast<size_t>(n0) * row_bytes +
-                         (lane & 3) * F::kLaneBytes;
-  const uint8_t* base1 = base0 + 8 * row_bytes;
-#pragma unroll
-  for (int gi = 0; gi < kGroupsPerStep; ++gi) {
-    const size_t off = static_cast<size_t>(gb * kGroupsPerStep + gi) * F::kGroupBytes;
-    if constexpr (F::kLaneBytes == 8) {
-      const uint2 v0 = __ldg(reinterpret_cast<const uint2*>(base0 + off));
-      const uint2 v1 = __ldg(reinterpret_cast<const uint2*>(base1 + off));
-      st.w0[gi][0] = v0.x; st.w0[gi][1] = v0.y;
-      st.w1[gi][0] = v1.x; st.w1[gi][1] = v1.y;
-    } else {
-#pragma unroll
-      for (int c = 0; c < F::kLaneBytes / 16; ++c) {
-        const uint4 v0 = ld_global_nc_v4(base0 + off + 16 * c);
-        const uint4 v1 = ld_global_nc_v4(base1 + off + 16 * c);
-        st.w0[gi][4 * c] = v0.x; st.w0[gi][4 * c + 1] = v0.y;
-        st.w0[gi][4 * c + 2] = v0.z; st.w0[gi][4 * c + 3] = v0.w;
-        st.w1[gi][4 * c] = v1.x; st.w1[gi][4 * c + 1] = v1.y;
-        st.w1[gi][4 * c + 2] = v1.z; st.w1[gi][4 * c + 3] = v1.w;
+// A position in a warp's list of steps: tile rows n0 .. n0 + 15 of block b,
+// step gb of the tile (advanced without divisions).
+struct StepPos {
+  int b, n0, gb;
+  __device__ __forceinline__ void advance(int steps_per_tile, int N) {
+    if (++gb == steps_per_tile) {
+      gb = 0;
+      n0 += 16;
+      if (n0 == N) {
+        n0 = 0;
+        ++b;
       }
     }
-    if constexpr (BITS != 0) {
-      const uint32_t* sbr = blk.sb + static_cast<size_t>(n0) * p.sb_stride + gb * kGroupsPerStep + gi;
-      st.sb0[gi] = __ldg(sbr);
-      st.sb1[gi] = __ldg(sbr + 8 * static_cast<size_t>(p.sb_stride));
-    }
   }
-  if ((gb + 1) * kGroupsPerStep * 64 == p.K) {  // the tile's last step: its rows' epilogue inputs
-    st.e0 = row_epi(p, blk, n0);
-    st.e1 = row_epi(p, blk, n0 + 8);
+};
+
+// Issues the copies of step `pos` into `slot` (this lane's share).
+template <int BITS>
+__device__ __forceinline__ void ring_load(const ModParams& p, const ModBlock* blocks, StepPos pos,
+                                          int lane, uint32_t slot) {
+  using R = RingFmt<BITS>;
+  const int b = pos.b, n0 = pos.n0, gb = pos.gb;
+  const ModBlock& blk = blocks[b];
+  const size_t row_bytes = static_cast<size_t>(p.K) * (BITS == 0 ? 16 : BITS) / 8;
+  const uint8_t* src = blk.w + static_cast<size_t>(n0) * row_bytes + static_cast<size_t>(gb) * R::kRowBytes;
+#pragma unroll
+  for (int c = lane; c < 16 * R::kCpr; c += 32) {
+    const int row = c / R::kCpr, cc = c % R::kCpr;
+    cp_async_16(slot + row * R::kRowBytes + ((cc ^ R::swz(row)) << 4),
+                src + static_cast<size_t>(row) * row_bytes + cc * 16);
+  }
+  if constexpr (BITS != 0) {
+    if (lane < 16)
+      cp_async_16(slot + R::kData + lane * 16,
+                  blk.sb + static_cast<size_t>(n0 + lane) * p.sb_stride + gb * kGroupsPerStep);
+  }
+  if ((gb + 1) * kGroupsPerStep * 64 == p.K && lane >= 16 && lane < 20) {
+    // the tile's last step: bias of its 16 rows, and the norm gain their
+    // (1 + scale) folds into (chunk 0: an1, chunk 2: fn1; none otherwise)
+    const uint32_t dst = slot + R::kData + R::kSb + 16 * (lane - 16);
+    const int half = (lane & 1) * 8;
+    if (lane < 18) {
+      cp_async_16(dst, blk.bias + n0 + half);
+    } else {
+      const uint16_t* g = nullptr;
+      if (n0 < p.H && blk.an1 != nullptr) g = blk.an1 + n0;
+      if (n0 >= 2 * p.H && n0 < 3 * p.H && blk.fn1 != nullptr) g = blk.fn1 + (n0 - 2 * p.H);
+      if (g != nullptr) cp_async_16(dst, g + half);
+    }
   }
 }
 
+// The lane's weights of (row, group gi) from a slot (a pointer into shared
+// memory), as the words mma_afrag takes.
 template <int BITS>
+__device__ __forceinline__ void ring_words(const uint8_t* slot, int row, int gi, int q,
+                                           uint32_t (&w)[MmaFmt<BITS>::kWords]) {
+  using R = RingFmt<BITS>;
+  const uint8_t* rb = slot + row * R::kRowBytes;
+  if constexpr (BITS == 8) {
+    const uint4 v = *reinterpret_cast<const uint4*>(rb + (((gi * 4 + q) ^ R::swz(row)) << 4));
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+  } else if constexpr (BITS == 4) {
+    const uint2 v = *reinterpret_cast<const uint2*>(
+        rb + (((gi * 2 + (q >> 1)) ^ R::swz(row)) << 4) + (q & 1) * 8);
+    w[0] = v.x; w[1] = v.y;
+  } else {
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const uint4 v = *reinterpret_cast<const uint4*>(rb + (((gi * 8 + 2 * q + c) ^ R::swz(row)) << 4));
+      w[4 * c] = v.x; w[4 * c + 1] = v.y; w[4 * c + 2] = v.z; w[4 * c + 3] = v.w;
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t pick4p(const uint4& v, int i) {
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+
+template <int BITS, int RING>
 __global__ void __launch_bounds__(kModThreads) mod_mma_kernel(const __grid_constant__ ModParams p) {
-  extern __shared__ uint8_t mod_smem[];
+  using R = RingFmt<BITS>;
+  extern __shared__ __align__(128) uint8_t mod_smem[];
   ModBlock* blocks = reinterpret_cast<ModBlock*>(mod_smem);
   const size_t blk_bytes = (static_cast<size_t>(p.n_blocks) * sizeof(ModBlock) + 15) & ~size_t(15);
   const int G = p.K / 64;
   uint2* bfrag = reinterpret_cast<uint2*>(mod_smem + blk_bytes);       // [G][4][32]
   float* tsum = reinterpret_cast<float*>(bfrag + static_cast<size_t>(G) * 4 * 32);  // [G][8]
+  const size_t ring_off = (blk_bytes + static_cast<size_t>(G) * 4 * 32 * 8 +
+                           static_cast<size_t>(G) * kMmaTok * 4 + 127) & ~size_t(127);
   for (int i = threadIdx.x; i < p.n_blocks; i += blockDim.x) blocks[i] = p.blocks[i];
   for (int i = threadIdx.x; i < G * 4 * 32; i += blockDim.x) {
     const int gi = i >> 7, s = (i >> 5) & 3, ln = i & 31;
@@ -331,7 +379,7 @@ __global__ void __launch_bounds__(kModThreads) mod_mma_kernel(const __grid_const
   __syncthreads();
 
   const int lane = threadIdx.x & 31;
-  const int q = lane & 3;
+  const int q = lane & 3, g = lane >> 2;
   const uint32_t code_xor = p.code_xor;
   // 1024 (affine) or 1152 (signed 8-bit codes, offset by 128), as f16x2
   const uint32_t magic2 = code_xor != 0u ? 0x64806480u : 0x64006400u;
@@ -342,45 +390,67 @@ __global__ void __launch_bounds__(kModThreads) mod_mma_kernel(const __grid_const
   long long t_begin, t_end;
   warp_slice(total_tiles, gw, nwarps, t_begin, t_end);
   if (t_begin >= t_end) return;
-  const long long st_end = (t_end - t_begin) * steps_per_tile;
+  const int st_end = static_cast<int>(t_end - t_begin) * steps_per_tile;
+  const int tiles_per_block = p.N / 16;
+  StepPos cpos;  // the step consumed next
+  cpos.b = static_cast<int>(t_begin / tiles_per_block);
+  cpos.n0 = static_cast<int>(t_begin - static_cast<long long>(cpos.b) * tiles_per_block) * 16;
+  cpos.gb = 0;
+  StepPos lpos = cpos;  // the step loaded next
+  uint8_t* const ring_p = mod_smem + ring_off + (threadIdx.x >> 5) * RING * R::kSlot;
+  const uint32_t ring = smem_u32(ring_p);
 
-  MmaStep<BITS> cur, nxt;
-  mma_load<BITS>(p, blocks, t_begin, 0, lane, cur);
+  // prologue: the first RING - 1 steps in flight (one commit group per step)
+#pragma unroll 1
+  for (int r = 0; r < RING - 1; ++r) {
+    if (r < st_end) {
+      ring_load<BITS>(p, blocks, lpos, lane, ring + r * R::kSlot);
+      lpos.advance(steps_per_tile, p.N);
+    }
+    cp_async_commit();
+  }
   float y[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // rows g, g + 8 x tokens 2q, 2q + 1
-  for (long long st = 0; st < st_end; ++st) {
-    const long long tile = t_begin + st / steps_per_tile;
-    const int gb = static_cast<int>(st % steps_per_tile);
-    if (st + 1 < st_end) {
-      const long long st1 = st + 1;
-      mma_load<BITS>(p, blocks, t_begin + st1 / steps_per_tile,
-                     static_cast<int>(st1 % steps_per_tile), lane, nxt);
+  int slot_c = 0, slot_l = RING - 1;  // ring slots of the consumed and the loaded step
+  for (int st = 0; st < st_end; ++st) {
+    if (st + RING - 1 < st_end) {
+      ring_load<BITS>(p, blocks, lpos, lane, ring + static_cast<uint32_t>(slot_l) * R::kSlot);
+      lpos.advance(steps_per_tile, p.N);
+    }
+    slot_l = slot_l + 1 == RING ? 0 : slot_l + 1;
+    cp_async_commit();
+    asm volatile("cp.async.wait_group %0;" ::"n"(RING - 1) : "memory");
+    __syncwarp();
+    const uint8_t* slot = ring_p + slot_c * R::kSlot;
+    slot_c = slot_c + 1 == RING ? 0 : slot_c + 1;
+    const int gb = cpos.gb;
+    uint4 sb0 = make_uint4(0u, 0u, 0u, 0u), sb1 = sb0;
+    if constexpr (BITS != 0) {
+      sb0 = *reinterpret_cast<const uint4*>(slot + R::kData + g * 16);
+      sb1 = *reinterpret_cast<const uint4*>(slot + R::kData + (g + 8) * 16);
     }
 #pragma unroll
     for (int gi = 0; gi < kGroupsPerStep; ++gi) {
       const int g_abs = gb * kGroupsPerStep + gi;
-      float c[4];
-      if constexpr (BITS == 0) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) c[j] = y[j];
-      } else {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) c[j] = 0.0f;
-      }
+      uint32_t w0[MmaFmt<BITS>::kWords], w1[MmaFmt<BITS>::kWords];
+      ring_words<BITS>(slot, g, gi, q, w0);
+      ring_words<BITS>(slot, g + 8, gi, q, w1);
+      float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // the group's own sums (independent chains)
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
         uint32_t a0, a2, a1, a3;
-        mma_afrag<BITS>(cur.w0[gi], s, code_xor, magic2, a0, a2);
-        mma_afrag<BITS>(cur.w1[gi], s, code_xor, magic2, a1, a3);
+        mma_afrag<BITS>(w0, s, code_xor, magic2, a0, a2);
+        mma_afrag<BITS>(w1, s, code_xor, magic2, a1, a3);
         const uint2 b = bfrag[(g_abs * 4 + s) * 32 + lane];
         mma_16816<BITS>(c, a0, a1, a2, a3, b.x, b.y);
       }
       if constexpr (BITS == 0) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) y[j] = c[j];
+        for (int j = 0; j < 4; ++j) y[j] += c[j];
       } else {
+        const uint32_t sw0 = pick4p(sb0, gi), sw1 = pick4p(sb1, gi);
         const float2 ts = *reinterpret_cast<const float2*>(&tsum[g_abs * kMmaTok + 2 * q]);
-        const float s0 = bf16_bits_to_f32(cur.sb0[gi] & 0xFFFFu), b0 = bf16_bits_to_f32(cur.sb0[gi] >> 16);
-        const float s1 = bf16_bits_to_f32(cur.sb1[gi] & 0xFFFFu), b1 = bf16_bits_to_f32(cur.sb1[gi] >> 16);
+        const float s0 = bf16_bits_to_f32(sw0 & 0xFFFFu), b0 = bf16_bits_to_f32(sw0 >> 16);
+        const float s1 = bf16_bits_to_f32(sw1 & 0xFFFFu), b1 = bf16_bits_to_f32(sw1 >> 16);
         y[0] += fmaf(s0, c[0], b0 * ts.x);
         y[1] += fmaf(s0, c[1], b0 * ts.y);
         y[2] += fmaf(s1, c[2], b1 * ts.x);
@@ -389,20 +459,27 @@ __global__ void __launch_bounds__(kModThreads) mod_mma_kernel(const __grid_const
     }
     if (gb + 1 == steps_per_tile) {
       // the tile's rows are complete: rows g and g + 8, tokens 2q and 2q + 1
-      const long long r0 = tile * 16 + (lane >> 2);
-      const int b = static_cast<int>(r0 / p.N);
-      const int n0 = static_cast<int>(r0 - static_cast<long long>(b) * p.N);
+      const int b = cpos.b, n0 = cpos.n0;
+      const bool has_gain = (n0 < p.H && blocks[b].an1 != nullptr) ||
+                            (n0 >= 2 * p.H && n0 < 3 * p.H && blocks[b].fn1 != nullptr);
       for (int h = 0; h < 2; ++h) {
-        for (int e = 0; e < 2; ++e) {
-          const int m = 2 * q + e;
-          if (m < p.M) write_token(p, blocks[b], b, n0 + 8 * h, m, y[2 * h + e], h ? cur.e1 : cur.e0);
+        const int rr = g + 8 * h;
+        const uint16_t* epi = reinterpret_cast<const uint16_t*>(slot + R::kData + R::kSb);
+        RowEpi e;
+        e.bias = epi[rr];
+        e.gain = has_gain ? epi[16 + rr] : 0u;
+        for (int ee = 0; ee < 2; ++ee) {
+          const int m = 2 * q + ee;
+          if (m < p.M) write_token(p, blocks[b], b, n0 + rr, m, y[2 * h + ee], e);
         }
       }
 #pragma unroll
       for (int j = 0; j < 4; ++j) y[j] = 0.0f;
     }
-    cur = nxt;
+    cpos.advance(steps_per_tile, p.N);
+    __syncwarp();  // every lane has read the slot before a later step's copies reuse it
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 // ---- generic path: a warp per row -------------------------------------------
@@ -453,9 +530,9 @@ __global__ void __launch_bounds__(kModThreads) mod_warp_kernel(const __grid_cons
   const long long gw = static_cast<long long>(blockIdx.x) * kModWarps + (threadIdx.x >> 5);
   long long r_begin, r_end;
   warp_slice(total_rows, gw, nwarps, r_begin, r_end);
-  for (long long r = r_begin; r < r_end; ++r) {
-    const int b = static_cast<int>(r / p.N);
-    const int n = static_cast<int>(r - static_cast<long long>(b) * p.N);
+  int b = static_cast<int>(r_begin / p.N);
+  int n = static_cast<int>(r_begin - static_cast<long long>(b) * p.N);
+  for (long long r = r_begin; r < r_end; ++r, n = (n + 1 == p.N ? 0 : n + 1), b += (n == 0)) {
     const ModBlock& blk = blocks[b];
     const uint8_t* row = blk.w + static_cast<size_t>(n) * row_bytes;
     float acc[MT];
@@ -555,18 +632,36 @@ cudaError_t launch_mod_warp(const ModParams& p, cudaStream_t stream) {
   return launch_persistent(mod_warp_kernel<BITS, MT>, p, smem, rows, cache, stream);
 }
 
-template <int BITS>
-cudaError_t launch_mod_mma(const ModParams& p, cudaStream_t stream) {
-  const size_t blk_bytes = (static_cast<size_t>(p.n_blocks) * sizeof(ModBlock) + 15) & ~size_t(15);
-  const int G = p.K / 64;
-  const size_t smem = blk_bytes + static_cast<size_t>(G) * 4 * 32 * 8 +
-                      static_cast<size_t>(G) * kMmaTok * 4;
+template <int BITS, int RING>
+cudaError_t launch_mod_mma_ring(const ModParams& p, size_t fixed, cudaStream_t stream) {
+  const size_t smem = fixed + static_cast<size_t>(kModWarps) * RING * RingFmt<BITS>::kSlot;
   const long long tiles = static_cast<long long>(p.n_blocks) * p.N / 16;
   static std::atomic<int> cache[64];
-  return launch_persistent(mod_mma_kernel<BITS>, p, smem, tiles, cache, stream);
+  return launch_persistent(mod_mma_kernel<BITS, RING>, p, smem, tiles, cache, stream);
 }
 
-bool mma_shape(int n, int k) { return k % (64 * kGroupsPerStep) == 0 && n % 16 == 0; }
+// The deepest ring (steps in flight per warp) that fits the shared memory
+// beside the block table and the B fragments (which grow with K).
+template <int BITS>
+cudaError_t launch_mod_mma(const ModParams& p, cudaStream_t stream) {
+  constexpr int kDeep = BITS == 4 ? 9 : (BITS == 8 ? 5 : 3);
+  const size_t blk_bytes = (static_cast<size_t>(p.n_blocks) * sizeof(ModBlock) + 15) & ~size_t(15);
+  const int G = p.K / 64;
+  const size_t fixed = (blk_bytes + static_cast<size_t>(G) * 4 * 32 * 8 +
+                        static_cast<size_t>(G) * kMmaTok * 4 + 127) & ~size_t(127);
+  constexpr size_t kLimit = 227 * 1024;
+  auto fits = [&](int ring, int slot) {
+    return fixed + static_cast<size_t>(kModWarps) * ring * slot <= kLimit;
+  };
+  if (fits(kDeep, RingFmt<BITS>::kSlot)) return launch_mod_mma_ring<BITS, kDeep>(p, fixed, stream);
+  if (fits(3, RingFmt<BITS>::kSlot)) return launch_mod_mma_ring<BITS, 3>(p, fixed, stream);
+  if (fits(2, RingFmt<BITS>::kSlot)) return launch_mod_mma_ring<BITS, 2>(p, fixed, stream);
+  return cudaErrorInvalidValue;
+}
+
+// K a multiple of 256 and N of 64 (so the 16 rows of a tile share a block and
+// a chunk of the 4H outputs)
+bool mma_shape(int n, int k) { return k % (64 * kGroupsPerStep) == 0 && n % 64 == 0; }
 
 // The generic path's token count rounded up to 1, 2 or 4: registers scale with it.
 template <int BITS>

@@ -466,7 +466,7 @@ __device__ void pair_mma(const ProjParams& p, const PairSmem& sm, uint32_t tmem,
     const uint32_t acc_cols = kTokRows<NT> ? 2u * kBlockN : static_cast<uint32_t>(t.sub);
     const uint32_t sub_bytes = static_cast<uint32_t>(t.half) * 128u;
     uint32_t acc = 0;
-    for (int kt = t.kt_begin; kt < t.kt_end; ++kt, ++it) {
+    for (int kt = t.kt_begin; kt < t.kt_end && !aborted; ++kt, ++it) {
       const int s = static_cast<int>(it % stages);
       const uint32_t ph = (it / stages) & 1u;
       MP_TRACE_MARK(kTrMmaPre, static_cast<int>(it));
