@@ -627,7 +627,7 @@ def main() -> None:
                                     4 * H * 2 * n_img)
     mod_us = mod_ms * 1e3 / args.steps
     roofline["modulation"] = {
-        "kernel": "mod_mma_kernel", "bound": "hbm", "us_per_step": mod_us,
+        "kernel": "mod_lane_kernel", "bound": "hbm", "us_per_step": mod_us,
         "bytes_per_step": mod_bytes, "achieved_gbs": mod_bytes / (mod_us * 1e-6) / 1e9,
         "peak_gbs": peaks["hbm_gbs"],
         "frac": mod_bytes / (mod_us * 1e-6) / 1e9 / peaks["hbm_gbs"]}

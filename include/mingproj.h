@@ -149,6 +149,17 @@ int mp_get_strength(const mp_ctx* ctx, int slot, float* s);
  * own strength vectors uses it. */
 int mp_set_strengths_rows(mp_ctx* ctx, const float* s, const int32_t* row_starts, int batch);
 
+/* Rows of ONE image in the x of the launches that follow, when a launch holds
+ * several images of equal length with the same strengths (a CFG pass over
+ * both captions); 0 (the default) = every launch is one image, unless row
+ * segments are set, whose longest segment then counts. The token tile and
+ * the K splits of a projection and of its rank-space pre-GEMM (which fix the
+ * fp32 summation order) are chosen from this count, so each image of such a
+ * batch has the bits of its own launch. Not part of the state version: a
+ * graph keeps the choices of its capture. No counterpart in the reference,
+ * whose batches are per image. */
+int mp_set_image_rows(mp_ctx* ctx, int rows);
+
 /* A counter that every change of a strength (to another value), of the row
  * segments or of a LoRA binding advances. Launches captured into a CUDA graph
  * keep the strengths, segments and stacked factors of their capture: a graph

@@ -415,3 +415,57 @@ def test_reference_rounding_order_within_the_bar(ctx, bits):
     exact = O.projection(x, pw.data, pw.scales, pw.biases, n, k, bits, False, slots)
     assert O.rel_l2(y, two) <= TOL, f"vs reference order {O.rel_l2(y, two):.3e}"
     assert O.rel_l2(y, exact) <= TOL, f"vs exact {O.rel_l2(y, exact):.3e}"
+
+
+@pytest.mark.parametrize("bits,m,k,ranks", [
+    (8, 256, 3840, [4, 8, 8, 16, 16, 32, 32, 64]),   # config-2 context refiner, to_out
+    (8, 256, 10240, [4, 8, 8, 16, 16, 32, 32, 64]),  # config-2 context refiner, w2
+    (4, 512, 3840, [32] * 8),                        # config-3 context refiner, to_out
+])
+def test_small_m_split_k_matches_oracle_and_batches(ctx, bits, m, k, ranks):
+    """Few rows per image (the context refiner over a caption,
+    src/ming-dit.cc:2388-2420): the projection splits K across CTA pairs and
+    adds the fp32 partial sums in split order. Parity with the oracle on
+    sampled rows, and a batch of two images (row segments with their own
+    strengths) has each image's bits of its own call, because the token tile
+    and the split counts are chosen from one image's rows."""
+    rng = np.random.default_rng(bits * 1000 + m + k)
+    n = 3840
+    pw = P.synthetic_affine(rng, n, k, bits)
+    w = _upload(ctx, pw)
+    facs = []
+    for i, r in enumerate(ranks):
+        a, b = P.synthetic_lora(rng, n, k, r, b_std=0.05)
+        w.bind(i, a, b)
+        facs.append((a, b))
+    S = rng.uniform(-1.0, 1.5, size=(2, 8)).astype(np.float32)
+    x = _x(rng, 2 * m, k)
+    singles = []
+    try:
+        for g in range(2):
+            for i in range(8):
+                ctx.set_strength(i, float(S[g, i]))
+            ctx.reset_engagement()
+            singles.append(_bits(ctx.linear(w, _to_dev(x[g * m:(g + 1) * m]))))
+            launched = ctx.engagement()["kernels"]
+        ctx.set_strengths_rows(S, np.array([0, m, 2 * m], dtype=np.int32))
+        yb = ctx.linear(w, _to_dev(x))
+        ctx.clear_strengths_rows()
+        ctx.sync_check()
+    finally:
+        for i in range(8):
+            ctx.set_strength(i, 1.0)
+        w.free()
+    # pre-GEMM (with or without its reduce), split projection and its reduce
+    assert launched >= 3, f"{launched} kernels: the projection did not split K"
+    yb_bits = _bits(yb)
+    for g in range(2):
+        assert np.array_equal(yb_bits[g * m:(g + 1) * m], singles[g]), \
+            f"image {g} of the batch differs from its own call"
+    rows = np.sort(rng.choice(m, size=48, replace=False))
+    for g in range(2):
+        slots = [(facs[i][0], facs[i][1], float(S[g, i])) for i in range(8)]
+        xr = x[g * m + rows]
+        ref = O.projection(xr, pw.data, pw.scales, pw.biases, n, k, bits, False, slots)
+        err = O.rel_l2(P.bf16_bits_to_f32(singles[g][rows]).astype(np.float64), ref)
+        assert err <= TOL, f"image {g}: rel-L2 {err:.3e}"

@@ -25,7 +25,7 @@ int resident_pairs();
 int pick_ntok_pair(int m, int pairs);
 cudaError_t launch_wait_selftest(uint64_t limit_ns, uint32_t* err, cudaStream_t stream);
 cudaError_t launch_mod(const ModParams& p, cudaStream_t stream);
-int mod_tokens_per_launch(int n, int k);
+int mod_tokens_per_launch(int n, int k, int n_blocks);
 cudaError_t launch_rms_residual(const RmsResidualParams& p, cudaStream_t stream);
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream);
 }  // namespace mp
@@ -116,6 +116,7 @@ struct mp_ctx {
   int device = 0;
   std::string err = "";
   float strength[mp::kMaxSlots];
+  int image_rows = 0;  // rows of one image per launch (0: the launch, or its longest segment)
   int n_seg = 0;
   int32_t seg_start[mp::kMaxSegments + 1] = {};
   float seg_scale[mp::kMaxSegments][mp::kMaxSlots] = {};
@@ -222,6 +223,24 @@ int sub_tok(int ntok) { return std::min(ntok, mp::kMaxTok); }
 
 // Feature pairs (256 output rows) a projection of n outputs occupies.
 int pairs_of(int n) { return (n + 2 * mp::kBlockN - 1) / (2 * mp::kBlockN); }
+
+// Rows of one image of an m-row call: mp_set_image_rows' count, else the
+// longest row segment (mp_set_strengths_rows) when the call holds several
+// images, else m. Every choice that changes a row's accumulation order (token
+// tile, K splits of the projection and of its rank-space pre-GEMM) is made
+// from this count, so a batch of equal-length images has each image's bits of
+// its own call.
+int image_rows(const mp_ctx* c, int m) {
+  if (c->image_rows > 0) return std::min(c->image_rows, m);
+  if (c->n_seg <= 1) return m;
+  int most = 0;
+  for (int g = 0; g < c->n_seg; ++g) {
+    const int lo = std::min(std::max(c->seg_start[g], 0), m);
+    const int hi = std::min(std::max(c->seg_start[g + 1], lo), m);
+    most = std::max(most, hi - lo);
+  }
+  return most > 0 ? most : m;
+}
 
 uint32_t live_mask(const mp_ctx* c, const mp_weight* w) {
   uint32_t mask = 0;
@@ -470,7 +489,7 @@ int begin_launch(mp_ctx* c, ProjParams* p, const void* x, int64_t ldx, int k, in
   p->n_pairs = pairs;
   p->M = m;
   p->K = k;
-  p->n_tok = n_tok > 0 ? n_tok : mp::pick_ntok_pair(m, pairs);
+  p->n_tok = n_tok > 0 ? n_tok : mp::pick_ntok_pair(image_rows(c, m), pairs);
   p->tile_group = tile_group_for(2.0 * m * static_cast<double>(k), w_bytes, pairs);
   if (!encode_2d(&p->tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, k, m,
                  static_cast<uint64_t>(ldx) * 2, 64, static_cast<uint32_t>(sub_tok(p->n_tok) / 2),
@@ -558,7 +577,7 @@ namespace {
 int launch_lora_down(mp_ctx* c, const CUtensorMap& tm_a, int rtot, const mp::EpilogueScale& es,
                      const void* x, int64_t ldx, int k, int m, cudaStream_t stream) {
   const int base_kt = (k + mp::kBlockK - 1) / mp::kBlockK;
-  const mp::SplitChoice sc = mp::choose_ksplit(m, pairs_of(rtot), base_kt, rtot);
+  const mp::SplitChoice sc = mp::choose_ksplit(image_rows(c, m), pairs_of(rtot), base_kt, rtot);
   const int ks = sc.ksplit;
   ProjParams p;
   int rc = begin_launch(c, &p, x, ldx, k, m, &rtot, 1, 2.0 * rtot * k, sc.n_tok);
@@ -603,6 +622,10 @@ struct Prologue {
   const mp::EpilogueScale* es = nullptr;
 };
 
+// Split-K projections: per-image rows at most, and fp32 partial sums per image at most.
+constexpr int kSplitRows = 1024;
+constexpr size_t kSplitBytes = 32u << 20;
+
 constexpr int kFallback = -1;  // fused launch not possible: run the pre-GEMM separately
 
 // `count` projections of one x in one launch; sts[i] (nullable) is member
@@ -618,7 +641,8 @@ struct SwiGluLaunch {
 
 // With `hds`, every member is an attention-head member: ys[i] is its
 // head-major output [n / 128][m][128]; norm_w[i] (nullable) turns on the
-// head RMSNorm + rotary embedding for member i.
+// head RMSNorm + rotary embedding for member i. With may_alloc false the
+// launch grows no context buffer (the allocation-free entry point): no K split.
 struct HeadsLaunch {
   const uint16_t* const* norm_w = nullptr;
   float eps = 0.0f;
@@ -630,7 +654,7 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
                        const int64_t* ldys, const Stack* const* sts, const int* t_cols, int t_ld,
                        int count, const void* x, int64_t ldx, int m, cudaStream_t stream,
                        const Prologue* pro = nullptr, const SwiGluLaunch* swi = nullptr,
-                       const HeadsLaunch* hds = nullptr) {
+                       const HeadsLaunch* hds = nullptr, bool may_alloc = true) {
   ProjParams p;
   int ns[mp::kMaxMembers] = {0, 0, 0, 0};
   for (int i = 0; i < count; ++i) ns[i] = ws[i]->d.n;
@@ -639,12 +663,28 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
   const int members = swi != nullptr ? 1 : count;
   // SwiGLU pairs and attention-head launches run on 256- or 512-token tiles
   // only (their kernel instantiations)
+  const int mi = image_rows(c, m);
   int n_tok = 0;
-  if (swi != nullptr) n_tok = std::max(mp::kMaxTok, mp::pick_ntok_pair(m, pairs_of(ns[0])));
+  if (swi != nullptr) n_tok = std::max(mp::kMaxTok, mp::pick_ntok_pair(mi, pairs_of(ns[0])));
   if (hds != nullptr) {
     int pairs = 0;
     for (int i = 0; i < count; ++i) pairs += pairs_of(ns[i]);
-    n_tok = std::max(mp::kMaxTok, mp::pick_ntok_pair(m, pairs));
+    n_tok = std::max(mp::kMaxTok, mp::pick_ntok_pair(mi, pairs));
+  }
+  // A plain projection over few rows per image splits K across pairs: each
+  // split writes fp32 partial sums (the last one after the appended LoRA K
+  // tiles), lora_reduce_kernel adds them in split order and rounds to bf16.
+  // The split count and the token tile come from one image's rows, at most
+  // kSplitBytes of partial sums per image.
+  mp::SplitChoice msplit{0, 1, 0.0};
+  if (may_alloc && count == 1 && swi == nullptr && hds == nullptr && pro == nullptr && mi <= kSplitRows &&
+      ns[0] % 4 == 0 && ldys[0] % 4 == 0 && reinterpret_cast<uintptr_t>(ys[0]) % 8 == 0) {
+    const int base_kt = (ws[0]->d.k + mp::kBlockK - 1) / mp::kBlockK;
+    const size_t per_split = static_cast<size_t>(mi) * ns[0] * sizeof(float);
+    const int most = static_cast<int>(
+        std::min<size_t>(mp::kMaxSplits, std::max<size_t>(1, kSplitBytes / per_split)));
+    msplit = mp::choose_ksplit(mi, pairs_of(ns[0]), base_kt, ns[0], most);
+    if (msplit.ksplit > 1) n_tok = msplit.n_tok;
   }
   double w_bytes = 0.0;
   for (int i = 0; i < count; ++i) w_bytes += static_cast<double>(ws[i]->w_bytes);
@@ -658,9 +698,11 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
     // fewer, lengthen the launch by less than a separate pre-GEMM would take
     // (cycle model: ~1300 / 1150 cycles per 512-token quantized / dense stage,
     // the prologue's stages dense, ~6000-8000 per tile of set-up and
-    // epilogue; 1900 cycles per microsecond).
+    // epilogue; 1900 cycles per microsecond), modelled on one image's rows:
+    // the fused prologue computes T unsplit, a separate pre-GEMM may split K,
+    // so the choice must be the same for an image alone and in a batch.
     const int P = mp::resident_pairs();
-    const long long n_main = static_cast<long long>(p.n_pairs) * ((m + p.n_tok - 1) / p.n_tok);
+    const long long n_main = static_cast<long long>(p.n_pairs) * ((mi + p.n_tok - 1) / p.n_tok);
     const long long light_pairs = P - n_main % P;
     const int base_kt = (ws[0]->d.k + mp::kBlockK - 1) / mp::kBlockK;
     int lora_kt = 0;
@@ -670,13 +712,13 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
     const double c_stage = (ws[0]->d.bits != 0 ? 1300.0 : 1150.0) * (p.n_tok > mp::kMaxTok ? 1.0 : 0.6);
     const double t_main = (base_kt + lora_kt) * c_stage + 6000.0;
     const double t_pre = base_kt * 1150.0 + 8000.0;
-    const long long n_pre = static_cast<long long>((m + mp::kPreTok - 1) / mp::kPreTok) *
+    const long long n_pre = static_cast<long long>((mi + mp::kPreTok - 1) / mp::kPreTok) *
                             pairs_of(pro->rtot);
     const double heavy = static_cast<double>((n_main + P - 1) / P) * t_main;
     const double light = static_cast<double>((n_pre + light_pairs - 1) / light_pairs) * t_pre +
                          static_cast<double>(n_main / P) * t_main;
     const double fused_extra = std::max(0.0, light - heavy);
-    const double separate = (mp::choose_ksplit(m, pairs_of(pro->rtot), base_kt, pro->rtot).us + 3.0) *
+    const double separate = (mp::choose_ksplit(mi, pairs_of(pro->rtot), base_kt, pro->rtot).us + 3.0) *
                             1900.0;
     if (fused_extra >= separate) return kFallback;
   }
@@ -757,6 +799,30 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
     }
     c->eng.kernels += 1;
     c->eng.lora_down += 1;
+  } else if (msplit.ksplit > 1) {
+    const int ks = msplit.ksplit;
+    const int n = ns[0];
+    rc = ensure_buf(c, &c->part, &c->part_cap, static_cast<size_t>(ks) * m * n, stream);
+    if (rc != MP_OK) return rc;
+    const int base_kt = (ws[0]->d.k + mp::kBlockK - 1) / mp::kBlockK;
+    p.ksplit = ks;
+    p.kt_per_split = (base_kt + ks - 1) / ks;
+    p.part = c->part;
+    p.part_ld = n;
+    rc = run_launch(c, p, stream, "proj_pair_kernel (split K)");
+    if (rc != MP_OK) return rc;
+    mp::ReduceParams rp;
+    std::memset(&rp, 0, sizeof(rp));  // scale.enabled = 0: the sums are stored unscaled
+    rp.part = c->part;
+    rp.ksplit = ks;
+    rp.M = m;
+    rp.R = n;
+    rp.part_ld = n;
+    rp.out = static_cast<uint16_t*>(ys[0]);
+    rp.out_ld = static_cast<int32_t>(ldys[0]);
+    cudaError_t e = mp::launch_lora_reduce(rp, stream);
+    if (e != cudaSuccess) return cuda_fail(c, e, "lora_reduce_kernel (split-K projection)");
+    c->eng.kernels += 1;
   } else {
     rc = run_launch(c, p, stream, "proj_pair_kernel");
     if (rc != MP_OK) return rc;
@@ -1161,6 +1227,13 @@ int mp_set_strengths_rows(mp_ctx* c, const float* s, const int32_t* row_starts, 
   return MP_OK;
 }
 
+int mp_set_image_rows(mp_ctx* c, int rows) {
+  if (c == nullptr) return MP_EINVAL;
+  if (rows < 0) return fail(c, MP_EINVAL, "image rows %d < 0", rows);
+  c->image_rows = rows;
+  return MP_OK;
+}
+
 int mp_linear(mp_ctx* c, const mp_weight* wc, const void* x, int64_t ldx, void* y, int64_t ldy,
               int m, void* stream) {
   if (c == nullptr || wc == nullptr) return MP_EINVAL;
@@ -1547,7 +1620,7 @@ int mp_modulation_all(mp_ctx* c, const mp_modset* set, const void* temb, int m, 
   p.m_stride = m;
   // launches of at most a few tokens (8 on the tensor-core path); every
   // token's row is computed the same way whichever launch holds it
-  const int per_launch = mp::mod_tokens_per_launch(set->n, set->k);
+  const int per_launch = mp::mod_tokens_per_launch(set->n, set->k, set->n_blocks);
   for (int m0 = 0; m0 < m; m0 += per_launch) {
     p.M = std::min(per_launch, m - m0);
     p.temb = static_cast<const uint16_t*>(temb) + static_cast<size_t>(m0) * set->k;
@@ -1652,7 +1725,8 @@ extern "C" int mp_linear_lora_static(mp_ctx* c, const mp_weight* w, const void* 
   if (strength == 0.0f) {
     const Stack* none[1] = {nullptr};
     const int cols[1] = {0};
-    return launch_projections(c, wl, yl, ll, none, cols, 0, 1, x, ldx, m, s);
+    return launch_projections(c, wl, yl, ll, none, cols, 0, 1, x, ldx, m, s, nullptr, nullptr,
+                              nullptr, /*may_alloc=*/false);
   }
 
   // Rank-space pre-GEMM into the static array: all rpad columns are written

@@ -159,7 +159,7 @@ struct ModParams {
   uint32_t code_xor;
   float code_magic;
   int32_t sb_stride;
-  int32_t M;               // tokens of this launch (<= kModMaxTok)
+  int32_t M;               // tokens of this launch (<= 8; <= kModMaxTok off the lane path)
   int32_t m_stride;        // tokens per block in the output arrays (>= M)
   const uint16_t* temb;    // bf16 [M, K]
   uint16_t* mods;          // bf16 [n_blocks, m_stride, N] (token 0 of this launch)
@@ -167,8 +167,8 @@ struct ModParams {
   uint16_t* nw3;           // bf16 [n_blocks, m_stride, H] or null
 };
 
-constexpr int kModMaxTok = 4;      // tokens of one launch (registers scale with it)
-constexpr int kModMaxBatch = 16;   // tokens of one mp_modulation_all call (launches of <= 4)
+constexpr int kModMaxTok = 4;      // tokens of one generic-path launch (registers scale with it)
+constexpr int kModMaxBatch = 16;   // tokens of one mp_modulation_all call (several launches)
 
 // The sandwich-norm residual step (mp_norm.cu), per token row r < M:
 //   s   = bf16(o * rsqrt(mean(o^2) + eps) * o_gain)          (o != null)

@@ -754,15 +754,24 @@ __device__ void rows_plain(const ProjParams& p, const ProjMember& mb, uint32_t a
     const int fcol = pf0 + 64 * r;
     if (fcol >= mb.N) break;
     const uint32_t buf = stg + (round & 1u) * kWarpStageBytes;
+    // both 32-column halves of the box in flight before one wait
+    uint32_t v0[32], v1[32];
+    MP_TMEM_LD_32X32B_X32(acc + static_cast<uint32_t>(64 * r), v0);
+    MP_TMEM_LD_32X32B_X32(acc + static_cast<uint32_t>(64 * r + 32), v1);
+    MP_TMEM_WAIT_LD_REGS32(v0);
+    MP_TMEM_WAIT_LD_REGS32(v1);
     stage_acquire(lane);
-    for (int h = 0; h < 2; ++h) {
-      uint32_t v[32];
-      MP_TMEM_LD_32X32B_X32(acc + static_cast<uint32_t>(64 * r + 32 * h), v);
-      MP_TMEM_WAIT_LD_REGS32(v);
-      if (scaled) scale_columns(p.scale, same_seg, g, 64 * r + 32 * h, slots, scales, v);
+    {
+      if (scaled) scale_columns(p.scale, same_seg, g, 64 * r, slots, scales, v0);
       uint32_t w[16];
-      pack_words(v, w);
-      stage_words(buf, lane, h, w);
+      pack_words(v0, w);
+      stage_words(buf, lane, 0, w);
+    }
+    {
+      if (scaled) scale_columns(p.scale, same_seg, g, 64 * r + 32, slots, scales, v1);
+      uint32_t w[16];
+      pack_words(v1, w);
+      stage_words(buf, lane, 1, w);
     }
     stage_store(mb, buf, fcol, tok0, lane);
     ++round;

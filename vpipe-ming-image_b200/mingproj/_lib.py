@@ -67,6 +67,7 @@ SIGNATURES = {
     "mp_set_strength": (C.c_int, [_vp, C.c_int, C.c_float]),
     "mp_get_strength": (C.c_int, [_vp, C.c_int, C.POINTER(C.c_float)]),
     "mp_set_strengths_rows": (C.c_int, [_vp, C.POINTER(C.c_float), C.POINTER(_i32), C.c_int]),
+    "mp_set_image_rows": (C.c_int, [_vp, C.c_int]),
     "mp_state_version": (C.c_int, [_vp, C.POINTER(C.c_uint64)]),
     "mp_linear": (C.c_int, [_vp, _vp, _vp, _i64, _vp, _i64, C.c_int, _vp]),
     "mp_linear_shared": (C.c_int, [_vp, C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_i64), C.c_int,

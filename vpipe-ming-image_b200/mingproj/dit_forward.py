@@ -234,6 +234,8 @@ class DitForward:
         cfg, pre = self.cfg, self.dims.block_prefix(b)
         t = self.t
         R = x.shape[0] // nb
+        # the kernels' tile and K-split choices follow one sequence's rows
+        self.ctx.set_image_rows(R if nb > 1 else 0)
         H, nh, hd, FF = cfg.dim, cfg.n_heads, cfg.head_dim, cfg.ffn
         p = self.proj.blocks[b].proj
         modulated = mod_idx is not None
@@ -376,6 +378,7 @@ class DitForward:
                       dim=0)
         for i in range(cfg.n_layers):
             j = self._block(2 * nref + i, j, cos, sin, nref + i, mods, nw1, nw3, nb=B)
+        self.ctx.set_image_rows(0)
         L = j.shape[0] // B
         out = []
         for bi in range(B):

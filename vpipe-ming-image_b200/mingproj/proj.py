@@ -223,6 +223,12 @@ class Context:
             self.h, s.ctypes.data_as(C.POINTER(C.c_float)),
             r.ctypes.data_as(C.POINTER(C.c_int32)), batch))
 
+    def set_image_rows(self, rows: int) -> None:
+        """Rows of one image in the launches that follow (0: each launch is
+        one image): a batch of equal-length images then has each image's bits
+        of its own launch."""
+        self._check(self.lib.mp_set_image_rows(self.h, int(rows)))
+
     def clear_strengths_rows(self) -> None:
         self._check(self.lib.mp_set_strengths_rows(self.h, None, None, 0))
 
