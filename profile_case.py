@@ -11,8 +11,9 @@ projection (mp_linear: rank-space pre-GEMM + fused projection) or the
 attention (mp_attention over head-major q / k / v of m rows), GB/s for the
 gated sandwich-norm residual step (mp_rms_residual over m rows of width k)
 and for the batched modulation (mp_modulation_all over 32 blocks' adaLN
-weights [4 * 3840, k] for m tokens; every call is preceded by a write of a
-256 MB buffer, so the weights come from HBM, not L2). Holds only that call's
+weights [4 * 3840, k] for m tokens; every call is preceded by a read of a
+256 MB buffer, so the weights come from HBM, not L2, and no dirty line is
+written back during the call). Holds only that call's
 tensors on the device, so it is a small case for `ncu`.
 """
 from __future__ import annotations
@@ -79,14 +80,16 @@ def _modulation(a, ctx, dev, gen) -> None:
         fn1.append(torch.ones(H, device=dev, dtype=torch.bfloat16))
     mset = ctx.modulation_set(ws, bias, an1, fn1)
     temb = torch.randn((a.m, K), device=dev, generator=gen).to(torch.bfloat16)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush = torch.ones(64 << 20, dtype=torch.int32, device=dev)  # 256 MB, read before each call
     for _ in range(a.warmup):
         ctx.modulation(mset, temb)
     ctx.sync_check()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(a.reps)]
     for e0, e1 in ev:
-        flush.fill_(1)  # evicts the weights from L2
+        # evicts the weights from L2 by reading, so no dirty line of the flush
+        # is written back while the timed call runs
+        flush.sum()
         e0.record()
         ctx.modulation(mset, temb)
         e1.record()

@@ -21,8 +21,9 @@ def _dev(bits):
 @pytest.mark.parametrize("m", [1, 2, 4, 8])
 @pytest.mark.parametrize("H,K", [(256, 256), (384, 3840), (256, 192)])
 def test_modulation_matches_oracle(ctx, bits, m, H, K):
-    """K 256 and 3840 take the tensor-core path (up to 8 tokens per launch),
-    K 192 the generic one (4 tokens per launch: 8 tokens are two launches)."""
+    """K 256 and 3840 take the lane-per-row path (up to 8 tokens per launch,
+    4 at K 3840), K 192 the generic one (4 tokens per launch: 8 tokens are two
+    launches)."""
     rng = np.random.default_rng(bits * 100 + m * 10 + H)
     nb = 3
     ws, pws, biases, an1, fn1 = [], [], [], [], []
@@ -60,9 +61,9 @@ def test_modulation_matches_oracle(ctx, bits, m, H, K):
 def test_modulation_rows_independent_of_batch(ctx, bits, H, K):
     """A token's modulation row has the same bits whether it is computed alone
     (M = 1, one image) or inside a batch (M = 2, 4 or 8: one launch on the
-    tensor-core path, where a token is one MMA column; two launches of 4 on
-    the generic path): the batched DiT forward relies on it for image i to
-    equal its own forward."""
+    lane-per-row path, where each token runs its own FMA chains; two launches
+    of 4 on the generic path): the batched DiT forward relies on it for image
+    i to equal its own forward."""
     rng = np.random.default_rng(7 + bits + K)
     nb = 2
     ws, biases, an1, fn1 = [], [], [], []

@@ -141,7 +141,7 @@ __device__ __forceinline__ void warp_slice(long long total, long long w, long lo
 
 // ---- lane-per-row path: K a multiple of 256, H a multiple of 32 -------------
 // A warp takes tiles of 32 weight rows of one block, lane r owning row r. Per
-// step (the rows' next kStepGroups 64-wide groups) the lane reads its row's
+// step (the rows' next 128 bytes: 2 groups w8, 4 w4, 1 bf16) the lane reads its row's
 // 16-byte chunks from the warp's ring slot, turns the codes into exact fp32
 // integers (chunk_pair: a byte-permute into the float 2^23 + q, one packed
 // subtraction) and forms every token's dot with packed fp32 FMAs against the
@@ -154,18 +154,21 @@ __device__ __forceinline__ void warp_slice(long long total, long long w, long lo
 constexpr int kLaneRows = 32;
 constexpr int kLaneTok = 8;  // tokens of one launch, at most
 
+// A step is 128 bytes of each of the tile's 32 rows: 2 groups (w8), 4 (w4)
+// or 1 (bf16).
 template <int BITS>
 struct LaneFmt {
-  static constexpr int kStepGroups = BITS == 0 ? 2 : 4;                  // 64-wide groups per step
   static constexpr int kGroupBytes = 64 * (BITS == 0 ? 16 : BITS) / 8;   // 128, 64, 32
-  static constexpr int kRowBytes = kStepGroups * kGroupBytes;            // one row, one step
+  static constexpr int kRowBytes = 128;                                  // one row, one step
+  static constexpr int kStepGroups = kRowBytes / kGroupBytes;
   static constexpr int kCpr = kRowBytes / 16;                            // 16-byte chunks per row
   static constexpr int kCpg = kGroupBytes / 16;                          // chunks per group
   static constexpr int kData = kLaneRows * kRowBytes;
-  static constexpr int kSb = BITS == 0 ? 0 : kLaneRows * 16;             // 4 groups' words per row
+  static constexpr int kSbRow = BITS == 0 ? 0 : 4 * kStepGroups;         // scale/bias bytes per row
+  static constexpr int kSb = kLaneRows * kSbRow;
   static constexpr int kEpi = 2 * kLaneRows * 2;                         // bias, gain (bf16)
   static constexpr int kSlot = (kData + kSb + kEpi + 127) / 128 * 128;
-  static_assert(kCpr >= 8, "the XOR swizzle needs 8 chunks per row");
+  static_assert(kCpr == 8, "the XOR swizzle spans 8 chunks per row");
 };
 
 // A position in a warp's list of steps: rows n0 .. n0 + 31 of block b, step
@@ -202,9 +205,16 @@ __device__ __forceinline__ void lane_load(const ModParams& p, const ModBlock* bl
     cp_async_16(slot + row * L::kRowBytes + ((cc ^ (row & 7)) << 4),
                 src + static_cast<size_t>(row) * row_bytes + cc * 16);
   }
-  if constexpr (BITS != 0)
-    cp_async_16(slot + L::kData + lane * 16,
-                blk.sb + static_cast<size_t>(pos.n0 + lane) * p.sb_stride + pos.gb * L::kStepGroups);
+  if constexpr (BITS != 0) {
+    const uint32_t* sb =
+        blk.sb + static_cast<size_t>(pos.n0 + lane) * p.sb_stride + pos.gb * L::kStepGroups;
+    if constexpr (L::kSbRow == 16)
+      cp_async_16(slot + L::kData + lane * 16, sb);
+    else
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(slot + L::kData + lane * 8),
+                   "l"(sb)
+                   : "memory");
+  }
   if (pos.gb + 1 == steps_per_tile && lane < 8) {
     // lanes 0-3: bias of rows 8j .. 8j + 7; lanes 4-7: the norm gain the
     // rows' (1 + scale) folds into (chunk 0: an1, chunk 2: fn1; none otherwise)
@@ -236,7 +246,7 @@ __host__ __device__ __forceinline__ size_t lane_fixed_bytes(int n_blocks, int K)
 }
 
 template <int BITS, int MT, int RING>
-__global__ void __launch_bounds__(kModThreads) mod_lane_kernel(const __grid_constant__ ModParams p) {
+__global__ void __launch_bounds__(kModThreads, 1) mod_lane_kernel(const __grid_constant__ ModParams p) {
   using L = LaneFmt<BITS>;
   using F = ModFmt<BITS>;
   extern __shared__ __align__(128) uint8_t mod_smem[];
@@ -324,7 +334,13 @@ __global__ void __launch_bounds__(kModThreads) mod_lane_kernel(const __grid_cons
     const uint8_t* rowp = slot + lane * L::kRowBytes;
     const int sw = lane & 7;
     uint4 sbv = make_uint4(0u, 0u, 0u, 0u);
-    if constexpr (BITS != 0) sbv = *reinterpret_cast<const uint4*>(slot + L::kData + lane * 16);
+    if constexpr (L::kSbRow == 16) {
+      sbv = *reinterpret_cast<const uint4*>(slot + L::kData + lane * 16);
+    } else if constexpr (L::kSbRow == 8) {
+      const uint2 v = *reinterpret_cast<const uint2*>(slot + L::kData + lane * 8);
+      sbv.x = v.x;
+      sbv.y = v.y;
+    }
     // temb quads of this step's K range (token 0)
     const float4* tstep = tq + cpos.gb * L::kStepGroups * 16;
 #pragma unroll
@@ -549,16 +565,17 @@ cudaError_t launch_mod_lane_ring(const ModParams& p, cudaStream_t stream) {
   return launch_persistent(mod_lane_kernel<BITS, MT, RING>, p, smem, tiles, cache, stream);
 }
 
-// The deepest ring (steps in flight per warp, kDeep at most) that fits the
+// The deepest ring (steps in flight per warp, 6 at most) that fits the
 // shared memory beside the block table and the temb copy (which grows with K).
 template <int BITS, int MT>
 cudaError_t launch_mod_lane(const ModParams& p, cudaStream_t stream) {
-  constexpr int kDeep = BITS == 4 ? 5 : 3;
   const size_t fixed = lane_fixed_bytes<BITS, MT>(p.n_blocks, p.K);
   auto fits = [&](int ring) {
     return fixed + static_cast<size_t>(kModWarps) * ring * LaneFmt<BITS>::kSlot <= kModSmemLimit;
   };
-  if (fits(kDeep)) return launch_mod_lane_ring<BITS, MT, kDeep>(p, stream);
+  if (fits(6)) return launch_mod_lane_ring<BITS, MT, 6>(p, stream);
+  if (fits(4)) return launch_mod_lane_ring<BITS, MT, 4>(p, stream);
+  if (fits(3)) return launch_mod_lane_ring<BITS, MT, 3>(p, stream);
   if (fits(2)) return launch_mod_lane_ring<BITS, MT, 2>(p, stream);
   return cudaErrorInvalidValue;
 }
@@ -590,7 +607,10 @@ cudaError_t launch_mod_bits(const ModParams& p, cudaStream_t stream) {
 // a two-slot ring beside the fp32 temb copy.
 int mod_tokens_per_launch(int n, int k, int n_blocks) {
   if (!lane_shape(n, k)) return kModMaxTok;
-  const size_t ring2 = static_cast<size_t>(kModWarps) * 2 * LaneFmt<8>::kSlot;
+  size_t slot = LaneFmt<8>::kSlot;
+  if (LaneFmt<4>::kSlot > slot) slot = LaneFmt<4>::kSlot;
+  if (LaneFmt<0>::kSlot > slot) slot = LaneFmt<0>::kSlot;
+  const size_t ring2 = static_cast<size_t>(kModWarps) * 2 * slot;
   for (int mt = kLaneTok; mt > 1; mt >>= 1) {
     const size_t blk = (static_cast<size_t>(n_blocks) * sizeof(ModBlock) + 15) & ~size_t(15);
     const size_t fixed = (blk + static_cast<size_t>(mt) * k * 4 + static_cast<size_t>(k / 64) * mt * 4 +
