@@ -131,9 +131,20 @@ class DitRef:
         f = rms(self.lin(h, pre + "feed_forward.w2", False), w[pre + "ffn_norm2.weight"], eps)
         return x + (torch.tanh(g_mlp) * f if temb is not None else f)
 
-    def forward(self, latents, cap, query_rows: int, grid_h: int, grid_w: int, sigma: float):
+    def forward(self, latents, cap, query_rows: int, grid_h: int, grid_w: int, sigma: float,
+                trace_dir: str | None = None):
         """latents [img, patch_dim]; cap [cap_len, >= dim] with stream A in
-        rows [0, query_rows) x columns [0, cap_feat_dim). Returns [img, patch_dim]."""
+        rows [0, query_rows) x columns [0, cap_feat_dim). Returns [img, patch_dim].
+        With trace_dir, writes the stages the reference traces
+        (src/ming-dit.cc:2304, 2413, 2545) as raw float32 files <tag>.f32:
+        embed, ctx, blk<L>."""
+        def trace(tag, rows):
+            if trace_dir is not None:
+                import os
+                os.makedirs(trace_dir, exist_ok=True)
+                rows.detach().float().numpy().astype("float32").tofile(
+                    os.path.join(trace_dir, tag + ".f32"))
+
         dt = self.dtype
         latents = torch.as_tensor(latents).to(dt)
         cap = torch.as_tensor(cap).to(dt)
@@ -146,16 +157,23 @@ class DitRef:
         te = torch.nn.functional.silu(self.lin(emb[None], "t_embedder.mlp.0"))
         temb = self.lin(te, "t_embedder.mlp.2")[0]
         x = self.lin(latents, X_EMBEDDER)
+        x0, xs = x, []
         for i in range(self.n_refiner):
             x = self.block(x, f"noise_refiner.{i}.", cos[:img], sin[:img], temb)
+            xs.append(x)
         ca = rms(cap[:query_rows, : self.cap_feat_dim], self.w["cap_embedder.0.weight"], self.eps)
         ca = self.lin(ca, "cap_embedder.1")
         cj = torch.cat([ca, cap[query_rows:, : self.dim]], dim=0)
+        trace("embed", torch.cat([x0, cj], dim=0))
         for i in range(self.n_refiner):
             cj = self.block(cj, f"context_refiner.{i}.", cos[img:], sin[img:], None)
+        trace("ctx", cj)
+        for i in range(self.n_refiner):
+            trace(f"blk{i}", torch.cat([xs[i], cj], dim=0))
         j = torch.cat([x, cj], dim=0)
         for i in range(self.n_layers):
             j = self.block(j, f"layers.{i}.", cos, sin, temb)
+            trace(f"blk{self.n_refiner + i}", j)
         scale = self.lin(torch.nn.functional.silu(temb)[None], FINAL + ".adaLN_modulation.1")[0]
         xi = torch.nn.functional.layer_norm(j[:img], (self.dim,), eps=1e-6) * (1.0 + scale)
         return self.lin(xi, FINAL + ".linear")

@@ -401,3 +401,27 @@ def test_config_keys_drive_the_slots(ctx, tmp_path):
     assert torch.equal(z.view(torch.int16), base.view(torch.int16)), "lora2_scale 0 != base"
     assert torch.equal(h2.view(torch.int16), h.view(torch.int16)), "back to 0.5 != first"
     assert torch.equal(h3.view(torch.int16), h.view(torch.int16)), "ignored path changed it"
+
+
+def test_stage_trace_matches_oracle(ctx, dense, tmp_path, monkeypatch):
+    """VPIPE_MING_DIT_TRACE (the reference's per-stage trace,
+    src/ming-dit.cc:1658-1687): the forward writes the reference's stages
+    (embed, ctx, blk<L>) as raw float32 rows, and each is within the forward's
+    bar of the fp32 restatement's same stage."""
+    fwd, w = dense
+    gd, rd = tmp_path / "gpu", tmp_path / "ref"
+    monkeypatch.setenv("VPIPE_MING_DIT_TRACE", str(gd))
+    _gpu(fwd, "case_a")
+    ctx.sync_check()
+    monkeypatch.delenv("VPIPE_MING_DIT_TRACE")
+    lat, cap, q, gh, gw = fx.make_inputs("case_a")
+    DitRef(fx.as_f32(w), fx.DIM, fx.HEADS, fx.NREF, fx.NLAY, fx.CAPF).forward(
+        P.bf16_bits_to_f32(lat), P.bf16_bits_to_f32(cap), q, gh, gw, fx.SIGMA, trace_dir=str(rd))
+    tags = ["embed", "ctx"] + [f"blk{i}" for i in range(fx.NREF + fx.NLAY)]
+    assert sorted(p.stem for p in gd.glob("*.f32")) == sorted(tags)
+    for tag in tags:
+        a = np.fromfile(gd / f"{tag}.f32", np.float32)
+        b = np.fromfile(rd / f"{tag}.f32", np.float32)
+        assert a.shape == b.shape and a.size > 0, tag
+        err = O.rel_l2(a, b)
+        assert err <= BAR, f"{tag}: rel-L2 {err:.4f} > {BAR}"

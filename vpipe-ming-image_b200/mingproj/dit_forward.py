@@ -15,6 +15,7 @@ RoPE, timestep sinusoid f32 then bf16.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -26,6 +27,7 @@ from .pack import PROJ_NAMES, PackedWeight, bf16_bits_to_f32
 from .packio import Pack
 from .proj import Context
 
+TRACE_ENV = "VPIPE_MING_DIT_TRACE"  # the reference's per-stage trace switch
 X_EMBEDDER = "all_x_embedder.2-1"
 FINAL = "all_final_layer.2-1"
 SEQ_MULTIPLE = 32
@@ -290,6 +292,26 @@ class DitForward:
                                   eps=cfg.norm_eps)
         return x
 
+    # ---- per-stage trace -----------------------------------------------------
+    def _trace_dir(self) -> str | None:
+        """The per-stage dump directory, read from VPIPE_MING_DIT_TRACE as the
+        reference's forward reads it (src/ming-dit.cc:1658-1687). When set, a
+        single-image eager forward writes each stage's rows as raw float32
+        files <dir>/<tag>.f32, the tags of the reference: `embed` (the joint
+        rows after the x and caption embedders), `ctx` (the caption rows after
+        the context refiner), `blk<L>` (the joint rows after block L of the
+        noise refiners, then the main layers). It synchronises the device, so
+        a traced run is not a timing run; a CUDA-graph capture never traces."""
+        d = os.environ.get(TRACE_ENV)
+        if not d or torch.cuda.is_current_stream_capturing():
+            return None
+        return d
+
+    @staticmethod
+    def _trace(d: str, tag: str, rows: torch.Tensor) -> None:
+        os.makedirs(d, exist_ok=True)
+        rows.float().cpu().numpy().astype(np.float32).tofile(os.path.join(d, tag + ".f32"))
+
     # ---- the forward -------------------------------------------------------
     @torch.no_grad()
     def forward(self, latents: torch.Tensor, cap: torch.Tensor, query_rows: int, grid_h: int,
@@ -312,9 +334,15 @@ class DitForward:
         B, sig = self._check_batch(latents, caps, sigmas)
         img = grid_h * grid_w
         cos, sin = self._rope_dev(grid_h, grid_w, caps[0].shape[0])
-        cj = [self._context(cp, query_rows, cos[img:], sin[img:]) for cp in caps]
-        return self._core(latents.to(self.dev), self._timestep_emb(sig).to(self.dev), cj,
-                          cos, sin, img)
+        self._tracing = self._trace_dir() if B == 1 else None
+        if self._tracing:
+            self._cap_cache.clear()  # the embedded caption rows are traced too
+        try:
+            cj = [self._context(cp, query_rows, cos[img:], sin[img:]) for cp in caps]
+            return self._core(latents.to(self.dev), self._timestep_emb(sig).to(self.dev), cj,
+                              cos, sin, img)
+        finally:
+            self._tracing = None
 
     def graph(self, batch: int, query_rows: int, grid_h: int, grid_w: int,
               cap_len: int) -> "ForwardGraph":
@@ -372,12 +400,19 @@ class DitForward:
         mods, nw1, nw3 = self.ctx.modulation(self.modset, temb.contiguous())
         x = torch.cat([self._linear(lat[bi], X_EMBEDDER) for bi in range(B)])
         nref = cfg.n_refiner
+        tr = getattr(self, "_tracing", None)
+        if tr:
+            self._trace(tr, "embed", torch.cat([x, self._trace_cap]))
         for i in range(nref):
             x = self._block(nref + i, x, cos[:img], sin[:img], i, mods, nw1, nw3, nb=B)
+            if tr:
+                self._trace(tr, f"blk{i}", torch.cat([x, cj[0]]))
         j = torch.cat([t for bi in range(B) for t in (x[bi * img:(bi + 1) * img], cj[bi])],
                       dim=0)
         for i in range(cfg.n_layers):
             j = self._block(2 * nref + i, j, cos, sin, nref + i, mods, nw1, nw3, nb=B)
+            if tr:
+                self._trace(tr, f"blk{nref + i}", j)
         self.ctx.set_image_rows(0)
         L = j.shape[0] // B
         out = []
@@ -416,8 +451,13 @@ class DitForward:
         ca = self._rms(key[:query_rows, : cfg.cap_feat_dim], self.t["cap_embedder.0.weight"])
         ca = self._linear(ca, "cap_embedder.1")
         cj = torch.cat([ca, key[query_rows:, : cfg.dim]], dim=0)
+        tr = getattr(self, "_tracing", None)
+        if tr:
+            self._trace_cap = cj.clone()
         for i in range(cfg.n_refiner):
             cj = self._block(i, cj, cos, sin, None, None, None, None)
+        if tr:
+            self._trace(tr, "ctx", cj)
         if self.cap_cache_entries > 0:
             if len(self._cap_cache) >= self.cap_cache_entries:
                 self._cap_cache.remove(min(self._cap_cache, key=lambda e: e["tick"]))
