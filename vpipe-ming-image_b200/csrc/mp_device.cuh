@@ -71,6 +71,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Programmatic dependent launch. pdl_wait: this grid's reads and writes of
+// global memory may start (the grids it depends on have completed and their
+// writes are visible); a no-op when the launch did not allow the overlap.
+// pdl_release: the next launch on the stream may begin its set-up (it still
+// waits in its own pdl_wait).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_release() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Waits until the phase with `parity` has completed. Gives up after
 // `limit_ns` (recording `site` in *abort) or as soon as another role of the
 // CTA has given up.

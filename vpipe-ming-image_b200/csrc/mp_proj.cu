@@ -1247,6 +1247,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = *sm.tmem_slot;
+  // set-up done (shared memory, TMEM, tensor maps): global memory from here on
+  pdl_wait();
+  pdl_release();
 
   if (warp == 0) {
     if (lane == 0) pair_producer<NT>(p, sm, leader, rank, base_kt);
@@ -1333,6 +1336,8 @@ cudaError_t launch_wait_selftest(uint64_t limit_ns, uint32_t* err, cudaStream_t 
 // split loads are in flight together and added in split order.
 __global__ void __launch_bounds__(256) lora_reduce_kernel(const __grid_constant__ ReduceParams p,
                                                           int rows_step) {
+  pdl_wait();
+  pdl_release();
   const int cols4 = p.R / 4;
   const int tid = static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x);
   if (tid >= cols4 * rows_step) return;
@@ -1388,8 +1393,16 @@ cudaError_t launch_lora_reduce(const ReduceParams& p, cudaStream_t stream) {
   if (rows_step < 1) rows_step = 1;
   const long long threads = static_cast<long long>(cols4) * rows_step;
   const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
-  lora_reduce_kernel<<<blocks, 256, 0, stream>>>(p, rows_step);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, lora_reduce_kernel, p, rows_step);
 }
 
 namespace {
@@ -1460,8 +1473,18 @@ cudaError_t launch_nt(const ProjParams& q, int pairs, bool cooperative, cudaStre
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, proj_pair_kernel<NT, EPI>, q);
   }
-  proj_pair_kernel<NT, EPI><<<dim3(2 * pairs, 1, 1), kPairThreads, smem_bytes<EPI>(), stream>>>(q);
-  return cudaGetLastError();
+  // may begin its set-up while the previous launch on the stream finishes
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kPairThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem_bytes<EPI>();
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, proj_pair_kernel<NT, EPI>, q);
 }
 
 }  // namespace
