@@ -17,9 +17,10 @@
 //  * Lane-per-row path (K a multiple of 256 -- the reference's 256 and the
 //    [4H, 3840] shape -- and H a multiple of 32): tiles of 32 rows, each
 //    lane one row, the rows streamed through a per-warp cp.async ring in
-//    shared memory; per 64-wide group every token's dot is packed fp32 FMAs
-//    against temb broadcast from shared memory, no cross-lane reduction (see
-//    mod_lane_kernel).
+//    shared memory; per 64-wide group every token's dot is exact integer
+//    dp4a against 8-bit limbs of its temb values (packed codes) or packed
+//    fp32 FMAs (bf16 weights), temb broadcast from shared memory, no
+//    cross-lane reduction (see mod_lane_kernel).
 //  * Generic path (any other K): a warp per row, lanes striding over the
 //    row's 16-byte chunks in fp32 FMAs, temb from shared memory, a full warp
 //    reduction per row.
@@ -141,16 +142,16 @@ __device__ __forceinline__ void warp_slice(long long total, long long w, long lo
 
 // ---- lane-per-row path: K a multiple of 256, H a multiple of 32 -------------
 // A warp takes tiles of 32 weight rows of one block, lane r owning row r. Per
-// step (the rows' next 128 bytes: 2 groups w8, 4 w4, 1 bf16) the lane reads its row's
-// 16-byte chunks from the warp's ring slot, turns the codes into exact fp32
-// integers (chunk_pair: a byte-permute into the float 2^23 + q, one packed
-// subtraction) and forms every token's dot with packed fp32 FMAs against the
-// token's temb values, read from shared memory at the same address by all
-// lanes (a broadcast). No lane exchanges anything: a packed group folds in as
-// s * sum(q t) + b * sum(t), bf16 weights add their group sums. A token's
-// group sum is two interleaved chains (even / odd weight pairs) in K order,
-// whatever the launch's token count, so a row's result has the same bits in
-// any launch (a CFG batch equals its per-image launches).
+// step (the rows' next 128 bytes: 2 groups w8, 4 w4, 1 bf16) the lane reads
+// its row's 16-byte chunks from the warp's ring slot and forms every token's
+// dot against values all lanes read from shared memory at the same address (a
+// broadcast): for packed codes exact integer dots (dp4a) with the token's temb
+// limbs (see lane_fixed_bytes), for bf16 weights packed fp32 FMAs with its
+// fp32 temb values in two interleaved chains in K order. No lane exchanges
+// anything: a packed group folds in as s * sum(q t) + b * sum(t), bf16
+// weights add their group sums. A token's operations do not depend on the
+// launch's token count, so a row's result has the same bits in any launch (a
+// CFG batch equals its per-image launches).
 constexpr int kLaneRows = 32;
 constexpr int kLaneTok = 8;  // tokens of one launch, at most
 
@@ -236,13 +237,41 @@ __device__ __forceinline__ uint32_t pick4p(const uint4& v, int i) {
   return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
 }
 
-// Shared memory: the block table, temb as fp32 [MT][K] (zero past M), the
-// per-(group, token) temb sums [K / 64][MT], then the warps' rings.
+// Packed codes take integer dot products. Each token's temb values of a
+// 64-wide group (bf16: 8 significant bits) are written exactly as integers
+// T = t * 2^(21 - E), E the exponent of the group's largest |t| (values more
+// than 14 binades below it are rounded to the nearest integer: an absolute
+// error of at most 2^(E - 22)), and T as three signed 8-bit limbs,
+// T = L0 + 2^8 L1 + 2^16 L2 (|L2| <= 64). Then sum_k q_k t_k =
+// 2^(E - 21) (A0 + 2^8 A1 + 2^16 A2) with A_l = sum_k q_k L_l,k exact in
+// 32-bit integers, formed four codes at a time with dp4a. Integer sums do
+// not depend on their order, so a token's result is the same in any launch.
+//
+// Shared memory for packed codes: the block table, the limbs int8
+// [MT][K / 64][3][64] (w4: within each 8 values the even ones first, as a
+// code word's low nibbles hold them), per (group, token) the scale 2^(E - 21),
+// the temb sum and the three limb sums [K / 64][MT]; for bf16 weights temb as
+// fp32 [MT][K] and nothing else. Then the warps' rings.
 template <int BITS, int MT>
 __host__ __device__ __forceinline__ size_t lane_fixed_bytes(int n_blocks, int K) {
   const size_t blk = (static_cast<size_t>(n_blocks) * sizeof(ModBlock) + 15) & ~size_t(15);
-  return (blk + static_cast<size_t>(MT) * K * 4 + static_cast<size_t>(K / 64) * MT * 4 + 127) &
-         ~size_t(127);
+  const size_t t = BITS == 0 ? static_cast<size_t>(MT) * K * 4
+                             : static_cast<size_t>(MT) * K * 3 + static_cast<size_t>(K / 64) * MT * 20;
+  return (blk + t + 127) & ~size_t(127);
+}
+
+// Position of value k (within its 64-wide group) in a limb row.
+template <int BITS>
+__device__ __forceinline__ int limb_pos(int k) {
+  if constexpr (BITS == 4) return (k & ~7) + ((k & 1) ? 4 : 0) + ((k & 7) >> 1);
+  return k;
+}
+
+// a: four unsigned 8-bit codes, b: four signed 8-bit limbs, c + sum a_i b_i.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
 }
 
 template <int BITS, int MT, int RING>
@@ -254,34 +283,74 @@ __global__ void __launch_bounds__(kModThreads, 1) mod_lane_kernel(const __grid_c
   const size_t blk_bytes = (static_cast<size_t>(p.n_blocks) * sizeof(ModBlock) + 15) & ~size_t(15);
   const int G = p.K / 64;
   const int K4 = p.K / 4;
-  float4* tq = reinterpret_cast<float4*>(mod_smem + blk_bytes);                 // [MT][K / 4]
-  float* tsum = reinterpret_cast<float*>(tq + static_cast<size_t>(MT) * K4);    // [G][MT]
+  float4* tq = reinterpret_cast<float4*>(mod_smem + blk_bytes);                 // bf16: [MT][K / 4]
+  int8_t* tl = reinterpret_cast<int8_t*>(mod_smem + blk_bytes);                 // packed: limbs
+  float* tmul = reinterpret_cast<float*>(tl + static_cast<size_t>(MT) * p.K * 3);  // [G][MT]
+  float* tsum = tmul + G * MT;                                                  // [G][MT]
+  int* tls = reinterpret_cast<int*>(tsum + G * MT);                             // [G][MT][3]
   for (int i = threadIdx.x; i < p.n_blocks; i += blockDim.x) blocks[i] = p.blocks[i];
-  for (int i = threadIdx.x; i < MT * K4; i += blockDim.x) {
-    const int m = i / K4, k4 = i - (i / K4) * K4;
-    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (m < p.M) {
-      const uint16_t* t = p.temb + static_cast<size_t>(m) * p.K + 4 * k4;
-      v = make_float4(bf16_bits_to_f32(t[0]), bf16_bits_to_f32(t[1]), bf16_bits_to_f32(t[2]),
-                      bf16_bits_to_f32(t[3]));
+  if constexpr (BITS == 0) {
+    for (int i = threadIdx.x; i < MT * K4; i += blockDim.x) {
+      const int m = i / K4, k4 = i - (i / K4) * K4;
+      float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (m < p.M) {
+        const uint16_t* t = p.temb + static_cast<size_t>(m) * p.K + 4 * k4;
+        v = make_float4(bf16_bits_to_f32(t[0]), bf16_bits_to_f32(t[1]), bf16_bits_to_f32(t[2]),
+                        bf16_bits_to_f32(t[3]));
+      }
+      tq[i] = v;
     }
-    tq[i] = v;
-  }
-  if constexpr (BITS != 0) {
-    // per (group, token) the sum of its 64 temb values: a warp each, lanes
-    // adding two values, then a fixed xor tree (the same bits for a token
-    // whatever else the launch holds)
+  } else {
+    // a warp per (group, token): lanes take values wl and 32 + wl; the
+    // group's largest |t|, its limbs, the limb sums (exact integers) and the
+    // temb sum (a fixed xor tree: the same bits for a token whatever else the
+    // launch holds)
     const int wl = threadIdx.x & 31;
     for (int i = threadIdx.x >> 5; i < G * MT; i += kModWarps) {
       const int gi = i / MT, n = i - (i / MT) * MT;
-      float v = 0.0f;
+      float t0 = 0.0f, t1 = 0.0f;
       if (n < p.M) {
         const uint16_t* t = p.temb + static_cast<size_t>(n) * p.K + gi * 64;
-        v = bf16_bits_to_f32(t[wl]) + bf16_bits_to_f32(t[32 + wl]);
+        t0 = bf16_bits_to_f32(t[wl]);
+        t1 = bf16_bits_to_f32(t[32 + wl]);
+      }
+      float amax = fmaxf(fabsf(t0), fabsf(t1));
+      float v = t0 + t1;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+        v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+      }
+      // E: the exponent of amax (0 for an all-zero group)
+      const int e = amax > 0.0f ? static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu) - 127 : 0;
+      int lsum[3] = {0, 0, 0};
+      int8_t* row = tl + (static_cast<size_t>(n) * G + gi) * 192;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int k = wl + 32 * h;
+        const int T = __float2int_rn(ldexpf(h == 0 ? t0 : t1, 21 - e));
+        const int l0 = static_cast<int>(static_cast<int8_t>(T & 0xFF));
+        const int t1r = (T - l0) >> 8;
+        const int l1 = static_cast<int>(static_cast<int8_t>(t1r & 0xFF));
+        const int l2 = (t1r - l1) >> 8;
+        row[limb_pos<BITS>(k)] = static_cast<int8_t>(l0);
+        row[64 + limb_pos<BITS>(k)] = static_cast<int8_t>(l1);
+        row[128 + limb_pos<BITS>(k)] = static_cast<int8_t>(l2);
+        lsum[0] += l0;
+        lsum[1] += l1;
+        lsum[2] += l2;
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
-      if (wl == 0) tsum[i] = v;
+      for (int l = 0; l < 3; ++l)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lsum[l] += __shfl_xor_sync(0xFFFFFFFFu, lsum[l], o);
+      if (wl == 0) {
+        tmul[i] = ldexpf(1.0f, e - 21);
+        tsum[i] = v;
+        tls[3 * i] = lsum[0];
+        tls[3 * i + 1] = lsum[1];
+        tls[3 * i + 2] = lsum[2];
+      }
     }
   }
   __syncthreads();
@@ -341,45 +410,96 @@ __global__ void __launch_bounds__(kModThreads, 1) mod_lane_kernel(const __grid_c
       sbv.x = v.x;
       sbv.y = v.y;
     }
-    // temb quads of this step's K range (token 0)
-    const float4* tstep = tq + cpos.gb * L::kStepGroups * 16;
 #pragma unroll
     for (int gi = 0; gi < L::kStepGroups; ++gi) {
-      uint64_t acc[MT][2];
+      const int g_abs = cpos.gb * L::kStepGroups + gi;
+      if constexpr (BITS == 0) {
+        // bf16 weights: packed fp32 FMAs against temb broadcast from shared memory
+        const float4* tstep = tq + cpos.gb * L::kStepGroups * 16;
+        uint64_t acc[MT][2];
 #pragma unroll
-      for (int m = 0; m < MT; ++m) acc[m][0] = acc[m][1] = f32x2(0.0f, 0.0f);
+        for (int m = 0; m < MT; ++m) acc[m][0] = acc[m][1] = f32x2(0.0f, 0.0f);
 #pragma unroll
-      for (int c = 0; c < L::kCpg; ++c) {
-        const int ch = gi * L::kCpg + c;
-        const uint4 w = *reinterpret_cast<const uint4*>(rowp + ((ch ^ sw) << 4));
-        uint64_t q[F::kPairs];
+        for (int c = 0; c < L::kCpg; ++c) {
+          const int ch = gi * L::kCpg + c;
+          const uint4 w = *reinterpret_cast<const uint4*>(rowp + ((ch ^ sw) << 4));
+          uint64_t q[F::kPairs];
 #pragma unroll
-        for (int pp = 0; pp < F::kPairs; ++pp) q[pp] = chunk_pair<BITS>(w, pp, p.code_xor, neg_magic2);
+          for (int pp = 0; pp < F::kPairs; ++pp) q[pp] = chunk_pair<0>(w, pp, 0u, neg_magic2);
 #pragma unroll
-        for (int m = 0; m < MT; ++m) {
-          const float4* tm = tstep + static_cast<size_t>(m) * K4 + ch * (F::kPer / 4);
+          for (int m = 0; m < MT; ++m) {
+            const float4* tm = tstep + static_cast<size_t>(m) * K4 + ch * (F::kPer / 4);
 #pragma unroll
-          for (int qq = 0; qq < F::kPer / 4; ++qq) {
-            const float4 t = tm[qq];
-            acc[m][0] = fma_f32x2(q[2 * qq], f32x2(t.x, t.y), acc[m][0]);
-            acc[m][1] = fma_f32x2(q[2 * qq + 1], f32x2(t.z, t.w), acc[m][1]);
+            for (int qq = 0; qq < F::kPer / 4; ++qq) {
+              const float4 t = tm[qq];
+              acc[m][0] = fma_f32x2(q[2 * qq], f32x2(t.x, t.y), acc[m][0]);
+              acc[m][1] = fma_f32x2(q[2 * qq + 1], f32x2(t.z, t.w), acc[m][1]);
+            }
           }
         }
-      }
-      if constexpr (BITS == 0) {
 #pragma unroll
         for (int m = 0; m < MT; ++m)
           y[m] += (f32x2_lo(acc[m][0]) + f32x2_hi(acc[m][0])) +
                   (f32x2_lo(acc[m][1]) + f32x2_hi(acc[m][1]));
       } else {
+        // packed codes: exact integer dots with the three temb limbs
+        int a[MT][3];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) a[m][0] = a[m][1] = a[m][2] = 0;
+#pragma unroll
+        for (int c = 0; c < L::kCpg; ++c) {
+          const int ch = gi * L::kCpg + c;
+          const uint4 w = *reinterpret_cast<const uint4*>(rowp + ((ch ^ sw) << 4));
+          uint32_t cw[8];  // w8: 4 words of 4 codes; w4: low / high nibbles of 4 words
+          if constexpr (BITS == 8) {
+            cw[0] = w.x ^ p.code_xor;
+            cw[1] = w.y ^ p.code_xor;
+            cw[2] = w.z ^ p.code_xor;
+            cw[3] = w.w ^ p.code_xor;
+          } else {
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              cw[2 * i] = ws[i] & 0x0F0F0F0Fu;
+              cw[2 * i + 1] = (ws[i] >> 4) & 0x0F0F0F0Fu;
+            }
+          }
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            const int8_t* lr = tl + (static_cast<size_t>(m) * G + g_abs) * 192 + c * F::kPer;
+#pragma unroll
+            for (int l = 0; l < 3; ++l) {
+              const uint4 l0 = *reinterpret_cast<const uint4*>(lr + 64 * l);
+              if constexpr (BITS == 8) {
+                a[m][l] = dp4a_us(cw[0], l0.x, a[m][l]);
+                a[m][l] = dp4a_us(cw[1], l0.y, a[m][l]);
+                a[m][l] = dp4a_us(cw[2], l0.z, a[m][l]);
+                a[m][l] = dp4a_us(cw[3], l0.w, a[m][l]);
+              } else {
+                const uint4 l1 = *reinterpret_cast<const uint4*>(lr + 64 * l + 16);
+                a[m][l] = dp4a_us(cw[0], l0.x, a[m][l]);
+                a[m][l] = dp4a_us(cw[1], l0.y, a[m][l]);
+                a[m][l] = dp4a_us(cw[2], l0.z, a[m][l]);
+                a[m][l] = dp4a_us(cw[3], l0.w, a[m][l]);
+                a[m][l] = dp4a_us(cw[4], l1.x, a[m][l]);
+                a[m][l] = dp4a_us(cw[5], l1.y, a[m][l]);
+                a[m][l] = dp4a_us(cw[6], l1.z, a[m][l]);
+                a[m][l] = dp4a_us(cw[7], l1.w, a[m][l]);
+              }
+            }
+          }
+        }
         const uint32_t sbw = pick4p(sbv, gi);
         const float sc = bf16_bits_to_f32(sbw & 0xFFFFu), bi = bf16_bits_to_f32(sbw >> 16);
-        const float* ts = tsum + (cpos.gb * L::kStepGroups + gi) * MT;
+        const int off = p.code_xor != 0u ? 128 : 0;  // signed codes entered as q + 128
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
-          const float d = (f32x2_lo(acc[m][0]) + f32x2_hi(acc[m][0])) +
-                          (f32x2_lo(acc[m][1]) + f32x2_hi(acc[m][1]));
-          y[m] += __fmaf_rn(sc, d, __fmul_rn(bi, ts[m]));
+          const int i = g_abs * MT + m;
+          const float a0 = static_cast<float>(a[m][0] - off * tls[3 * i]);
+          const float a1 = static_cast<float>(a[m][1] - off * tls[3 * i + 1]);
+          const float a2 = static_cast<float>(a[m][2] - off * tls[3 * i + 2]);
+          const float d = __fmul_rn(__fmaf_rn(65536.0f, a2, __fmaf_rn(256.0f, a1, a0)), tmul[i]);
+          y[m] += __fmaf_rn(sc, d, __fmul_rn(bi, tsum[i]));
         }
       }
     }
