@@ -91,6 +91,7 @@ struct mp_modset {
   int n_blocks = 0;
   int n = 0, k = 0, bits = 0, mode = 0, sb_stride = 0;
   mp::ModBlock* dev_blocks = nullptr;
+  CUtensorMap* dev_maps = nullptr;  // per block: weight rows, 128-byte x 32-row boxes
   std::vector<void*> owned;  // bias / gain copies
 };
 
@@ -1575,12 +1576,38 @@ int mp_modulation_create(mp_ctx* c, int n_blocks, const mp_weight* const* ada,
       return r;
     }
   }
+  // the lane-per-row kernel (K a multiple of 256, N of 128) streams 32 rows x
+  // 128 bytes per step with one TMA; other shapes take the generic kernel
+  const bool lane_maps = d0.k % 256 == 0 && d0.n % 128 == 0;
+  std::vector<CUtensorMap> hm(lane_maps ? n_blocks : 0);
+  for (int i = 0; i < static_cast<int>(hm.size()); ++i) {
+    const mp_weight* w = ada[i];
+    bool ok;
+    if (d0.bits != 0) {
+      const uint64_t row_bytes = static_cast<uint64_t>(d0.k) * d0.bits / 8;
+      ok = encode_2d(&hm[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, w->w, row_bytes, d0.n, row_bytes, 128,
+                     32, CU_TENSOR_MAP_SWIZZLE_128B);
+    } else {
+      ok = encode_2d(&hm[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w->w, d0.k, d0.n,
+                     static_cast<uint64_t>(w->kp) * 2, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    if (!ok) {
+      for (void* p : set->owned) cudaFree(p);
+      delete set;
+      return fail(c, MP_ECUDA, "tensor map encode failed (modulation weights)");
+    }
+  }
   cudaError_t e = cudaMalloc(&set->dev_blocks, sizeof(mp::ModBlock) * n_blocks);
   if (e == cudaSuccess)
     e = cudaMemcpy(set->dev_blocks, hb.data(), sizeof(mp::ModBlock) * n_blocks,
                    cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && lane_maps) e = cudaMalloc(&set->dev_maps, sizeof(CUtensorMap) * n_blocks);
+  if (e == cudaSuccess && lane_maps)
+    e = cudaMemcpy(set->dev_maps, hm.data(), sizeof(CUtensorMap) * n_blocks, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) {
     for (void* p : set->owned) cudaFree(p);
+    cudaFree(set->dev_blocks);
+    cudaFree(set->dev_maps);
     delete set;
     return cuda_fail(c, e, "modulation table upload");
   }
@@ -1594,6 +1621,7 @@ int mp_modulation_free(mp_ctx* c, mp_modset* set) {
   cudaDeviceSynchronize();
   for (void* p : set->owned) cudaFree(p);
   cudaFree(set->dev_blocks);
+  cudaFree(set->dev_maps);
   delete set;
   return MP_OK;
 }
@@ -1618,6 +1646,9 @@ int mp_modulation_all(mp_ctx* c, const mp_modset* set, const void* temb, int m, 
   p.code_magic = sym ? 8388736.0f : 8388608.0f;
   p.sb_stride = set->sb_stride;
   p.m_stride = m;
+  p.maps = set->dev_maps;
+  p.err = c->err_word;
+  p.wait_limit_ns = c->wait_limit_ns;
   // launches of at most a few tokens (8 on the tensor-core path); every
   // token's row is computed the same way whichever launch holds it
   const int per_launch = mp::mod_tokens_per_launch(set->n, set->k, set->n_blocks);

@@ -165,6 +165,11 @@ struct ModParams {
   uint16_t* mods;          // bf16 [n_blocks, m_stride, N] (token 0 of this launch)
   uint16_t* nw1;           // bf16 [n_blocks, m_stride, H] or null
   uint16_t* nw3;           // bf16 [n_blocks, m_stride, H] or null
+  // per block: its weight rows [N, K] as a 2-D tensor map with 128-byte x
+  // 32-row boxes and the 128-byte swizzle (lane-per-row path)
+  const CUtensorMap* maps;
+  uint32_t* err;           // device error word
+  uint64_t wait_limit_ns;
 };
 
 constexpr int kModMaxTok = 4;      // tokens of one generic-path launch (registers scale with it)

@@ -16,8 +16,8 @@
 //
 //  * Lane-per-row path (K a multiple of 256 -- the reference's 256 and the
 //    [4H, 3840] shape -- and H a multiple of 32): tiles of 32 rows, each
-//    lane one row, the rows streamed through a per-warp cp.async ring in
-//    shared memory; per 64-wide group every token's dot is exact integer
+//    lane one row, the rows streamed through a per-warp ring in shared
+//    memory (one TMA per step); per 64-wide group every token's dot is exact integer
 //    dp4a against 8-bit limbs of its temb values (packed codes) or packed
 //    fp32 FMAs (bf16 weights), temb broadcast from shared memory, no
 //    cross-lane reduction (see mod_lane_kernel).
@@ -154,6 +154,11 @@ __device__ __forceinline__ void warp_slice(long long total, long long w, long lo
 // CFG batch equals its per-image launches).
 constexpr int kLaneRows = 32;
 constexpr int kLaneTok = 8;  // tokens of one launch, at most
+#ifndef MP_LANE_WARPS
+#define MP_LANE_WARPS 16
+#endif
+constexpr int kLaneWarps = MP_LANE_WARPS;  // warps per CTA (one CTA per SM: the rings)
+constexpr int kLaneThreads = 32 * kLaneWarps;
 
 // A step is 128 bytes of each of the tile's 32 rows: 2 groups (w8), 4 (w4)
 // or 1 (bf16).
@@ -164,12 +169,13 @@ struct LaneFmt {
   static constexpr int kStepGroups = kRowBytes / kGroupBytes;
   static constexpr int kCpr = kRowBytes / 16;                            // 16-byte chunks per row
   static constexpr int kCpg = kGroupBytes / 16;                          // chunks per group
-  static constexpr int kData = kLaneRows * kRowBytes;
+  static constexpr int kData = kLaneRows * kRowBytes;                    // one TMA box
   static constexpr int kSbRow = BITS == 0 ? 0 : 4 * kStepGroups;         // scale/bias bytes per row
   static constexpr int kSb = kLaneRows * kSbRow;
   static constexpr int kEpi = 2 * kLaneRows * 2;                         // bias, gain (bf16)
-  static constexpr int kSlot = (kData + kSb + kEpi + 127) / 128 * 128;
-  static_assert(kCpr == 8, "the XOR swizzle spans 8 chunks per row");
+  static constexpr int kAux = (kSb + kEpi + 15) / 16 * 16;
+  static constexpr int kSlot = kData + kAux + 8;                         // data, aux, barrier
+  static_assert(kCpr == 8, "the 128-byte swizzle spans 8 chunks per row");
 };
 
 // A position in a warp's list of steps: rows n0 .. n0 + 31 of block b, step
@@ -188,38 +194,36 @@ struct StepPos {
   }
 };
 
-// Issues the copies of step `pos` into `slot` (this lane's share): the 32
-// rows' chunks (chunk c of row r at chunk position c ^ (r & 7), so the lanes'
-// row reads are conflict-free), their scale/bias words, and with the tile's
-// last step their bias and norm gain.
+// Issues the copies of step `pos` (this lane's share): lane 0 the 32 rows'
+// 128 bytes by one TMA into `data` (the 128-byte swizzle puts chunk c of row r
+// at chunk position c ^ (r & 7), so the lanes' row reads are conflict-free),
+// completing on `bar`; every lane its row's scale/bias words, and with the
+// tile's last step lanes 0-7 the rows' bias and norm gain, into `aux`
+// (cp.async).
 template <int BITS>
 __device__ __forceinline__ void lane_load(const ModParams& p, const ModBlock* blocks, StepPos pos,
-                                          int steps_per_tile, int lane, uint32_t slot) {
+                                          int steps_per_tile, int lane, uint32_t data, uint32_t aux,
+                                          uint32_t bar) {
   using L = LaneFmt<BITS>;
   const ModBlock& blk = blocks[pos.b];
-  const size_t row_bytes = static_cast<size_t>(p.K) * (BITS == 0 ? 16 : BITS) / 8;
-  const uint8_t* src =
-      blk.w + static_cast<size_t>(pos.n0) * row_bytes + static_cast<size_t>(pos.gb) * L::kRowBytes;
-#pragma unroll
-  for (int c = lane; c < kLaneRows * L::kCpr; c += 32) {
-    const int row = c / L::kCpr, cc = c % L::kCpr;
-    cp_async_16(slot + row * L::kRowBytes + ((cc ^ (row & 7)) << 4),
-                src + static_cast<size_t>(row) * row_bytes + cc * 16);
+  if (lane == 0) {
+    // the 32 rows' next 128 bytes: chunk c of row r lands at c ^ (r & 7)
+    mbar_arrive_expect_tx(bar, L::kData);
+    tma_load_2d(data, p.maps + pos.b, bar, pos.gb * (BITS == 0 ? 64 : L::kRowBytes), pos.n0);
   }
   if constexpr (BITS != 0) {
     const uint32_t* sb =
         blk.sb + static_cast<size_t>(pos.n0 + lane) * p.sb_stride + pos.gb * L::kStepGroups;
     if constexpr (L::kSbRow == 16)
-      cp_async_16(slot + L::kData + lane * 16, sb);
+      cp_async_16(aux + lane * 16, sb);
     else
-      asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(slot + L::kData + lane * 8),
-                   "l"(sb)
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(aux + lane * 8), "l"(sb)
                    : "memory");
   }
   if (pos.gb + 1 == steps_per_tile && lane < 8) {
     // lanes 0-3: bias of rows 8j .. 8j + 7; lanes 4-7: the norm gain the
     // rows' (1 + scale) folds into (chunk 0: an1, chunk 2: fn1; none otherwise)
-    const uint32_t dst = slot + L::kData + L::kSb + 16 * lane;
+    const uint32_t dst = aux + L::kSb + 16 * lane;
     const int part = 8 * (lane & 3);
     if (lane < 4) {
       cp_async_16(dst, blk.bias + pos.n0 + part);
@@ -275,7 +279,7 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
 }
 
 template <int BITS, int MT, int RING>
-__global__ void __launch_bounds__(kModThreads, 1) mod_lane_kernel(const __grid_constant__ ModParams p) {
+__global__ void __launch_bounds__(kLaneThreads, 1) mod_lane_kernel(const __grid_constant__ ModParams p) {
   using L = LaneFmt<BITS>;
   using F = ModFmt<BITS>;
   extern __shared__ __align__(128) uint8_t mod_smem[];
@@ -288,7 +292,58 @@ __global__ void __launch_bounds__(kModThreads, 1) mod_lane_kernel(const __grid_c
   float* tmul = reinterpret_cast<float*>(tl + static_cast<size_t>(MT) * p.K * 3);  // [G][MT]
   float* tsum = tmul + G * MT;                                                  // [G][MT]
   int* tls = reinterpret_cast<int*>(tsum + G * MT);                             // [G][MT][3]
+  // global memory only once the kernels this launch depends on are done
+  pdl_wait();
+  pdl_release();
   for (int i = threadIdx.x; i < p.n_blocks; i += blockDim.x) blocks[i] = p.blocks[i];
+  __syncthreads();
+
+  const int lane = threadIdx.x & 31;
+  const uint64_t neg_magic2 = f32x2(-p.code_magic, -p.code_magic);
+  const int steps_per_tile = G / L::kStepGroups;
+  const int tiles_per_block = p.N / kLaneRows;
+  const long long total_tiles = static_cast<long long>(p.n_blocks) * tiles_per_block;
+  const long long nwarps = static_cast<long long>(gridDim.x) * kLaneWarps;
+  const long long gw = static_cast<long long>(blockIdx.x) * kLaneWarps + (threadIdx.x >> 5);
+  long long t_begin, t_end;
+  warp_slice(total_tiles, gw, nwarps, t_begin, t_end);
+  const bool work = t_begin < t_end;
+  const int st_end = work ? static_cast<int>(t_end - t_begin) * steps_per_tile : 0;
+  StepPos cpos;  // the step consumed next
+  cpos.b = static_cast<int>(t_begin / tiles_per_block);
+  cpos.n0 = static_cast<int>(t_begin - static_cast<long long>(cpos.b) * tiles_per_block) * kLaneRows;
+  cpos.gb = 0;
+  StepPos lpos = cpos;  // the step loaded next
+  // this warp's ring: RING data slots (TMA boxes, 1024-byte aligned for the
+  // 128-byte swizzle), their scale/bias and epilogue words, their barriers
+  const int wi = threadIdx.x >> 5;
+  const uint32_t smem0 = smem_u32(mod_smem);
+  const uint32_t data0 =
+      (smem0 + static_cast<uint32_t>(lane_fixed_bytes<BITS, MT>(p.n_blocks, p.K)) + 1023u) & ~1023u;
+  const uint32_t aux0 = data0 + static_cast<uint32_t>(kLaneWarps * RING * L::kData);
+  const uint32_t bar0 = aux0 + static_cast<uint32_t>(kLaneWarps * RING * L::kAux);
+  const uint32_t wdata = data0 + static_cast<uint32_t>(wi * RING * L::kData);
+  const uint32_t waux = aux0 + static_cast<uint32_t>(wi * RING * L::kAux);
+  const uint32_t wbar = bar0 + static_cast<uint32_t>(wi * RING * 8);
+  const uint8_t* const data_p = mod_smem + (wdata - smem0);
+  const uint8_t* const aux_p = mod_smem + (waux - smem0);
+  if (lane == 0 && work) {
+    for (int r = 0; r < RING; ++r) mbar_init(wbar + 8 * r, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+
+  // prologue: the first RING - 1 steps in flight (one commit group per step)
+#pragma unroll 1
+  for (int r = 0; r < RING - 1; ++r) {
+    if (r < st_end) {
+      lane_load<BITS>(p, blocks, lpos, steps_per_tile, lane, wdata + r * L::kData,
+                      waux + r * L::kAux, wbar + 8 * r);
+      lpos.advance(steps_per_tile, p.N);
+    }
+    cp_async_commit();
+  }
+  // the temb values (packed codes: their limbs) while the first steps' copies fly
   if constexpr (BITS == 0) {
     for (int i = threadIdx.x; i < MT * K4; i += blockDim.x) {
       const int m = i / K4, k4 = i - (i / K4) * K4;
@@ -306,7 +361,7 @@ __global__ void __launch_bounds__(kModThreads, 1) mod_lane_kernel(const __grid_c
     // temb sum (a fixed xor tree: the same bits for a token whatever else the
     // launch holds)
     const int wl = threadIdx.x & 31;
-    for (int i = threadIdx.x >> 5; i < G * MT; i += kModWarps) {
+    for (int i = threadIdx.x >> 5; i < G * MT; i += kLaneWarps) {
       const int gi = i / MT, n = i - (i / MT) * MT;
       float t0 = 0.0f, t1 = 0.0f;
       if (n < p.M) {
@@ -354,59 +409,51 @@ __global__ void __launch_bounds__(kModThreads, 1) mod_lane_kernel(const __grid_c
     }
   }
   __syncthreads();
-
-  const int lane = threadIdx.x & 31;
-  const uint64_t neg_magic2 = f32x2(-p.code_magic, -p.code_magic);
-  const int steps_per_tile = G / L::kStepGroups;
-  const int tiles_per_block = p.N / kLaneRows;
-  const long long total_tiles = static_cast<long long>(p.n_blocks) * tiles_per_block;
-  const long long nwarps = static_cast<long long>(gridDim.x) * kModWarps;
-  const long long gw = static_cast<long long>(blockIdx.x) * kModWarps + (threadIdx.x >> 5);
-  long long t_begin, t_end;
-  warp_slice(total_tiles, gw, nwarps, t_begin, t_end);
-  if (t_begin >= t_end) return;
-  const int st_end = static_cast<int>(t_end - t_begin) * steps_per_tile;
-  StepPos cpos;  // the step consumed next
-  cpos.b = static_cast<int>(t_begin / tiles_per_block);
-  cpos.n0 = static_cast<int>(t_begin - static_cast<long long>(cpos.b) * tiles_per_block) * kLaneRows;
-  cpos.gb = 0;
-  StepPos lpos = cpos;  // the step loaded next
-  uint8_t* const ring_p =
-      mod_smem + lane_fixed_bytes<BITS, MT>(p.n_blocks, p.K) + (threadIdx.x >> 5) * RING * L::kSlot;
-  const uint32_t ring = smem_u32(ring_p);
-
-  // prologue: the first RING - 1 steps in flight (one commit group per step)
-#pragma unroll 1
-  for (int r = 0; r < RING - 1; ++r) {
-    if (r < st_end) {
-      lane_load<BITS>(p, blocks, lpos, steps_per_tile, lane, ring + r * L::kSlot);
-      lpos.advance(steps_per_tile, p.N);
-    }
-    cp_async_commit();
-  }
+  if (!work) return;
   float y[MT];
 #pragma unroll
   for (int m = 0; m < MT; ++m) y[m] = 0.0f;
   int slot_c = 0, slot_l = RING - 1;  // ring slots of the consumed and the loaded step
+  uint32_t dpar = 0;                  // per slot: parity of its data barrier's next phase
   for (int st = 0; st < st_end; ++st) {
     if (st + RING - 1 < st_end) {
       lane_load<BITS>(p, blocks, lpos, steps_per_tile, lane,
-                      ring + static_cast<uint32_t>(slot_l) * L::kSlot);
+                      wdata + static_cast<uint32_t>(slot_l) * L::kData,
+                      waux + static_cast<uint32_t>(slot_l) * L::kAux,
+                      wbar + 8u * static_cast<uint32_t>(slot_l));
       lpos.advance(steps_per_tile, p.N);
     }
     slot_l = slot_l + 1 == RING ? 0 : slot_l + 1;
     cp_async_commit();
     asm volatile("cp.async.wait_group %0;" ::"n"(RING - 1) : "memory");
+    {
+      // the step's TMA box (bounded wait: on a timeout the error word is set
+      // and the warp stops)
+      const uint32_t bar = wbar + 8u * static_cast<uint32_t>(slot_c);
+      const uint32_t par = (dpar >> slot_c) & 1u;
+      bool ok = mbar_try_wait(bar, par);
+      if (!ok) {
+        const uint64_t t0 = global_timer_ns();
+        while (!(ok = mbar_try_wait(bar, par)) && global_timer_ns() - t0 < p.wait_limit_ns) {
+        }
+      }
+      if (__any_sync(0xFFFFFFFFu, !ok)) {
+        if (lane == 0) atomicOr(p.err, kErrTimeout);
+        break;
+      }
+      dpar ^= 1u << slot_c;
+    }
     __syncwarp();
-    const uint8_t* slot = ring_p + slot_c * L::kSlot;
+    const uint8_t* slot = data_p + slot_c * L::kData;
+    const uint8_t* aux = aux_p + slot_c * L::kAux;
     slot_c = slot_c + 1 == RING ? 0 : slot_c + 1;
     const uint8_t* rowp = slot + lane * L::kRowBytes;
     const int sw = lane & 7;
     uint4 sbv = make_uint4(0u, 0u, 0u, 0u);
     if constexpr (L::kSbRow == 16) {
-      sbv = *reinterpret_cast<const uint4*>(slot + L::kData + lane * 16);
+      sbv = *reinterpret_cast<const uint4*>(aux + lane * 16);
     } else if constexpr (L::kSbRow == 8) {
-      const uint2 v = *reinterpret_cast<const uint2*>(slot + L::kData + lane * 8);
+      const uint2 v = *reinterpret_cast<const uint2*>(aux + lane * 8);
       sbv.x = v.x;
       sbv.y = v.y;
     }
@@ -443,9 +490,18 @@ __global__ void __launch_bounds__(kModThreads, 1) mod_lane_kernel(const __grid_c
                   (f32x2_lo(acc[m][1]) + f32x2_hi(acc[m][1]));
       } else {
         // packed codes: exact integer dots with the three temb limbs
-        int a[MT][3];
+        // two accumulators per limb (even / odd code words) up to 4 tokens:
+        // integer sums, so the split changes nothing but the dependency chains
+        constexpr int kB = MT <= 4 ? MT : 1;
+        int a[MT][3], b[kB][3];
 #pragma unroll
-        for (int m = 0; m < MT; ++m) a[m][0] = a[m][1] = a[m][2] = 0;
+        for (int m = 0; m < MT; ++m)
+#pragma unroll
+          for (int l = 0; l < 3; ++l) a[m][l] = 0;
+#pragma unroll
+        for (int m = 0; m < kB; ++m)
+#pragma unroll
+          for (int l = 0; l < 3; ++l) b[m][l] = 0;
 #pragma unroll
         for (int c = 0; c < L::kCpg; ++c) {
           const int ch = gi * L::kCpg + c;
@@ -469,22 +525,23 @@ __global__ void __launch_bounds__(kModThreads, 1) mod_lane_kernel(const __grid_c
             const int8_t* lr = tl + (static_cast<size_t>(m) * G + g_abs) * 192 + c * F::kPer;
 #pragma unroll
             for (int l = 0; l < 3; ++l) {
+              int& bb = MT <= 4 ? b[m < kB ? m : 0][l] : a[m][l];
               const uint4 l0 = *reinterpret_cast<const uint4*>(lr + 64 * l);
               if constexpr (BITS == 8) {
                 a[m][l] = dp4a_us(cw[0], l0.x, a[m][l]);
-                a[m][l] = dp4a_us(cw[1], l0.y, a[m][l]);
+                bb = dp4a_us(cw[1], l0.y, bb);
                 a[m][l] = dp4a_us(cw[2], l0.z, a[m][l]);
-                a[m][l] = dp4a_us(cw[3], l0.w, a[m][l]);
+                bb = dp4a_us(cw[3], l0.w, bb);
               } else {
                 const uint4 l1 = *reinterpret_cast<const uint4*>(lr + 64 * l + 16);
                 a[m][l] = dp4a_us(cw[0], l0.x, a[m][l]);
-                a[m][l] = dp4a_us(cw[1], l0.y, a[m][l]);
+                bb = dp4a_us(cw[1], l0.y, bb);
                 a[m][l] = dp4a_us(cw[2], l0.z, a[m][l]);
-                a[m][l] = dp4a_us(cw[3], l0.w, a[m][l]);
+                bb = dp4a_us(cw[3], l0.w, bb);
                 a[m][l] = dp4a_us(cw[4], l1.x, a[m][l]);
-                a[m][l] = dp4a_us(cw[5], l1.y, a[m][l]);
+                bb = dp4a_us(cw[5], l1.y, bb);
                 a[m][l] = dp4a_us(cw[6], l1.z, a[m][l]);
-                a[m][l] = dp4a_us(cw[7], l1.w, a[m][l]);
+                bb = dp4a_us(cw[7], l1.w, bb);
               }
             }
           }
@@ -495,9 +552,13 @@ __global__ void __launch_bounds__(kModThreads, 1) mod_lane_kernel(const __grid_c
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
           const int i = g_abs * MT + m;
-          const float a0 = static_cast<float>(a[m][0] - off * tls[3 * i]);
-          const float a1 = static_cast<float>(a[m][1] - off * tls[3 * i + 1]);
-          const float a2 = static_cast<float>(a[m][2] - off * tls[3 * i + 2]);
+          int s3[3];
+#pragma unroll
+          for (int l = 0; l < 3; ++l)
+            s3[l] = (MT <= 4 ? a[m][l] + b[m < kB ? m : 0][l] : a[m][l]) - off * tls[3 * i + l];
+          const float a0 = static_cast<float>(s3[0]);
+          const float a1 = static_cast<float>(s3[1]);
+          const float a2 = static_cast<float>(s3[2]);
           const float d = __fmul_rn(__fmaf_rn(65536.0f, a2, __fmaf_rn(256.0f, a1, a0)), tmul[i]);
           y[m] += __fmaf_rn(sc, d, __fmul_rn(bi, tsum[i]));
         }
@@ -506,7 +567,7 @@ __global__ void __launch_bounds__(kModThreads, 1) mod_lane_kernel(const __grid_c
     if (cpos.gb + 1 == steps_per_tile) {
       // the tile's rows are complete: row n0 + lane for every token
       const int b = cpos.b, n = cpos.n0 + lane;
-      const uint16_t* epi = reinterpret_cast<const uint16_t*>(slot + L::kData + L::kSb);
+      const uint16_t* epi = reinterpret_cast<const uint16_t*>(aux + L::kSb);
       const bool has_gain = (cpos.n0 < p.H && blocks[b].an1 != nullptr) ||
                             (cpos.n0 >= 2 * p.H && cpos.n0 < 3 * p.H && blocks[b].fn1 != nullptr);
       RowEpi e;
@@ -533,6 +594,8 @@ __global__ void __launch_bounds__(kModThreads) mod_warp_kernel(const __grid_cons
   using F = ModFmt<BITS>;
   constexpr int Q = F::kPer / 4;  // float quads per chunk
   extern __shared__ uint8_t mod_smem[];
+  pdl_wait();
+  pdl_release();
   ModBlock* blocks = reinterpret_cast<ModBlock*>(mod_smem);
   const int row_bytes = BITS == 0 ? p.K * 2 : p.K * BITS / 8;
   const int C = row_bytes / 16;
@@ -628,13 +691,13 @@ __global__ void __launch_bounds__(kModThreads) mod_warp_kernel(const __grid_cons
 
 // Resident CTAs per SM of a kernel at `smem` bytes (looked up once per device).
 template <typename K>
-int resident_ctas(K kernel, size_t smem, std::atomic<int>* cache) {
+int resident_ctas(K kernel, int threads, size_t smem, std::atomic<int>* cache) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
   int v = cache[dev].load(std::memory_order_relaxed);
   if (v > 0) return v;
   int per_sm = 0, sms = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kModThreads, smem) !=
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) !=
           cudaSuccess ||
       per_sm <= 0) {
     (void)cudaGetLastError();
@@ -648,18 +711,30 @@ int resident_ctas(K kernel, size_t smem, std::atomic<int>* cache) {
 }
 
 template <typename K>
-cudaError_t launch_persistent(K kernel, const ModParams& p, size_t smem, long long work_warps,
-                              std::atomic<int>* cache, cudaStream_t stream) {
+cudaError_t launch_persistent(K kernel, int threads, const ModParams& p, size_t smem,
+                              long long work_warps, std::atomic<int>* cache, cudaStream_t stream) {
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
-  const long long want = (work_warps + kModWarps - 1) / kModWarps;
-  const long long most = resident_ctas(kernel, smem, cache);
+  const int warps = threads / 32;
+  const long long want = (work_warps + warps - 1) / warps;
+  const long long most = resident_ctas(kernel, threads, smem, cache);
   const int grid = static_cast<int>(want < most ? (want > 0 ? want : 1) : most);
-  kernel<<<grid, kModThreads, smem, stream>>>(p);
-  return cudaGetLastError();
+  // may begin while the previous kernel on the stream finishes (the kernel
+  // waits for it before touching global memory)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
 template <int BITS, int MT>
@@ -671,18 +746,19 @@ cudaError_t launch_mod_warp(const ModParams& p, cudaStream_t stream) {
   constexpr int Q = ModFmt<BITS>::kPer / 4;
   const size_t smem = blk_bytes + static_cast<size_t>(MT) * Q * C * 16 + static_cast<size_t>(MT) * C * 4;
   static std::atomic<int> cache[64];
-  return launch_persistent(mod_warp_kernel<BITS, MT>, p, smem, rows, cache, stream);
+  return launch_persistent(mod_warp_kernel<BITS, MT>, kModThreads, p, smem, rows, cache, stream);
 }
 
 constexpr size_t kModSmemLimit = 227 * 1024;
 
 template <int BITS, int MT, int RING>
 cudaError_t launch_mod_lane_ring(const ModParams& p, cudaStream_t stream) {
-  const size_t smem = lane_fixed_bytes<BITS, MT>(p.n_blocks, p.K) +
-                      static_cast<size_t>(kModWarps) * RING * LaneFmt<BITS>::kSlot;
+  const size_t smem = lane_fixed_bytes<BITS, MT>(p.n_blocks, p.K) + 1024 +
+                      static_cast<size_t>(kLaneWarps) * RING * LaneFmt<BITS>::kSlot;
   const long long tiles = static_cast<long long>(p.n_blocks) * p.N / kLaneRows;
   static std::atomic<int> cache[64];
-  return launch_persistent(mod_lane_kernel<BITS, MT, RING>, p, smem, tiles, cache, stream);
+  return launch_persistent(mod_lane_kernel<BITS, MT, RING>, kLaneThreads, p, smem, tiles, cache,
+                           stream);
 }
 
 // The deepest ring (steps in flight per warp, 6 at most) that fits the
@@ -691,7 +767,8 @@ template <int BITS, int MT>
 cudaError_t launch_mod_lane(const ModParams& p, cudaStream_t stream) {
   const size_t fixed = lane_fixed_bytes<BITS, MT>(p.n_blocks, p.K);
   auto fits = [&](int ring) {
-    return fixed + static_cast<size_t>(kModWarps) * ring * LaneFmt<BITS>::kSlot <= kModSmemLimit;
+    return fixed + 1024 + static_cast<size_t>(kLaneWarps) * ring * LaneFmt<BITS>::kSlot <=
+           kModSmemLimit;
   };
   if (fits(6)) return launch_mod_lane_ring<BITS, MT, 6>(p, stream);
   if (fits(4)) return launch_mod_lane_ring<BITS, MT, 4>(p, stream);
@@ -709,6 +786,7 @@ bool lane_shape(int n, int k) { return k % 256 == 0 && n % (4 * kLaneRows) == 0;
 template <int BITS>
 cudaError_t launch_mod_bits(const ModParams& p, cudaStream_t stream) {
   if (lane_shape(p.N, p.K)) {
+    if (p.maps == nullptr || p.err == nullptr) return cudaErrorInvalidValue;
     if (p.M > kLaneTok) return cudaErrorInvalidValue;
     if (p.M == 1) return launch_mod_lane<BITS, 1>(p, stream);
     if (p.M == 2) return launch_mod_lane<BITS, 2>(p, stream);
@@ -730,7 +808,7 @@ int mod_tokens_per_launch(int n, int k, int n_blocks) {
   size_t slot = LaneFmt<8>::kSlot;
   if (LaneFmt<4>::kSlot > slot) slot = LaneFmt<4>::kSlot;
   if (LaneFmt<0>::kSlot > slot) slot = LaneFmt<0>::kSlot;
-  const size_t ring2 = static_cast<size_t>(kModWarps) * 2 * slot;
+  const size_t ring2 = 1024 + static_cast<size_t>(kLaneWarps) * 2 * slot;  // with the alignment
   for (int mt = kLaneTok; mt > 1; mt >>= 1) {
     const size_t blk = (static_cast<size_t>(n_blocks) * sizeof(ModBlock) + 15) & ~size_t(15);
     const size_t fixed = (blk + static_cast<size_t>(mt) * k * 4 + static_cast<size_t>(k / 64) * mt * 4 +
