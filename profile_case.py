@@ -7,7 +7,8 @@
     python profile_case.py --op modulation --m 1 --bits 8 --reps 20
 
 Prints the CUDA-event time per call and the algorithmic rate: TFLOP/s for a
-projection (mp_linear: rank-space pre-GEMM + fused projection) or the
+projection (mp_linear: rank-space pre-GEMM + fused projection; back to back,
+or with --flush each call alone after a 256 MB read, the median) or the
 attention (mp_attention over head-major q / k / v of m rows), GB/s for the
 gated sandwich-norm residual step (mp_rms_residual over m rows of width k)
 and for the batched modulation (mp_modulation_all over 32 blocks' adaLN
@@ -117,6 +118,8 @@ def main() -> None:
     ap.add_argument("--ranks", type=str, default="4,8,8,16,16,32,32,64")
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--flush", action="store_true",
+                    help="projection: time each call alone after an L2-evicting read (median)")
     a = ap.parse_args()
     a.op_k_set = "--k" in sys.argv
     dev = torch.device("cuda", 0)
@@ -142,17 +145,37 @@ def main() -> None:
     for _ in range(a.warmup):
         ctx.linear(w, x, y)
     ctx.sync_check()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(a.reps):
-        ctx.linear(w, x, y)
-    e1.record()
-    torch.cuda.synchronize()
-    ctx.sync_check()
-    us = e0.elapsed_time(e1) * 1e3 / a.reps
+    if a.flush:
+        # each call timed alone after a read of a 256 MB buffer: the weights
+        # and x come from HBM, as in a forward whose other layers evicted them
+        flush = torch.ones(64 << 20, dtype=torch.int32, device=dev)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(a.reps)]
+        for e0, e1 in ev:
+            flush.sum()
+            e0.record()
+            ctx.linear(w, x, y)
+            e1.record()
+        torch.cuda.synchronize()
+        ctx.sync_check()
+        us = float(np.median([e0.elapsed_time(e1) * 1e3 for e0, e1 in ev]))
+    else:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.reps):
+            ctx.linear(w, x, y)
+        e1.record()
+        torch.cuda.synchronize()
+        ctx.sync_check()
+        us = e0.elapsed_time(e1) * 1e3 / a.reps
     flops = 2.0 * a.m * a.n * a.k + sum(2.0 * a.m * r * (a.k + a.n) for r in ranks)
+    # algorithmic bytes: codes (or bf16 weights), the group scale/bias words,
+    # x, y and the LoRA A / B stacks
+    wbytes = a.n * a.k * a.bits / 8 + a.n * (a.k // 64) * 4 if a.bits else 2.0 * a.n * a.k
+    nbytes = wbytes + 2.0 * a.m * (a.k + a.n) + sum(2.0 * r * (a.k + a.n) for r in ranks)
     print(json.dumps({"m": a.m, "n": a.n, "k": a.k, "bits": a.bits, "ranks": ranks,
-                      "us_per_call": us, "tflops": flops / (us * 1e-6) / 1e12}))
+                      "flush": a.flush, "us_per_call": us, "tflops": flops / (us * 1e-6) / 1e12,
+                      "bytes": nbytes, "gbs": nbytes / (us * 1e-6) / 1e9}))
     w.free()
     ctx.close()
 
