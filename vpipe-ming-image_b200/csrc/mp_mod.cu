@@ -194,23 +194,28 @@ struct StepPos {
   }
 };
 
-// Issues the copies of step `pos` (this lane's share): lane 0 the 32 rows'
-// 128 bytes by one TMA into `data` (the 128-byte swizzle puts chunk c of row r
-// at chunk position c ^ (r & 7), so the lanes' row reads are conflict-free),
-// completing on `bar`; every lane its row's scale/bias words, and with the
-// tile's last step lanes 0-7 the rows' bias and norm gain, into `aux`
-// (cp.async).
+// The copies of step `pos`. lane_load_rows: lane 0 the 32 rows' 128 bytes by
+// one TMA into `data` (the 128-byte swizzle puts chunk c of row r at chunk
+// position c ^ (r & 7), so the lanes' row reads are conflict-free), completing
+// on `bar` (needs only the block's tensor map). lane_load_aux: every lane its
+// row's scale/bias words, and with the tile's last step lanes 0-7 the rows'
+// bias and norm gain, into `aux` (cp.async; needs the block table).
 template <int BITS>
-__device__ __forceinline__ void lane_load(const ModParams& p, const ModBlock* blocks, StepPos pos,
-                                          int steps_per_tile, int lane, uint32_t data, uint32_t aux,
-                                          uint32_t bar) {
+__device__ __forceinline__ void lane_load_rows(const ModParams& p, StepPos pos, int lane,
+                                               uint32_t data, uint32_t bar) {
   using L = LaneFmt<BITS>;
-  const ModBlock& blk = blocks[pos.b];
   if (lane == 0) {
-    // the 32 rows' next 128 bytes: chunk c of row r lands at c ^ (r & 7)
     mbar_arrive_expect_tx(bar, L::kData);
     tma_load_2d(data, p.maps + pos.b, bar, pos.gb * (BITS == 0 ? 64 : L::kRowBytes), pos.n0);
   }
+}
+
+template <int BITS>
+__device__ __forceinline__ void lane_load_aux(const ModParams& p, const ModBlock* blocks,
+                                              StepPos pos, int steps_per_tile, int lane,
+                                              uint32_t aux) {
+  using L = LaneFmt<BITS>;
+  const ModBlock& blk = blocks[pos.b];
   if constexpr (BITS != 0) {
     const uint32_t* sb =
         blk.sb + static_cast<size_t>(pos.n0 + lane) * p.sb_stride + pos.gb * L::kStepGroups;
@@ -292,25 +297,28 @@ __global__ void __launch_bounds__(kLaneThreads, 1) mod_lane_kernel(const __grid_
   float* tmul = reinterpret_cast<float*>(tl + static_cast<size_t>(MT) * p.K * 3);  // [G][MT]
   float* tsum = tmul + G * MT;                                                  // [G][MT]
   int* tls = reinterpret_cast<int*>(tsum + G * MT);                             // [G][MT][3]
-  // global memory only once the kernels this launch depends on are done
-  pdl_wait();
-  pdl_release();
-  for (int i = threadIdx.x; i < p.n_blocks; i += blockDim.x) blocks[i] = p.blocks[i];
-  __syncthreads();
-
   const int lane = threadIdx.x & 31;
   const uint64_t neg_magic2 = f32x2(-p.code_magic, -p.code_magic);
   const int steps_per_tile = G / L::kStepGroups;
   const int tiles_per_block = p.N / kLaneRows;
+  // this warp's tiles [t_begin, t_end) of the launch's n_blocks * tiles_per_block
+  // (32-bit arithmetic when the products fit: 64-bit divisions cost ~1 us here)
   const long long total_tiles = static_cast<long long>(p.n_blocks) * tiles_per_block;
   const long long nwarps = static_cast<long long>(gridDim.x) * kLaneWarps;
   const long long gw = static_cast<long long>(blockIdx.x) * kLaneWarps + (threadIdx.x >> 5);
   long long t_begin, t_end;
-  warp_slice(total_tiles, gw, nwarps, t_begin, t_end);
+  if (total_tiles * nwarps < (1ll << 32)) {
+    const uint32_t tt = static_cast<uint32_t>(total_tiles), nw = static_cast<uint32_t>(nwarps),
+                   w = static_cast<uint32_t>(gw);
+    t_begin = tt * w / nw;
+    t_end = tt * (w + 1u) / nw;
+  } else {
+    warp_slice(total_tiles, gw, nwarps, t_begin, t_end);
+  }
   const bool work = t_begin < t_end;
   const int st_end = work ? static_cast<int>(t_end - t_begin) * steps_per_tile : 0;
   StepPos cpos;  // the step consumed next
-  cpos.b = static_cast<int>(t_begin / tiles_per_block);
+  cpos.b = static_cast<int>(static_cast<uint32_t>(t_begin) / static_cast<uint32_t>(tiles_per_block));
   cpos.n0 = static_cast<int>(t_begin - static_cast<long long>(cpos.b) * tiles_per_block) * kLaneRows;
   cpos.gb = 0;
   StepPos lpos = cpos;  // the step loaded next
@@ -333,15 +341,42 @@ __global__ void __launch_bounds__(kLaneThreads, 1) mod_lane_kernel(const __grid_
   }
   __syncwarp();
 
-  // prologue: the first RING - 1 steps in flight (one commit group per step)
+  // global memory only once the kernels this launch depends on are done
+  pdl_wait();
+  pdl_release();
+  // packed codes: this warp's first (group, token) temb values, loaded before
+  // the copies below queue behind the first steps' weight rows
+  float tp0 = 0.0f, tp1 = 0.0f;
+  if constexpr (BITS != 0) {
+    const int i = threadIdx.x >> 5;
+    if (i < G * MT && i % MT < p.M) {
+      const uint16_t* t = p.temb + static_cast<size_t>(i % MT) * p.K + (i / MT) * 64;
+      tp0 = bf16_bits_to_f32(t[lane]);
+      tp1 = bf16_bits_to_f32(t[32 + lane]);
+    }
+  }
+  // prologue: the first RING - 1 steps' weight rows in flight (they need only
+  // the tensor maps), then the block table, then those steps' scale/bias and
+  // epilogue words (one commit group per step)
 #pragma unroll 1
   for (int r = 0; r < RING - 1; ++r) {
     if (r < st_end) {
-      lane_load<BITS>(p, blocks, lpos, steps_per_tile, lane, wdata + r * L::kData,
-                      waux + r * L::kAux, wbar + 8 * r);
+      lane_load_rows<BITS>(p, lpos, lane, wdata + r * L::kData, wbar + 8 * r);
       lpos.advance(steps_per_tile, p.N);
     }
-    cp_async_commit();
+  }
+  for (int i = threadIdx.x; i < p.n_blocks; i += blockDim.x) blocks[i] = p.blocks[i];
+  __syncthreads();
+  {
+    StepPos apos = cpos;
+#pragma unroll 1
+    for (int r = 0; r < RING - 1; ++r) {
+      if (r < st_end) {
+        lane_load_aux<BITS>(p, blocks, apos, steps_per_tile, lane, waux + r * L::kAux);
+        apos.advance(steps_per_tile, p.N);
+      }
+      cp_async_commit();
+    }
   }
   // the temb values (packed codes: their limbs) while the first steps' copies fly
   if constexpr (BITS == 0) {
@@ -363,11 +398,13 @@ __global__ void __launch_bounds__(kLaneThreads, 1) mod_lane_kernel(const __grid_
     const int wl = threadIdx.x & 31;
     for (int i = threadIdx.x >> 5; i < G * MT; i += kLaneWarps) {
       const int gi = i / MT, n = i - (i / MT) * MT;
-      float t0 = 0.0f, t1 = 0.0f;
-      if (n < p.M) {
+      float t0 = tp0, t1 = tp1;  // the first pair's values are loaded
+      if (i >= kLaneWarps && n < p.M) {
         const uint16_t* t = p.temb + static_cast<size_t>(n) * p.K + gi * 64;
         t0 = bf16_bits_to_f32(t[wl]);
         t1 = bf16_bits_to_f32(t[32 + wl]);
+      } else if (i >= kLaneWarps) {
+        t0 = t1 = 0.0f;
       }
       float amax = fmaxf(fabsf(t0), fabsf(t1));
       float v = t0 + t1;
@@ -417,10 +454,10 @@ __global__ void __launch_bounds__(kLaneThreads, 1) mod_lane_kernel(const __grid_
   uint32_t dpar = 0;                  // per slot: parity of its data barrier's next phase
   for (int st = 0; st < st_end; ++st) {
     if (st + RING - 1 < st_end) {
-      lane_load<BITS>(p, blocks, lpos, steps_per_tile, lane,
-                      wdata + static_cast<uint32_t>(slot_l) * L::kData,
-                      waux + static_cast<uint32_t>(slot_l) * L::kAux,
-                      wbar + 8u * static_cast<uint32_t>(slot_l));
+      lane_load_rows<BITS>(p, lpos, lane, wdata + static_cast<uint32_t>(slot_l) * L::kData,
+                           wbar + 8u * static_cast<uint32_t>(slot_l));
+      lane_load_aux<BITS>(p, blocks, lpos, steps_per_tile, lane,
+                          waux + static_cast<uint32_t>(slot_l) * L::kAux);
       lpos.advance(steps_per_tile, p.N);
     }
     slot_l = slot_l + 1 == RING ? 0 : slot_l + 1;

@@ -370,7 +370,7 @@ __device__ void pair_producer(const ProjParams& p, const PairSmem& sm, bool lead
       const uint32_t ph = (it / stages) & 1u;
       const uint32_t bit = 1u << s;
       if (it >= stages &&
-          !mbar_wait(smem_u32(&sm.empty[s]), ph ^ 1u, sm.abort, kSiteEmpty | s, p.wait_limit_ns)) {
+          !mbar_wait<true>(smem_u32(&sm.empty[s]), ph ^ 1u, sm.abort, kSiteEmpty | s, p.wait_limit_ns)) {
         aborted = true;
         break;
       }
@@ -470,7 +470,7 @@ __device__ void pair_mma(const ProjParams& p, const PairSmem& sm, uint32_t tmem,
       const int s = static_cast<int>(it % stages);
       const uint32_t ph = (it / stages) & 1u;
       MP_TRACE_MARK(kTrMmaPre, static_cast<int>(it));
-      if (!mbar_wait(smem_u32(&sm.full[s]), ph, sm.abort, kSiteFull | s, p.wait_limit_ns)) {
+      if (!mbar_wait<true>(smem_u32(&sm.full[s]), ph, sm.abort, kSiteFull | s, p.wait_limit_ns)) {
         aborted = true;
         break;
       }
@@ -486,7 +486,7 @@ __device__ void pair_mma(const ProjParams& p, const PairSmem& sm, uint32_t tmem,
             // Accumulator j holds the previous tile until its epilogue has read
             // it out. Both accumulators' phases are waited every tile (also one
             // this tile leaves unused), so no phase is ever skipped.
-            if (!mbar_wait(smem_u32(&sm.tempty[j]), (tcount - 1) & 1u, sm.abort, kSiteTmem | j,
+            if (!mbar_wait<true>(smem_u32(&sm.tempty[j]), (tcount - 1) & 1u, sm.abort, kSiteTmem | j,
                            p.wait_limit_ns)) {
               aborted = true;
               break;
@@ -568,7 +568,7 @@ __device__ void pair_dequant(const ProjParams& p, const PairSmem& sm, int rank, 
       const float bi = bf16_bits_to_f32(sbw >> 16);
       const float bf = fmaf(-sc, mb.code_offset, bi);
       const uint64_t sc2 = f32x2(sc, sc), bf2 = f32x2(bf, bf);
-      if (!mbar_wait(smem_u32(&sm.cfull[s]), (cpar >> s) & 1u, sm.abort, kSiteCodes | s,
+      if (!mbar_wait<true>(smem_u32(&sm.cfull[s]), (cpar >> s) & 1u, sm.abort, kSiteCodes | s,
                      p.wait_limit_ns)) {
         aborted = true;
         break;
@@ -1003,7 +1003,7 @@ __device__ void pair_epilogue_rows(const ProjParams& p, const PairSmem& sm, uint
     // strengths apply to a rank-space pre-GEMM launch and to prologue units
     const bool scaled = p.scale.enabled && (p.n_pre == 0 || t.mi < 0);
     const bool ok_mine =
-        mbar_wait(smem_u32(sm.tfull), tcount & 1u, sm.abort, kSiteEpi, p.wait_limit_ns);
+        mbar_wait<true>(smem_u32(sm.tfull), tcount & 1u, sm.abort, kSiteEpi, p.wait_limit_ns);
     if (!named_barrier_and(kEpiBarrier, kEpiThreads, ok_mine)) break;
     tc_fence_after();
     if (threadIdx.x == 32 * kEpiWarp0) MP_TRACE_MARK(kTrEpiStart, static_cast<int>(tcount));
@@ -1080,7 +1080,7 @@ __device__ void pair_epilogue_cols(const ProjParams& p, const PairSmem& sm, uint
     // strengths apply to a rank-space pre-GEMM launch and to prologue units
     const bool scaled = p.scale.enabled && (p.n_pre == 0 || t.mi < 0);
     const bool ok_mine =
-        mbar_wait(smem_u32(sm.tfull), tcount & 1u, sm.abort, kSiteEpi, p.wait_limit_ns);
+        mbar_wait<true>(smem_u32(sm.tfull), tcount & 1u, sm.abort, kSiteEpi, p.wait_limit_ns);
     if (!named_barrier_and(kEpiBarrier, kEpiThreads, ok_mine)) break;
     tc_fence_after();
     if (threadIdx.x == 32 * kEpiWarp0) MP_TRACE_MARK(kTrEpiStart, static_cast<int>(tcount));
@@ -1320,7 +1320,7 @@ __global__ void __launch_bounds__(32) wait_selftest_kernel(uint64_t limit_ns, ui
     fence_mbar_init();
   }
   __syncwarp();
-  const bool ok = mbar_wait(smem_u32(&bar), 0, &abort_word, 0x1900u, limit_ns);
+  const bool ok = mbar_wait<true>(smem_u32(&bar), 0, &abort_word, 0x1900u, limit_ns);
   __syncwarp();
   if (threadIdx.x == 0 && (!ok || abort_word != 0u)) atomicOr(err, kErrTimeout);
 }
