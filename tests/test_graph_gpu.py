@@ -75,3 +75,51 @@ def test_fused_prologue_replays_bit_identical(ctx):
             ctx.set_strength(i, 1.0)
         for w in ws:
             w.free()
+
+
+def test_side_stream_lora_chain_replays_bit_identical(ctx):
+    """A split-K projection over few rows with live slots forks a side stream
+    (rank-space pre-GEMM, its reduce and the LoRA split) and joins it before
+    the final reduce: captured into a CUDA graph, the fork and join are graph
+    edges, and every replay gives the bits of the same eager call."""
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(11)
+    m = 256
+    c, sc, bi = _device_affine(gen, H, H, 8, dev)
+    w = ctx.upload(H, H, 8, c, sc, bi)
+    for slot in range(8):
+        a = (torch.randn((32, H), device=dev, generator=gen) / 32 ** 0.5).to(torch.bfloat16)
+        b = (torch.randn((H, 32), device=dev, generator=gen) * 0.01).to(torch.bfloat16)
+        w.bind(slot, a, b)
+    strengths = np.random.default_rng(5).uniform(-1.0, 1.5, size=8)
+    for i, s in enumerate(strengths):
+        ctx.set_strength(i, float(s))
+    try:
+        xs = torch.randn((m, H), device=dev, generator=gen).to(torch.bfloat16)
+        ctx.reset_engagement()
+        ctx.linear(w, xs)
+        torch.cuda.synchronize(dev)
+        # pre-GEMM, its reduce, LoRA split, base splits, final reduce (the
+        # sequential form is four launches: no LoRA split of its own)
+        assert ctx.engagement()["kernels"] == 5, "the side-stream chain did not run"
+        out = torch.empty((m, H), dtype=torch.bfloat16, device=dev)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            ctx.linear(w, xs, out)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            ctx.linear(w, xs, out)
+        for trial in range(3):
+            xs.copy_(torch.randn((m, H), device=dev, generator=gen).to(torch.bfloat16))
+            g.replay()
+            ref = ctx.linear(w, xs)
+            torch.cuda.synchronize(dev)
+            assert torch.equal(_bits(out), _bits(ref)), f"replay {trial} differs"
+        del g
+        ctx.sync_check()
+    finally:
+        for i in range(8):
+            ctx.set_strength(i, 1.0)
+        w.free()

@@ -124,8 +124,16 @@ struct mp_ctx {
   uint32_t* err_word = nullptr;
   uint16_t* scratch = nullptr;  // rank-space intermediate
   size_t scratch_cap = 0;       // elements
-  float* part = nullptr;        // split-K partial sums of the rank-space pre-GEMM
+  float* part = nullptr;        // split-K partial sums (pre-GEMM or projection)
   size_t part_cap = 0;          // elements
+  // A split-K projection with live slots runs its rank-space pre-GEMM and the
+  // LoRA split on a side stream, beside the base splits: that chain's
+  // partial sums, the stream and its fork / join events.
+  float* part_side = nullptr;
+  size_t part_side_cap = 0;
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_fork = nullptr;
+  cudaEvent_t ev_join = nullptr;
   uint32_t* flags = nullptr;    // fused-prologue ready flags (zeroed on allocation)
   size_t flags_cap = 0;         // entries
   uint32_t epoch = 0;           // value of a flag that is set, per fused launch
@@ -309,6 +317,16 @@ int ensure_flags(mp_ctx* c, size_t n, cudaStream_t stream) {
   int rc = ensure_buf(c, &c->flags, &c->flags_cap, cap, stream);
   if (rc != MP_OK) return rc;
   MP_CUDA(c, cudaMemsetAsync(c->flags, 0, cap * sizeof(uint32_t), stream));
+  return MP_OK;
+}
+
+// The side stream and fork / join events of the concurrent LoRA chain,
+// created on first use (the context's device is current).
+int ensure_side(mp_ctx* c) {
+  if (c->side != nullptr) return MP_OK;
+  MP_CUDA(c, cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking));
+  MP_CUDA(c, cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming));
+  MP_CUDA(c, cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming));
   return MP_OK;
 }
 
@@ -574,11 +592,15 @@ namespace {
 
 // Rank-space pre-GEMM: T[m, 0:rtot] = scale ⊙ (x · A^T), into ctx scratch.
 // When the K loop is split, each split writes fp32 partial sums and
-// lora_reduce_kernel adds them (in split order), scales and rounds.
+// lora_reduce_kernel adds them (in split order), scales and rounds. The split
+// count comes from one image's rows (at most max_split); with `side` the
+// partial sums go to the side chain's buffer, which the caller has sized.
 int launch_lora_down(mp_ctx* c, const CUtensorMap& tm_a, int rtot, const mp::EpilogueScale& es,
-                     const void* x, int64_t ldx, int k, int m, cudaStream_t stream) {
+                     const void* x, int64_t ldx, int k, int m, cudaStream_t stream,
+                     int max_split = mp::kMaxSplits, bool side = false) {
   const int base_kt = (k + mp::kBlockK - 1) / mp::kBlockK;
-  const mp::SplitChoice sc = mp::choose_ksplit(image_rows(c, m), pairs_of(rtot), base_kt, rtot);
+  const mp::SplitChoice sc =
+      mp::choose_ksplit(image_rows(c, m), pairs_of(rtot), base_kt, rtot, max_split);
   const int ks = sc.ksplit;
   ProjParams p;
   int rc = begin_launch(c, &p, x, ldx, k, m, &rtot, 1, 2.0 * rtot * k, sc.n_tok);
@@ -586,12 +608,20 @@ int launch_lora_down(mp_ctx* c, const CUtensorMap& tm_a, int rtot, const mp::Epi
   p.scale = es;
   rc = fill_member(c, &p, 0, tm_a, nullptr, 0, rtot, 0, 0, c->scratch, rtot, LoraTiles{});
   if (rc != MP_OK) return rc;
+  float* part = c->part;
   if (ks > 1) {
-    rc = ensure_buf(c, &c->part, &c->part_cap, static_cast<size_t>(ks) * m * rtot, stream);
-    if (rc != MP_OK) return rc;
+    if (side) {
+      if (c->part_side_cap < static_cast<size_t>(ks) * m * rtot)
+        return fail(c, MP_EINVAL, "side partial-sum buffer too small");
+      part = c->part_side;
+    } else {
+      rc = ensure_buf(c, &c->part, &c->part_cap, static_cast<size_t>(ks) * m * rtot, stream);
+      if (rc != MP_OK) return rc;
+      part = c->part;
+    }
     p.ksplit = ks;
     p.kt_per_split = (base_kt + ks - 1) / ks;
-    p.part = c->part;
+    p.part = part;
     p.part_ld = rtot;
   }
   rc = run_launch(c, p, stream, "proj_pair_kernel (rank-space pre-GEMM)");
@@ -599,7 +629,7 @@ int launch_lora_down(mp_ctx* c, const CUtensorMap& tm_a, int rtot, const mp::Epi
   if (ks > 1) {
     mp::ReduceParams rp;
     std::memset(&rp, 0, sizeof(rp));
-    rp.part = c->part;
+    rp.part = part;
     rp.ksplit = ks;
     rp.M = m;
     rp.R = rtot;
@@ -628,6 +658,7 @@ constexpr int kSplitRows = 1024;
 constexpr size_t kSplitBytes = 32u << 20;
 
 constexpr int kFallback = -1;  // fused launch not possible: run the pre-GEMM separately
+constexpr int kSidePairs = 4;  // CTA pairs the concurrent LoRA chain needs at least
 
 // `count` projections of one x in one launch; sts[i] (nullable) is member
 // i's live stack, whose intermediate starts at column t_cols[i] of the
@@ -655,7 +686,8 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
                        const int64_t* ldys, const Stack* const* sts, const int* t_cols, int t_ld,
                        int count, const void* x, int64_t ldx, int m, cudaStream_t stream,
                        const Prologue* pro = nullptr, const SwiGluLaunch* swi = nullptr,
-                       const HeadsLaunch* hds = nullptr, bool may_alloc = true) {
+                       const HeadsLaunch* hds = nullptr, bool may_alloc = true,
+                       const Prologue* sep = nullptr) {
   ProjParams p;
   int ns[mp::kMaxMembers] = {0, 0, 0, 0};
   for (int i = 0; i < count; ++i) ns[i] = ws[i]->d.n;
@@ -686,6 +718,37 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
         std::min<size_t>(mp::kMaxSplits, std::max<size_t>(1, kSplitBytes / per_split)));
     msplit = mp::choose_ksplit(mi, pairs_of(ns[0]), base_kt, ns[0], most);
     if (msplit.ksplit > 1) n_tok = msplit.n_tok;
+  }
+  // With `sep` (live slots whose rank-space pre-GEMM has not run yet), a
+  // split-K launch runs the pre-GEMM, its reduce and the LoRA K tiles (as a
+  // split of their own) on the side stream while the base splits run, on the
+  // CTA pairs the base splits leave free; the final reduce adds the LoRA
+  // split last. The base splits are limited so that the LoRA split's tiles
+  // all fit beside them (a LoRA tile that has to wait for a base tile to end
+  // would put a whole tile on the critical path). Counted on one image's
+  // rows. Anything else returns kFallback having launched nothing: the caller
+  // runs the pre-GEMM first and the LoRA K tiles stay in the last split.
+  int side_pairs = 0;
+  if (sep != nullptr) {
+    if (msplit.ksplit > 1) {
+      const int P = mp::resident_pairs();
+      const int base_kt = (ws[0]->d.k + mp::kBlockK - 1) / mp::kBlockK;
+      for (int pass = 0; pass < 2 && side_pairs == 0 && msplit.ksplit > 1; ++pass) {
+        const long long per_split =
+            static_cast<long long>(pairs_of(ns[0])) * ((mi + msplit.n_tok - 1) / msplit.n_tok);
+        const long long free_pairs = P - per_split * msplit.ksplit;
+        if (free_pairs >= std::max<long long>(per_split, kSidePairs)) {
+          side_pairs = static_cast<int>(free_pairs);
+        } else if (pass == 0) {
+          const long long fit = (P - per_split) / per_split;  // base splits that leave room
+          if (fit < 2) break;
+          msplit = mp::choose_ksplit(mi, pairs_of(ns[0]), base_kt, ns[0],
+                                     static_cast<int>(std::min<long long>(fit, msplit.ksplit)));
+          if (msplit.ksplit > 1) n_tok = msplit.n_tok;
+        }
+      }
+    }
+    if (side_pairs == 0) return kFallback;
   }
   double w_bytes = 0.0;
   for (int i = 0; i < count; ++i) w_bytes += static_cast<double>(ws[i]->w_bytes);
@@ -802,20 +865,63 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
     c->eng.lora_down += 1;
   } else if (msplit.ksplit > 1) {
     const int ks = msplit.ksplit;
+    const bool apart = sep != nullptr;
+    const int zs = apart ? ks + 1 : ks;  // partial-sum slices: the LoRA split last
     const int n = ns[0];
-    rc = ensure_buf(c, &c->part, &c->part_cap, static_cast<size_t>(ks) * m * n, stream);
+    rc = ensure_buf(c, &c->part, &c->part_cap, static_cast<size_t>(zs) * m * n, stream);
     if (rc != MP_OK) return rc;
-    const int base_kt = (ws[0]->d.k + mp::kBlockK - 1) / mp::kBlockK;
-    p.ksplit = ks;
+    const int k = ws[0]->d.k;
+    const int base_kt = (k + mp::kBlockK - 1) / mp::kBlockK;
+    p.ksplit = zs;
     p.kt_per_split = (base_kt + ks - 1) / ks;
     p.part = c->part;
     p.part_ld = n;
+    if (apart) {
+      // every buffer of the side chain is sized before the fork, so nothing
+      // grows (or is freed) while it runs
+      // pre-GEMM splits: as many as fit on the free pairs (256-token tiles)
+      const int pre_max = std::max(
+          1, std::min(mp::kMaxSplits,
+                      side_pairs / (pairs_of(sep->rtot) * ((mi + mp::kMaxTok - 1) / mp::kMaxTok))));
+      const mp::SplitChoice pre =
+          mp::choose_ksplit(mi, pairs_of(sep->rtot), base_kt, sep->rtot, pre_max);
+      if (pre.ksplit > 1) {
+        rc = ensure_buf(c, &c->part_side, &c->part_side_cap,
+                        static_cast<size_t>(pre.ksplit) * m * sep->rtot, stream);
+        if (rc != MP_OK) return rc;
+      }
+      rc = ensure_side(c);
+      if (rc != MP_OK) return rc;
+      p.lora_apart = 1;
+      MP_CUDA(c, cudaEventRecord(c->ev_fork, stream));
+      MP_CUDA(c, cudaStreamWaitEvent(c->side, c->ev_fork, 0));
+      rc = launch_lora_down(c, *sep->tm_a, sep->rtot, *sep->es, x, ldx, k, m, c->side, pre_max,
+                            true);
+      if (rc == MP_OK) {
+        ProjParams pl = p;
+        pl.z_first = ks;
+        pl.z_count = 1;
+        rc = run_launch(c, pl, c->side, "proj_pair_kernel (LoRA split)");
+      }
+      // joined even after a failed launch, so a capture never ends with the
+      // side stream forked
+      cudaError_t ej = cudaEventRecord(c->ev_join, c->side);
+      if (rc != MP_OK) return rc;
+      if (ej != cudaSuccess) return cuda_fail(c, ej, "cudaEventRecord (join)");
+      p.z_first = 0;
+      p.z_count = ks;
+    }
     rc = run_launch(c, p, stream, "proj_pair_kernel (split K)");
+    if (apart) {
+      cudaError_t ew = cudaStreamWaitEvent(stream, c->ev_join, 0);
+      if (rc != MP_OK) return rc;
+      if (ew != cudaSuccess) return cuda_fail(c, ew, "cudaStreamWaitEvent (join)");
+    }
     if (rc != MP_OK) return rc;
     mp::ReduceParams rp;
     std::memset(&rp, 0, sizeof(rp));  // scale.enabled = 0: the sums are stored unscaled
     rp.part = c->part;
-    rp.ksplit = ks;
+    rp.ksplit = zs;
     rp.M = m;
     rp.R = n;
     rp.part_ld = n;
@@ -983,7 +1089,11 @@ int mp_destroy(mp_ctx* c) {
   cudaFree(c->err_word);
   cudaFree(c->scratch);
   cudaFree(c->part);
+  cudaFree(c->part_side);
   cudaFree(c->flags);
+  if (c->side != nullptr) cudaStreamDestroy(c->side);
+  if (c->ev_fork != nullptr) cudaEventDestroy(c->ev_fork);
+  if (c->ev_join != nullptr) cudaEventDestroy(c->ev_join);
   for (void* p : c->retired) cudaFree(p);
   for (auto& kv : c->shared) {
     cudaFree(kv.second.a);
@@ -1268,6 +1378,9 @@ int mp_linear(mp_ctx* c, const mp_weight* wc, const void* x, int64_t ldx, void* 
     pro.rtot = st->rpad;
     pro.es = &es;
     rc = launch_projections(c, wl, yl, ll, sl, cl, st->rpad, 1, x, ldx, m, s, &pro);
+    if (rc != kFallback) return rc;
+    rc = launch_projections(c, wl, yl, ll, sl, cl, st->rpad, 1, x, ldx, m, s, nullptr, nullptr,
+                            nullptr, true, &pro);
     if (rc != kFallback) return rc;
     rc = launch_lora_down(c, st->tm_a, st->rpad, es, x, ldx, w->d.k, m, s);
     if (rc != MP_OK) return rc;

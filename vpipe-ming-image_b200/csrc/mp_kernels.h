@@ -108,6 +108,14 @@ struct ProjParams {
   int32_t kt_per_split;
   float* part;
   int32_t part_ld;
+  // With lora_apart != 0 the appended LoRA K tiles are a split of their own:
+  // splits z < ksplit - 1 run base K tiles only, split ksplit - 1 runs only
+  // the LoRA K tiles (its partial sums are T·B_stack^T). A launch runs the
+  // splits [z_first, z_first + z_count) (z_count 0: all of them), so the
+  // LoRA split can go in a launch of its own once T is ready.
+  int32_t lora_apart;
+  int32_t z_first;
+  int32_t z_count;
   // Fused rank-space prologue (n_pre > 0): before their member tiles, the
   // pairs with the fewest member tiles run n_pre prologue units, each the
   // full-K product of 512 token rows x 256 rank rows of T = scale ⊙ (x ·

@@ -209,8 +209,9 @@ struct Tile {
 __device__ __forceinline__ Tile decode_tile(const ProjParams& p, int tile, int rank, int base_kt) {
   Tile t;
   const int per_split = p.n_pairs * p.n_ttiles;
-  t.z = tile / per_split;
-  const int rem = tile - t.z * per_split;
+  const int zl = tile / per_split;  // split within this launch
+  const int rem = tile - zl * per_split;
+  t.z = p.z_first + zl;
   int pair, tt;
   if (p.tile_group <= 1) {
     // token tile fastest: the pairs running at one time share a few feature
@@ -245,8 +246,13 @@ __device__ __forceinline__ Tile decode_tile(const ProjParams& p, int tile, int r
   t.kt_begin = 0;
   t.kt_end = base_kt + p.mem[mi].lora_ktiles;
   if (p.ksplit > 1) {
-    t.kt_begin = t.z * p.kt_per_split;
-    if (t.z + 1 < p.ksplit) t.kt_end = min(base_kt, t.kt_begin + p.kt_per_split);
+    const int base_splits = p.lora_apart ? p.ksplit - 1 : p.ksplit;
+    if (t.z >= base_splits) {
+      t.kt_begin = base_kt;  // the LoRA split: the appended K tiles only
+    } else {
+      t.kt_begin = t.z * p.kt_per_split;
+      if (t.z + 1 < p.ksplit) t.kt_end = min(base_kt, t.kt_begin + p.kt_per_split);
+    }
   }
   return t;
 }
@@ -1501,7 +1507,8 @@ cudaError_t launch_proj_pair(const ProjParams& p, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   ProjParams q = p;
   q.n_ttiles = (p.M + p.n_tok - 1) / p.n_tok;
-  q.n_tiles = q.n_pairs * q.n_ttiles * (p.ksplit > 1 ? p.ksplit : 1);
+  q.n_tiles = q.n_pairs * q.n_ttiles *
+              (p.ksplit > 1 ? (p.z_count > 0 ? p.z_count : p.ksplit - p.z_first) : 1);
   const bool coop = q.n_pre > 0;
   if (coop && p.n_tok != kMaxTileTok) return cudaErrorInvalidValue;  // prologue units need NT 512
   const int pairs = coop ? g_max_pairs[dev]
