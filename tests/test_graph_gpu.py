@@ -123,3 +123,40 @@ def test_side_stream_lora_chain_replays_bit_identical(ctx):
         for i in range(8):
             ctx.set_strength(i, 1.0)
         w.free()
+
+
+def test_side_stream_first_use_inside_a_capture():
+    """The side stream, its events and the partial-sum buffers are created by
+    the first split-K call with live slots; when that first call is made
+    inside a CUDA-graph capture, the capture holds it and replays the eager
+    bits."""
+    from mingproj.proj import Context
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(13)
+    c2 = Context(0)
+    m = 256
+    try:
+        cc, sc, bi = _device_affine(gen, H, H, 8, dev)
+        w = c2.upload(H, H, 8, cc, sc, bi)
+        for slot in range(8):
+            a = (torch.randn((32, H), device=dev, generator=gen) / 32 ** 0.5).to(torch.bfloat16)
+            b = (torch.randn((H, 32), device=dev, generator=gen) * 0.01).to(torch.bfloat16)
+            w.bind(slot, a, b)
+            c2.set_strength(slot, 0.25 * (slot - 3))
+        xs = torch.randn((m, H), device=dev, generator=gen).to(torch.bfloat16)
+        out = torch.empty((m, H), dtype=torch.bfloat16, device=dev)
+        torch.cuda.synchronize(dev)
+        c2.reset_engagement()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            c2.linear(w, xs, out)
+        assert c2.engagement()["kernels"] == 5, "the side-stream chain was not captured"
+        g.replay()
+        ref = c2.linear(w, xs)
+        torch.cuda.synchronize(dev)
+        assert torch.equal(_bits(out), _bits(ref))
+        del g
+        c2.sync_check()
+        w.free()
+    finally:
+        c2.close()

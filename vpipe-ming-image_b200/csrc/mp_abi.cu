@@ -323,10 +323,19 @@ int ensure_flags(mp_ctx* c, size_t n, cudaStream_t stream) {
 // The side stream and fork / join events of the concurrent LoRA chain,
 // created on first use (the context's device is current).
 int ensure_side(mp_ctx* c) {
-  if (c->side != nullptr) return MP_OK;
-  MP_CUDA(c, cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking));
-  MP_CUDA(c, cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming));
-  MP_CUDA(c, cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming));
+  if (c->side != nullptr && c->ev_fork != nullptr && c->ev_join != nullptr) return MP_OK;
+  // not stream operations; relaxed, so a first use inside a capture in
+  // global mode is not refused
+  cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+  cudaThreadExchangeStreamCaptureMode(&mode);
+  cudaError_t e = cudaSuccess;
+  if (c->side == nullptr) e = cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking);
+  if (e == cudaSuccess && c->ev_fork == nullptr)
+    e = cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming);
+  if (e == cudaSuccess && c->ev_join == nullptr)
+    e = cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming);
+  cudaThreadExchangeStreamCaptureMode(&mode);
+  if (e != cudaSuccess) return cuda_fail(c, e, "side stream / events");
   return MP_OK;
 }
 
