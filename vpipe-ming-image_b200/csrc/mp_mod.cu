@@ -17,7 +17,7 @@
 //  * Lane-per-row path (K a multiple of 256 -- the reference's 256 and the
 //    [4H, 3840] shape -- and H a multiple of 32): tiles of 32 rows, each
 //    lane one row, the rows streamed through a per-warp ring in shared
-//    memory (one TMA per step); per 64-wide group every token's dot is exact integer
+//    memory (one TMA per step); per 64-wide group every token's dot is an integer
 //    dp4a against 8-bit limbs of its temb values (packed codes) or packed
 //    fp32 FMAs (bf16 weights), temb broadcast from shared memory, no
 //    cross-lane reduction (see mod_lane_kernel).
@@ -145,7 +145,7 @@ __device__ __forceinline__ void warp_slice(long long total, long long w, long lo
 // step (the rows' next 128 bytes: 2 groups w8, 4 w4, 1 bf16) the lane reads
 // its row's 16-byte chunks from the warp's ring slot and forms every token's
 // dot against values all lanes read from shared memory at the same address (a
-// broadcast): for packed codes exact integer dots (dp4a) with the token's temb
+// broadcast): for packed codes integer dots (dp4a) with the token's temb
 // limbs (see lane_fixed_bytes), for bf16 weights packed fp32 FMAs with its
 // fp32 temb values in two interleaved chains in K order. No lane exchanges
 // anything: a packed group folds in as s * sum(q t) + b * sum(t), bf16
@@ -247,25 +247,31 @@ __device__ __forceinline__ uint32_t pick4p(const uint4& v, int i) {
 }
 
 // Packed codes take integer dot products. Each token's temb values of a
-// 64-wide group (bf16: 8 significant bits) are written exactly as integers
-// T = t * 2^(21 - E), E the exponent of the group's largest |t| (values more
-// than 14 binades below it are rounded to the nearest integer: an absolute
-// error of at most 2^(E - 22)), and T as three signed 8-bit limbs,
-// T = L0 + 2^8 L1 + 2^16 L2 (|L2| <= 64). Then sum_k q_k t_k =
-// 2^(E - 21) (A0 + 2^8 A1 + 2^16 A2) with A_l = sum_k q_k L_l,k exact in
-// 32-bit integers, formed four codes at a time with dp4a. Integer sums do
+// 64-wide group (bf16: 8 significant bits) are written as integers
+// T = round(t * 2^(13 - E)), E the exponent of the group's largest |t|:
+// exact for every value within 6 binades of the largest, the smaller ones
+// rounded to the nearest integer (an absolute error of at most 2^(E - 14),
+// 2^-14 of the group's largest value; the output is rounded to bf16, 2^-9),
+// and T as two signed 8-bit limbs, T = L0 + 2^8 L1 (|L1| <= 64). Then
+// sum_k q_k t_k = 2^(E - 13) (A0 + 2^8 A1) with A_l = sum_k q_k L_l,k exact
+// in 32-bit integers, formed four codes at a time with dp4a. Integer sums do
 // not depend on their order, so a token's result is the same in any launch.
+// (Three limbs, exact to 14 binades, cost a third more dp4a and limb loads:
+// the w4 call is bound by its instruction stream.)
 //
 // Shared memory for packed codes: the block table, the limbs int8
-// [MT][K / 64][3][64] (w4: within each 8 values the even ones first, as a
-// code word's low nibbles hold them), per (group, token) the scale 2^(E - 21),
-// the temb sum and the three limb sums [K / 64][MT]; for bf16 weights temb as
-// fp32 [MT][K] and nothing else. Then the warps' rings.
+// [MT][K / 64][kLimbs][64] (w4: within each 8 values the even ones first, as
+// a code word's low nibbles hold them), per (group, token) the scale
+// 2^(E - 13), the temb sum and the limb sums [K / 64][MT]; for bf16 weights
+// temb as fp32 [MT][K] and nothing else. Then the warps' rings.
+constexpr int kLimbs = 2;
+constexpr int kLimbShift = 8 * kLimbs - 3;  // T = t * 2^(kLimbShift - E), |T| < 2^(kLimbShift + 1)
 template <int BITS, int MT>
 __host__ __device__ __forceinline__ size_t lane_fixed_bytes(int n_blocks, int K) {
   const size_t blk = (static_cast<size_t>(n_blocks) * sizeof(ModBlock) + 15) & ~size_t(15);
   const size_t t = BITS == 0 ? static_cast<size_t>(MT) * K * 4
-                             : static_cast<size_t>(MT) * K * 3 + static_cast<size_t>(K / 64) * MT * 20;
+                             : static_cast<size_t>(MT) * K * kLimbs +
+                                   static_cast<size_t>(K / 64) * MT * (8 + 4 * kLimbs);
   return (blk + t + 127) & ~size_t(127);
 }
 
@@ -294,9 +300,9 @@ __global__ void __launch_bounds__(kLaneThreads, 1) mod_lane_kernel(const __grid_
   const int K4 = p.K / 4;
   float4* tq = reinterpret_cast<float4*>(mod_smem + blk_bytes);                 // bf16: [MT][K / 4]
   int8_t* tl = reinterpret_cast<int8_t*>(mod_smem + blk_bytes);                 // packed: limbs
-  float* tmul = reinterpret_cast<float*>(tl + static_cast<size_t>(MT) * p.K * 3);  // [G][MT]
-  float* tsum = tmul + G * MT;                                                  // [G][MT]
-  int* tls = reinterpret_cast<int*>(tsum + G * MT);                             // [G][MT][3]
+  float* tmul = reinterpret_cast<float*>(tl + static_cast<size_t>(MT) * p.K * kLimbs);  // [G][MT]
+  float* tsum = tmul + G * MT;                                                       // [G][MT]
+  int* tls = reinterpret_cast<int*>(tsum + G * MT);                                  // [G][MT][kLimbs]
   const int lane = threadIdx.x & 31;
   const uint64_t neg_magic2 = f32x2(-p.code_magic, -p.code_magic);
   const int steps_per_tile = G / L::kStepGroups;
@@ -415,33 +421,31 @@ __global__ void __launch_bounds__(kLaneThreads, 1) mod_lane_kernel(const __grid_
       }
       // E: the exponent of amax (0 for an all-zero group)
       const int e = amax > 0.0f ? static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu) - 127 : 0;
-      int lsum[3] = {0, 0, 0};
-      int8_t* row = tl + (static_cast<size_t>(n) * G + gi) * 192;
+      int lsum[kLimbs] = {};
+      int8_t* row = tl + (static_cast<size_t>(n) * G + gi) * (64 * kLimbs);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int k = wl + 32 * h;
-        const int T = __float2int_rn(ldexpf(h == 0 ? t0 : t1, 21 - e));
-        const int l0 = static_cast<int>(static_cast<int8_t>(T & 0xFF));
-        const int t1r = (T - l0) >> 8;
-        const int l1 = static_cast<int>(static_cast<int8_t>(t1r & 0xFF));
-        const int l2 = (t1r - l1) >> 8;
-        row[limb_pos<BITS>(k)] = static_cast<int8_t>(l0);
-        row[64 + limb_pos<BITS>(k)] = static_cast<int8_t>(l1);
-        row[128 + limb_pos<BITS>(k)] = static_cast<int8_t>(l2);
-        lsum[0] += l0;
-        lsum[1] += l1;
-        lsum[2] += l2;
+        int T = __float2int_rn(ldexpf(h == 0 ? t0 : t1, kLimbShift - e));
+#pragma unroll
+        for (int l = 0; l < kLimbs; ++l) {
+          // the last limb keeps the rest (|L| <= 64); the others are the
+          // signed low byte, the remainder shifted down exactly
+          const int lv = l + 1 < kLimbs ? static_cast<int>(static_cast<int8_t>(T & 0xFF)) : T;
+          row[64 * l + limb_pos<BITS>(k)] = static_cast<int8_t>(lv);
+          lsum[l] += lv;
+          T = (T - lv) >> 8;
+        }
       }
 #pragma unroll
-      for (int l = 0; l < 3; ++l)
+      for (int l = 0; l < kLimbs; ++l)
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) lsum[l] += __shfl_xor_sync(0xFFFFFFFFu, lsum[l], o);
       if (wl == 0) {
-        tmul[i] = ldexpf(1.0f, e - 21);
+        tmul[i] = ldexpf(1.0f, e - kLimbShift);
         tsum[i] = v;
-        tls[3 * i] = lsum[0];
-        tls[3 * i + 1] = lsum[1];
-        tls[3 * i + 2] = lsum[2];
+#pragma unroll
+        for (int l = 0; l < kLimbs; ++l) tls[kLimbs * i + l] = lsum[l];
       }
     }
   }
@@ -526,19 +530,19 @@ __global__ void __launch_bounds__(kLaneThreads, 1) mod_lane_kernel(const __grid_
           y[m] += (f32x2_lo(acc[m][0]) + f32x2_hi(acc[m][0])) +
                   (f32x2_lo(acc[m][1]) + f32x2_hi(acc[m][1]));
       } else {
-        // packed codes: exact integer dots with the three temb limbs
+        // packed codes: integer dots (exact in 32 bits) with the temb limbs
         // two accumulators per limb (even / odd code words) up to 4 tokens:
         // integer sums, so the split changes nothing but the dependency chains
         constexpr int kB = MT <= 4 ? MT : 1;
-        int a[MT][3], b[kB][3];
+        int a[MT][kLimbs], b[kB][kLimbs];
 #pragma unroll
         for (int m = 0; m < MT; ++m)
 #pragma unroll
-          for (int l = 0; l < 3; ++l) a[m][l] = 0;
+          for (int l = 0; l < kLimbs; ++l) a[m][l] = 0;
 #pragma unroll
         for (int m = 0; m < kB; ++m)
 #pragma unroll
-          for (int l = 0; l < 3; ++l) b[m][l] = 0;
+          for (int l = 0; l < kLimbs; ++l) b[m][l] = 0;
 #pragma unroll
         for (int c = 0; c < L::kCpg; ++c) {
           const int ch = gi * L::kCpg + c;
@@ -559,9 +563,9 @@ __global__ void __launch_bounds__(kLaneThreads, 1) mod_lane_kernel(const __grid_
           }
 #pragma unroll
           for (int m = 0; m < MT; ++m) {
-            const int8_t* lr = tl + (static_cast<size_t>(m) * G + g_abs) * 192 + c * F::kPer;
+            const int8_t* lr = tl + (static_cast<size_t>(m) * G + g_abs) * (64 * kLimbs) + c * F::kPer;
 #pragma unroll
-            for (int l = 0; l < 3; ++l) {
+            for (int l = 0; l < kLimbs; ++l) {
               int& bb = MT <= 4 ? b[m < kB ? m : 0][l] : a[m][l];
               const uint4 l0 = *reinterpret_cast<const uint4*>(lr + 64 * l);
               if constexpr (BITS == 8) {
@@ -589,14 +593,14 @@ __global__ void __launch_bounds__(kLaneThreads, 1) mod_lane_kernel(const __grid_
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
           const int i = g_abs * MT + m;
-          int s3[3];
+          int sl[kLimbs];
 #pragma unroll
-          for (int l = 0; l < 3; ++l)
-            s3[l] = (MT <= 4 ? a[m][l] + b[m < kB ? m : 0][l] : a[m][l]) - off * tls[3 * i + l];
-          const float a0 = static_cast<float>(s3[0]);
-          const float a1 = static_cast<float>(s3[1]);
-          const float a2 = static_cast<float>(s3[2]);
-          const float d = __fmul_rn(__fmaf_rn(65536.0f, a2, __fmaf_rn(256.0f, a1, a0)), tmul[i]);
+          for (int l = 0; l < kLimbs; ++l)
+            sl[l] = (MT <= 4 ? a[m][l] + b[m < kB ? m : 0][l] : a[m][l]) - off * tls[kLimbs * i + l];
+          float dsum = static_cast<float>(sl[kLimbs - 1]);
+#pragma unroll
+          for (int l = kLimbs - 2; l >= 0; --l) dsum = __fmaf_rn(256.0f, dsum, static_cast<float>(sl[l]));
+          const float d = __fmul_rn(dsum, tmul[i]);
           y[m] += __fmaf_rn(sc, d, __fmul_rn(bi, tsum[i]));
         }
       }
