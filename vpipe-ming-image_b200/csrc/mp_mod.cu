@@ -158,7 +158,6 @@ constexpr int kLaneTok = 8;  // tokens of one launch, at most
 #define MP_LANE_WARPS 16
 #endif
 constexpr int kLaneWarps = MP_LANE_WARPS;  // warps per CTA (one CTA per SM: the rings)
-constexpr int kLaneThreads = 32 * kLaneWarps;
 
 // A step is 128 bytes of each of the tile's 32 rows: 2 groups (w8), 4 (w4)
 // or 1 (bf16).
@@ -289,8 +288,8 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
   return d;
 }
 
-template <int BITS, int MT, int RING>
-__global__ void __launch_bounds__(kLaneThreads, 1) mod_lane_kernel(const __grid_constant__ ModParams p) {
+template <int BITS, int MT, int RING, int W>
+__global__ void __launch_bounds__(32 * W, 1) mod_lane_kernel(const __grid_constant__ ModParams p) {
   using L = LaneFmt<BITS>;
   using F = ModFmt<BITS>;
   extern __shared__ __align__(128) uint8_t mod_smem[];
@@ -310,8 +309,8 @@ __global__ void __launch_bounds__(kLaneThreads, 1) mod_lane_kernel(const __grid_
   // this warp's tiles [t_begin, t_end) of the launch's n_blocks * tiles_per_block
   // (32-bit arithmetic when the products fit: 64-bit divisions cost ~1 us here)
   const long long total_tiles = static_cast<long long>(p.n_blocks) * tiles_per_block;
-  const long long nwarps = static_cast<long long>(gridDim.x) * kLaneWarps;
-  const long long gw = static_cast<long long>(blockIdx.x) * kLaneWarps + (threadIdx.x >> 5);
+  const long long nwarps = static_cast<long long>(gridDim.x) * W;
+  const long long gw = static_cast<long long>(blockIdx.x) * W + (threadIdx.x >> 5);
   long long t_begin, t_end;
   if (total_tiles * nwarps < (1ll << 32)) {
     const uint32_t tt = static_cast<uint32_t>(total_tiles), nw = static_cast<uint32_t>(nwarps),
@@ -334,8 +333,8 @@ __global__ void __launch_bounds__(kLaneThreads, 1) mod_lane_kernel(const __grid_
   const uint32_t smem0 = smem_u32(mod_smem);
   const uint32_t data0 =
       (smem0 + static_cast<uint32_t>(lane_fixed_bytes<BITS, MT>(p.n_blocks, p.K)) + 1023u) & ~1023u;
-  const uint32_t aux0 = data0 + static_cast<uint32_t>(kLaneWarps * RING * L::kData);
-  const uint32_t bar0 = aux0 + static_cast<uint32_t>(kLaneWarps * RING * L::kAux);
+  const uint32_t aux0 = data0 + static_cast<uint32_t>(W * RING * L::kData);
+  const uint32_t bar0 = aux0 + static_cast<uint32_t>(W * RING * L::kAux);
   const uint32_t wdata = data0 + static_cast<uint32_t>(wi * RING * L::kData);
   const uint32_t waux = aux0 + static_cast<uint32_t>(wi * RING * L::kAux);
   const uint32_t wbar = bar0 + static_cast<uint32_t>(wi * RING * 8);
@@ -402,14 +401,14 @@ __global__ void __launch_bounds__(kLaneThreads, 1) mod_lane_kernel(const __grid_
     // temb sum (a fixed xor tree: the same bits for a token whatever else the
     // launch holds)
     const int wl = threadIdx.x & 31;
-    for (int i = threadIdx.x >> 5; i < G * MT; i += kLaneWarps) {
+    for (int i = threadIdx.x >> 5; i < G * MT; i += W) {
       const int gi = i / MT, n = i - (i / MT) * MT;
       float t0 = tp0, t1 = tp1;  // the first pair's values are loaded
-      if (i >= kLaneWarps && n < p.M) {
+      if (i >= W && n < p.M) {
         const uint16_t* t = p.temb + static_cast<size_t>(n) * p.K + gi * 64;
         t0 = bf16_bits_to_f32(t[wl]);
         t1 = bf16_bits_to_f32(t[32 + wl]);
-      } else if (i >= kLaneWarps) {
+      } else if (i >= W) {
         t0 = t1 = 0.0f;
       }
       float amax = fmaxf(fabsf(t0), fabsf(t1));
@@ -792,29 +791,38 @@ cudaError_t launch_mod_warp(const ModParams& p, cudaStream_t stream) {
 
 constexpr size_t kModSmemLimit = 227 * 1024;
 
-template <int BITS, int MT, int RING>
+template <int BITS, int MT, int RING, int W>
 cudaError_t launch_mod_lane_ring(const ModParams& p, cudaStream_t stream) {
   const size_t smem = lane_fixed_bytes<BITS, MT>(p.n_blocks, p.K) + 1024 +
-                      static_cast<size_t>(kLaneWarps) * RING * LaneFmt<BITS>::kSlot;
+                      static_cast<size_t>(W) * RING * LaneFmt<BITS>::kSlot;
   const long long tiles = static_cast<long long>(p.n_blocks) * p.N / kLaneRows;
   static std::atomic<int> cache[64];
-  return launch_persistent(mod_lane_kernel<BITS, MT, RING>, kLaneThreads, p, smem, tiles, cache,
+  return launch_persistent(mod_lane_kernel<BITS, MT, RING, W>, 32 * W, p, smem, tiles, cache,
                            stream);
 }
 
-// The deepest ring (steps in flight per warp, 6 at most) that fits the
+// Packed codes for one or two tokens take kLaneWarpsWide warps per CTA with
+// two-slot rings when those fit (the w4 call is paced by its instruction
+// stream, and more warps hide its shared-memory and dp4a latencies: K 256,
+// w4 M = 1 22.5 -> 20.7 us, M = 2 28.7 -> 26.7 us, w8 M = 1 30.8 -> 28.7 us);
+// more tokens per launch need the registers of kLaneWarps warps. Otherwise
+// the deepest ring (steps in flight per warp, 6 at most) that fits the
 // shared memory beside the block table and the temb copy (which grows with K).
+constexpr int kLaneWarpsWide = 24;
 template <int BITS, int MT>
 cudaError_t launch_mod_lane(const ModParams& p, cudaStream_t stream) {
   const size_t fixed = lane_fixed_bytes<BITS, MT>(p.n_blocks, p.K);
-  auto fits = [&](int ring) {
-    return fixed + 1024 + static_cast<size_t>(kLaneWarps) * ring * LaneFmt<BITS>::kSlot <=
+  auto fits = [&](int warps, int ring) {
+    return fixed + 1024 + static_cast<size_t>(warps) * ring * LaneFmt<BITS>::kSlot <=
            kModSmemLimit;
   };
-  if (fits(6)) return launch_mod_lane_ring<BITS, MT, 6>(p, stream);
-  if (fits(4)) return launch_mod_lane_ring<BITS, MT, 4>(p, stream);
-  if (fits(3)) return launch_mod_lane_ring<BITS, MT, 3>(p, stream);
-  if (fits(2)) return launch_mod_lane_ring<BITS, MT, 2>(p, stream);
+  if constexpr (BITS != 0 && MT <= 2) {
+    if (fits(kLaneWarpsWide, 2)) return launch_mod_lane_ring<BITS, MT, 2, kLaneWarpsWide>(p, stream);
+  }
+  if (fits(kLaneWarps, 6)) return launch_mod_lane_ring<BITS, MT, 6, kLaneWarps>(p, stream);
+  if (fits(kLaneWarps, 4)) return launch_mod_lane_ring<BITS, MT, 4, kLaneWarps>(p, stream);
+  if (fits(kLaneWarps, 3)) return launch_mod_lane_ring<BITS, MT, 3, kLaneWarps>(p, stream);
+  if (fits(kLaneWarps, 2)) return launch_mod_lane_ring<BITS, MT, 2, kLaneWarps>(p, stream);
   return cudaErrorInvalidValue;
 }
 
