@@ -557,7 +557,10 @@ __global__ void __launch_bounds__(32 * W, 1) mod_lane_kernel(const __grid_consta
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               cw[2 * i] = ws[i] & 0x0F0F0F0Fu;
-              cw[2 * i + 1] = (ws[i] >> 4) & 0x0F0F0F0Fu;
+              // the high nibbles in place (16 q) when they have accumulators
+              // of their own (divided by 16 at the group's end, exactly):
+              // one instruction fewer than shifting them down
+              cw[2 * i + 1] = MT <= 4 ? ws[i] & 0xF0F0F0F0u : (ws[i] >> 4) & 0x0F0F0F0Fu;
             }
           }
 #pragma unroll
@@ -595,7 +598,9 @@ __global__ void __launch_bounds__(32 * W, 1) mod_lane_kernel(const __grid_consta
           int sl[kLimbs];
 #pragma unroll
           for (int l = 0; l < kLimbs; ++l)
-            sl[l] = (MT <= 4 ? a[m][l] + b[m < kB ? m : 0][l] : a[m][l]) - off * tls[kLimbs * i + l];
+            sl[l] = (MT <= 4 ? a[m][l] + (BITS == 4 ? b[m < kB ? m : 0][l] >> 4 : b[m < kB ? m : 0][l])
+                             : a[m][l]) -
+                    off * tls[kLimbs * i + l];
           float dsum = static_cast<float>(sl[kLimbs - 1]);
 #pragma unroll
           for (int l = kLimbs - 2; l >= 0; --l) dsum = __fmaf_rn(256.0f, dsum, static_cast<float>(sl[l]));
