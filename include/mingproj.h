@@ -179,6 +179,12 @@ int mp_state_version(const mp_ctx* ctx, uint64_t* version);
  * bf16 in / bf16 out, f32 accumulation, one pass over K with the adapters
  * appended as extra K tiles. x: device bf16, 16-byte aligned, ldx a
  * multiple of 8 elements. y: device bf16, 16-byte aligned, ldy >= n and a multiple of 8.
+ * Over few rows per image (K split across CTA pairs) with live slots, the
+ * call forks a stream of the context's own (an event record on `stream` and
+ * a wait), runs the rank-space pre-GEMM and the LoRA K tiles there beside the
+ * base K splits, and joins it back into `stream` before the final reduce: the
+ * call stays ordered on `stream` like every other, and a CUDA-graph capture
+ * of `stream` holds the fork and the join.
  * Replaces: lin (src/ming-dit.cc:1763-1771). */
 int mp_linear(mp_ctx* ctx, const mp_weight* w, const void* x, int64_t ldx, void* y, int64_t ldy,
               int m, void* stream);
