@@ -912,11 +912,14 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
         pl.z_count = 1;
         rc = run_launch(c, pl, c->side, "proj_pair_kernel (LoRA split)");
       }
-      // joined even after a failed launch, so a capture never ends with the
-      // side stream forked
-      cudaError_t ej = cudaEventRecord(c->ev_join, c->side);
-      if (rc != MP_OK) return rc;
-      if (ej != cudaSuccess) return cuda_fail(c, ej, "cudaEventRecord (join)");
+      if (rc != MP_OK) {
+        // joined even after a failed launch, so a capture never ends with
+        // the side stream forked
+        if (cudaEventRecord(c->ev_join, c->side) == cudaSuccess)
+          (void)cudaStreamWaitEvent(stream, c->ev_join, 0);
+        return rc;
+      }
+      MP_CUDA(c, cudaEventRecord(c->ev_join, c->side));
       p.z_first = 0;
       p.z_count = ks;
     }
