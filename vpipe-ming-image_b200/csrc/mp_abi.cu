@@ -574,7 +574,10 @@ struct SplitChoice {
 // set-up and epilogue, 74 pairs run at once (one CTA per SM), and the second
 // pass of a split launch costs ~2 us plus its traffic at ~4 TB/s. At most
 // `max_split` splits.
-SplitChoice choose_ksplit(int m, int pairs, int base_kt, int r, int max_split = kMaxSplits) {
+// With room_pairs > 0 only the choices whose splits leave room for one more
+// split's tiles beside them within room_pairs CTA pairs are considered.
+SplitChoice choose_ksplit(int m, int pairs, int base_kt, int r, int max_split = kMaxSplits,
+                          int room_pairs = 0) {
   SplitChoice best{kMaxTok, 1, 0.0};
   double best_us = 1e300;
   for (int nt : {kMaxTileTok, kMaxTok}) {
@@ -583,6 +586,7 @@ SplitChoice choose_ksplit(int m, int pairs, int base_kt, int r, int max_split = 
     for (int s = 1; s <= max_split && s <= base_kt; ++s) {
       const int kps = (base_kt + s - 1) / s;
       if ((base_kt + kps - 1) / kps != s) continue;  // every split gets at least one tile
+      if (room_pairs > 0 && pairs * tiles * (s + 1) > room_pairs) continue;
       const long long waves = (pairs * tiles * s + 73) / 74;
       double us = static_cast<double>(waves) * (kps * stage_cycles + 6000.0) / 1900.0;
       if (s > 1) us += 2.0 + (static_cast<double>(s) * 4.0 + 2.0) * m * r / 4.0e6;
@@ -742,18 +746,19 @@ int launch_projections(mp_ctx* c, const mp_weight* const* ws, void* const* ys,
     if (msplit.ksplit > 1) {
       const int P = mp::resident_pairs();
       const int base_kt = (ws[0]->d.k + mp::kBlockK - 1) / mp::kBlockK;
-      for (int pass = 0; pass < 2 && side_pairs == 0 && msplit.ksplit > 1; ++pass) {
-        const long long per_split =
-            static_cast<long long>(pairs_of(ns[0])) * ((mi + msplit.n_tok - 1) / msplit.n_tok);
-        const long long free_pairs = P - per_split * msplit.ksplit;
-        if (free_pairs >= std::max<long long>(per_split, kSidePairs)) {
-          side_pairs = static_cast<int>(free_pairs);
-        } else if (pass == 0) {
-          const long long fit = (P - per_split) / per_split;  // base splits that leave room
-          if (fit < 2) break;
-          msplit = mp::choose_ksplit(mi, pairs_of(ns[0]), base_kt, ns[0],
-                                     static_cast<int>(std::min<long long>(fit, msplit.ksplit)));
-          if (msplit.ksplit > 1) n_tok = msplit.n_tok;
+      const size_t per_split = static_cast<size_t>(mi) * ns[0] * sizeof(float);
+      const int most = static_cast<int>(
+          std::min<size_t>(mp::kMaxSplits, std::max<size_t>(1, kSplitBytes / per_split)));
+      // the base splits (token tile and count) that leave room for the LoRA split
+      const mp::SplitChoice room =
+          mp::choose_ksplit(mi, pairs_of(ns[0]), base_kt, ns[0], most, P);
+      if (room.ksplit > 1) {
+        const long long used = static_cast<long long>(pairs_of(ns[0])) *
+                               ((mi + room.n_tok - 1) / room.n_tok) * room.ksplit;
+        if (P - used >= kSidePairs) {
+          msplit = room;
+          n_tok = room.n_tok;
+          side_pairs = static_cast<int>(P - used);
         }
       }
     }
