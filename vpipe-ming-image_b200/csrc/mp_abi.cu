@@ -292,6 +292,8 @@ int ensure_buf(mp_ctx* c, T** p, size_t* cap, size_t elems, cudaStream_t stream)
       c->retired.push_back(*p);
     } else {
       cudaStreamSynchronize(stream);
+      // the side stream's LoRA chain may still read or write context buffers
+      if (c->side != nullptr) cudaStreamSynchronize(c->side);
       cudaFree(*p);
     }
     *p = nullptr;
